@@ -1,0 +1,517 @@
+/*
+ * gdr_oracle.c -- TEST INFRASTRUCTURE ONLY.
+ *
+ * An f64 CPU restatement of RHIZOME's gated delta-rule (GDR) reference op and
+ * of the helpers its tests use. It is the checker for the CUDA library in
+ * rhizome_b200/ and the timed CPU baseline in bench.py; no product code path
+ * links, loads or calls it.
+ *
+ * Parity pin: the reference is Rust (crates/ops) and no Rust toolchain exists
+ * where this is built, so the reference cannot be run here. This file is
+ * pinned instead by (1) every known-answer test and equivalence property the
+ * reference's own tests hold for this path (crates/ops/src/delta.rs:245-369,
+ * crates/ops/src/rng.rs:109-182), re-run against this file in
+ * tests/test_oracle.py, (2) analytic closed forms (d = 1, alpha = 0, beta = 0)
+ * and (3) an independent implementation of the same Philox-4x32-10 block
+ * function (cuRAND's), compared through tests/golden/philox_kat.json.
+ *
+ * Arithmetic follows the Rust code's operation order exactly. Build with
+ * -ffp-contract=off (no FMA contraction, as rustc emits none) so each
+ * expression rounds the way the Rust expression does; ln/cos/exp come from
+ * the platform libm as they do for Rust std on Linux.
+ */
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------------ */
+/* Philox-4x32-10, crates/ops/src/rng.rs:7-107                               */
+/* ------------------------------------------------------------------------ */
+
+/* Round constants and key bumps: crates/ops/src/rng.rs:7-10. */
+#define PHX_W0 0x9E3779B9u
+#define PHX_W1 0xBB67AE85u
+#define PHX_M0 0xD2511F53u
+#define PHX_M1 0xCD9E8D57u
+
+typedef struct {
+    uint32_t key0, key1;  /* (seed >> 32, seed as u32), rng.rs:27 */
+    uint64_t counter;
+    uint64_t stream;
+    uint32_t buffer[4];
+    int cursor;
+} rhzo_philox;
+
+/* Philox::new, rng.rs:25-33. */
+void rhzo_philox_init(rhzo_philox *p, uint64_t seed, uint64_t stream) {
+    p->key0 = (uint32_t)(seed >> 32);
+    p->key1 = (uint32_t)seed;
+    p->counter = 0;
+    p->stream = stream;
+    memset(p->buffer, 0, sizeof(p->buffer));
+    p->cursor = 4;
+}
+
+/* Philox::seek, rng.rs:36-39. */
+void rhzo_philox_seek(rhzo_philox *p, uint64_t counter) {
+    p->counter = counter;
+    p->cursor = 4;
+}
+
+/* Philox::block, rng.rs:43-60: ten rounds of the 4x32 bijection. */
+void rhzo_philox_block(const rhzo_philox *p, uint64_t counter, uint32_t out[4]) {
+    uint32_t c0 = (uint32_t)counter, c1 = (uint32_t)(counter >> 32);
+    uint32_t c2 = (uint32_t)p->stream, c3 = (uint32_t)(p->stream >> 32);
+    uint32_t k0 = p->key0, k1 = p->key1;
+    for (int r = 0; r < 10; ++r) {
+        uint64_t prod0 = (uint64_t)c0 * (uint64_t)PHX_M0;
+        uint64_t prod1 = (uint64_t)c2 * (uint64_t)PHX_M1;
+        uint32_t hi0 = (uint32_t)(prod0 >> 32), lo0 = (uint32_t)prod0;
+        uint32_t hi1 = (uint32_t)(prod1 >> 32), lo1 = (uint32_t)prod1;
+        uint32_t n0 = hi1 ^ c1 ^ k0;
+        uint32_t n1 = lo1;
+        uint32_t n2 = hi0 ^ c3 ^ k1;
+        uint32_t n3 = lo0;
+        c0 = n0; c1 = n1; c2 = n2; c3 = n3;
+        k0 += PHX_W0;
+        k1 += PHX_W1;
+    }
+    out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
+}
+
+/* Philox::next_u32, rng.rs:63-72. */
+uint32_t rhzo_philox_next_u32(rhzo_philox *p) {
+    if (p->cursor >= 4) {
+        rhzo_philox_block(p, p->counter, p->buffer);
+        p->counter += 1;
+        p->cursor = 0;
+    }
+    return p->buffer[p->cursor++];
+}
+
+/* Philox::next_f64, rng.rs:78-82: 27 + 26 = 53 mantissa bits. */
+double rhzo_philox_next_f64(rhzo_philox *p) {
+    uint64_t hi = (uint64_t)(rhzo_philox_next_u32(p) >> 5);
+    uint64_t lo = (uint64_t)(rhzo_philox_next_u32(p) >> 6);
+    return (double)((hi << 26) | lo) / (double)(1ull << 53);
+}
+
+/* Philox::next_normal, rng.rs:85-89 (Box-Muller, cosine branch only). */
+double rhzo_philox_next_normal(rhzo_philox *p) {
+    double u1 = rhzo_philox_next_f64(p);
+    if (u1 < 1e-300) u1 = 1e-300; /* f64::max(1e-300); u1 is never NaN */
+    double u2 = rhzo_philox_next_f64(p);
+    const double tau = 6.283185307179586; /* core::f64::consts::TAU */
+    return sqrt(-2.0 * log(u1)) * cos(tau * u2);
+}
+
+/* stateless_uniform, rng.rs:101-107. */
+double rhzo_stateless_uniform(uint64_t seed, uint64_t stream, uint64_t index) {
+    rhzo_philox p;
+    uint32_t b[4];
+    rhzo_philox_init(&p, seed, stream);
+    rhzo_philox_block(&p, index, b);
+    uint64_t hi = (uint64_t)(b[0] >> 5);
+    uint64_t lo = (uint64_t)(b[1] >> 6);
+    return (double)((hi << 26) | lo) / (double)(1ull << 53);
+}
+
+/* Bulk helpers for the Python test harness. */
+void rhzo_philox_fill_u32(uint64_t seed, uint64_t stream, uint64_t n, uint32_t *out) {
+    rhzo_philox p;
+    rhzo_philox_init(&p, seed, stream);
+    for (uint64_t i = 0; i < n; ++i) out[i] = rhzo_philox_next_u32(&p);
+}
+
+void rhzo_philox_fill_f64(uint64_t seed, uint64_t stream, uint64_t n, double *out) {
+    rhzo_philox p;
+    rhzo_philox_init(&p, seed, stream);
+    for (uint64_t i = 0; i < n; ++i) out[i] = rhzo_philox_next_f64(&p);
+}
+
+void rhzo_philox_fill_normal(uint64_t seed, uint64_t stream, uint64_t n, double *out) {
+    rhzo_philox p;
+    rhzo_philox_init(&p, seed, stream);
+    for (uint64_t i = 0; i < n; ++i) out[i] = rhzo_philox_next_normal(&p);
+}
+
+/* Block function for an explicit (key, counter, stream) triple: the form in
+ * which an independent Philox implementation is compared against this one. */
+void rhzo_philox_block_raw(uint32_t key0, uint32_t key1, uint64_t counter,
+                           uint64_t stream, uint32_t out[4]) {
+    rhzo_philox p;
+    p.key0 = key0;
+    p.key1 = key1;
+    p.counter = 0;
+    p.stream = stream;
+    p.cursor = 4;
+    rhzo_philox_block(&p, counter, out);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Input producers, crates/ops/src/elementwise.rs                            */
+/* ------------------------------------------------------------------------ */
+
+/* sigmoid, elementwise.rs:5-12. */
+double rhzo_sigmoid(double x) {
+    if (x >= 0.0) {
+        return 1.0 / (1.0 + exp(-x));
+    }
+    double e = exp(x);
+    return e / (1.0 + e);
+}
+
+/* softplus, elementwise.rs:36-42. */
+double rhzo_softplus(double x) {
+    if (x > 30.0) return x;
+    return log(1.0 + exp(x));
+}
+
+/* l2norm, elementwise.rs:125-129. */
+void rhzo_l2norm(const double *x, int64_t n, double scale, double *out) {
+    double acc = -0.0; /* Sum for f64 starts from -0.0 */
+    for (int64_t i = 0; i < n; ++i) acc = acc + x[i] * x[i];
+    double nrm = sqrt(acc);
+    if (!(nrm >= 1e-12)) nrm = 1e-12; /* f64::max(1e-12) */
+    for (int64_t i = 0; i < n; ++i) out[i] = x[i] / nrm * scale;
+}
+
+/* ------------------------------------------------------------------------ */
+/* GDR op, crates/ops/src/delta.rs                                          */
+/* ------------------------------------------------------------------------ */
+
+/* gated_delta_step, delta.rs:93-127. `s` is d x d row-major, S[i][j] at
+ * i*d + j with i indexing v and j indexing k. `sk` is d doubles of scratch
+ * (the reference allocates it per call). Writes o (d doubles). */
+static void step_impl(double *s, int64_t d, const double *q, const double *k,
+                      const double *v, double alpha, double beta, double *sk,
+                      double *o) {
+    for (int64_t i = 0; i < d; ++i) {
+        double acc = 0.0;
+        for (int64_t j = 0; j < d; ++j) acc = acc + s[i * d + j] * k[j];
+        sk[i] = acc;
+    }
+    for (int64_t i = 0; i < d; ++i) {
+        for (int64_t j = 0; j < d; ++j) {
+            double decayed = alpha * (s[i * d + j] - beta * sk[i] * k[j]);
+            s[i * d + j] = decayed + beta * v[i] * k[j];
+        }
+    }
+    for (int64_t i = 0; i < d; ++i) {
+        double acc = 0.0;
+        for (int64_t j = 0; j < d; ++j) acc = acc + s[i * d + j] * q[j];
+        o[i] = acc;
+    }
+}
+
+void rhzo_gated_delta_step(double *s, int64_t d, const double *q, const double *k,
+                           const double *v, double alpha, double beta, double *o) {
+    double *sk = (double *)malloc((size_t)d * sizeof(double));
+    step_impl(s, d, q, k, v, alpha, beta, sk, o);
+    free(sk);
+}
+
+/* DeltaInputs::is_consistent, delta.rs:46-55, on explicit lengths. */
+int rhzo_inputs_consistent(int64_t head_dim, int64_t q_len, int64_t k_len, int64_t v_len,
+                           int64_t alpha_len, int64_t beta_len, int64_t segment_len) {
+    int64_t t = alpha_len;
+    int64_t d = head_dim;
+    return d > 0 && q_len == t * d && k_len == t * d && v_len == t * d &&
+           beta_len == t && segment_len == t;
+}
+
+/* gated_delta_sequential, delta.rs:132-154. The state is reset at t = 0
+ * (prev_segment starts as None) and on every segment change, so `init` never
+ * reaches the output; it is accepted for signature parity. */
+void rhzo_gated_delta_sequential(int64_t d, int64_t t_len, const double *q, const double *k,
+                                 const double *v, const double *alpha, const double *beta,
+                                 const int64_t *segment, const double *init, double *out,
+                                 double *final_state) {
+    double *s = final_state;
+    double *sk = (double *)malloc((size_t)d * sizeof(double));
+    memcpy(s, init, (size_t)(d * d) * sizeof(double));
+    int have_prev = 0;
+    int64_t prev = 0;
+    for (int64_t t = 0; t < t_len; ++t) {
+        if (!have_prev || prev != segment[t]) {
+            memset(s, 0, (size_t)(d * d) * sizeof(double));
+            prev = segment[t];
+            have_prev = 1;
+        }
+        step_impl(s, d, q + t * d, k + t * d, v + t * d, alpha[t], beta[t], sk, out + t * d);
+    }
+    free(sk);
+}
+
+/* gated_delta_scan_chunked, delta.rs:158-197. Chunks never cross a segment
+ * boundary; the state resets at t = 0 and at each segment start. */
+void rhzo_gated_delta_scan_chunked(int64_t d, int64_t t_len, const double *q, const double *k,
+                                   const double *v, const double *alpha, const double *beta,
+                                   const int64_t *segment, const double *init, int64_t chunk,
+                                   double *out, double *final_state) {
+    if (chunk < 1) chunk = 1; /* chunk.max(1) */
+    double *s = final_state;
+    double *sk = (double *)malloc((size_t)d * sizeof(double));
+    memcpy(s, init, (size_t)(d * d) * sizeof(double));
+    int64_t start = 0;
+    while (start < t_len) {
+        int64_t end = start + chunk < t_len ? start + chunk : t_len;
+        for (int64_t t = start + 1; t < end; ++t) {
+            if (segment[t] != segment[start]) {
+                end = t;
+                break;
+            }
+        }
+        if (start == 0 || segment[start] != segment[start - 1]) {
+            memset(s, 0, (size_t)(d * d) * sizeof(double));
+        }
+        for (int64_t t = start; t < end; ++t) {
+            step_impl(s, d, q + t * d, k + t * d, v + t * d, alpha[t], beta[t], sk, out + t * d);
+        }
+        start = end;
+    }
+    free(sk);
+}
+
+/* gated_delta_multistep, delta.rs:201-230. Returns n = min(T, max_positions);
+ * writes n output rows and n states (each d*d). */
+int64_t rhzo_gated_delta_multistep(int64_t d, int64_t t_len, const double *q, const double *k,
+                                   const double *v, const double *alpha, const double *beta,
+                                   const int64_t *segment, const double *init,
+                                   int64_t max_positions, double *outs, double *states) {
+    int64_t n = t_len < max_positions ? t_len : max_positions;
+    if (n < 0) n = 0;
+    double *s = (double *)malloc((size_t)(d * d) * sizeof(double));
+    double *sk = (double *)malloc((size_t)d * sizeof(double));
+    memcpy(s, init, (size_t)(d * d) * sizeof(double));
+    int have_prev = 0;
+    int64_t prev = 0;
+    for (int64_t t = 0; t < n; ++t) {
+        if (!have_prev || prev != segment[t]) {
+            memset(s, 0, (size_t)(d * d) * sizeof(double));
+            prev = segment[t];
+            have_prev = 1;
+        }
+        step_impl(s, d, q + t * d, k + t * d, v + t * d, alpha[t], beta[t], sk, outs + t * d);
+        memcpy(states + t * d * d, s, (size_t)(d * d) * sizeof(double));
+    }
+    free(sk);
+    free(s);
+    return n;
+}
+
+/* causal_conv1d_step, delta.rs:236-243. */
+double rhzo_causal_conv1d_step(double state[3], const double weight[4], double x, double bias) {
+    double y = weight[0] * state[0] + weight[1] * state[1] + weight[2] * state[2] +
+               weight[3] * x + bias;
+    state[0] = state[1];
+    state[1] = state[2];
+    state[2] = x;
+    return y;
+}
+
+/* A step loop that honours its initial state: gated_delta_step applied to
+ * every position in order with no reset. This is what the decode path
+ * (delta.rs:93-127 called per token) and a continuous-batching prefill that
+ * resumes from a slot compute. */
+void rhzo_gated_delta_step_loop(int64_t d, int64_t t_len, const double *q, const double *k,
+                                const double *v, const double *alpha, const double *beta,
+                                const double *init, double *out, double *final_state) {
+    double *s = final_state;
+    double *sk = (double *)malloc((size_t)d * sizeof(double));
+    memcpy(s, init, (size_t)(d * d) * sizeof(double));
+    for (int64_t t = 0; t < t_len; ++t) {
+        step_impl(s, d, q + t * d, k + t * d, v + t * d, alpha[t], beta[t], sk, out + t * d);
+    }
+    free(sk);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Batched drivers over the device layouts, one head per task, pthreads.    */
+/* Layouts: q/k/v/o [tokens][H][d]; alpha/beta [tokens][H]; states          */
+/* [.. ][H][d][d]. `tokens` is B*T for dense batches or the packed total.    */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+    /* common */
+    int64_t H, d;
+    const double *q, *k, *v, *alpha, *beta;
+    double *o;
+    /* sequences: [seq_start[i], seq_start[i] + seq_len[i]) token rows */
+    const int64_t *seq_start, *seq_len;
+    int64_t n_seq;
+    /* initial states: NULL => zeros (reference reset semantics) */
+    const double *state_in;       /* indexed by state_in_index[i] */
+    const int64_t *state_in_index;
+    double *state_out;            /* indexed by state_out_index[i] */
+    const int64_t *state_out_index;
+    /* work distribution */
+    int64_t next_task; /* task = seq * H + h */
+    pthread_mutex_t lock;
+} batch_job;
+
+static void run_one_head(batch_job *job, int64_t seq, int64_t h, double *buf) {
+    const int64_t d = job->d, H = job->H;
+    const int64_t L = job->seq_len[seq], t0 = job->seq_start[seq];
+    double *q = buf, *k = q + L * d, *v = k + L * d, *al = v + L * d, *be = al + L;
+    double *o = be + L, *s = o + L * d, *sk = s + d * d;
+    for (int64_t t = 0; t < L; ++t) {
+        const int64_t row = (t0 + t) * H + h;
+        memcpy(q + t * d, job->q + row * d, (size_t)d * sizeof(double));
+        memcpy(k + t * d, job->k + row * d, (size_t)d * sizeof(double));
+        memcpy(v + t * d, job->v + row * d, (size_t)d * sizeof(double));
+        al[t] = job->alpha[row];
+        be[t] = job->beta[row];
+    }
+    if (job->state_in) {
+        const int64_t slot = job->state_in_index ? job->state_in_index[seq] : seq;
+        memcpy(s, job->state_in + (slot * H + h) * d * d, (size_t)(d * d) * sizeof(double));
+    } else {
+        memset(s, 0, (size_t)(d * d) * sizeof(double));
+    }
+    for (int64_t t = 0; t < L; ++t) {
+        step_impl(s, d, q + t * d, k + t * d, v + t * d, al[t], be[t], sk, o + t * d);
+    }
+    for (int64_t t = 0; t < L; ++t) {
+        const int64_t row = (t0 + t) * H + h;
+        memcpy(job->o + row * d, o + t * d, (size_t)d * sizeof(double));
+    }
+    if (job->state_out) {
+        const int64_t slot = job->state_out_index ? job->state_out_index[seq] : seq;
+        memcpy(job->state_out + (slot * H + h) * d * d, s, (size_t)(d * d) * sizeof(double));
+    }
+}
+
+static void *batch_worker(void *arg) {
+    batch_job *job = (batch_job *)arg;
+    int64_t max_len = 0;
+    for (int64_t i = 0; i < job->n_seq; ++i)
+        if (job->seq_len[i] > max_len) max_len = job->seq_len[i];
+    const int64_t d = job->d;
+    double *buf = (double *)malloc((size_t)(max_len * (4 * d + 2) + d * d + d + 1) * sizeof(double));
+    for (;;) {
+        pthread_mutex_lock(&job->lock);
+        int64_t task = job->next_task++;
+        pthread_mutex_unlock(&job->lock);
+        if (task >= job->n_seq * job->H) break;
+        run_one_head(job, task / job->H, task % job->H, buf);
+    }
+    free(buf);
+    return NULL;
+}
+
+static void run_job(batch_job *job, int nthreads) {
+    if (nthreads < 1) nthreads = 1;
+    pthread_mutex_init(&job->lock, NULL);
+    job->next_task = 0;
+    pthread_t *th = (pthread_t *)malloc((size_t)nthreads * sizeof(pthread_t));
+    for (int i = 0; i < nthreads; ++i) pthread_create(&th[i], NULL, batch_worker, job);
+    for (int i = 0; i < nthreads; ++i) pthread_join(th[i], NULL);
+    free(th);
+    pthread_mutex_destroy(&job->lock);
+}
+
+/* Packed variable-length batch: sequence i occupies token rows
+ * [cu_seqlens[i], cu_seqlens[i+1]). Each (sequence, head) runs the step loop
+ * from its initial state (zeros when state_in is NULL, which equals the
+ * reference's reset at the segment start). */
+void rhzo_gdr_varlen(int64_t n_seq, const int64_t *cu_seqlens, int64_t H, int64_t d,
+                     const double *q, const double *k, const double *v, const double *alpha,
+                     const double *beta, const double *state_in, const int64_t *state_in_index,
+                     double *o, double *state_out, const int64_t *state_out_index,
+                     int nthreads) {
+    int64_t *start = (int64_t *)malloc((size_t)(n_seq + 1) * sizeof(int64_t));
+    int64_t *len = (int64_t *)malloc((size_t)(n_seq + 1) * sizeof(int64_t));
+    for (int64_t i = 0; i < n_seq; ++i) {
+        start[i] = cu_seqlens[i];
+        len[i] = cu_seqlens[i + 1] - cu_seqlens[i];
+    }
+    batch_job job;
+    memset(&job, 0, sizeof(job));
+    job.H = H; job.d = d;
+    job.q = q; job.k = k; job.v = v; job.alpha = alpha; job.beta = beta; job.o = o;
+    job.seq_start = start; job.seq_len = len; job.n_seq = n_seq;
+    job.state_in = state_in; job.state_in_index = state_in_index;
+    job.state_out = state_out; job.state_out_index = state_out_index;
+    run_job(&job, nthreads);
+    free(start);
+    free(len);
+}
+
+/* Dense batch [B][T][H][d]: B sequences of T tokens. */
+void rhzo_gdr_dense(int64_t B, int64_t T, int64_t H, int64_t d, const double *q, const double *k,
+                    const double *v, const double *alpha, const double *beta,
+                    const double *state_in, double *o, double *state_out, int nthreads) {
+    int64_t *cu = (int64_t *)malloc((size_t)(B + 1) * sizeof(int64_t));
+    for (int64_t b = 0; b <= B; ++b) cu[b] = b * T;
+    rhzo_gdr_varlen(B, cu, H, d, q, k, v, alpha, beta, state_in, NULL, o, state_out, NULL,
+                    nthreads);
+    free(cu);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Seeded synthetic inputs with the benchmark configurations' distributions. */
+/* Streams: 17 q, 18 k, 19 v, 20 beta logits, 21 alpha logits, 22 states.  */
+/* q, k: N(0,1) rows L2-normalised per (token, head) (l2norm, scale 1);     */
+/* v: N(0,1); beta = sigmoid(N(0,1)); alpha = exp(-softplus(N(0,1) + 2)).   */
+/* ------------------------------------------------------------------------ */
+
+void rhzo_make_qkv_gates(uint64_t seed, int64_t tokens, int64_t H, int64_t d, double *q,
+                         double *k, double *v, double *alpha, double *beta) {
+    rhzo_philox pq, pk, pv, pb, pa;
+    rhzo_philox_init(&pq, seed, 17);
+    rhzo_philox_init(&pk, seed, 18);
+    rhzo_philox_init(&pv, seed, 19);
+    rhzo_philox_init(&pb, seed, 20);
+    rhzo_philox_init(&pa, seed, 21);
+    double *row = (double *)malloc((size_t)d * sizeof(double));
+    for (int64_t r = 0; r < tokens * H; ++r) {
+        for (int64_t j = 0; j < d; ++j) row[j] = rhzo_philox_next_normal(&pq);
+        rhzo_l2norm(row, d, 1.0, q + r * d);
+        for (int64_t j = 0; j < d; ++j) row[j] = rhzo_philox_next_normal(&pk);
+        rhzo_l2norm(row, d, 1.0, k + r * d);
+        for (int64_t j = 0; j < d; ++j) v[r * d + j] = rhzo_philox_next_normal(&pv);
+        beta[r] = rhzo_sigmoid(rhzo_philox_next_normal(&pb));
+        alpha[r] = exp(-rhzo_softplus(rhzo_philox_next_normal(&pa) + 2.0));
+    }
+    free(row);
+}
+
+/* The reference tests' fixture make_inputs, delta.rs:254-280: q rows are
+ * L2-normalised and scaled by sqrt(d), k rows L2-normalised (both from
+ * Philox(seed, 17), q first), then Philox(seed, 18) gives v ~ N(0,1),
+ * alpha = 0.5 + 0.5 U and beta = 0.1 + 0.8 U. The row norm floors at 1e-9. */
+void rhzo_make_test_inputs(int64_t t_len, int64_t d, uint64_t seed, double *q, double *k,
+                           double *v, double *alpha, double *beta) {
+    rhzo_philox r, r2;
+    rhzo_philox_init(&r, seed, 17);
+    double *row = (double *)malloc((size_t)d * sizeof(double));
+    for (int pass = 0; pass < 2; ++pass) {
+        double *dst = pass == 0 ? q : k;
+        double scale = pass == 0 ? sqrt((double)d) : 1.0;
+        for (int64_t t = 0; t < t_len; ++t) {
+            double acc = -0.0;
+            for (int64_t j = 0; j < d; ++j) {
+                row[j] = rhzo_philox_next_normal(&r);
+            }
+            for (int64_t j = 0; j < d; ++j) acc = acc + row[j] * row[j];
+            double nrm = sqrt(acc);
+            if (!(nrm >= 1e-9)) nrm = 1e-9;
+            for (int64_t j = 0; j < d; ++j) dst[t * d + j] = row[j] / nrm * scale;
+        }
+    }
+    free(row);
+    rhzo_philox_init(&r2, seed, 18);
+    for (int64_t i = 0; i < t_len * d; ++i) v[i] = rhzo_philox_next_normal(&r2);
+    for (int64_t t = 0; t < t_len; ++t) alpha[t] = 0.5 + 0.5 * rhzo_philox_next_f64(&r2);
+    for (int64_t t = 0; t < t_len; ++t) beta[t] = 0.1 + 0.8 * rhzo_philox_next_f64(&r2);
+}
+
+/* N(0, sigma^2) fill (states), stream 22 unless told otherwise. */
+void rhzo_make_normal(uint64_t seed, uint64_t stream, int64_t n, double sigma, double *out) {
+    rhzo_philox p;
+    rhzo_philox_init(&p, seed, stream);
+    for (int64_t i = 0; i < n; ++i) out[i] = sigma * rhzo_philox_next_normal(&p);
+}
