@@ -1,0 +1,217 @@
+/*
+ * rhizome_gdr.h -- C ABI of the B200 (sm_100a) gated delta-rule library.
+ *
+ * The library is the first optimised backend for RHIZOME's GDR op
+ * (crates/ops/src/delta.rs). Each entry below names the reference function
+ * it stands in for. Conventions, shared by every entry point:
+ *
+ *  - Ownership: the caller owns every buffer. All tensor arguments are
+ *    DEVICE pointers (the plan arena's model: one base plus 256-byte aligned
+ *    offsets, crates/plan/src/arena.rs:71-144). No entry point allocates
+ *    device memory; scratch comes in through `workspace` and its size from
+ *    rhz_gdr_workspace_bytes().
+ *  - Streams: every call is asynchronous and ordered on `stream` (a
+ *    cudaStream_t; NULL is the legacy default stream). A returned RHZ_OK
+ *    means the work was validated and enqueued.
+ *  - Errors: the return value is a status code; rhz_last_error() gives the
+ *    message of this host thread's last failure. Shape problems return
+ *    RHZ_ERR_SHAPE, the counterpart of rhizome_core::Error::Shape
+ *    (crates/core/src/error.rs:27); no entry point aborts on user input
+ *    (rule R10). An unsupported (op, dtype, shape) combination is a hard
+ *    error, never a silent substitute (rule R4).
+ *  - Threads: entry points are reentrant and hold no per-call global state;
+ *    calls on different streams from different threads are independent.
+ *  - Layouts (row-major, innermost last):
+ *      q, k, v, o   [tokens][H][d]      dtype (f32 or bf16); o has q's dtype
+ *      alpha, beta  [tokens][H]         f32  (alpha: decay in [0,1], beta: write strength)
+ *      states       [n][H][d][d]        f32, S[i][j] with i indexing v and j indexing k
+ *                                         (DeltaState, delta.rs:59-66)
+ *    "tokens" is B*T for a dense batch ([B][T][H][d]) or the packed total of a
+ *    variable-length batch addressed by cu_seqlens.
+ *  - Math: per (sequence, head), o_t = S_t q_t with
+ *      S_t = alpha_t (S_{t-1} - beta_t (S_{t-1} k_t) k_t^T) + beta_t v_t k_t^T
+ *    (delta.rs:93-127). q is used as given (callers pre-scale it), d_k = d_v = d.
+ *  - Precision: RHZ_DTYPE_F32 runs an fp32 kernel that applies the recurrence
+ *    position by position (matches the f64 reference to rtol 1e-5);
+ *    RHZ_DTYPE_BF16 runs the chunked (chunk 64) WY/UT tensor-core kernel with
+ *    fp32 state and accumulation (rtol 2e-2, atol 1e-2). Index and packing
+ *    entries are bit-exact.
+ */
+#ifndef RHIZOME_GDR_H
+#define RHIZOME_GDR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers. */
+typedef struct CUstream_st *rhz_stream_t;
+
+/* Status codes. */
+enum rhz_status {
+    RHZ_OK = 0,
+    RHZ_ERR_SHAPE = 1,   /* shape/size mismatch (rhizome_core::Error::Shape) */
+    RHZ_ERR_INVALID = 2, /* bad argument value: null or misaligned pointer, bad flag */
+    RHZ_ERR_DTYPE = 3,   /* unsupported dtype for this entry point */
+    RHZ_ERR_DEVICE = 4,  /* CUDA launch/driver error or a device that is not sm_100 */
+    RHZ_ERR_TIMEOUT = 5, /* a bounded device-side wait ran out */
+    RHZ_ERR_NCCL = 6     /* collective failure (sharded entry points) */
+};
+
+/* Element types of q, k, v and o. alpha, beta and states are always f32. */
+enum rhz_dtype { RHZ_DTYPE_F32 = 0, RHZ_DTYPE_BF16 = 1 };
+
+/* Flags for rhz_gdr_varlen_fwd. */
+#define RHZ_FLAG_ZERO_INIT 1u /* ignore the slots' contents; start every sequence from S = 0 */
+#define RHZ_FLAG_NO_STATE_WRITE 2u /* do not write final states back to the slots */
+
+/* Message of this thread's last failing call ("" if none). Never NULL. */
+const char *rhz_last_error(void);
+
+/* ABI version of this header (major * 100 + minor). */
+int rhz_abi_version(void);
+
+/* --------------------------------------------------------------------- */
+/* GDR op family                                                          */
+/* --------------------------------------------------------------------- */
+
+/*
+ * rhz_gdr_step -- replaces gated_delta_step (crates/ops/src/delta.rs:93-127)
+ * batched over n sequences x H heads, one new position each (ragged decode
+ * for continuous batching). Sequence i's state for head h is
+ * state_pool[slot_idx[i]][h] and is updated in place; slot_idx == NULL means
+ * slot i. Like the reference step it honours the state it is given (no
+ * reset). q, k, v: [n][H][d]; alpha, beta: [n][H]; o: [n][H][d].
+ * A slot index outside [0, num_slots) leaves that pool entry untouched and
+ * writes NaN to the sequence's output rows.
+ */
+int rhz_gdr_step(void *o, float *state_pool, const int32_t *slot_idx, const void *q,
+                 const void *k, const void *v, const float *alpha, const float *beta,
+                 int64_t n, int64_t num_slots, int32_t H, int32_t d, int32_t dtype,
+                 rhz_stream_t stream);
+
+/*
+ * rhz_gdr_sequential -- replaces gated_delta_sequential
+ * (crates/ops/src/delta.rs:132-154) for B x H heads of T positions. The
+ * state resets at t = 0 and wherever segment[b][t] != segment[b][t-1]
+ * (segment: [B][T] int64, or NULL for one segment per batch row). As in the
+ * reference, the reset at t = 0 means `state_init` never reaches the
+ * result: it is accepted (may be NULL) and ignored. state_final: [B][H][d][d]
+ * (may be NULL). Needs `workspace` of rhz_gdr_workspace_bytes(B, T) bytes
+ * when segment != NULL (NULL/0 otherwise).
+ */
+int rhz_gdr_sequential(void *o, float *state_final, const void *q, const void *k,
+                       const void *v, const float *alpha, const float *beta,
+                       const int64_t *segment, const float *state_init, int64_t B, int64_t T,
+                       int32_t H, int32_t d, int32_t dtype, void *workspace,
+                       size_t workspace_bytes, rhz_stream_t stream);
+
+/*
+ * rhz_gdr_scan_chunked -- replaces gated_delta_scan_chunked
+ * (crates/ops/src/delta.rs:158-197): same arguments and result as
+ * rhz_gdr_sequential plus `chunk`. The reference's result does not depend
+ * on `chunk` (chunks only bound its loop); any chunk >= 0 is accepted (0 is
+ * treated as 1, as chunk.max(1) does) and the device kernels tile by 64
+ * positions, anchored at every segment start.
+ */
+int rhz_gdr_scan_chunked(void *o, float *state_final, const void *q, const void *k,
+                         const void *v, const float *alpha, const float *beta,
+                         const int64_t *segment, const float *state_init, int64_t chunk,
+                         int64_t B, int64_t T, int32_t H, int32_t d, int32_t dtype,
+                         void *workspace, size_t workspace_bytes, rhz_stream_t stream);
+
+/*
+ * rhz_gdr_varlen_fwd -- continuous-batching prefill over one packed stream.
+ * Sequence i occupies token rows [cu_seqlens[i], cu_seqlens[i+1]) of
+ * q/k/v/alpha/beta/o (cu_seqlens: n_seq + 1 int32, device, non-decreasing,
+ * cu_seqlens[0] = 0, cu_seqlens[n_seq] <= total_tokens). Each (sequence, head)
+ * starts from state_pool[slot_idx[i]][h] (zeros with RHZ_FLAG_ZERO_INIT) and
+ * writes its final state back there (unless RHZ_FLAG_NO_STATE_WRITE). This is
+ * gated_delta_step applied over the sequence from the slot's state -- the
+ * reference's scan with the segment-start reset replaced by the slot's
+ * contents. slot_idx == NULL means slot i. Slots must be distinct.
+ */
+int rhz_gdr_varlen_fwd(void *o, float *state_pool, const int32_t *slot_idx,
+                       const int32_t *cu_seqlens, const void *q, const void *k, const void *v,
+                       const float *alpha, const float *beta, int64_t n_seq,
+                       int64_t total_tokens, int64_t num_slots, int32_t H, int32_t d,
+                       int32_t dtype, uint32_t flags, rhz_stream_t stream);
+
+/*
+ * rhz_gdr_workspace_bytes -- scratch needed by rhz_gdr_sequential /
+ * rhz_gdr_scan_chunked with a segment array of B x T positions.
+ */
+size_t rhz_gdr_workspace_bytes(int64_t B, int64_t T);
+
+/* --------------------------------------------------------------------- */
+/* Variable-length packing (bit-exact index work)                         */
+/* --------------------------------------------------------------------- */
+
+/*
+ * rhz_varlen_prefix_sum -- cu_seqlens[0] = 0, cu_seqlens[i+1] =
+ * cu_seqlens[i] + lengths[i] for i < n (int32, device). The packed layout of
+ * continuous batching: it replaces building segment ids position by
+ * position (delta.rs:21-28, SPEC.md:21-22).
+ */
+int rhz_varlen_prefix_sum(int32_t *cu_seqlens, const int32_t *lengths, int64_t n,
+                          rhz_stream_t stream);
+
+/*
+ * rhz_varlen_segments_to_cu_seqlens -- turns a [B][T] int64 segment-id array
+ * (delta.rs:27-28) into segment boundaries over the flattened B*T positions:
+ * a boundary at every t where b changes, t = 0 within a row, or the id
+ * changes (the reset rule of delta.rs:137-141). Writes n_seg + 1 offsets to
+ * cu_seqlens (room for B*T + 1) and n_seg to *n_seg_out (device int32).
+ */
+int rhz_varlen_segments_to_cu_seqlens(int32_t *cu_seqlens, int32_t *n_seg_out,
+                                      const int64_t *segment, int64_t B, int64_t T,
+                                      void *workspace, size_t workspace_bytes,
+                                      rhz_stream_t stream);
+
+/*
+ * rhz_varlen_chunk_map -- the chunk list of a packed batch: chunks of
+ * `chunk` positions anchored at each sequence's own start (never crossing a
+ * sequence end, delta.rs:171-178). Writes chunk_seq[c] (sequence id) and
+ * chunk_start[c] (first token row) in (sequence, position) order and the count
+ * to *n_chunks_out; max_chunks bounds the output arrays (the count is still
+ * reported if larger).
+ */
+int rhz_varlen_chunk_map(int32_t *chunk_seq, int32_t *chunk_start, int32_t *n_chunks_out,
+                         const int32_t *cu_seqlens, int64_t n_seq, int32_t chunk,
+                         int64_t max_chunks, void *workspace, size_t workspace_bytes,
+                         rhz_stream_t stream);
+
+/* Scratch for rhz_varlen_chunk_map / rhz_varlen_segments_to_cu_seqlens. */
+size_t rhz_varlen_workspace_bytes(int64_t n);
+
+/*
+ * rhz_varlen_gather_states / rhz_varlen_scatter_states -- copy the d x d
+ * states of n sequences x H heads between a slot pool [num_slots][H][d][d]
+ * and a dense [n][H][d][d] buffer (dense[i] = pool[slot_idx[i]] and back).
+ */
+int rhz_varlen_gather_states(float *dense, const float *pool, const int32_t *slot_idx,
+                             int64_t n, int64_t num_slots, int32_t H, int32_t d,
+                             rhz_stream_t stream);
+int rhz_varlen_scatter_states(float *pool, const float *dense, const int32_t *slot_idx,
+                              int64_t n, int64_t num_slots, int32_t H, int32_t d,
+                              rhz_stream_t stream);
+
+/*
+ * rhz_varlen_pack_tokens / rhz_varlen_unpack_tokens -- move rows of
+ * row_bytes bytes between a padded [n][max_len] layout and the packed
+ * stream addressed by cu_seqlens (padded rows past a sequence's length are
+ * left untouched by unpack). row_bytes must be a multiple of 4.
+ */
+int rhz_varlen_pack_tokens(void *packed, const void *padded, const int32_t *cu_seqlens,
+                           int64_t n, int64_t max_len, int64_t row_bytes, rhz_stream_t stream);
+int rhz_varlen_unpack_tokens(void *padded, const void *packed, const int32_t *cu_seqlens,
+                             int64_t n, int64_t max_len, int64_t row_bytes, rhz_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RHIZOME_GDR_H */

@@ -1,0 +1,407 @@
+// C ABI of the GDR library: argument validation (the shape rules of
+// DeltaInputs::is_consistent, crates/ops/src/delta.rs:46-55, on the batched
+// layouts), status codes with a per-thread message, and dispatch to the
+// kernels. Nothing here allocates device memory.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/rhizome_gdr.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rhz {
+
+namespace {
+thread_local char g_last_error[512] = "";
+
+// Immutable per-device properties, filled on first use (the library's only
+// global state).
+struct DevInfo {
+    std::atomic<int> ready{0};
+    int sm_count = 0;
+    bool sm100 = false;
+};
+DevInfo g_dev[64];
+}  // namespace
+
+int set_error(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+void clear_error() { g_last_error[0] = '\0'; }
+
+int check_launch(const char *what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(RHZ_ERR_DEVICE, "%s: %s", what, cudaGetErrorString(e));
+    return RHZ_OK;
+}
+
+int device_info(int *sm_count, bool *is_sm100) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_error(RHZ_ERR_DEVICE, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return set_error(RHZ_ERR_DEVICE, "device ordinal %d out of range", dev);
+    DevInfo &d = g_dev[dev];
+    if (!d.ready.load(std::memory_order_acquire)) {
+        cudaDeviceProp p;
+        e = cudaGetDeviceProperties(&p, dev);
+        if (e != cudaSuccess)
+            return set_error(RHZ_ERR_DEVICE, "cudaGetDeviceProperties: %s", cudaGetErrorString(e));
+        d.sm_count = p.multiProcessorCount;
+        d.sm100 = p.major == 10 && p.minor == 0;
+        d.ready.store(1, std::memory_order_release);
+    }
+    *sm_count = d.sm_count;
+    *is_sm100 = d.sm100;
+    return RHZ_OK;
+}
+
+namespace {
+
+int require_sm100() {
+    int sms = 0;
+    bool ok = false;
+    int st = device_info(&sms, &ok);
+    if (st != RHZ_OK) return st;
+    if (!ok) return set_error(RHZ_ERR_DEVICE, "this library is built for sm_100a (B200) only");
+    return RHZ_OK;
+}
+
+int check_dtype(int32_t dtype) {
+    if (dtype != RHZ_DTYPE_F32 && dtype != RHZ_DTYPE_BF16)
+        return set_error(RHZ_ERR_DTYPE, "unsupported dtype %d (expected RHZ_DTYPE_F32 or RHZ_DTYPE_BF16)", dtype);
+    return RHZ_OK;
+}
+
+int check_heads(int32_t H, int32_t d) {
+    if (H < 1) return set_error(RHZ_ERR_SHAPE, "H = %d: need at least one head", H);
+    // DeltaInputs::is_consistent requires head_dim > 0 (delta.rs:50).
+    if (d < 1) return set_error(RHZ_ERR_SHAPE, "head_dim = %d: must be > 0", d);
+    if (d > 256) return set_error(RHZ_ERR_SHAPE, "head_dim = %d: kernels tile head widths up to 256", d);
+    return RHZ_OK;
+}
+
+int check_ptr(const void *p, const char *name, size_t align, bool needed) {
+    if (!needed) return RHZ_OK;
+    if (p == nullptr) return set_error(RHZ_ERR_INVALID, "%s is NULL", name);
+    if (!aligned(p, align)) return set_error(RHZ_ERR_INVALID, "%s is not %zu-byte aligned", name, align);
+    return RHZ_OK;
+}
+
+#define RHZ_TRY(x)                  \
+    do {                            \
+        int _st = (x);              \
+        if (_st != RHZ_OK) return _st; \
+    } while (0)
+
+// Offsets of the sequential/chunked entry points' workspace.
+struct SegWs {
+    size_t cu_off, nseg_off, slot_off, scan_off, total;
+};
+
+SegWs seg_ws(int64_t B, int64_t T) {
+    auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+    SegWs w;
+    const size_t N = static_cast<size_t>(B * T);
+    w.cu_off = 0;
+    w.nseg_off = up(w.cu_off + (N + 1) * sizeof(int32_t));
+    w.slot_off = up(w.nseg_off + sizeof(int32_t));
+    w.scan_off = up(w.slot_off + (N + 1) * sizeof(int32_t));
+    w.total = w.scan_off + varlen_ws_bytes(static_cast<int64_t>(N));
+    return w;
+}
+
+// Segment s writes its final state to batch row b only if it is the last
+// segment of row b (it ends where the row ends): the state
+// gated_delta_sequential returns (delta.rs:153).
+__global__ void final_slot_kernel(const int32_t *cu, const int32_t *n_seg, int64_t T, int32_t *slot) {
+    const int64_t n = *n_seg;
+    for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < n;
+         s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t end = cu[s + 1];
+        slot[s] = (end % T == 0) ? static_cast<int32_t>(end / T - 1) : -1;
+    }
+}
+
+int run_seq(const SeqArgs &a) {
+    if (chunk_tc_supports(a.d, a.dtype)) return launch_chunk_tc(a);
+    return launch_seq(a);
+}
+
+int sequential_impl(void *o, float *state_final, const void *q, const void *k, const void *v,
+                    const float *alpha, const float *beta, const int64_t *segment,
+                    const float *state_init, int64_t B, int64_t T, int32_t H, int32_t d,
+                    int32_t dtype, void *workspace, size_t workspace_bytes,
+                    rhz_stream_t stream) {
+    RHZ_TRY(check_dtype(dtype));
+    RHZ_TRY(check_heads(H, d));
+    if (B < 0 || T < 0) return set_error(RHZ_ERR_SHAPE, "B = %lld, T = %lld: must be >= 0", (long long)B, (long long)T);
+    if (B * T > INT32_MAX - 1) return set_error(RHZ_ERR_SHAPE, "B*T = %lld positions exceeds int32 indexing", (long long)(B * T));
+    const bool any = B * T > 0;
+    RHZ_TRY(check_ptr(q, "q", 16, any));
+    RHZ_TRY(check_ptr(k, "k", 16, any));
+    RHZ_TRY(check_ptr(v, "v", 16, any));
+    RHZ_TRY(check_ptr(o, "o", 16, any));
+    RHZ_TRY(check_ptr(alpha, "alpha", 4, any));
+    RHZ_TRY(check_ptr(beta, "beta", 4, any));
+    RHZ_TRY(check_ptr(state_final, "state_final", 16, state_final != nullptr));
+    RHZ_TRY(check_ptr(segment, "segment", 8, segment != nullptr));
+    RHZ_TRY(require_sm100());
+    cudaStream_t s = as_cuda(stream);
+    const size_t state_bytes = static_cast<size_t>(B) * H * d * d * sizeof(float);
+    if (T == 0) {
+        // The loop never runs: the reference returns init.clone() (delta.rs:135).
+        if (state_final && state_bytes) {
+            cudaError_t e = state_init
+                                ? cudaMemcpyAsync(state_final, state_init, state_bytes,
+                                                  cudaMemcpyDeviceToDevice, s)
+                                : cudaMemsetAsync(state_final, 0, state_bytes, s);
+            if (e != cudaSuccess) return set_error(RHZ_ERR_DEVICE, "state copy: %s", cudaGetErrorString(e));
+        }
+        return RHZ_OK;
+    }
+    if (B == 0) return RHZ_OK;
+
+    SeqArgs a{};
+    a.o = o; a.q = q; a.k = k; a.v = v; a.alpha = alpha; a.beta = beta;
+    a.total_tokens = B * T;
+    a.H = H; a.d = d; a.dtype = dtype; a.stream = s;
+    a.state_in = nullptr;  // reset at t = 0: the initial state never contributes
+    if (segment == nullptr) {
+        a.cu_seqlens = nullptr;
+        a.n_seq = B;
+        a.seq_len = T;
+        a.state_out = state_final;
+        a.num_slots = B;
+        return run_seq(a);
+    }
+    const SegWs w = seg_ws(B, T);
+    if (workspace == nullptr || workspace_bytes < w.total)
+        return set_error(RHZ_ERR_INVALID, "workspace too small: need %zu bytes, got %zu", w.total, workspace_bytes);
+    RHZ_TRY(check_ptr(workspace, "workspace", 256, true));
+    char *ws = static_cast<char *>(workspace);
+    int32_t *cu = reinterpret_cast<int32_t *>(ws + w.cu_off);
+    int32_t *nseg = reinterpret_cast<int32_t *>(ws + w.nseg_off);
+    int32_t *slots = reinterpret_cast<int32_t *>(ws + w.slot_off);
+    RHZ_TRY(launch_segments_to_cu(cu, nseg, segment, B, T, ws + w.scan_off, w.total - w.scan_off, s));
+    if (state_final) {
+        final_slot_kernel<<<64, 256, 0, s>>>(cu, nseg, T, slots);
+        RHZ_TRY(check_launch("final_slot_kernel"));
+    }
+    a.cu_seqlens = cu;
+    a.n_seq_dev = nseg;
+    a.n_seq = B * T;
+    a.seq_len = 0;
+    a.state_out = state_final;
+    a.out_slots = state_final ? slots : nullptr;
+    a.num_slots = B;
+    return run_seq(a);
+}
+
+}  // namespace
+}  // namespace rhz
+
+using namespace rhz;
+
+extern "C" {
+
+const char *rhz_last_error(void) { return g_last_error; }
+
+int rhz_abi_version(void) { return 100; }
+
+int rhz_gdr_step(void *o, float *state_pool, const int32_t *slot_idx, const void *q,
+                 const void *k, const void *v, const float *alpha, const float *beta, int64_t n,
+                 int64_t num_slots, int32_t H, int32_t d, int32_t dtype, rhz_stream_t stream) {
+    clear_error();
+    RHZ_TRY(check_dtype(dtype));
+    RHZ_TRY(check_heads(H, d));
+    if (n < 0 || num_slots < 0) return set_error(RHZ_ERR_SHAPE, "n = %lld, num_slots = %lld: must be >= 0", (long long)n, (long long)num_slots);
+    if (slot_idx == nullptr && n > num_slots)
+        return set_error(RHZ_ERR_SHAPE, "n = %lld sequences but only %lld slots (slot_idx is NULL)", (long long)n, (long long)num_slots);
+    if (n * H > INT32_MAX) return set_error(RHZ_ERR_SHAPE, "n*H = %lld exceeds the grid", (long long)(n * H));
+    if (n == 0) return RHZ_OK;
+    RHZ_TRY(check_ptr(q, "q", 16, true));
+    RHZ_TRY(check_ptr(k, "k", 16, true));
+    RHZ_TRY(check_ptr(v, "v", 16, true));
+    RHZ_TRY(check_ptr(o, "o", 16, true));
+    RHZ_TRY(check_ptr(alpha, "alpha", 4, true));
+    RHZ_TRY(check_ptr(beta, "beta", 4, true));
+    RHZ_TRY(check_ptr(state_pool, "state_pool", 16, true));
+    RHZ_TRY(check_ptr(slot_idx, "slot_idx", 4, slot_idx != nullptr));
+    RHZ_TRY(require_sm100());
+    StepArgs a{o, state_pool, slot_idx, q, k, v, alpha, beta, n, num_slots, H, d, dtype, as_cuda(stream)};
+    return launch_step(a);
+}
+
+int rhz_gdr_sequential(void *o, float *state_final, const void *q, const void *k, const void *v,
+                       const float *alpha, const float *beta, const int64_t *segment,
+                       const float *state_init, int64_t B, int64_t T, int32_t H, int32_t d,
+                       int32_t dtype, void *workspace, size_t workspace_bytes,
+                       rhz_stream_t stream) {
+    clear_error();
+    return sequential_impl(o, state_final, q, k, v, alpha, beta, segment, state_init, B, T, H, d,
+                           dtype, workspace, workspace_bytes, stream);
+}
+
+int rhz_gdr_scan_chunked(void *o, float *state_final, const void *q, const void *k,
+                         const void *v, const float *alpha, const float *beta,
+                         const int64_t *segment, const float *state_init, int64_t chunk,
+                         int64_t B, int64_t T, int32_t H, int32_t d, int32_t dtype,
+                         void *workspace, size_t workspace_bytes, rhz_stream_t stream) {
+    clear_error();
+    if (chunk < 0) return set_error(RHZ_ERR_SHAPE, "chunk = %lld: must be >= 0", (long long)chunk);
+    return sequential_impl(o, state_final, q, k, v, alpha, beta, segment, state_init, B, T, H, d,
+                           dtype, workspace, workspace_bytes, stream);
+}
+
+int rhz_gdr_varlen_fwd(void *o, float *state_pool, const int32_t *slot_idx,
+                       const int32_t *cu_seqlens, const void *q, const void *k, const void *v,
+                       const float *alpha, const float *beta, int64_t n_seq,
+                       int64_t total_tokens, int64_t num_slots, int32_t H, int32_t d,
+                       int32_t dtype, uint32_t flags, rhz_stream_t stream) {
+    clear_error();
+    RHZ_TRY(check_dtype(dtype));
+    RHZ_TRY(check_heads(H, d));
+    if (flags & ~(RHZ_FLAG_ZERO_INIT | RHZ_FLAG_NO_STATE_WRITE))
+        return set_error(RHZ_ERR_INVALID, "unknown flags 0x%x", flags);
+    if (n_seq < 0 || total_tokens < 0 || num_slots < 0)
+        return set_error(RHZ_ERR_SHAPE, "negative size (n_seq %lld, total_tokens %lld, num_slots %lld)",
+                         (long long)n_seq, (long long)total_tokens, (long long)num_slots);
+    if (total_tokens > INT32_MAX) return set_error(RHZ_ERR_SHAPE, "total_tokens exceeds int32 offsets");
+    if (slot_idx == nullptr && n_seq > num_slots)
+        return set_error(RHZ_ERR_SHAPE, "n_seq = %lld but only %lld slots (slot_idx is NULL)", (long long)n_seq, (long long)num_slots);
+    if (n_seq == 0) return RHZ_OK;
+    const bool any = total_tokens > 0;
+    RHZ_TRY(check_ptr(cu_seqlens, "cu_seqlens", 4, true));
+    RHZ_TRY(check_ptr(q, "q", 16, any));
+    RHZ_TRY(check_ptr(k, "k", 16, any));
+    RHZ_TRY(check_ptr(v, "v", 16, any));
+    RHZ_TRY(check_ptr(o, "o", 16, any));
+    RHZ_TRY(check_ptr(alpha, "alpha", 4, any));
+    RHZ_TRY(check_ptr(beta, "beta", 4, any));
+    const bool need_pool = !(flags & RHZ_FLAG_ZERO_INIT) || !(flags & RHZ_FLAG_NO_STATE_WRITE);
+    RHZ_TRY(check_ptr(state_pool, "state_pool", 16, need_pool));
+    RHZ_TRY(check_ptr(slot_idx, "slot_idx", 4, slot_idx != nullptr));
+    RHZ_TRY(require_sm100());
+    SeqArgs a{};
+    a.o = o; a.q = q; a.k = k; a.v = v; a.alpha = alpha; a.beta = beta;
+    a.cu_seqlens = cu_seqlens;
+    a.n_seq = n_seq;
+    a.total_tokens = total_tokens;
+    a.state_in = (flags & RHZ_FLAG_ZERO_INIT) ? nullptr : state_pool;
+    a.in_slots = slot_idx;
+    a.state_out = (flags & RHZ_FLAG_NO_STATE_WRITE) ? nullptr : state_pool;
+    a.out_slots = slot_idx;
+    a.num_slots = num_slots;
+    a.H = H; a.d = d; a.dtype = dtype; a.stream = as_cuda(stream);
+    return run_seq(a);
+}
+
+size_t rhz_gdr_workspace_bytes(int64_t B, int64_t T) {
+    if (B < 0 || T < 0) return 0;
+    return seg_ws(B, T).total;
+}
+
+int rhz_varlen_prefix_sum(int32_t *cu_seqlens, const int32_t *lengths, int64_t n,
+                          rhz_stream_t stream) {
+    clear_error();
+    if (n < 0) return set_error(RHZ_ERR_SHAPE, "n = %lld: must be >= 0", (long long)n);
+    RHZ_TRY(check_ptr(cu_seqlens, "cu_seqlens", 4, true));
+    RHZ_TRY(check_ptr(lengths, "lengths", 4, n > 0));
+    RHZ_TRY(require_sm100());
+    return launch_prefix_sum(cu_seqlens, lengths, n, as_cuda(stream));
+}
+
+int rhz_varlen_segments_to_cu_seqlens(int32_t *cu_seqlens, int32_t *n_seg_out,
+                                      const int64_t *segment, int64_t B, int64_t T,
+                                      void *workspace, size_t workspace_bytes,
+                                      rhz_stream_t stream) {
+    clear_error();
+    if (B < 0 || T < 0) return set_error(RHZ_ERR_SHAPE, "B = %lld, T = %lld: must be >= 0", (long long)B, (long long)T);
+    if (B * T > INT32_MAX - 1) return set_error(RHZ_ERR_SHAPE, "B*T exceeds int32 offsets");
+    RHZ_TRY(check_ptr(cu_seqlens, "cu_seqlens", 4, true));
+    RHZ_TRY(check_ptr(n_seg_out, "n_seg_out", 4, true));
+    RHZ_TRY(check_ptr(segment, "segment", 8, B * T > 0));
+    RHZ_TRY(require_sm100());
+    return launch_segments_to_cu(cu_seqlens, n_seg_out, segment, B, T, workspace, workspace_bytes,
+                                 as_cuda(stream));
+}
+
+int rhz_varlen_chunk_map(int32_t *chunk_seq, int32_t *chunk_start, int32_t *n_chunks_out,
+                         const int32_t *cu_seqlens, int64_t n_seq, int32_t chunk,
+                         int64_t max_chunks, void *workspace, size_t workspace_bytes,
+                         rhz_stream_t stream) {
+    clear_error();
+    if (n_seq < 0 || max_chunks < 0) return set_error(RHZ_ERR_SHAPE, "negative size");
+    if (chunk < 1) return set_error(RHZ_ERR_SHAPE, "chunk = %d: must be >= 1", chunk);
+    RHZ_TRY(check_ptr(n_chunks_out, "n_chunks_out", 4, true));
+    RHZ_TRY(check_ptr(cu_seqlens, "cu_seqlens", 4, n_seq > 0));
+    RHZ_TRY(check_ptr(chunk_seq, "chunk_seq", 4, max_chunks > 0));
+    RHZ_TRY(check_ptr(chunk_start, "chunk_start", 4, max_chunks > 0));
+    RHZ_TRY(require_sm100());
+    return launch_chunk_map(chunk_seq, chunk_start, n_chunks_out, cu_seqlens, n_seq, chunk,
+                            max_chunks, workspace, workspace_bytes, as_cuda(stream));
+}
+
+size_t rhz_varlen_workspace_bytes(int64_t n) { return varlen_ws_bytes(n); }
+
+int rhz_varlen_gather_states(float *dense, const float *pool, const int32_t *slot_idx,
+                             int64_t n, int64_t num_slots, int32_t H, int32_t d,
+                             rhz_stream_t stream) {
+    clear_error();
+    RHZ_TRY(check_heads(H, d));
+    if (n < 0 || num_slots < 0) return set_error(RHZ_ERR_SHAPE, "negative size");
+    if (slot_idx == nullptr && n > num_slots) return set_error(RHZ_ERR_SHAPE, "n > num_slots with slot_idx NULL");
+    RHZ_TRY(check_ptr(dense, "dense", 4, n > 0));
+    RHZ_TRY(check_ptr(pool, "pool", 4, n > 0));
+    RHZ_TRY(require_sm100());
+    return launch_gather_states(dense, pool, slot_idx, n, num_slots, H, d, false, as_cuda(stream));
+}
+
+int rhz_varlen_scatter_states(float *pool, const float *dense, const int32_t *slot_idx,
+                              int64_t n, int64_t num_slots, int32_t H, int32_t d,
+                              rhz_stream_t stream) {
+    clear_error();
+    RHZ_TRY(check_heads(H, d));
+    if (n < 0 || num_slots < 0) return set_error(RHZ_ERR_SHAPE, "negative size");
+    if (slot_idx == nullptr && n > num_slots) return set_error(RHZ_ERR_SHAPE, "n > num_slots with slot_idx NULL");
+    RHZ_TRY(check_ptr(dense, "dense", 4, n > 0));
+    RHZ_TRY(check_ptr(pool, "pool", 4, n > 0));
+    RHZ_TRY(require_sm100());
+    return launch_gather_states(const_cast<float *>(dense), pool, slot_idx, n, num_slots, H, d,
+                                true, as_cuda(stream));
+}
+
+int rhz_varlen_pack_tokens(void *packed, const void *padded, const int32_t *cu_seqlens,
+                           int64_t n, int64_t max_len, int64_t row_bytes, rhz_stream_t stream) {
+    clear_error();
+    if (n < 0 || max_len < 0 || row_bytes < 0) return set_error(RHZ_ERR_SHAPE, "negative size");
+    if (row_bytes % 4) return set_error(RHZ_ERR_SHAPE, "row_bytes = %lld: must be a multiple of 4", (long long)row_bytes);
+    RHZ_TRY(check_ptr(packed, "packed", 4, n > 0));
+    RHZ_TRY(check_ptr(padded, "padded", 4, n > 0));
+    RHZ_TRY(check_ptr(cu_seqlens, "cu_seqlens", 4, n > 0));
+    RHZ_TRY(require_sm100());
+    return launch_pack_tokens(packed, padded, cu_seqlens, n, max_len, row_bytes, false, as_cuda(stream));
+}
+
+int rhz_varlen_unpack_tokens(void *padded, const void *packed, const int32_t *cu_seqlens,
+                             int64_t n, int64_t max_len, int64_t row_bytes, rhz_stream_t stream) {
+    clear_error();
+    if (n < 0 || max_len < 0 || row_bytes < 0) return set_error(RHZ_ERR_SHAPE, "negative size");
+    if (row_bytes % 4) return set_error(RHZ_ERR_SHAPE, "row_bytes = %lld: must be a multiple of 4", (long long)row_bytes);
+    RHZ_TRY(check_ptr(packed, "packed", 4, n > 0));
+    RHZ_TRY(check_ptr(padded, "padded", 4, n > 0));
+    RHZ_TRY(check_ptr(cu_seqlens, "cu_seqlens", 4, n > 0));
+    RHZ_TRY(require_sm100());
+    return launch_pack_tokens(padded, packed, cu_seqlens, n, max_len, row_bytes, true, as_cuda(stream));
+}
+
+}  // extern "C"

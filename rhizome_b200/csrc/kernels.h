@@ -1,0 +1,66 @@
+// Internal launcher interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace rhz {
+
+// One recurrence position for a ragged batch (gdr_simt.cu).
+struct StepArgs {
+    void *o;
+    float *pool;
+    const int32_t *slots;
+    const void *q, *k, *v;
+    const float *alpha, *beta;
+    int64_t n, num_slots;
+    int H, d, dtype;
+    cudaStream_t stream;
+};
+
+// Whole sequences, position by position in fp32 (gdr_simt.cu) or chunked on
+// tensor cores (gdr_chunk_tc.cu). Sequence i covers token rows
+// [cu_seqlens[i], cu_seqlens[i+1]) or, with cu_seqlens == nullptr,
+// [i * seq_len, (i + 1) * seq_len). n_seq is the host-side upper bound; when
+// n_seq_dev is set the device count is used.
+struct SeqArgs {
+    void *o;
+    const void *q, *k, *v;
+    const float *alpha, *beta;
+    const int32_t *cu_seqlens;
+    const int32_t *n_seq_dev;
+    int64_t n_seq;
+    int64_t seq_len;
+    int64_t total_tokens;
+    const float *state_in;      // nullptr => zeros
+    const int32_t *in_slots;    // nullptr => sequence i uses slot i
+    float *state_out;           // nullptr => not written
+    const int32_t *out_slots;   // nullptr => sequence i uses slot i
+    int64_t num_slots;
+    int H, d, dtype;
+    cudaStream_t stream;
+};
+
+int launch_step(const StepArgs &a);
+int launch_seq(const SeqArgs &a);
+// Tensor-core chunked kernel (bf16, d == 128). Returns RHZ_ERR_SHAPE for
+// shapes it does not tile.
+int launch_chunk_tc(const SeqArgs &a);
+bool chunk_tc_supports(int d, int dtype);
+
+// Variable-length index work (varlen.cu).
+int launch_prefix_sum(int32_t *cu, const int32_t *lengths, int64_t n, cudaStream_t s);
+size_t varlen_ws_bytes(int64_t n);
+int launch_segments_to_cu(int32_t *cu, int32_t *n_seg, const int64_t *segment, int64_t B,
+                          int64_t T, void *ws, size_t ws_bytes, cudaStream_t s);
+int launch_chunk_map(int32_t *chunk_seq, int32_t *chunk_start, int32_t *n_chunks,
+                     const int32_t *cu, int64_t n_seq, int chunk, int64_t max_chunks, void *ws,
+                     size_t ws_bytes, cudaStream_t s);
+int launch_gather_states(float *dense, const float *pool, const int32_t *slots, int64_t n,
+                         int64_t num_slots, int H, int d, bool scatter, cudaStream_t s);
+int launch_pack_tokens(void *dst, const void *src, const int32_t *cu, int64_t n, int64_t max_len,
+                       int64_t row_bytes, bool unpack, cudaStream_t s);
+
+}  // namespace rhz

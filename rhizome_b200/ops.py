@@ -1,0 +1,215 @@
+"""torch-facing wrappers of the C ABI (device tensors in, device tensors out).
+
+torch only supplies device memory and the current stream; every op is one
+C-ABI call into librhizome_gdr.so. Layouts follow include/rhizome_gdr.h:
+q/k/v/o [tokens, H, d] (dense batches [B, T, H, d]), alpha/beta [tokens, H]
+f32, states [n, H, d, d] f32 with S[i][j], i the v index and j the k index.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import capi
+
+_DTYPES = {torch.float32: capi.RHZ_DTYPE_F32, torch.bfloat16: capi.RHZ_DTYPE_BF16}
+
+
+def _dt(x: torch.Tensor) -> int:
+    try:
+        return _DTYPES[x.dtype]
+    except KeyError:
+        raise capi.DtypeError(capi.RHZ_ERR_DTYPE, f"unsupported dtype {x.dtype}") from None
+
+
+def _p(x):
+    return None if x is None else x.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _need(x: torch.Tensor, name: str, dtype=None, shape=None):
+    if not x.is_cuda:
+        raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"{name} must be a CUDA tensor")
+    if not x.is_contiguous():
+        raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"{name} must be contiguous")
+    if dtype is not None and x.dtype != dtype:
+        raise capi.DtypeError(capi.RHZ_ERR_DTYPE, f"{name} must be {dtype}, got {x.dtype}")
+    if shape is not None and tuple(x.shape) != tuple(shape):
+        raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"{name} has shape {tuple(x.shape)}, expected {tuple(shape)}")
+
+
+def _qkv(q, k, v, alpha, beta, lead):
+    d = q.shape[-1]
+    H = q.shape[-2]
+    for name, x in (("q", q), ("k", k), ("v", v)):
+        _need(x, name, q.dtype, (*lead, H, d))
+    _need(alpha, "alpha", torch.float32, (*lead, H))
+    _need(beta, "beta", torch.float32, (*lead, H))
+    return H, d
+
+
+def gdr_step(q, k, v, alpha, beta, state_pool, slot_idx=None, out=None):
+    """gated_delta_step (delta.rs:93-127) for n sequences x H heads, in place
+    on state_pool[slot_idx[i]]. q/k/v [n, H, d]; returns o [n, H, d]."""
+    n = q.shape[0]
+    H, d = _qkv(q, k, v, alpha, beta, (n,))
+    _need(state_pool, "state_pool", torch.float32)
+    if state_pool.dim() != 4 or tuple(state_pool.shape[1:]) != (H, d, d):
+        raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"state_pool shape {tuple(state_pool.shape)} != [slots, {H}, {d}, {d}]")
+    if slot_idx is not None:
+        _need(slot_idx, "slot_idx", torch.int32, (n,))
+    o = torch.empty_like(q) if out is None else out
+    capi.call("rhz_gdr_step", _p(o), _p(state_pool), _p(slot_idx), _p(q), _p(k), _p(v),
+              _p(alpha), _p(beta), n, state_pool.shape[0], H, d, _dt(q), _stream(q.device))
+    return o
+
+
+def workspace_bytes(B: int, T: int) -> int:
+    return int(capi.lib().rhz_gdr_workspace_bytes(B, T))
+
+
+def _seq_common(name, q, k, v, alpha, beta, segment, state_init, chunk, with_state, workspace):
+    B, T = q.shape[0], q.shape[1]
+    H, d = _qkv(q, k, v, alpha, beta, (B, T))
+    if segment is not None:
+        _need(segment, "segment", torch.int64, (B, T))
+    if state_init is not None:
+        _need(state_init, "state_init", torch.float32, (B, H, d, d))
+    o = torch.empty_like(q)
+    fin = torch.empty((B, H, d, d), device=q.device, dtype=torch.float32) if with_state else None
+    ws = workspace
+    nbytes = 0
+    if segment is not None:
+        nbytes = workspace_bytes(B, T)
+        if ws is None:
+            ws = torch.empty(nbytes, device=q.device, dtype=torch.uint8)
+    args = [_p(o), _p(fin), _p(q), _p(k), _p(v), _p(alpha), _p(beta), _p(segment), _p(state_init)]
+    if name == "rhz_gdr_scan_chunked":
+        args.append(chunk)
+    args += [B, T, H, d, _dt(q), _p(ws), nbytes if ws is not None else 0, _stream(q.device)]
+    capi.call(name, *args)
+    return o, fin
+
+
+def gdr_sequential(q, k, v, alpha, beta, segment=None, state_init=None, with_state=True,
+                   workspace=None):
+    """gated_delta_sequential (delta.rs:132-154) on [B, T, H, d]: resets at
+    t = 0 and at segment changes; state_init is accepted and, as in the
+    reference, never reaches the result. Returns (o, final_state|None)."""
+    return _seq_common("rhz_gdr_sequential", q, k, v, alpha, beta, segment, state_init, 0,
+                       with_state, workspace)
+
+
+def gdr_scan_chunked(q, k, v, alpha, beta, chunk=64, segment=None, state_init=None,
+                     with_state=True, workspace=None):
+    """gated_delta_scan_chunked (delta.rs:158-197); the result does not
+    depend on `chunk`."""
+    return _seq_common("rhz_gdr_scan_chunked", q, k, v, alpha, beta, segment, state_init, chunk,
+                       with_state, workspace)
+
+
+def gdr_varlen_fwd(q, k, v, alpha, beta, cu_seqlens, state_pool=None, slot_idx=None,
+                   zero_init=False, write_state=True, out=None):
+    """Continuous-batching prefill over a packed stream q/k/v [tokens, H, d]:
+    sequence i = rows [cu_seqlens[i], cu_seqlens[i+1]) resumes from
+    state_pool[slot_idx[i]] (zeros if zero_init) and writes its final state
+    back (if write_state). Returns o [tokens, H, d]."""
+    tokens = q.shape[0]
+    H, d = _qkv(q, k, v, alpha, beta, (tokens,))
+    _need(cu_seqlens, "cu_seqlens", torch.int32)
+    n_seq = cu_seqlens.numel() - 1
+    flags = (capi.RHZ_FLAG_ZERO_INIT if zero_init else 0) | (0 if write_state else capi.RHZ_FLAG_NO_STATE_WRITE)
+    num_slots = 0
+    if state_pool is not None:
+        _need(state_pool, "state_pool", torch.float32)
+        num_slots = state_pool.shape[0]
+    if slot_idx is not None:
+        _need(slot_idx, "slot_idx", torch.int32, (n_seq,))
+    o = torch.empty_like(q) if out is None else out
+    capi.call("rhz_gdr_varlen_fwd", _p(o), _p(state_pool), _p(slot_idx), _p(cu_seqlens), _p(q),
+              _p(k), _p(v), _p(alpha), _p(beta), n_seq, tokens, num_slots, H, d, _dt(q), flags,
+              _stream(q.device))
+    return o
+
+
+# ---------------------------------------------------------------- varlen helpers
+
+def prefix_sum(lengths: torch.Tensor) -> torch.Tensor:
+    _need(lengths, "lengths", torch.int32)
+    cu = torch.empty(lengths.numel() + 1, device=lengths.device, dtype=torch.int32)
+    capi.call("rhz_varlen_prefix_sum", _p(cu), _p(lengths), lengths.numel(), _stream(lengths.device))
+    return cu
+
+
+def segments_to_cu_seqlens(segment: torch.Tensor):
+    """[B, T] int64 segment ids -> (cu_seqlens [B*T+1] int32 (first n_seg+1
+    valid), n_seg int32[1]) on the device."""
+    _need(segment, "segment", torch.int64)
+    B, T = segment.shape
+    cu = torch.zeros(B * T + 1, device=segment.device, dtype=torch.int32)
+    n = torch.zeros(1, device=segment.device, dtype=torch.int32)
+    nbytes = int(capi.lib().rhz_varlen_workspace_bytes(B * T))
+    ws = torch.empty(nbytes, device=segment.device, dtype=torch.uint8)
+    capi.call("rhz_varlen_segments_to_cu_seqlens", _p(cu), _p(n), _p(segment), B, T, _p(ws),
+              nbytes, _stream(segment.device))
+    return cu, n
+
+
+def chunk_map(cu_seqlens: torch.Tensor, chunk: int = 64, max_chunks: int | None = None):
+    _need(cu_seqlens, "cu_seqlens", torch.int32)
+    n_seq = cu_seqlens.numel() - 1
+    if max_chunks is None:
+        total = int(cu_seqlens[-1].item()) if n_seq > 0 else 0
+        max_chunks = total // chunk + n_seq + 1
+    dev = cu_seqlens.device
+    cs = torch.full((max_chunks,), -1, device=dev, dtype=torch.int32)
+    st = torch.full((max_chunks,), -1, device=dev, dtype=torch.int32)
+    n = torch.zeros(1, device=dev, dtype=torch.int32)
+    nbytes = int(capi.lib().rhz_varlen_workspace_bytes(max(n_seq, 1)))
+    ws = torch.empty(nbytes, device=dev, dtype=torch.uint8)
+    capi.call("rhz_varlen_chunk_map", _p(cs), _p(st), _p(n), _p(cu_seqlens), n_seq, chunk,
+              max_chunks, _p(ws), nbytes, _stream(dev))
+    return cs, st, n
+
+
+def gather_states(pool: torch.Tensor, slot_idx: torch.Tensor | None, n: int | None = None):
+    _need(pool, "pool", torch.float32)
+    S, H, d, _ = pool.shape
+    n = slot_idx.numel() if slot_idx is not None else (n if n is not None else S)
+    dense = torch.empty((n, H, d, d), device=pool.device, dtype=torch.float32)
+    capi.call("rhz_varlen_gather_states", _p(dense), _p(pool), _p(slot_idx), n, S, H, d,
+              _stream(pool.device))
+    return dense
+
+
+def scatter_states(pool: torch.Tensor, dense: torch.Tensor, slot_idx: torch.Tensor | None):
+    _need(pool, "pool", torch.float32)
+    _need(dense, "dense", torch.float32)
+    S, H, d, _ = pool.shape
+    n = dense.shape[0]
+    capi.call("rhz_varlen_scatter_states", _p(pool), _p(dense), _p(slot_idx), n, S, H, d,
+              _stream(pool.device))
+    return pool
+
+
+def pack_tokens(padded: torch.Tensor, cu_seqlens: torch.Tensor, total: int) -> torch.Tensor:
+    """padded [n, max_len, ...] -> packed [total, ...] by cu_seqlens."""
+    _need(padded, "padded")
+    n, max_len = padded.shape[0], padded.shape[1]
+    row_bytes = padded[0, 0].numel() * padded.element_size()
+    packed = torch.zeros((total, *padded.shape[2:]), device=padded.device, dtype=padded.dtype)
+    capi.call("rhz_varlen_pack_tokens", _p(packed), _p(padded), _p(cu_seqlens), n, max_len,
+              row_bytes, _stream(padded.device))
+    return packed
+
+
+def unpack_tokens(packed: torch.Tensor, cu_seqlens: torch.Tensor, max_len: int) -> torch.Tensor:
+    _need(packed, "packed")
+    n = cu_seqlens.numel() - 1
+    row_bytes = packed[0].numel() * packed.element_size() if packed.shape[0] else 4
+    padded = torch.zeros((n, max_len, *packed.shape[1:]), device=packed.device, dtype=packed.dtype)
+    capi.call("rhz_varlen_unpack_tokens", _p(padded), _p(packed), _p(cu_seqlens), n, max_len,
+              row_bytes, _stream(packed.device))
+    return padded

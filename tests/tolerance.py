@@ -1,0 +1,59 @@
+"""Tolerances of the GDR path against the f64 oracle.
+
+Both forms are checked:
+  - docs/kernels.md:3,16,25 (elementwise |out - ref| <= atol + rtol |ref|):
+      fp32: atol 1e-6, rtol 1e-5;  bf16: atol 1e-2 * RMS(ref), rtol 2e-2;
+  - the benchmark's statement: fp32 max relative error <= 1e-5 and bf16
+    <= 2e-2 relative and <= 1e-2 absolute, relative taken against max |ref|.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+FP32 = dict(rtol=1e-5, atol=1e-6, max_rel=1e-5, max_abs=None)
+BF16 = dict(rtol=2e-2, atol_rms=1e-2, max_rel=2e-2, max_abs=1e-2)
+
+
+def error_stats(out, ref):
+    out = np.asarray(out, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    diff = np.abs(out - ref)
+    scale = float(np.max(np.abs(ref))) if ref.size else 0.0
+    return dict(max_abs=float(diff.max()) if diff.size else 0.0,
+                max_rel=(float(diff.max()) / scale) if scale > 0 else float(diff.max(initial=0.0)),
+                rms_ref=float(np.sqrt(np.mean(ref ** 2))) if ref.size else 0.0,
+                finite=bool(np.all(np.isfinite(out))))
+
+
+def assert_fp32(out, ref, what=""):
+    out = np.asarray(out, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    st = error_stats(out, ref)
+    assert st["finite"], f"{what}: non-finite output"
+    bound = FP32["atol"] + FP32["rtol"] * np.abs(ref)
+    bad = np.abs(out - ref) > bound
+    assert not bad.any(), f"{what}: {bad.sum()} elements over atol 1e-6 + rtol 1e-5 |ref|; {st}"
+    assert st["max_rel"] <= FP32["max_rel"], f"{what}: max rel {st['max_rel']:.3e} > 1e-5"
+    return st
+
+
+def assert_bf16(out, ref, what=""):
+    out = np.asarray(out, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    st = error_stats(out, ref)
+    assert st["finite"], f"{what}: non-finite output"
+    atol = BF16["atol_rms"] * st["rms_ref"]
+    bad = np.abs(out - ref) > atol + BF16["rtol"] * np.abs(ref)
+    assert not bad.any(), f"{what}: {bad.sum()} elements over 1e-2 RMS + 2e-2 |ref|; {st}"
+    assert st["max_rel"] <= BF16["max_rel"], f"{what}: max rel {st['max_rel']:.3e} > 2e-2"
+    assert st["max_abs"] <= BF16["max_abs"], f"{what}: max abs {st['max_abs']:.3e} > 1e-2"
+    return st
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """Round f64 values to bf16 (via f32, nearest-even) and return them as f64:
+    the exact values a bf16 kernel receives."""
+    f = np.asarray(x, dtype=np.float32)
+    u = f.view(np.uint32).astype(np.uint64)
+    rounded = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return rounded.astype(np.uint32).view(np.float32).astype(np.float64)
