@@ -94,7 +94,7 @@ struct TcParams {
     __nv_bfloat16 *o;
     const float *alpha, *beta;
     const int32_t *cu_seqlens, *n_seq_dev;
-    int64_t n_seq, seq_len;
+    int64_t n_seq, seq_len, total_tokens;
     const float *state_in;
     const int32_t *in_slots;
     float *state_out;
@@ -277,9 +277,11 @@ __global__ void __launch_bounds__(NT, 1)
         const int h = static_cast<int>(item - seq * H);
         int64_t t0, t1;
         if (p.cu_seqlens) {
+            // Offsets are caller data: clamp them to the packed stream.
             t0 = p.cu_seqlens[seq];
             t1 = p.cu_seqlens[seq + 1];
-            if (t1 < t0) t1 = t0;
+            t0 = t0 < 0 ? 0 : (t0 > p.total_tokens ? p.total_tokens : t0);
+            t1 = t1 < t0 ? t0 : (t1 > p.total_tokens ? p.total_tokens : t1);
         } else {
             t0 = seq * p.seq_len;
             t1 = t0 + p.seq_len;
@@ -607,6 +609,7 @@ int launch_chunk_tc(const SeqArgs &a) {
     p.n_seq_dev = a.n_seq_dev;
     p.n_seq = a.n_seq;
     p.seq_len = a.seq_len;
+    p.total_tokens = tokens;
     p.state_in = a.state_in;
     p.in_slots = a.in_slots;
     p.state_out = a.state_out;

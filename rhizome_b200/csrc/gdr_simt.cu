@@ -187,6 +187,7 @@ __global__ void __launch_bounds__(WARPS * 32)
                    const T *__restrict__ v, const float *__restrict__ alpha,
                    const float *__restrict__ beta, const int32_t *__restrict__ cu_seqlens,
                    const int32_t *__restrict__ n_seq_dev, int64_t n_seq_host, int64_t seq_len,
+                   int64_t total_tokens,
                    const float *__restrict__ state_in, const int32_t *__restrict__ in_slots,
                    float *__restrict__ state_out, const int32_t *__restrict__ out_slots,
                    int64_t num_slots, int H, int d, bool vec) {
@@ -221,9 +222,11 @@ __global__ void __launch_bounds__(WARPS * 32)
         const int h = static_cast<int>(item - seq * H);
         int64_t t0, t1;
         if (cu_seqlens) {
+            // Offsets are caller data: clamp them to the packed stream.
             t0 = cu_seqlens[seq];
             t1 = cu_seqlens[seq + 1];
-            if (t1 < t0) t1 = t0;
+            t0 = t0 < 0 ? 0 : (t0 > total_tokens ? total_tokens : t0);
+            t1 = t1 < t0 ? t0 : (t1 > total_tokens ? total_tokens : t1);
         } else {
             t0 = seq * seq_len;
             t1 = t0 + seq_len;
@@ -357,6 +360,7 @@ int launch_seq_t(const SeqArgs &a) {
     kern<<<grid, WARPS * 32, smem, a.stream>>>(
         static_cast<T *>(a.o), static_cast<const T *>(a.q), static_cast<const T *>(a.k),
         static_cast<const T *>(a.v), a.alpha, a.beta, a.cu_seqlens, a.n_seq_dev, a.n_seq, a.seq_len,
+        a.cu_seqlens ? a.total_tokens : a.n_seq * a.seq_len,
         a.state_in, a.in_slots, a.state_out, a.out_slots, a.num_slots, a.H, a.d, vec);
     return check_launch("gdr_seq_kernel");
 }
