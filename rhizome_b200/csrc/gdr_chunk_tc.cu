@@ -21,7 +21,7 @@
 //   D_W  = K^T (T diag bg)^T   (128 x 64, K = C)     -> -W^T (bf16 smem)
 //   D_SQ = S0 Q^T              (128 x 64, K = d)
 //   D_U += S0 (-W^T)           (128 x 64, K = d)     -> Delta^T (bf16 smem)
-//   D_O2 = Delta^T M^T         (128 x 64, K = C)
+//   D_O2 = Delta^T M^T         (128 x 64, K = C)     fp16 operands (computed here)
 //   D_S += (P[C-1] Delta)^T K  (128 x 128, K = C)    (D_S pre-scaled by gamma_{C-1})
 // The 64 x 64 unit-lower-triangular inverse is done in fp32 on the SIMT
 // cores (blocked 16 x 16). Q, K, V tiles arrive by TMA (128-byte swizzle,
@@ -35,6 +35,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -65,10 +66,10 @@ constexpr uint32_t V_STAGE = 16384;
 constexpr uint32_t OFF_S = 98304;                  // bf16 state [half][128 rows][64]
 constexpr uint32_t OFF_TT = 131072;                // bf16 (T diag beta)        [t][s]
 constexpr uint32_t OFF_TH = 139264;                // bf16 (T diag beta gamma)  [t][s]
-constexpr uint32_t OFF_M = 147456;                 // bf16 masked decayed Q K^T [t][s]
+constexpr uint32_t OFF_M = 147456;                 // fp16 masked decayed Q K^T [t][s]
 constexpr uint32_t OFF_R = 155648;                 // 48 KB, phase-aliased region:
 constexpr uint32_t OFF_WT = OFF_R;                 //   -W^T  [j][t]   (16 KB)
-constexpr uint32_t OFF_DT = OFF_R + 16384;         //   Delta^T [i][s] (16 KB)
+constexpr uint32_t OFF_DT = OFF_R + 16384;         //   Delta^T [i][s] fp16 (16 KB)
 constexpr uint32_t OFF_DTS = OFF_R + 32768;        //   (P[C-1] Delta)^T [i][s] (16 KB)
 constexpr uint32_t OFF_AF = OFF_R;                 //   A fp32 [64][65]   (solve phase)
 constexpr uint32_t OFF_TF = OFF_R + 64 * AST * 4;  //   T fp32 [64][65]
@@ -88,6 +89,7 @@ constexpr uint32_t ID_KK64 = idesc_bf16(128, 64, false, false);
 constexpr uint32_t ID_MK64 = idesc_bf16(128, 64, true, false);
 constexpr uint32_t ID_KM64 = idesc_bf16(128, 64, false, true);
 constexpr uint32_t ID_KM128 = idesc_bf16(128, 128, false, true);
+constexpr uint32_t ID_KK64_F16 = idesc_f16(128, 64, false, false);
 constexpr uint32_t LOAD_BYTES = 6 * 8192;  // K, Q, V: two 64 x 64 bf16 boxes each
 
 struct TcParams {
@@ -118,6 +120,25 @@ __device__ __forceinline__ void st_row64_bf16(uint8_t *blk, uint32_t row, const 
         w.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
         w.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
         w.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
+        *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c)) = w;
+    }
+}
+
+// Same, as fp16: the intra-chunk output product M Delta runs in fp16 (both
+// operands are computed here, not loaded), which carries 3 more mantissa bits
+// than bf16 where the output is most sensitive.
+__device__ __forceinline__ void st_row64_f16(uint8_t *blk, uint32_t row, const float *v) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        uint4 w;
+        __half2 h0 = __floats2half2_rn(v[8 * c + 0], v[8 * c + 1]);
+        __half2 h1 = __floats2half2_rn(v[8 * c + 2], v[8 * c + 3]);
+        __half2 h2 = __floats2half2_rn(v[8 * c + 4], v[8 * c + 5]);
+        __half2 h3 = __floats2half2_rn(v[8 * c + 6], v[8 * c + 7]);
+        w.x = *reinterpret_cast<uint32_t *>(&h0);
+        w.y = *reinterpret_cast<uint32_t *>(&h1);
+        w.z = *reinterpret_cast<uint32_t *>(&h2);
+        w.w = *reinterpret_cast<uint32_t *>(&h3);
         *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c)) = w;
     }
 }
@@ -374,7 +395,7 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
                     for (int s = 0; s < 64; ++s) Af[r * AST + s] = x[s];
                 } else {
-                    st_row64_bf16(smem + OFF_M, r, x);
+                    st_row64_f16(smem + OFF_M, r, x);
                 }
             }
             __syncthreads();
@@ -436,7 +457,7 @@ __global__ void __launch_bounds__(NT, 1)
                 float x[64];
                 tmem_ld64(trow + TM_U, x);  // Delta[s][i = tid] for all s
                 tmem_wait_ld();
-                st_row64_bf16(smem + OFF_DT, tid, x);
+                st_row64_f16(smem + OFF_DT, tid, x);
 #pragma unroll
                 for (int s = 0; s < 64; ++s) x[s] *= spend[s];
                 st_row64_bf16(smem + OFF_DTS, tid, x);
@@ -460,7 +481,7 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     umma_bf16(tmem + TM_O2, sdesc_sw128(sbase + OFF_DT + kk * 32, 16, 1024),
-                              sdesc_sw128(sbase + OFF_M + kk * 32, 16, 1024), ID_KK64, kk > 0);
+                              sdesc_sw128(sbase + OFF_M + kk * 32, 16, 1024), ID_KK64_F16, kk > 0);
                 }
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {

@@ -202,6 +202,11 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major,
            | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
 }
 
+// Instruction descriptor: kind::f16 with fp16 A/B, f32 D, dense.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn_major, bool b_mn_major) {
+    return idesc_bf16(M, N, a_mn_major, b_mn_major) & ~((7u << 7) | (7u << 10));
+}
+
 // Byte offset of element (row, col) inside a block of 128-byte rows stored
 // with the 128-byte swizzle (16-byte chunk c of row r lives at chunk c ^ (r & 7)).
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t chunk16) {

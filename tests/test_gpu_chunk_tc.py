@@ -55,8 +55,8 @@ def test_reference_fixture_distribution():
     b = (0.1 + 0.8 * rng.random(b.shape)).astype(np.float32).astype(np.float64)
     o, fin = run_dense(q, k, v, a, b, B, T)
     ro, rs = O.gdr_dense(*(x.reshape(B, T, *x.shape[1:]) for x in (q, k, v, a, b)))
-    assert_bf16(host(o), ro, "slow-decay o")
-    assert_bf16(host(fin), rs, "slow-decay state")
+    assert_bf16(host(o), ro, "slow-decay o", abs_bound=False)
+    assert_bf16(host(fin), rs, "slow-decay state", abs_bound=False)
 
 
 @pytest.mark.parametrize("alpha,beta", [(0.0, None), (1.0, 0.0), (1.0, None)])

@@ -37,7 +37,11 @@ def assert_fp32(out, ref, what=""):
     return st
 
 
-def assert_bf16(out, ref, what=""):
+def assert_bf16(out, ref, what="", abs_bound=True):
+    """abs_bound=False drops the absolute 1e-2 cap for inputs whose outputs are
+    O(1) or larger (e.g. q scaled by sqrt(d)): a bf16 result alone rounds
+    by up to 2^-9 |o|, so a fixed 1e-2 cap would only test the output format.
+    The elementwise docs/kernels.md bound and the relative bound still apply."""
     out = np.asarray(out, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     st = error_stats(out, ref)
@@ -46,7 +50,8 @@ def assert_bf16(out, ref, what=""):
     bad = np.abs(out - ref) > atol + BF16["rtol"] * np.abs(ref)
     assert not bad.any(), f"{what}: {bad.sum()} elements over 1e-2 RMS + 2e-2 |ref|; {st}"
     assert st["max_rel"] <= BF16["max_rel"], f"{what}: max rel {st['max_rel']:.3e} > 2e-2"
-    assert st["max_abs"] <= BF16["max_abs"], f"{what}: max abs {st['max_abs']:.3e} > 1e-2"
+    if abs_bound:
+        assert st["max_abs"] <= BF16["max_abs"], f"{what}: max abs {st['max_abs']:.3e} > 1e-2"
     return st
 
 
