@@ -1,0 +1,413 @@
+"""Benchmark of the GDR hot path on B200 (one JSON line on rank 0).
+
+Default workload (the one the headline metric is quoted on): chunked GDR
+prefill, B=4, T=4096, H=16, d_k=d_v=128, chunk 64, bf16 q/k/v, f32 alpha/beta,
+f32 state, synthetic inputs with the benchmark distributions (q, k
+L2-normalised N(0,1) rows, v ~ N(0,1), beta = sigmoid(N(0,1)),
+alpha = exp(-softplus(N(0,1) + 2))). A step is one launch of the
+chunked kernel over the whole batch. With --gpus N (one process per GPU,
+torchrun) every rank runs its own batch of (sequence, head) units: the path
+shards with no data-path collective, so scaling is weak.
+
+Keys beyond the driver contract: `roofline` (dominant kernel, HBM bound at
+this arithmetic intensity, with the tensor-core fraction beside it),
+`cpu_baseline` (the f64 oracle restating crates/ops/src/delta.rs, timed on
+this host's cores), `e2e` (same metric through the C-ABI call with host
+buffers and the copies inside the timed region), `decode` (ragged decode
+step: 512 sequences x 16 heads from a 1024-slot fp32 pool), `clocks`.
+
+`--impl reference` times the reference's CPU implementation of the path (the
+oracle port, all host threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, T, H, D, CHUNK = 4, 4096, 16, 128, 64
+FLOP_PER_TOKEN_HEAD = 6 * D * D + 2 * CHUNK * (3 * D + 2 * D) + (2 / 3) * CHUNK * CHUNK  # 182,955
+DEC_N, DEC_SLOTS = 512, 1024
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return PEAKS_FALLBACK, "fallback"
+
+
+def algorithmic_bytes(b, t, h, d, with_state_in=False):
+    tok_heads = b * t * h
+    per = 3 * d * 2 + d * 2 + 8  # q, k, v, o (bf16) + alpha, beta (f32)
+    states = b * h * d * d * 4 * (2 if with_state_in else 1)
+    return tok_heads * per + states
+
+
+def decode_bytes(n, h, d):
+    # state read + write (f32), q/k/v in, o out (bf16), alpha/beta
+    return n * h * (2 * d * d * 4 + 3 * d * 2 + 8 + d * 2)
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.reader.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def dist_setup():
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_inputs(seed, dev):
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    n = torch.nn.functional.normalize
+    q = n(torch.randn(B, T, H, D, device=dev, generator=g), dim=-1).to(torch.bfloat16)
+    k = n(torch.randn(B, T, H, D, device=dev, generator=g), dim=-1).to(torch.bfloat16)
+    v = torch.randn(B, T, H, D, device=dev, generator=g).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn(B, T, H, device=dev, generator=g))
+    alpha = torch.exp(-torch.nn.functional.softplus(torch.randn(B, T, H, device=dev, generator=g) + 2))
+    return q, k, v, alpha.contiguous(), beta.contiguous()
+
+
+def cpu_reference_rate(sample_b: int, min_seconds: float, threads: int):
+    """Tokens/s of the f64 oracle (crates/ops/src/delta.rs restated) on
+    `sample_b` sequences of the workload, all heads, `threads` host threads."""
+    import numpy as np
+    from oracle import oracle as O
+    rng = np.random.default_rng(1)
+
+    def rows(shape):
+        x = rng.standard_normal(shape)
+        return x / np.linalg.norm(x, axis=-1, keepdims=True)
+
+    q, k = rows((sample_b, T, H, D)), rows((sample_b, T, H, D))
+    v = rng.standard_normal((sample_b, T, H, D))
+    beta = 1 / (1 + np.exp(-rng.standard_normal((sample_b, T, H))))
+    alpha = np.exp(-np.log1p(np.exp(rng.standard_normal((sample_b, T, H)) + 2)))
+    O.lib()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        O.gdr_dense(q, k, v, alpha, beta, nthreads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds and reps >= 1:
+            break
+    return reps * sample_b * T / el, reps, el
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU implementation (oracle port)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    import numpy as np
+    from oracle import oracle as O
+    rng = np.random.default_rng(1)
+    sb = 1  # one sequence (4096 tokens x 16 heads) per step: a bounded sample
+
+    def rows(shape):
+        x = rng.standard_normal(shape)
+        return x / np.linalg.norm(x, axis=-1, keepdims=True)
+
+    q, k = rows((sb, T, H, D)), rows((sb, T, H, D))
+    v = rng.standard_normal((sb, T, H, D))
+    beta = 1 / (1 + np.exp(-rng.standard_normal((sb, T, H))))
+    alpha = np.exp(-np.log1p(np.exp(rng.standard_normal((sb, T, H)) + 2)))
+    O.lib()
+    for _ in range(args.warmup):
+        O.gdr_dense(q, k, v, alpha, beta, nthreads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.gdr_dense(q, k, v, alpha, beta, nthreads=threads)
+    el = time.perf_counter() - t0
+    rate = args.steps * sb * T / el
+    sample = f"{sb} of {B} sequences per step ({T} tokens x {H} heads, d={D}), f64"
+    line = {
+        "impl": "reference", "metric": "GDR prefill tokens/s", "value": rate, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "chunked GDR prefill B=4 T=4096 H=16 d=128 chunk=64",
+                   "global_batch": B, "seq_len": T, "heads": H, "head_dim": D,
+                   "parallelism": "host threads over (sequence, head)"},
+        "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    from rhizome_b200 import capi, ops
+
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    capi.lib()
+    peaks, peaks_kind = load_peaks()
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+
+    # Two input sets (2 x 270 MB > L2), alternated between steps.
+    sets = [make_inputs(1000 * rank + s, dev) for s in range(2)]
+    o = torch.empty((B, T, H, D), device=dev, dtype=torch.bfloat16)
+    fin = torch.empty((B, H, D, D), device=dev, dtype=torch.float32)
+
+    def launch(i):
+        q, k, v, a, b = sets[i % 2]
+        capi.call("rhz_gdr_scan_chunked", o.data_ptr(), fin.data_ptr(), q.data_ptr(),
+                  k.data_ptr(), v.data_ptr(), a.data_ptr(), b.data_ptr(), None, None, CHUNK, B, T,
+                  H, D, capi.RHZ_DTYPE_BF16, None, 0, sptr)
+
+    for i in range(args.warmup):
+        launch(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        launch(i)
+        ev[i][1].record(stream)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
+    kernel_ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    kernel_ms = max_over_ranks(kernel_ms, world)
+    tokens = B * T * world * args.steps
+    value = tokens / (elapsed_ms / 1e3)
+
+    # Roofline of the dominant kernel (the chunked prefill).
+    abytes = algorithmic_bytes(B, T, H, D)
+    aflops = FLOP_PER_TOKEN_HEAD * B * T * H
+    gbs = abytes / (kernel_ms / 1e3) / 1e9
+    tflops = aflops / (kernel_ms / 1e3) / 1e12
+    roofline = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                "traffic": args.traffic, "peaks": f"of {peaks_kind}",
+                "kernel": "gdr_chunk_tc_kernel", "kernel_ms": round(kernel_ms, 4),
+                "algorithmic_bytes": abytes, "algorithmic_flops": aflops,
+                "tensor": {"achieved": round(tflops, 1), "peak": peaks["bf16_tflops"],
+                           "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4)}}
+
+    # End to end through the C ABI with host buffers: pinned inputs copied in,
+    # outputs and final states copied out, every step.
+    hq, hk, hv, ha, hb = (x.cpu().pin_memory() for x in sets[0])
+    ho = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
+    hfin = torch.empty(fin.shape, dtype=fin.dtype, pin_memory=True)
+    dq, dk, dv, da, db = (torch.empty_like(x) for x in sets[0])
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, ha, hb))
+    d2h = ho.numel() * ho.element_size() + hfin.numel() * hfin.element_size()
+
+    def e2e_step():
+        for dst, src in ((dq, hq), (dk, hk), (dv, hv), (da, ha), (db, hb)):
+            dst.copy_(src, non_blocking=True)
+        capi.call("rhz_gdr_scan_chunked", o.data_ptr(), fin.data_ptr(), dq.data_ptr(),
+                  dk.data_ptr(), dv.data_ptr(), da.data_ptr(), db.data_ptr(), None, None, CHUNK,
+                  B, T, H, D, capi.RHZ_DTYPE_BF16, None, 0, sptr)
+        ho.copy_(o, non_blocking=True)
+        hfin.copy_(fin, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2), world)
+    e2e_value = B * T * world * e2e_steps / (e2e_ms / 1e3)
+
+    # Ragged decode step (512 sequences x 16 heads, 1024-slot fp32 pool).
+    pool = torch.randn((DEC_SLOTS, H, D, D), device=dev) * 0.02
+    g = torch.Generator(device=dev).manual_seed(5 + rank)
+    slots = torch.randperm(DEC_SLOTS, device=dev, generator=g)[:DEC_N].to(torch.int32)
+    dqk = [sets[0][i][0, :DEC_N].contiguous() for i in range(3)]
+    da1, db1 = sets[0][3][0, :DEC_N].contiguous(), sets[0][4][0, :DEC_N].contiguous()
+    o1 = torch.empty_like(dqk[0])
+
+    def dec():
+        capi.call("rhz_gdr_step", o1.data_ptr(), pool.data_ptr(), slots.data_ptr(),
+                  dqk[0].data_ptr(), dqk[1].data_ptr(), dqk[2].data_ptr(), da1.data_ptr(),
+                  db1.data_ptr(), DEC_N, DEC_SLOTS, H, D, capi.RHZ_DTYPE_BF16, sptr)
+
+    for _ in range(5):
+        dec()
+    torch.cuda.synchronize()
+    dsteps = 50
+    s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s3.record(stream)
+    for _ in range(dsteps):
+        dec()
+    e3.record(stream)
+    torch.cuda.synchronize()
+    dec_ms = max_over_ranks(s3.elapsed_time(e3) / dsteps, world)
+    dbytes = decode_bytes(DEC_N, H, D)
+    dgbs = dbytes / (dec_ms / 1e3) / 1e9
+    decode = {"metric": "GDR decode tokens/s", "value": DEC_N * world / (dec_ms / 1e3),
+              "unit": "tokens/s", "ms_per_step": round(dec_ms, 4),
+              "config": {"sequences": DEC_N, "heads": H, "head_dim": D, "slots": DEC_SLOTS,
+                         "dtype": "bf16 q/k/v, f32 state"},
+              "roofline": {"bound": "hbm", "achieved": round(dgbs, 1), "peak": peaks["hbm_gbs"],
+                           "unit": "GB/s", "frac": round(dgbs / peaks["hbm_gbs"], 4),
+                           "kernel": "gdr_step_kernel", "algorithmic_bytes": dbytes}}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        rate, reps, el = cpu_reference_rate(1, 5.0, threads)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"1 of {B} sequences ({T} tokens x {H} heads, d={D}), f64, "
+                         f"{reps} repetition(s) in {el:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": "GDR prefill tokens/s", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "chunked GDR prefill B=4 T=4096 H=16 d=128 chunk=64",
+                       "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": D,
+                       "chunk": CHUNK, "parallelism": f"shard{world} over (sequence, head)",
+                       "l2": "inputs larger than L2 (2 x 270 MB sets, alternated)"},
+            "roofline": roofline, "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps, "clocks": clock_info, "decode": decode,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="measured DRAM bytes per launch of the dominant kernel (ncu)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -18,15 +18,20 @@
 // accumulator row maps to one TMEM lane and one thread (thread i <-> lane i):
 //   D1   = [K; Q] K^T          (128 x 64, K = d)     -> A (fp32 smem) and masked M
 //   D_U  = V^T (T diag b)^T    (128 x 64, K = C)
-//   D_W  = K^T (T diag bg)^T   (128 x 64, K = C)     -> -W^T (bf16 smem)
+//   D_W  = K^T (T diag bg)^T   (128 x 64, K = C)     -> -W^T (fp16 smem)
 //   D_SQ = S0 Q^T              (128 x 64, K = d)
-//   D_U += S0 (-W^T)           (128 x 64, K = d)     -> Delta^T (bf16 smem)
-//   D_O2 = Delta^T M^T         (128 x 64, K = C)     fp16 operands (computed here)
+//   D_U += S0 (-W^T)           (128 x 64, K = d)     -> Delta^T (fp16 smem)
+//   D_O2 = Delta^T M^T         (128 x 64, K = C)
 //   D_S += (P[C-1] Delta)^T K  (128 x 128, K = C)    (D_S pre-scaled by gamma_{C-1})
 // The 64 x 64 unit-lower-triangular inverse is done in fp32 on the SIMT
 // cores (blocked 16 x 16). Q, K, V tiles arrive by TMA (128-byte swizzle,
-// double-buffered one chunk ahead; no multicast). The state stays in TMEM in
-// fp32 for the whole sequence; a bf16 copy in shared memory feeds the MMAs.
+// double-buffered one chunk ahead; no multicast). D1 consumes them as bf16;
+// they are then converted to fp16 in place and every later product takes
+// fp16 operands (A and B of one MMA always share a type): 3 more mantissa
+// bits for T, W, Delta, M and the state copy than bf16 would give. The
+// state stays in TMEM in fp32 for the whole sequence; an fp16 copy in shared
+// memory feeds the MMAs. fp16 intermediates bound |q.k|, |v|, |S| to
+// < 65504 (unit-norm keys, as the reference specifies, keep them far below).
 //
 // One CTA (128 threads, one warpgroup) per SM, persistent over
 // (sequence, head) items. Every wait is bounded; a timeout sets a sticky
@@ -63,14 +68,14 @@ constexpr uint32_t OFF_KQ = 0;                     // 2 stages x 32 KB: [half][K
 constexpr uint32_t KQ_STAGE = 32768;
 constexpr uint32_t OFF_V = 65536;                  // 2 stages x 16 KB: [half][V rows]
 constexpr uint32_t V_STAGE = 16384;
-constexpr uint32_t OFF_S = 98304;                  // bf16 state [half][128 rows][64]
-constexpr uint32_t OFF_TT = 131072;                // bf16 (T diag beta)        [t][s]
-constexpr uint32_t OFF_TH = 139264;                // bf16 (T diag beta gamma)  [t][s]
+constexpr uint32_t OFF_S = 98304;                  // fp16 state [half][128 rows][64]
+constexpr uint32_t OFF_TT = 131072;                // fp16 (T diag beta)        [t][s]
+constexpr uint32_t OFF_TH = 139264;                // fp16 (T diag beta gamma)  [t][s]
 constexpr uint32_t OFF_M = 147456;                 // fp16 masked decayed Q K^T [t][s]
 constexpr uint32_t OFF_R = 155648;                 // 48 KB, phase-aliased region:
-constexpr uint32_t OFF_WT = OFF_R;                 //   -W^T  [j][t]   (16 KB)
+constexpr uint32_t OFF_WT = OFF_R;                 //   -W^T  [j][t] fp16 (16 KB)
 constexpr uint32_t OFF_DT = OFF_R + 16384;         //   Delta^T [i][s] fp16 (16 KB)
-constexpr uint32_t OFF_DTS = OFF_R + 32768;        //   (P[C-1] Delta)^T [i][s] (16 KB)
+constexpr uint32_t OFF_DTS = OFF_R + 32768;        //   (P[C-1] Delta)^T [i][s] fp16 (16 KB)
 constexpr uint32_t OFF_AF = OFF_R;                 //   A fp32 [64][65]   (solve phase)
 constexpr uint32_t OFF_TF = OFF_R + 64 * AST * 4;  //   T fp32 [64][65]
 constexpr uint32_t OFF_XF = OFF_TF + 64 * AST * 4; //   3 x 16x16 fp32 scratch
@@ -85,11 +90,13 @@ static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in shared memory");
 constexpr uint32_t TM_D1 = 0, TM_U = 64, TM_W = 128, TM_SQ = 192, TM_O2 = 256, TM_S = 320;
 constexpr uint32_t TM_COLS = 512;
 
-constexpr uint32_t ID_KK64 = idesc_bf16(128, 64, false, false);
-constexpr uint32_t ID_MK64 = idesc_bf16(128, 64, true, false);
-constexpr uint32_t ID_KM64 = idesc_bf16(128, 64, false, true);
-constexpr uint32_t ID_KM128 = idesc_bf16(128, 128, false, true);
-constexpr uint32_t ID_KK64_F16 = idesc_f16(128, 64, false, false);
+// D1 runs on the bf16 tiles as loaded; every later product runs in fp16
+// (the tiles are converted in place after D1), 3 more mantissa bits than bf16.
+constexpr uint32_t ID_D1 = idesc_bf16(128, 64, false, false);
+constexpr uint32_t ID_KK64 = idesc_f16(128, 64, false, false);
+constexpr uint32_t ID_MK64 = idesc_f16(128, 64, true, false);
+constexpr uint32_t ID_KM64 = idesc_f16(128, 64, false, true);
+constexpr uint32_t ID_KM128 = idesc_f16(128, 128, false, true);
 constexpr uint32_t LOAD_BYTES = 6 * 8192;  // K, Q, V: two 64 x 64 bf16 boxes each
 
 struct TcParams {
@@ -105,41 +112,42 @@ struct TcParams {
     int H;
 };
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t *>(&v);
 }
 
-// Row `row` (64 values, scaled by `scale[s]` when non-null) as bf16 into a
-// 128-byte-swizzled block of 128-byte rows.
-__device__ __forceinline__ void st_row64_bf16(uint8_t *blk, uint32_t row, const float *v) {
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        uint4 w;
-        w.x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
-        w.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
-        w.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
-        w.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
-        *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c)) = w;
-    }
-}
-
-// Same, as fp16: the intra-chunk output product M Delta runs in fp16 (both
-// operands are computed here, not loaded), which carries 3 more mantissa bits
-// than bf16 where the output is most sensitive.
+// 64 values as fp16 into row `row` of a 128-byte-swizzled block of
+// 128-byte rows (the canonical SWIZZLE_128B operand layout).
 __device__ __forceinline__ void st_row64_f16(uint8_t *blk, uint32_t row, const float *v) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
         uint4 w;
-        __half2 h0 = __floats2half2_rn(v[8 * c + 0], v[8 * c + 1]);
-        __half2 h1 = __floats2half2_rn(v[8 * c + 2], v[8 * c + 3]);
-        __half2 h2 = __floats2half2_rn(v[8 * c + 4], v[8 * c + 5]);
-        __half2 h3 = __floats2half2_rn(v[8 * c + 6], v[8 * c + 7]);
-        w.x = *reinterpret_cast<uint32_t *>(&h0);
-        w.y = *reinterpret_cast<uint32_t *>(&h1);
-        w.z = *reinterpret_cast<uint32_t *>(&h2);
-        w.w = *reinterpret_cast<uint32_t *>(&h3);
+        w.x = pack_f16x2(v[8 * c + 0], v[8 * c + 1]);
+        w.y = pack_f16x2(v[8 * c + 2], v[8 * c + 3]);
+        w.z = pack_f16x2(v[8 * c + 4], v[8 * c + 5]);
+        w.w = pack_f16x2(v[8 * c + 6], v[8 * c + 7]);
         *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c)) = w;
+    }
+}
+
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x) {
+    __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162 *>(&x);
+    return pack_f16x2(__low2float(b), __high2float(b));
+}
+
+// K, Q (32 KB) and V (16 KB) tiles of one stage, bf16 -> fp16 in place (the
+// swizzled layout is elementwise, so it is unchanged). bf16 values inside the
+// fp16 normal range convert exactly.
+__device__ __forceinline__ void tiles_to_f16(uint8_t *kq, uint8_t *vv, int tid) {
+    for (int i = tid; i < 3072; i += NT) {
+        uint4 *ptr = reinterpret_cast<uint4 *>(i < 2048 ? kq + i * 16 : vv + (i - 2048) * 16);
+        uint4 w = *ptr;
+        w.x = bf16x2_to_f16x2(w.x);
+        w.y = bf16x2_to_f16x2(w.y);
+        w.z = bf16x2_to_f16x2(w.z);
+        w.w = bf16x2_to_f16x2(w.w);
+        *ptr = w;
     }
 }
 
@@ -309,7 +317,7 @@ __global__ void __launch_bounds__(NT, 1)
         }
         const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
 
-        // ---- initial state: row tid of S -> TMEM (fp32) and the bf16 copy
+        // ---- initial state: row tid of S -> TMEM (fp32) and the fp16 copy
         {
             int64_t slot = -1;
             if (p.state_in) slot = p.in_slots ? static_cast<int64_t>(p.in_slots[seq]) : seq;
@@ -325,15 +333,15 @@ __global__ void __launch_bounds__(NT, 1)
                     v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
                 }
                 tmem_st32(trow + TM_S + 32 * q4, v);
-                // bf16 copy: columns 32*q4 .. +31 -> half q4/2, chunks (q4&1)*4 .. +3
+                // fp16 copy: columns 32*q4 .. +31 -> half q4/2, chunks (q4&1)*4 .. +3
                 uint8_t *blk = smem + OFF_S + (q4 >> 1) * 16384;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint4 w;
-                    w.x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
-                    w.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
-                    w.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
-                    w.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
+                    w.x = pack_f16x2(v[8 * c + 0], v[8 * c + 1]);
+                    w.y = pack_f16x2(v[8 * c + 2], v[8 * c + 3]);
+                    w.z = pack_f16x2(v[8 * c + 4], v[8 * c + 5]);
+                    w.w = pack_f16x2(v[8 * c + 6], v[8 * c + 7]);
                     *reinterpret_cast<uint4 *>(blk + sw128_offset(tid, (q4 & 1) * 4 + c)) = w;
                 }
             }
@@ -369,11 +377,12 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16(tmem + TM_D1, sdesc_sw128(kq + off, 16, 1024),
-                              sdesc_sw128(kq + off, 16, 1024), ID_KK64, kk > 0);
+                    umma_f16(tmem + TM_D1, sdesc_sw128(kq + off, 16, 1024),
+                              sdesc_sw128(kq + off, 16, 1024), ID_D1, kk > 0);
                 }
             }
             if (!mma_sync()) { failed = true; break; }
+            tiles_to_f16(smem + OFF_KQ + st * KQ_STAGE, smem + OFF_V + st * V_STAGE, tid);
             {
                 float x[64];
                 tmem_ld64(trow + TM_D1, x);
@@ -409,7 +418,7 @@ __global__ void __launch_bounds__(NT, 1)
                     const float sc = hat ? sb[s] * sg[s] : sb[s];
                     x[s] = Tf[t * AST + s] * sc;
                 }
-                st_row64_bf16(smem + (hat ? OFF_TH : OFF_TT), t, x);
+                st_row64_f16(smem + (hat ? OFF_TH : OFF_TT), t, x);
             }
             operands_ready();
 
@@ -417,18 +426,18 @@ __global__ void __launch_bounds__(NT, 1)
             if (tid == 0) {
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    umma_bf16(tmem + TM_U, sdesc_sw128(vb + kk * 2048, 8192, 1024),
+                    umma_f16(tmem + TM_U, sdesc_sw128(vb + kk * 2048, 8192, 1024),
                               sdesc_sw128(sbase + OFF_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
                 }
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    umma_bf16(tmem + TM_W, sdesc_sw128(kq + kk * 2048, 16384, 1024),
+                    umma_f16(tmem + TM_W, sdesc_sw128(kq + kk * 2048, 16384, 1024),
                               sdesc_sw128(sbase + OFF_TH + kk * 32, 16, 1024), ID_MK64, kk > 0);
                 }
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16(tmem + TM_SQ, sdesc_sw128(sbase + OFF_S + off, 16, 1024),
+                    umma_f16(tmem + TM_SQ, sdesc_sw128(sbase + OFF_S + off, 16, 1024),
                               sdesc_sw128(kq + off + 8192, 16, 1024), ID_KK64, kk > 0);
                 }
             }
@@ -439,7 +448,7 @@ __global__ void __launch_bounds__(NT, 1)
                 tmem_wait_ld();
 #pragma unroll
                 for (int t = 0; t < 64; ++t) x[t] = -x[t];
-                st_row64_bf16(smem + OFF_WT, tid, x);
+                st_row64_f16(smem + OFF_WT, tid, x);
             }
             operands_ready();
 
@@ -448,7 +457,7 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16(tmem + TM_U, sdesc_sw128(sbase + OFF_S + off, 16, 1024),
+                    umma_f16(tmem + TM_U, sdesc_sw128(sbase + OFF_S + off, 16, 1024),
                               sdesc_sw128(sbase + OFF_WT + kk * 2048, 8192, 1024), ID_KM64, 1);
                 }
             }
@@ -460,7 +469,7 @@ __global__ void __launch_bounds__(NT, 1)
                 st_row64_f16(smem + OFF_DT, tid, x);
 #pragma unroll
                 for (int s = 0; s < 64; ++s) x[s] *= spend[s];
-                st_row64_bf16(smem + OFF_DTS, tid, x);
+                st_row64_f16(smem + OFF_DTS, tid, x);
                 // D_S <- gamma_{C-1} D_S before the rank-C update accumulates.
                 const float gC = sg[63];
 #pragma unroll
@@ -480,18 +489,18 @@ __global__ void __launch_bounds__(NT, 1)
             if (tid == 0) {
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    umma_bf16(tmem + TM_O2, sdesc_sw128(sbase + OFF_DT + kk * 32, 16, 1024),
-                              sdesc_sw128(sbase + OFF_M + kk * 32, 16, 1024), ID_KK64_F16, kk > 0);
+                    umma_f16(tmem + TM_O2, sdesc_sw128(sbase + OFF_DT + kk * 32, 16, 1024),
+                              sdesc_sw128(sbase + OFF_M + kk * 32, 16, 1024), ID_KK64, kk > 0);
                 }
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    umma_bf16(tmem + TM_S, sdesc_sw128(sbase + OFF_DTS + kk * 32, 16, 1024),
+                    umma_f16(tmem + TM_S, sdesc_sw128(sbase + OFF_DTS + kk * 32, 16, 1024),
                               sdesc_sw128(kq + kk * 2048, 16384, 1024), ID_KM128, 1);
                 }
             }
             if (!mma_sync()) { failed = true; break; }
 
-            // ---- epilogue: O = gamma (S0 Q^T) + Delta^T M^T; refresh the bf16 state
+            // ---- epilogue: O = gamma (S0 Q^T) + Delta^T M^T; refresh the fp16 state
             {
                 float sq[64], o2[64];
                 tmem_ld64(trow + TM_SQ, sq);
@@ -511,10 +520,10 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
                     for (int cc = 0; cc < 4; ++cc) {
                         uint4 w;
-                        w.x = pack_bf16x2(v[8 * cc + 0], v[8 * cc + 1]);
-                        w.y = pack_bf16x2(v[8 * cc + 2], v[8 * cc + 3]);
-                        w.z = pack_bf16x2(v[8 * cc + 4], v[8 * cc + 5]);
-                        w.w = pack_bf16x2(v[8 * cc + 6], v[8 * cc + 7]);
+                        w.x = pack_f16x2(v[8 * cc + 0], v[8 * cc + 1]);
+                        w.y = pack_f16x2(v[8 * cc + 2], v[8 * cc + 3]);
+                        w.z = pack_f16x2(v[8 * cc + 4], v[8 * cc + 5]);
+                        w.w = pack_f16x2(v[8 * cc + 6], v[8 * cc + 7]);
                         *reinterpret_cast<uint4 *>(blk + sw128_offset(tid, (q4 & 1) * 4 + cc)) = w;
                     }
                 }
