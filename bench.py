@@ -26,7 +26,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -38,6 +37,9 @@ B, T, H, D, CHUNK = 4, 4096, 16, 128, 64
 FLOP_PER_TOKEN_HEAD = 6 * D * D + 2 * CHUNK * (3 * D + 2 * D) + (2 / 3) * CHUNK * CHUNK  # 182,955
 DEC_N, DEC_SLOTS = 512, 1024
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
+# the chunked kernel on this workload, from an ncu capture of that launch.
+NCU_TRAFFIC_BYTES = 203_900_928 + 49_683_200
 
 
 def load_peaks():
@@ -63,59 +65,75 @@ def decode_bytes(n, h, d):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons during the timed region."""
+    """SM clocks and clock-event (throttle) reasons during the timed region,
+    polled through NVML every 5 ms (the timed region can be tens of ms)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown", 0x8),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap", 0x4),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80))
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+        self.samples = []
+        self._stop = threading.Event()
+        self.thread = None
+        self.max_mhz = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.reader = threading.Thread(target=self._read, daemon=True)
-            self.reader.start()
+            import pynvml as N
+            N.nvmlInit()
+            self.N = N
+            uuid = None
+            try:
+                import torch
+                uuid = str(torch.cuda.get_device_properties(self.gpu).uuid)
+            except Exception:
+                pass
+            h = None
+            if uuid:
+                try:
+                    h = N.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+                except Exception:
+                    h = None
+            self.h = h if h is not None else N.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+            self.getreasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                N.nvmlDeviceGetCurrentClocksThrottleReasons
         except Exception:
-            self.proc = None
+            self.h = None
+            return
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        N = self.N
+        while not self._stop.is_set():
+            try:
+                mhz = N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)
+                reasons = self.getreasons(self.h)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(0.005)
 
     def stop(self):
-        if self.proc is None:
+        if self.thread is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.reader.join(timeout=2)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for nm, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(nm)
-        if not sm:
+        self._stop.set()
+        self.thread.join(timeout=2)
+        if not self.samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
-                "reasons": sorted(reasons)}
+        names = set()
+        for _, bits in self.samples:
+            for nm, const, default in self.REASONS:
+                if bits & getattr(self.N, const, default):
+                    names.add(nm)
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "reasons": sorted(names), "source": "NVML, 5 ms polling"}
 
 
 def dist_setup():
@@ -289,7 +307,8 @@ def run_ours(args):
     tflops = aflops / (kernel_ms / 1e3) / 1e12
     roofline = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
-                "traffic": args.traffic, "peaks": f"of {peaks_kind}",
+                "traffic": args.traffic if args.traffic else NCU_TRAFFIC_BYTES,
+                "peaks": f"of {peaks_kind}",
                 "kernel": "gdr_chunk_tc_kernel", "kernel_ms": round(kernel_ms, 4),
                 "algorithmic_bytes": abytes, "algorithmic_flops": aflops,
                 "tensor": {"achieved": round(tflops, 1), "peak": peaks["bf16_tflops"],
