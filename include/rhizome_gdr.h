@@ -210,6 +210,37 @@ int rhz_varlen_pack_tokens(void *packed, const void *padded, const int32_t *cu_s
 int rhz_varlen_unpack_tokens(void *padded, const void *packed, const int32_t *cu_seqlens,
                              int64_t n, int64_t max_len, int64_t row_bytes, rhz_stream_t stream);
 
+/* --------------------------------------------------------------------- */
+/* No-allocation variant                                                  */
+/* --------------------------------------------------------------------- */
+
+/* Largest B*T accepted by rhz_varlen_segments_to_cu_seqlens_noalloc. */
+#define RHZ_NOALLOC_MAX_POSITIONS (1LL << 26)
+
+/*
+ * rhz_varlen_segments_to_cu_seqlens_noalloc -- no counterpart in the
+ * reference (an addition of this library). Same arguments and results as
+ * rhz_varlen_segments_to_cu_seqlens minus the workspace: the scan's scratch
+ * lives in a 64 KiB array inside the library (on every GPU that loads it,
+ * until the process exits), so the call allocates no device memory at all.
+ * It is for callers that cannot allocate: a plan executor that only owns the
+ * arena its planner sized ahead of time (crates/plan/src/arena.rs, every
+ * offset fixed before the step) and has no slot for an op's private
+ * scratch, or a serving process that reserved all device memory up front
+ * for its state slots, where a cudaMalloc in the middle of a step can fail.
+ * Limits and rules:
+ *   - B*T must not exceed RHZ_NOALLOC_MAX_POSITIONS (2^26); larger inputs
+ *     return RHZ_ERR_SHAPE (use the workspace entry point instead);
+ *   - the first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture;
+ *   - every call shares the one array: calls whose work overlaps on the GPU
+ *     (different streams, or different host threads on one device) race.
+ */
+int rhz_varlen_segments_to_cu_seqlens_noalloc(int32_t *cu_seqlens, int32_t *n_seg_out,
+                                              const int64_t *segment, int64_t B, int64_t T,
+                                              rhz_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

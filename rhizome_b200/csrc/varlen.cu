@@ -12,6 +12,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -325,4 +326,83 @@ int launch_pack_tokens(void *dst, const void *src, const int32_t *cu, int64_t n,
     return check_launch(unpack ? "unpack_tokens" : "pack_tokens");
 }
 
+// ---------------------------------------------------------------- no-allocation variant
+//
+// rhz_varlen_segments_to_cu_seqlens_noalloc keeps the scan's per-tile totals
+// (its only scratch) in a file-scope device array instead of a caller
+// workspace, for callers that have no way to allocate device memory (see the
+// header). Limit: RHZ_NOALLOC_MAX_POSITIONS = 2^26 positions, i.e. 16384
+// tiles of 4096 -> 64 KiB per GPU, held from library load until process exit.
+// Every call shares this one array and it keeps the last call's contents;
+// nothing needs clearing because each call writes every tile total it reads
+// before reading it. Calls whose kernels overlap on the GPU (different
+// streams, or different host threads on the same device) race on it.
+
+namespace {
+constexpr int64_t NOALLOC_TILES = RHZ_NOALLOC_MAX_POSITIONS / SCAN_TILE;
+static_assert(NOALLOC_TILES * SCAN_TILE == RHZ_NOALLOC_MAX_POSITIONS, "limit is a whole number of tiles");
+}  // namespace
+
+static __device__ __align__(256) int32_t g_noalloc_tile_sums[NOALLOC_TILES];
+
+namespace {
+
+// Device address of g_noalloc_tile_sums on the current device. The name is a
+// host-side stand-in, not a device address, so it is resolved with
+// cudaGetSymbolAddress once per device (with that device current) and cached.
+struct NoallocScratch {
+    std::mutex mu;
+    int32_t *ptr = nullptr;
+};
+NoallocScratch g_noalloc[64];
+
+int noalloc_scratch(int32_t **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_error(RHZ_ERR_DEVICE, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return set_error(RHZ_ERR_DEVICE, "device ordinal %d out of range", dev);
+    NoallocScratch &s = g_noalloc[dev];
+    std::lock_guard<std::mutex> lock(s.mu);
+    if (s.ptr == nullptr) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_tile_sums);
+        if (e != cudaSuccess)
+            return set_error(RHZ_ERR_DEVICE, "cudaGetSymbolAddress(no-allocation scratch): %s",
+                             cudaGetErrorString(e));
+        s.ptr = static_cast<int32_t *>(p);
+    }
+    *out = s.ptr;
+    return RHZ_OK;
+}
+
+}  // namespace
 }  // namespace rhz
+
+extern "C" int rhz_varlen_segments_to_cu_seqlens_noalloc(int32_t *cu_seqlens, int32_t *n_seg_out,
+                                                         const int64_t *segment, int64_t B,
+                                                         int64_t T, rhz_stream_t stream) {
+    using namespace rhz;
+    clear_error();
+    if (B < 0 || T < 0)
+        return set_error(RHZ_ERR_SHAPE, "B = %lld, T = %lld: must be >= 0", (long long)B, (long long)T);
+    if (T > 0 && B > RHZ_NOALLOC_MAX_POSITIONS / T)
+        return set_error(RHZ_ERR_SHAPE,
+                         "B*T = %lld x %lld exceeds the no-allocation limit of %lld positions; "
+                         "use rhz_varlen_segments_to_cu_seqlens with a workspace",
+                         (long long)B, (long long)T, (long long)RHZ_NOALLOC_MAX_POSITIONS);
+    if (cu_seqlens == nullptr || n_seg_out == nullptr || !aligned(cu_seqlens, 4) || !aligned(n_seg_out, 4))
+        return set_error(RHZ_ERR_INVALID, "cu_seqlens / n_seg_out must be non-NULL int32 pointers");
+    if (B * T > 0 && (segment == nullptr || !aligned(segment, 8)))
+        return set_error(RHZ_ERR_INVALID, "segment must be a non-NULL 8-byte aligned int64 pointer");
+    int sms = 0;
+    bool sm100 = false;
+    int st = device_info(&sms, &sm100);
+    if (st != RHZ_OK) return st;
+    if (!sm100) return set_error(RHZ_ERR_DEVICE, "this library is built for sm_100a (B200) only");
+    int32_t *scratch = nullptr;
+    st = noalloc_scratch(&scratch);
+    if (st != RHZ_OK) return st;
+    return launch_segments_to_cu(cu_seqlens, n_seg_out, segment, B, T, scratch,
+                                 static_cast<size_t>(NOALLOC_TILES) * sizeof(int32_t),
+                                 as_cuda(stream));
+}
