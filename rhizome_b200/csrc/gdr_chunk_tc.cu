@@ -10,30 +10,41 @@
 //   S_C = gamma_{C-1} S0 + sum_s P[C-1][s] Delta_s k_s^T
 // which equals C applications of gated_delta_step (crates/ops/src/delta.rs:
 // 93-127): S_t = alpha_t S_{t-1} + Delta_t k_t^T with
-// Delta_t = beta_t (v_t - alpha_t S_{t-1} k_t). Decays are products of alphas
-// (never exp of a difference of large logs, never division by a decay), so
-// alpha = 0 and deep underflow are exact.
+// Delta_t = beta_t (v_t - alpha_t S_{t-1} k_t).
 //
-// All products are M = 128 tcgen05 MMAs with the d dimension on M, so every
-// accumulator row maps to one TMEM lane and one thread (thread i <-> lane i):
+// Decays: with gl_t the prefix sum of log2(alpha) over the chunk's nonzero
+// alphas and z_t the number of zero alphas so far,
+//   P[t][s] = (z_t == z_s) ? exp2(gl_t - gl_s) : 0,
+// so alpha = 0 (a reset) gives exactly zero and the table costs one exp2 per
+// entry with no sequential product chain; only differences t >= s are ever
+// exponentiated (never above 1, no overflow).
+//
+// The state products put the d dimension on M (= 128), so every accumulator
+// row maps to one TMEM lane (thread pair: warps w and w+4 share lanes
+// 32 (w & 3) .. +31 and split the columns); the output is an M = 64 product
+// so each of its rows (one position) is a contiguous 256-byte store:
 //   D1   = [K; Q] K^T          (128 x 64, K = d)     -> A (fp32 smem) and masked M
 //   D_U  = V^T (T diag b)^T    (128 x 64, K = C)
 //   D_W  = K^T (T diag bg)^T   (128 x 64, K = C)     -> -W^T (fp16 smem)
-//   D_SQ = S0 Q^T              (128 x 64, K = d)
+//   D_O  = Q~ S0^T             ( 64 x 128, K = d)    Q~ = diag(gamma) Q
 //   D_U += S0 (-W^T)           (128 x 64, K = d)     -> Delta^T (fp16 smem)
-//   D_O2 = Delta^T M^T         (128 x 64, K = C)
+//   D_O += M Delta             ( 64 x 128, K = C)
 //   D_S += (P[C-1] Delta)^T K  (128 x 128, K = C)    (D_S pre-scaled by gamma_{C-1})
-// The 64 x 64 unit-lower-triangular inverse is done in fp32 on the SIMT
-// cores (blocked 16 x 16). Q, K, V tiles arrive by TMA (128-byte swizzle,
-// double-buffered one chunk ahead; no multicast). D1 consumes them as bf16;
-// they are then converted to fp16 in place and every later product takes
-// fp16 operands (A and B of one MMA always share a type): 3 more mantissa
-// bits for T, W, Delta, M and the state copy than bf16 would give. The
-// state stays in TMEM in fp32 for the whole sequence; an fp16 copy in shared
-// memory feeds the MMAs. fp16 intermediates bound |q.k|, |v|, |S| to
-// < 65504 (unit-norm keys, as the reference specifies, keep them far below).
+// Q, K, V tiles arrive by TMA (128-byte swizzle, double-buffered one chunk
+// ahead; no multicast). D1 consumes them as bf16; they are then converted to
+// fp16 in place and every later product takes fp16 operands (A and B of one
+// MMA always share a type): 3 more mantissa bits for T, W, Delta, M and the
+// state copy than bf16 would give. The state stays in TMEM in fp32 for the
+// whole sequence; an fp16 copy in shared memory feeds the MMAs. fp16
+// intermediates bound |q.k|, |v|, |S| to < 65504 (unit-norm keys, as the
+// reference specifies, keep them far below).
 //
-// One CTA (128 threads, one warpgroup) per SM, persistent over
+// The 64 x 64 unit-lower-triangular inverse: the four diagonal 16 x 16 tiles
+// by fp32 forward substitution (overlapped with the fp16 conversion), the rest
+// by a 2 x 2 recursion whose tile products run on mma.sync (fp16 operands,
+// fp32 accumulate).
+//
+// One CTA (256 threads, two warpgroups) per SM, persistent over
 // (sequence, head) items. Every wait is bounded; a timeout sets a sticky
 // device flag, drains in-flight copies and MMAs (bounded), frees TMEM and
 // returns.
@@ -60,8 +71,8 @@ using namespace sm100;
 
 constexpr int CH = 64;    // chunk length
 constexpr int HD = 128;   // head dim (d_k = d_v)
-constexpr int NT = 128;   // threads per CTA
-constexpr int AST = 65;   // fp32 row stride of the A / T tables (bank spread)
+constexpr int NT = 256;   // threads per CTA
+constexpr int AST = 68;   // fp32 row stride of the A / T tables (16-byte rows, bank spread)
 
 // Shared memory map (offsets from a 1024-byte aligned base).
 constexpr uint32_t OFF_KQ = 0;                     // 2 stages x 32 KB: [half][K rows | Q rows]
@@ -73,30 +84,30 @@ constexpr uint32_t OFF_TT = 131072;                // fp16 (T diag beta)        
 constexpr uint32_t OFF_TH = 139264;                // fp16 (T diag beta gamma)  [t][s]
 constexpr uint32_t OFF_M = 147456;                 // fp16 masked decayed Q K^T [t][s]
 constexpr uint32_t OFF_R = 155648;                 // 48 KB, phase-aliased region:
-constexpr uint32_t OFF_WT = OFF_R;                 //   -W^T  [j][t] fp16 (16 KB)
+constexpr uint32_t OFF_WT = OFF_R;                 //   -W^T [j][t] fp16 (16 KB)
 constexpr uint32_t OFF_DT = OFF_R + 16384;         //   Delta^T [i][s] fp16 (16 KB)
 constexpr uint32_t OFF_DTS = OFF_R + 32768;        //   (P[C-1] Delta)^T [i][s] fp16 (16 KB)
-constexpr uint32_t OFF_AF = OFF_R;                 //   A fp32 [64][65]   (solve phase)
-constexpr uint32_t OFF_TF = OFF_R + 64 * AST * 4;  //   T fp32 [64][65]
-constexpr uint32_t OFF_XF = OFF_TF + 64 * AST * 4; //   3 x 16x16 fp32 scratch
-constexpr uint32_t OFF_SMALL = OFF_R + 49152;      // alpha, beta, gamma, P[C-1][.] (4 x 64 f32)
-constexpr uint32_t OFF_BAR = OFF_SMALL + 1024;     // 3 mbarriers + TMEM base address
+constexpr uint32_t OFF_AF = OFF_R;                 //   A fp32 [64][AST]   (solve phase)
+constexpr uint32_t OFF_TF = OFF_AF + 64 * AST * 4; //   T fp32 [64][AST]
+constexpr uint32_t OFF_XF = OFF_TF + 64 * AST * 4; //   32 x 32 fp32 partial products
+constexpr uint32_t OFF_SMALL = OFF_R + 49152;      // gl, z, beta, gamma, P[C-1][.], beta*gamma
+constexpr uint32_t OFF_BAR = OFF_SMALL + 2048;     // 3 mbarriers + TMEM base address
 constexpr uint32_t SMEM_USED = OFF_BAR + 64;
 constexpr size_t SMEM_ALLOC = SMEM_USED + 1024;    // slack for 1024-byte alignment
-static_assert(OFF_XF + 3 * 256 * 4 <= OFF_R + 49152, "solve scratch overflows its region");
+static_assert(OFF_XF + 4 * 256 * 4 <= OFF_R + 49152, "solve scratch overflows its region");
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in shared memory");
 
-// TMEM columns (f32 accumulators, 128 lanes each).
-constexpr uint32_t TM_D1 = 0, TM_U = 64, TM_W = 128, TM_SQ = 192, TM_O2 = 256, TM_S = 320;
+// TMEM columns (f32 accumulators). D_O is an M = 64 accumulator (row t in
+// lane 32 (t / 16) + t % 16) over 128 columns; the others use all 128 lanes.
+constexpr uint32_t TM_D1 = 0, TM_U = 64, TM_W = 128, TM_O = 192, TM_S = 320;
 constexpr uint32_t TM_COLS = 512;
 
-// D1 runs on the bf16 tiles as loaded; every later product runs in fp16
-// (the tiles are converted in place after D1), 3 more mantissa bits than bf16.
+// D1 runs on the bf16 tiles as loaded; every later product runs in fp16.
 constexpr uint32_t ID_D1 = idesc_bf16(128, 64, false, false);
-constexpr uint32_t ID_KK64 = idesc_f16(128, 64, false, false);
 constexpr uint32_t ID_MK64 = idesc_f16(128, 64, true, false);
 constexpr uint32_t ID_KM64 = idesc_f16(128, 64, false, true);
 constexpr uint32_t ID_KM128 = idesc_f16(128, 128, false, true);
+constexpr uint32_t ID_O = idesc_f16(64, 128, false, false);
 constexpr uint32_t LOAD_BYTES = 6 * 8192;  // K, Q, V: two 64 x 64 bf16 boxes each
 
 struct TcParams {
@@ -112,23 +123,51 @@ struct TcParams {
     int H;
 };
 
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float lg2(float x) {
+    float y;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
 __device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
     __half2 v = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t *>(&v);
 }
 
-// 64 values as fp16 into row `row` of a 128-byte-swizzled block of
-// 128-byte rows (the canonical SWIZZLE_128B operand layout).
-__device__ __forceinline__ void st_row64_f16(uint8_t *blk, uint32_t row, const float *v) {
+// 8 consecutive values as one 16-byte fp16 chunk.
+__device__ __forceinline__ uint4 pack8_f16(const float *v) {
+    uint4 w;
+    w.x = pack_f16x2(v[0], v[1]);
+    w.y = pack_f16x2(v[2], v[3]);
+    w.z = pack_f16x2(v[4], v[5]);
+    w.w = pack_f16x2(v[6], v[7]);
+    return w;
+}
+
+// 32 values as fp16 into 16-byte chunks c0 .. c0+3 of row `row` of a
+// 128-byte-swizzled block of 128-byte rows (canonical SWIZZLE_128B layout).
+__device__ __forceinline__ void st_row32_f16(uint8_t *blk, uint32_t row, uint32_t c0,
+                                             const float *v) {
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        uint4 w;
-        w.x = pack_f16x2(v[8 * c + 0], v[8 * c + 1]);
-        w.y = pack_f16x2(v[8 * c + 2], v[8 * c + 3]);
-        w.z = pack_f16x2(v[8 * c + 4], v[8 * c + 5]);
-        w.w = pack_f16x2(v[8 * c + 6], v[8 * c + 7]);
-        *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c)) = w;
-    }
+    for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + c)) = pack8_f16(v + 8 * c);
+}
+
+__device__ __forceinline__ void st_zero32(uint8_t *blk, uint32_t row, uint32_t c0) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + c)) = make_uint4(0, 0, 0, 0);
 }
 
 __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x) {
@@ -136,82 +175,130 @@ __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x) {
     return pack_f16x2(__low2float(b), __high2float(b));
 }
 
-// K, Q (32 KB) and V (16 KB) tiles of one stage, bf16 -> fp16 in place (the
-// swizzled layout is elementwise, so it is unchanged). bf16 values inside the
-// fp16 normal range convert exactly.
-__device__ __forceinline__ void tiles_to_f16(uint8_t *kq, uint8_t *vv, int tid) {
-    for (int i = tid; i < 3072; i += NT) {
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2_scaled(uint32_t x, float s) {
+    __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162 *>(&x);
+    return pack_f16x2(s * __low2float(b), s * __high2float(b));
+}
+
+// bf16 -> fp16 in place on 16-byte chunks [first, 3072) of one stage's K, Q
+// (32 KB) and V (16 KB) tiles, stepping by `stride`. Q rows are scaled by
+// gamma_t on the way (Q~ = diag(gamma) Q feeds O = Q~ S0^T + M Delta). The
+// swizzled layout is elementwise, so it is unchanged; bf16 values in the fp16
+// normal range convert exactly.
+__device__ __forceinline__ void tiles_to_f16(uint8_t *kq, uint8_t *vv, const float *gam, int first,
+                                             int stride) {
+    for (int i = first; i < 3072; i += stride) {
         uint4 *ptr = reinterpret_cast<uint4 *>(i < 2048 ? kq + i * 16 : vv + (i - 2048) * 16);
         uint4 w = *ptr;
-        w.x = bf16x2_to_f16x2(w.x);
-        w.y = bf16x2_to_f16x2(w.y);
-        w.z = bf16x2_to_f16x2(w.z);
-        w.w = bf16x2_to_f16x2(w.w);
+        // KQ stage: [half][K 64 rows | Q 64 rows] of 128-byte rows.
+        const bool is_q = i < 2048 && (i & 1023) >= 512;
+        if (is_q) {
+            const float g = gam[(i & 511) >> 3];
+            w.x = bf16x2_to_f16x2_scaled(w.x, g);
+            w.y = bf16x2_to_f16x2_scaled(w.y, g);
+            w.z = bf16x2_to_f16x2_scaled(w.z, g);
+            w.w = bf16x2_to_f16x2_scaled(w.w, g);
+        } else {
+            w.x = bf16x2_to_f16x2(w.x);
+            w.y = bf16x2_to_f16x2(w.y);
+            w.z = bf16x2_to_f16x2(w.z);
+            w.w = bf16x2_to_f16x2(w.w);
+        }
         *ptr = w;
     }
 }
 
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
-    tmem_ld32(taddr, *reinterpret_cast<float(*)[32]>(&v[0]));
-    tmem_ld32(taddr + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+__device__ __forceinline__ uint32_t h2(float a, float b) { return pack_f16x2(a, b); }
+
+// D (16 x 8, fp32) += A (16 x 16, fp16) * B (16 x 8, fp16) on the warp's
+// legacy tensor-core path (mma.sync m16n8k16); fragments per the PTX layout
+// with g = lane / 4, t = lane % 4.
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-// 64 x 64 unit lower triangular inverse T = (I + A)^-1 of a strictly lower A,
-// fp32, blocked 4 x 4 in 16 x 16 tiles. All 128 threads; ends synchronised.
-__device__ void solve_unit_lower(const float *Af, float *Tf, float *Xf, int tid) {
-    // Diagonal tiles by forward substitution: thread (I, j) solves column j.
-    if (tid < 64) {
-        const int I = tid >> 4, j = tid & 15;
-        const float *A = Af + (16 * I) * AST + 16 * I;
-        float x[16];
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            float acc = (r == j) ? 1.f : 0.f;
-#pragma unroll
-            for (int c = 0; c < r; ++c)
-                if (c >= j) acc = fmaf(-A[r * AST + c], x[c], acc);
-            x[r] = (r >= j) ? acc : 0.f;
-        }
-        float *T = Tf + (16 * I) * AST + 16 * I;
-#pragma unroll
-        for (int r = 0; r < 16; ++r) T[r * AST + j] = x[r];
-    }
-    // Tiles above the diagonal are zero.
-    for (int idx = tid; idx < 6 * 256; idx += NT) {
-        const int b = idx >> 8, e = idx & 255;
-        const int I = b < 3 ? 0 : (b < 5 ? 1 : 2);
-        const int J = b < 3 ? b + 1 : (b < 5 ? b - 1 : 3);
-        Tf[(16 * I + (e >> 4)) * AST + 16 * J + (e & 15)] = 0.f;
+// A fragment of the 16 x 16 fp32 tile at L (row stride ls), rounded to fp16.
+__device__ __forceinline__ void frag_a(const float *L, int ls, int lane, uint32_t (&a)[4]) {
+    const int g = lane >> 2, t = lane & 3;
+    const float2 x0 = *reinterpret_cast<const float2 *>(L + g * ls + 2 * t);
+    const float2 x1 = *reinterpret_cast<const float2 *>(L + (g + 8) * ls + 2 * t);
+    const float2 x2 = *reinterpret_cast<const float2 *>(L + g * ls + 2 * t + 8);
+    const float2 x3 = *reinterpret_cast<const float2 *>(L + (g + 8) * ls + 2 * t + 8);
+    a[0] = h2(x0.x, x0.y);
+    a[1] = h2(x1.x, x1.y);
+    a[2] = h2(x2.x, x2.y);
+    a[3] = h2(x3.x, x3.y);
+}
+
+// B fragment of the 16 x 8 fp32 tile at R (row-major [k][n], row stride rs).
+__device__ __forceinline__ void frag_b(const float *R, int rs, int lane, uint32_t (&b)[2]) {
+    const int g = lane >> 2, t = lane & 3;
+    b[0] = h2(R[(2 * t) * rs + g], R[(2 * t + 1) * rs + g]);
+    b[1] = h2(R[(2 * t + 8) * rs + g], R[(2 * t + 9) * rs + g]);
+}
+
+// Store the 16 x 8 accumulator (times `sign`) into fp32 rows at C (stride cs).
+__device__ __forceinline__ void st_frag_c(float *C, int cs, int lane, const float (&d)[4], float sign) {
+    const int g = lane >> 2, t = lane & 3;
+    *reinterpret_cast<float2 *>(C + g * cs + 2 * t) = make_float2(sign * d[0], sign * d[1]);
+    *reinterpret_cast<float2 *>(C + (g + 8) * cs + 2 * t) = make_float2(sign * d[2], sign * d[3]);
+}
+
+// Off-diagonal part of T = (I + A)^-1 once the four diagonal 16 x 16 inverses
+// D_I are in Tf (and Tf's tiles (0,1) and (2,3) are zero), by a 2 x 2
+// recursion: T_{2p+1,2p} = -D_{2p+1} (A_{2p+1,2p} D_{2p}) for p = 0, 1, then
+// T[32:64, 0:32] = -T[32:64, 32:64] (A[32:64, 0:32] T[0:32, 0:32]). The
+// products run on mma.sync with fp16 operands (T is rounded to fp16 for the
+// tcgen05 products anyway). Ends synchronised.
+__device__ void solve_offdiag(const float *Af, float *Tf, float *Xf, int warp, int lane) {
+    if (warp < 4) {
+        const int pb = warp >> 1, nt = warp & 1;
+        const int r0 = 32 * pb + 16, c0 = 32 * pb;  // tile (2p+1, 2p)
+        uint32_t a[4], b[2];
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        frag_a(Af + r0 * AST + c0, AST, lane, a);
+        frag_b(Tf + c0 * AST + c0 + 8 * nt, AST, lane, b);
+        mma16816(x, a, b);
+        float *X = Xf + pb * 256 + 8 * nt;  // [16][16]
+        st_frag_c(X, 16, lane, x, 1.f);
+        __syncwarp();
+        float y[4] = {0.f, 0.f, 0.f, 0.f};
+        frag_a(Tf + r0 * AST + r0, AST, lane, a);
+        frag_b(X, 16, lane, b);
+        mma16816(y, a, b);
+        st_frag_c(Tf + r0 * AST + c0 + 8 * nt, AST, lane, y, -1.f);
     }
     __syncthreads();
-    // Off-diagonal tiles by distance: T_IJ = -T_II sum_{K=J}^{I-1} A_IK T_KJ.
-#pragma unroll 1
-    for (int dist = 1; dist < 4; ++dist) {
-        const int nb = 4 - dist;
-        for (int idx = tid; idx < nb * 256; idx += NT) {
-            const int b = idx >> 8, e = idx & 255, r = e >> 4, c = e & 15;
-            const int I = b + dist, J = b;
-            float acc = 0.f;
-            for (int K = J; K < I; ++K) {
-                const float *A = Af + (16 * I + r) * AST + 16 * K;
-                const float *T = Tf + (16 * K) * AST + 16 * J + c;
+    {
+        const int mt = warp >> 2, nt = warp & 3;
+        float y[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int kk = 0; kk < 16; ++kk) acc = fmaf(A[kk], T[kk * AST], acc);
-            }
-            Xf[b * 256 + e] = acc;
+        for (int ks = 0; ks < 2; ++ks) {
+            uint32_t a[4], b[2];
+            frag_a(Af + (32 + 16 * mt) * AST + 16 * ks, AST, lane, a);
+            frag_b(Tf + (16 * ks) * AST + 8 * nt, AST, lane, b);
+            mma16816(y, a, b);
         }
-        __syncthreads();
-        for (int idx = tid; idx < nb * 256; idx += NT) {
-            const int b = idx >> 8, e = idx & 255, r = e >> 4, c = e & 15;
-            const int I = b + dist, J = b;
-            const float *D = Tf + (16 * I + r) * AST + 16 * I;
-            float acc = 0.f;
-#pragma unroll
-            for (int kk = 0; kk < 16; ++kk) acc = fmaf(D[kk], Xf[b * 256 + kk * 16 + c], acc);
-            Tf[(16 * I + r) * AST + 16 * J + c] = -acc;
-        }
-        __syncthreads();
+        st_frag_c(Xf + (16 * mt) * 32 + 8 * nt, 32, lane, y, 1.f);  // Y [32][32]
     }
+    __syncthreads();
+    {
+        const int mt = warp >> 2, nt = warp & 3;
+        float y[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+            uint32_t a[4], b[2];
+            frag_a(Tf + (32 + 16 * mt) * AST + 32 + 16 * ks, AST, lane, a);
+            frag_b(Xf + (16 * ks) * 32 + 8 * nt, 32, lane, b);
+            mma16816(y, a, b);
+        }
+        st_frag_c(Tf + (32 + 16 * mt) * AST + 8 * nt, AST, lane, y, -1.f);
+    }
+    __syncthreads();
 }
 
 __global__ void __launch_bounds__(NT, 1)
@@ -221,9 +308,13 @@ __global__ void __launch_bounds__(NT, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    const int tid = threadIdx.x, warp = tid >> 5;
-    float *sa = reinterpret_cast<float *>(smem + OFF_SMALL);
-    float *sb = sa + 64, *sg = sa + 128, *spend = sa + 192;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // TMEM lane (accumulator row) of this thread and the column half it owns.
+    const int row = 32 * (warp & 3) + lane;
+    const int half = warp >> 2;
+    float *sgl = reinterpret_cast<float *>(smem + OFF_SMALL);  // [64] prefix log2 alpha
+    int *sz = reinterpret_cast<int *>(sgl + 64);                // [64] zero-alpha count
+    float *sbeta = sgl + 128, *sgam = sgl + 192, *spl = sgl + 256, *sbg = sgl + 320;
     uint64_t *bar_load = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
     uint64_t *bar_mma = bar_load + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_load + 3);
@@ -249,7 +340,7 @@ __global__ void __launch_bounds__(NT, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);  // this thread's lane
+    const uint32_t trow = tmem + (static_cast<uint32_t>(warp & 3) << 21);  // lane (32 (w&3)) << 16
 
     const int H = p.H;
     int64_t n_seq = p.n_seq;
@@ -265,6 +356,7 @@ __global__ void __launch_bounds__(NT, 1)
     int pending_stage = -1;  // thread 0: a requested tile not yet consumed
     uint32_t pending_parity = 0;
     bool failed = false, mma_pending = false;
+    float ga0 = 1.f, ga1 = 1.f, gb0 = 0.f, gb1 = 0.f;  // warp 0: gates of the chunk ahead
 
     auto issue_loads = [&](uint32_t iter, int64_t tok, int h) {
         const uint32_t st = iter & 1u;
@@ -317,33 +409,23 @@ __global__ void __launch_bounds__(NT, 1)
         }
         const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
 
-        // ---- initial state: row tid of S -> TMEM (fp32) and the fp16 copy
+        // ---- initial state: (row, half) -> TMEM (fp32) and the fp16 copy
         {
             int64_t slot = -1;
             if (p.state_in) slot = p.in_slots ? static_cast<int64_t>(p.in_slots[seq]) : seq;
             const bool have = p.state_in && slot >= 0 && slot < p.num_slots;
-            const float *src = have ? p.state_in + ((slot * H + h) * HD + tid) * HD : nullptr;
+            const float *src = have ? p.state_in + ((slot * H + h) * HD + row) * HD + 64 * half : nullptr;
 #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
+            for (int q2 = 0; q2 < 2; ++q2) {
                 float v[32];
 #pragma unroll
                 for (int e = 0; e < 32; e += 4) {
-                    float4 f = have ? *reinterpret_cast<const float4 *>(src + 32 * q4 + e)
+                    float4 f = have ? *reinterpret_cast<const float4 *>(src + 32 * q2 + e)
                                     : make_float4(0.f, 0.f, 0.f, 0.f);
                     v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
                 }
-                tmem_st32(trow + TM_S + 32 * q4, v);
-                // fp16 copy: columns 32*q4 .. +31 -> half q4/2, chunks (q4&1)*4 .. +3
-                uint8_t *blk = smem + OFF_S + (q4 >> 1) * 16384;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint4 w;
-                    w.x = pack_f16x2(v[8 * c + 0], v[8 * c + 1]);
-                    w.y = pack_f16x2(v[8 * c + 2], v[8 * c + 3]);
-                    w.z = pack_f16x2(v[8 * c + 4], v[8 * c + 5]);
-                    w.w = pack_f16x2(v[8 * c + 6], v[8 * c + 7]);
-                    *reinterpret_cast<uint4 *>(blk + sw128_offset(tid, (q4 & 1) * 4 + c)) = w;
-                }
+                tmem_st32(trow + TM_S + 64 * half + 32 * q2, v);
+                st_row32_f16(smem + OFF_S + half * 16384, row, 4 * q2, v);
             }
             tmem_wait_st();
         }
@@ -358,11 +440,51 @@ __global__ void __launch_bounds__(NT, 1)
             const uint32_t kq = sbase + OFF_KQ + st * KQ_STAGE;
             const uint32_t vb = sbase + OFF_V + st * V_STAGE;
 
-            // Gates (padded rows: alpha = 1, beta = 0 -> they write nothing).
-            if (tid < CH) {
-                const bool in = tid < L;
-                sa[tid] = in ? p.alpha[(ts + tid) * H + h] : 1.f;
-                sb[tid] = in ? p.beta[(ts + tid) * H + h] : 0.f;
+            // ---- gate tables (warp 0, two positions per lane): prefix sums of
+            // log2 alpha over nonzero alphas and of zero-alpha counts; padded
+            // rows get alpha = 1, beta = 0 so they write nothing. The gates of
+            // the next chunk of the same sequence are fetched here too, so
+            // their global-load latency is hidden behind this chunk.
+            if (warp == 0) {
+                const int p0 = 2 * lane, p1 = p0 + 1;
+                if (c == 0) {
+                    ga0 = p0 < L ? p.alpha[(ts + p0) * H + h] : 1.f;
+                    ga1 = p1 < L ? p.alpha[(ts + p1) * H + h] : 1.f;
+                    gb0 = p0 < L ? p.beta[(ts + p0) * H + h] : 0.f;
+                    gb1 = p1 < L ? p.beta[(ts + p1) * H + h] : 0.f;
+                }
+                const float a0 = ga0, a1 = ga1, b0 = gb0, b1 = gb1;
+                if (c + 1 < nch) {
+                    const int64_t tn = ts + CH;
+                    const int Ln = static_cast<int>((t1 - tn) < CH ? (t1 - tn) : CH);
+                    ga0 = p0 < Ln ? p.alpha[(tn + p0) * H + h] : 1.f;
+                    ga1 = p1 < Ln ? p.alpha[(tn + p1) * H + h] : 1.f;
+                    gb0 = p0 < Ln ? p.beta[(tn + p0) * H + h] : 0.f;
+                    gb1 = p1 < Ln ? p.beta[(tn + p1) * H + h] : 0.f;
+                }
+                const bool nz0 = a0 >= 1.17549435e-38f, nz1 = a1 >= 1.17549435e-38f;
+                const float l0 = nz0 ? lg2(a0) : 0.f, l1 = nz1 ? lg2(a1) : 0.f;
+                const int z0 = nz0 ? 0 : 1, z1 = nz1 ? 0 : 1;
+                float ls = l0 + l1;
+                int zs = z0 + z1;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const float lo = __shfl_up_sync(0xffffffffu, ls, off);
+                    const int zo = __shfl_up_sync(0xffffffffu, zs, off);
+                    if (lane >= off) { ls += lo; zs += zo; }
+                }
+                const float g1 = ls, g0 = ls - l1;   // inclusive prefix at p1, p0
+                const int y1 = zs, y0 = zs - z1;
+                const float g63 = __shfl_sync(0xffffffffu, g1, 31);
+                const int y63 = __shfl_sync(0xffffffffu, y1, 31);
+                sgl[p0] = g0; sgl[p1] = g1;
+                sz[p0] = y0; sz[p1] = y1;
+                sbeta[p0] = b0; sbeta[p1] = b1;
+                const float gm0 = y0 == 0 ? ex2(g0) : 0.f, gm1 = y1 == 0 ? ex2(g1) : 0.f;
+                sgam[p0] = gm0; sgam[p1] = gm1;
+                sbg[p0] = b0 * gm0; sbg[p1] = b1 * gm1;
+                spl[p0] = y0 == y63 ? ex2(g63 - g0) : 0.f;
+                spl[p1] = y1 == y63 ? ex2(g63 - g1) : 0.f;
             }
             const bool ok = mbar_wait(&bar_load[st], lpar);
             if (__syncthreads_or(!ok)) { failed = true; break; }
@@ -378,77 +500,139 @@ __global__ void __launch_bounds__(NT, 1)
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
                     umma_f16(tmem + TM_D1, sdesc_sw128(kq + off, 16, 1024),
-                              sdesc_sw128(kq + off, 16, 1024), ID_D1, kk > 0);
+                             sdesc_sw128(kq + off, 16, 1024), ID_D1, kk > 0);
                 }
             }
             if (!mma_sync()) { failed = true; break; }
-            tiles_to_f16(smem + OFF_KQ + st * KQ_STAGE, smem + OFF_V + st * V_STAGE, tid);
+
+            // ---- A = beta P (K K^T) (fp32) and M = P (Q K^T) (fp16), 32 columns per thread
             {
-                float x[64];
-                tmem_ld64(trow + TM_D1, x);
-                tmem_wait_ld();
-                const int r = tid & 63;
-                const bool qk = tid >= 64;
-                const float br = sb[r];
-                float run = 1.f;
-#pragma unroll
-                for (int s = 63; s >= 0; --s) {
-                    const bool in = s <= r;
-                    const float ps = in ? run : 0.f;
-                    if (tid == 63) spend[s] = ps;
-                    x[s] = qk ? (in ? ps * x[s] : 0.f) : (s < r ? br * ps * x[s] : 0.f);
-                    run = in ? run * sa[s] : run;
-                }
-                if (!qk) {
-                    sg[r] = run;
-#pragma unroll
-                    for (int s = 0; s < 64; ++s) Af[r * AST + s] = x[s];
+                const bool qk = row >= 64;
+                const int t = row & 63;
+                const int s0 = 32 * half;
+                // Warp-uniform: the whole 32 x 32 block lies above the diagonal.
+                if (half == 1 && (warp & 1) == 0) {
+                    if (qk) st_zero32(smem + OFF_M, t, 4);
                 } else {
-                    st_row64_f16(smem + OFF_M, r, x);
+                    float v[32];
+                    tmem_ld32(trow + TM_D1 + s0, v);
+                    tmem_wait_ld();
+                    const float glt = sgl[t];
+                    const int zt = sz[t];
+                    const float bt = qk ? 1.f : sbeta[t];
+#pragma unroll
+                    for (int j4 = 0; j4 < 8; ++j4) {
+                        const float4 g4 = *reinterpret_cast<const float4 *>(sgl + s0 + 4 * j4);
+                        const int4 z4 = *reinterpret_cast<const int4 *>(sz + s0 + 4 * j4);
+                        const float gs[4] = {g4.x, g4.y, g4.z, g4.w};
+                        const int zs[4] = {z4.x, z4.y, z4.z, z4.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int j = 4 * j4 + e, s = s0 + j;
+                            const float pv = zs[e] == zt ? ex2(glt - gs[e]) : 0.f;
+                            const bool keep = qk ? (s <= t) : (s < t);
+                            v[j] = keep ? bt * pv * v[j] : 0.f;
+                        }
+                    }
+                    if (qk) {
+                        st_row32_f16(smem + OFF_M, t, 4 * half, v);
+                    } else {
+#pragma unroll
+                        for (int j4 = 0; j4 < 8; ++j4)
+                            *reinterpret_cast<float4 *>(Af + t * AST + s0 + 4 * j4) =
+                                make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+                    }
                 }
             }
             __syncthreads();
-            solve_unit_lower(Af, Tf, Xf, tid);
+
+            // ---- diagonal 16 x 16 tiles of T (warps 0-1) while warps 2-7
+            // convert this stage's tiles to fp16
+            if (tid < 64) {
+                const int I = tid >> 4, j = tid & 15;
+                float x[16];
+#pragma unroll
+                for (int r = 0; r < 16; ++r) {
+                    const float *arow = Af + (16 * I + r) * AST + 16 * I;
+                    float a[16];
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        const float4 f = *reinterpret_cast<const float4 *>(arow + 4 * c4);
+                        a[4 * c4] = f.x; a[4 * c4 + 1] = f.y; a[4 * c4 + 2] = f.z; a[4 * c4 + 3] = f.w;
+                    }
+                    float acc = (r == j) ? 1.f : 0.f;
+#pragma unroll
+                    for (int cc = 0; cc < r; ++cc)
+                        if (cc >= j) acc = fmaf(-a[cc], x[cc], acc);
+                    x[r] = (r >= j) ? acc : 0.f;
+                    Tf[(16 * I + r) * AST + 16 * I + j] = x[r];
+                }
+            } else {
+                // Tiles (0,1) and (2,3) of T are zero (read by the 32 x 32 products).
+                for (int e = tid - 64; e < 512; e += NT - 64) {
+                    const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
+                    Tf[(32 * blk + rr) * AST + 32 * blk + 16 + cc] = 0.f;
+                }
+                tiles_to_f16(smem + OFF_KQ + st * KQ_STAGE, smem + OFF_V + st * V_STAGE, sgam,
+                             tid - 64, NT - 64);
+            }
+            __syncthreads();
+            solve_offdiag(Af, Tf, Xf, warp, lane);
+
+            // ---- T diag(beta) and T diag(beta gamma) as fp16 operands
             {
                 const int t = tid & 63;
-                const bool hat = tid >= 64;
-                float x[64];
+                const bool hat = (tid >> 6) & 1;
+                const int hh = tid >> 7;
+                const int s0 = 32 * hh;
+                uint8_t *dst = smem + (hat ? OFF_TH : OFF_TT);
+                if (hh == 1 && t < 32) {
+                    st_zero32(dst, t, 4);
+                } else {
+                    const float *sc = hat ? sbg : sbeta;
+                    float v[32];
 #pragma unroll
-                for (int s = 0; s < 64; ++s) {
-                    const float sc = hat ? sb[s] * sg[s] : sb[s];
-                    x[s] = Tf[t * AST + s] * sc;
+                    for (int j4 = 0; j4 < 8; ++j4) {
+                        const float4 tv = *reinterpret_cast<const float4 *>(Tf + t * AST + s0 + 4 * j4);
+                        const float4 sv = *reinterpret_cast<const float4 *>(sc + s0 + 4 * j4);
+                        const int s = s0 + 4 * j4;
+                        v[4 * j4 + 0] = s + 0 <= t ? tv.x * sv.x : 0.f;
+                        v[4 * j4 + 1] = s + 1 <= t ? tv.y * sv.y : 0.f;
+                        v[4 * j4 + 2] = s + 2 <= t ? tv.z * sv.z : 0.f;
+                        v[4 * j4 + 3] = s + 3 <= t ? tv.w * sv.w : 0.f;
+                    }
+                    st_row32_f16(dst, t, 4 * hh, v);
                 }
-                st_row64_f16(smem + (hat ? OFF_TH : OFF_TT), t, x);
             }
             operands_ready();
 
-            // ---- D_U = V^T (T diag b)^T, D_W = K^T (T diag bg)^T, D_SQ = S0 Q^T
+            // ---- D_U = V^T (T diag b)^T, D_W = K^T (T diag bg)^T, D_O = Q~ S0^T
             if (tid == 0) {
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     umma_f16(tmem + TM_U, sdesc_sw128(vb + kk * 2048, 8192, 1024),
-                              sdesc_sw128(sbase + OFF_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
+                             sdesc_sw128(sbase + OFF_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
                 }
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     umma_f16(tmem + TM_W, sdesc_sw128(kq + kk * 2048, 16384, 1024),
-                              sdesc_sw128(sbase + OFF_TH + kk * 32, 16, 1024), ID_MK64, kk > 0);
+                             sdesc_sw128(sbase + OFF_TH + kk * 32, 16, 1024), ID_MK64, kk > 0);
                 }
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_f16(tmem + TM_SQ, sdesc_sw128(sbase + OFF_S + off, 16, 1024),
-                              sdesc_sw128(kq + off + 8192, 16, 1024), ID_KK64, kk > 0);
+                    umma_f16(tmem + TM_O, sdesc_sw128(kq + off + 8192, 16, 1024),
+                             sdesc_sw128(sbase + OFF_S + off, 16, 1024), ID_O, kk > 0);
                 }
             }
             if (!mma_sync()) { failed = true; break; }
             {
-                float x[64];
-                tmem_ld64(trow + TM_W, x);  // W[t][j = tid] for all t
+                float x[32];
+                tmem_ld32(trow + TM_W + 32 * half, x);  // W[t][j = row], t in this half
                 tmem_wait_ld();
 #pragma unroll
-                for (int t = 0; t < 64; ++t) x[t] = -x[t];
-                st_row64_f16(smem + OFF_WT, tid, x);
+                for (int t = 0; t < 32; ++t) x[t] = -x[t];
+                st_row32_f16(smem + OFF_WT, row, 4 * half, x);
             }
             operands_ready();
 
@@ -458,74 +642,81 @@ __global__ void __launch_bounds__(NT, 1)
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
                     umma_f16(tmem + TM_U, sdesc_sw128(sbase + OFF_S + off, 16, 1024),
-                              sdesc_sw128(sbase + OFF_WT + kk * 2048, 8192, 1024), ID_KM64, 1);
+                             sdesc_sw128(sbase + OFF_WT + kk * 2048, 8192, 1024), ID_KM64, 1);
                 }
             }
             if (!mma_sync()) { failed = true; break; }
             {
-                float x[64];
-                tmem_ld64(trow + TM_U, x);  // Delta[s][i = tid] for all s
+                float x[32];
+                tmem_ld32(trow + TM_U + 32 * half, x);  // Delta[s][i = row], s in this half
                 tmem_wait_ld();
-                st_row64_f16(smem + OFF_DT, tid, x);
+                st_row32_f16(smem + OFF_DT, row, 4 * half, x);
 #pragma unroll
-                for (int s = 0; s < 64; ++s) x[s] *= spend[s];
-                st_row64_f16(smem + OFF_DTS, tid, x);
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    const float4 pl = *reinterpret_cast<const float4 *>(spl + 32 * half + 4 * j4);
+                    x[4 * j4] *= pl.x; x[4 * j4 + 1] *= pl.y; x[4 * j4 + 2] *= pl.z; x[4 * j4 + 3] *= pl.w;
+                }
+                st_row32_f16(smem + OFF_DTS, row, 4 * half, x);
                 // D_S <- gamma_{C-1} D_S before the rank-C update accumulates.
-                const float gC = sg[63];
+                const float gC = sgam[63];
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
+                for (int q2 = 0; q2 < 2; ++q2) {
                     float v[32];
-                    tmem_ld32(trow + TM_S + 32 * q4, v);
+                    tmem_ld32(trow + TM_S + 64 * half + 32 * q2, v);
                     tmem_wait_ld();
 #pragma unroll
                     for (int e = 0; e < 32; ++e) v[e] *= gC;
-                    tmem_st32(trow + TM_S + 32 * q4, v);
+                    tmem_st32(trow + TM_S + 64 * half + 32 * q2, v);
                 }
                 tmem_wait_st();
             }
             operands_ready();
 
-            // ---- D_O2 = Delta^T M^T ; D_S += (P[C-1] Delta)^T K
+            // ---- D_O += M Delta ; D_S += (P[C-1] Delta)^T K
             if (tid == 0) {
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    umma_f16(tmem + TM_O2, sdesc_sw128(sbase + OFF_DT + kk * 32, 16, 1024),
-                              sdesc_sw128(sbase + OFF_M + kk * 32, 16, 1024), ID_KK64, kk > 0);
+                    umma_f16(tmem + TM_O, sdesc_sw128(sbase + OFF_M + kk * 32, 16, 1024),
+                             sdesc_sw128(sbase + OFF_DT + kk * 32, 16, 1024), ID_O, 1);
                 }
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     umma_f16(tmem + TM_S, sdesc_sw128(sbase + OFF_DTS + kk * 32, 16, 1024),
-                              sdesc_sw128(kq + kk * 2048, 16384, 1024), ID_KM128, 1);
+                             sdesc_sw128(kq + kk * 2048, 16384, 1024), ID_KM128, 1);
                 }
             }
             if (!mma_sync()) { failed = true; break; }
 
-            // ---- epilogue: O = gamma (S0 Q^T) + Delta^T M^T; refresh the fp16 state
+            // ---- epilogue: O rows (D_O row t sits in lane 32 (t / 16) + t % 16;
+            // lanes 16..31 of each warp hold no row) go out as 16-byte stores;
+            // refresh the fp16 state copy
             {
-                float sq[64], o2[64];
-                tmem_ld64(trow + TM_SQ, sq);
-                tmem_ld64(trow + TM_O2, o2);
-                tmem_wait_ld();
-                __nv_bfloat16 *op = p.o + ts * tok_stride + static_cast<int64_t>(h) * HD + tid;
+                float o[32];
+                const int t = 16 * (warp & 3) + lane;
+                const bool has_row = lane < 16 && t < L;
+                __nv_bfloat16 *op = p.o + (ts + t) * tok_stride + static_cast<int64_t>(h) * HD + 64 * half;
 #pragma unroll
-                for (int t = 0; t < 64; ++t) {
-                    if (t < L) op[t * tok_stride] = __float2bfloat16_rn(fmaf(sg[t], sq[t], o2[t]));
+                for (int q2 = 0; q2 < 2; ++q2) {
+                    tmem_ld32(trow + TM_O + 64 * half + 32 * q2, o);
+                    tmem_wait_ld();
+                    if (has_row) {
+#pragma unroll
+                        for (int c8 = 0; c8 < 4; ++c8) {
+                            uint4 w;
+                            w.x = pack_bf16x2(o[8 * c8 + 0], o[8 * c8 + 1]);
+                            w.y = pack_bf16x2(o[8 * c8 + 2], o[8 * c8 + 3]);
+                            w.z = pack_bf16x2(o[8 * c8 + 4], o[8 * c8 + 5]);
+                            w.w = pack_bf16x2(o[8 * c8 + 6], o[8 * c8 + 7]);
+                            *reinterpret_cast<uint4 *>(op + 32 * q2 + 8 * c8) = w;
+                        }
+                    }
                 }
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
+                for (int q2 = 0; q2 < 2; ++q2) {
                     float v[32];
-                    tmem_ld32(trow + TM_S + 32 * q4, v);
+                    tmem_ld32(trow + TM_S + 64 * half + 32 * q2, v);
                     tmem_wait_ld();
-                    uint8_t *blk = smem + OFF_S + (q4 >> 1) * 16384;
-#pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) {
-                        uint4 w;
-                        w.x = pack_f16x2(v[8 * cc + 0], v[8 * cc + 1]);
-                        w.y = pack_f16x2(v[8 * cc + 2], v[8 * cc + 3]);
-                        w.z = pack_f16x2(v[8 * cc + 4], v[8 * cc + 5]);
-                        w.w = pack_f16x2(v[8 * cc + 6], v[8 * cc + 7]);
-                        *reinterpret_cast<uint4 *>(blk + sw128_offset(tid, (q4 & 1) * 4 + cc)) = w;
-                    }
+                    st_row32_f16(smem + OFF_S + half * 16384, row, 4 * q2, v);
                 }
             }
             operands_ready();
@@ -536,15 +727,15 @@ __global__ void __launch_bounds__(NT, 1)
         if (p.state_out) {
             const int64_t slot = p.out_slots ? static_cast<int64_t>(p.out_slots[seq]) : seq;
             if (slot >= 0 && slot < p.num_slots) {
-                float *dst = p.state_out + ((slot * H + h) * HD + tid) * HD;
+                float *dst = p.state_out + ((slot * H + h) * HD + row) * HD + 64 * half;
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
+                for (int q2 = 0; q2 < 2; ++q2) {
                     float v[32];
-                    tmem_ld32(trow + TM_S + 32 * q4, v);
+                    tmem_ld32(trow + TM_S + 64 * half + 32 * q2, v);
                     tmem_wait_ld();
 #pragma unroll
                     for (int e = 0; e < 32; e += 4)
-                        *reinterpret_cast<float4 *>(dst + 32 * q4 + e) =
+                        *reinterpret_cast<float4 *>(dst + 32 * q2 + e) =
                             make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
                 }
             }
