@@ -90,8 +90,8 @@ constexpr uint32_t OFF_DTS = OFF_R + 32768;        //   (P[C-1] Delta)^T [i][s] 
 constexpr uint32_t OFF_AF = OFF_R;                 //   A fp32 [64][AST]   (solve phase)
 constexpr uint32_t OFF_TF = OFF_AF + 64 * AST * 4; //   T fp32 [64][AST]
 constexpr uint32_t OFF_XF = OFF_TF + 64 * AST * 4; //   32 x 32 fp32 partial products
-constexpr uint32_t OFF_SMALL = OFF_R + 49152;      // gl, z, beta, gamma, P[C-1][.], beta*gamma
-constexpr uint32_t OFF_BAR = OFF_SMALL + 2048;     // 3 mbarriers + TMEM base address
+constexpr uint32_t OFF_SMALL = OFF_R + 49152;      // 2 x {gl, z, beta, gamma, P[C-1][.], beta*gamma}
+constexpr uint32_t OFF_BAR = OFF_SMALL + 3072;     // 4 mbarriers + TMEM base address
 constexpr uint32_t SMEM_USED = OFF_BAR + 64;
 constexpr size_t SMEM_ALLOC = SMEM_USED + 1024;    // slack for 1024-byte alignment
 static_assert(OFF_XF + 4 * 256 * 4 <= OFF_R + 49152, "solve scratch overflows its region");
@@ -102,8 +102,8 @@ static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in shared memory");
 constexpr uint32_t TM_D1 = 0, TM_U = 64, TM_W = 128, TM_O = 192, TM_S = 320;
 constexpr uint32_t TM_COLS = 512;
 
-// D1 runs on the bf16 tiles as loaded; every later product runs in fp16.
-constexpr uint32_t ID_D1 = idesc_bf16(128, 64, false, false);
+// Every product runs on fp16 operands (the bf16 tiles are converted in place).
+constexpr uint32_t ID_D1 = idesc_f16(128, 64, false, false);
 constexpr uint32_t ID_MK64 = idesc_f16(128, 64, true, false);
 constexpr uint32_t ID_KM64 = idesc_f16(128, 64, false, true);
 constexpr uint32_t ID_KM128 = idesc_f16(128, 128, false, true);
@@ -175,35 +175,18 @@ __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x) {
     return pack_f16x2(__low2float(b), __high2float(b));
 }
 
-__device__ __forceinline__ uint32_t bf16x2_to_f16x2_scaled(uint32_t x, float s) {
-    __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162 *>(&x);
-    return pack_f16x2(s * __low2float(b), s * __high2float(b));
-}
-
 // bf16 -> fp16 in place on 16-byte chunks [first, 3072) of one stage's K, Q
-// (32 KB) and V (16 KB) tiles, stepping by `stride`. Q rows are scaled by
-// gamma_t on the way (Q~ = diag(gamma) Q feeds O = Q~ S0^T + M Delta). The
-// swizzled layout is elementwise, so it is unchanged; bf16 values in the fp16
-// normal range convert exactly.
-__device__ __forceinline__ void tiles_to_f16(uint8_t *kq, uint8_t *vv, const float *gam, int first,
-                                             int stride) {
+// (32 KB) and V (16 KB) tiles, stepping by `stride`. The swizzled layout is
+// elementwise, so it is unchanged; bf16 values in the fp16 normal range
+// convert exactly.
+__device__ __forceinline__ void tiles_to_f16(uint8_t *kq, uint8_t *vv, int first, int stride) {
     for (int i = first; i < 3072; i += stride) {
         uint4 *ptr = reinterpret_cast<uint4 *>(i < 2048 ? kq + i * 16 : vv + (i - 2048) * 16);
         uint4 w = *ptr;
-        // KQ stage: [half][K 64 rows | Q 64 rows] of 128-byte rows.
-        const bool is_q = i < 2048 && (i & 1023) >= 512;
-        if (is_q) {
-            const float g = gam[(i & 511) >> 3];
-            w.x = bf16x2_to_f16x2_scaled(w.x, g);
-            w.y = bf16x2_to_f16x2_scaled(w.y, g);
-            w.z = bf16x2_to_f16x2_scaled(w.z, g);
-            w.w = bf16x2_to_f16x2_scaled(w.w, g);
-        } else {
-            w.x = bf16x2_to_f16x2(w.x);
-            w.y = bf16x2_to_f16x2(w.y);
-            w.z = bf16x2_to_f16x2(w.z);
-            w.w = bf16x2_to_f16x2(w.w);
-        }
+        w.x = bf16x2_to_f16x2(w.x);
+        w.y = bf16x2_to_f16x2(w.y);
+        w.z = bf16x2_to_f16x2(w.z);
+        w.w = bf16x2_to_f16x2(w.w);
         *ptr = w;
     }
 }
@@ -312,12 +295,10 @@ __global__ void __launch_bounds__(NT, 1)
     // TMEM lane (accumulator row) of this thread and the column half it owns.
     const int row = 32 * (warp & 3) + lane;
     const int half = warp >> 2;
-    float *sgl = reinterpret_cast<float *>(smem + OFF_SMALL);  // [64] prefix log2 alpha
-    int *sz = reinterpret_cast<int *>(sgl + 64);                // [64] zero-alpha count
-    float *sbeta = sgl + 128, *sgam = sgl + 192, *spl = sgl + 256, *sbg = sgl + 320;
-    uint64_t *bar_load = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
-    uint64_t *bar_mma = bar_load + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_load + 3);
+    uint64_t *bar_load = reinterpret_cast<uint64_t *>(smem + OFF_BAR);  // [2] TMA per stage
+    uint64_t *bar_mma = bar_load + 2;                                   // state-chain MMAs
+    uint64_t *bar_d1 = bar_load + 3;                                    // D1 of the next chunk
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_load + 4);
     float *Af = reinterpret_cast<float *>(smem + OFF_AF);
     float *Tf = reinterpret_cast<float *>(smem + OFF_TF);
     float *Xf = reinterpret_cast<float *>(smem + OFF_XF);
@@ -327,6 +308,7 @@ __global__ void __launch_bounds__(NT, 1)
         mbar_init(&bar_load[0], 1);
         mbar_init(&bar_load[1], 1);
         mbar_init(bar_mma, 1);
+        mbar_init(bar_d1, 1);
         mbar_fence_init();
         prefetch_tmap(&tm_q);
         prefetch_tmap(&tm_k);
@@ -351,52 +333,11 @@ __global__ void __launch_bounds__(NT, 1)
     const int64_t n_items = n_seq * H;
     const int64_t tok_stride = static_cast<int64_t>(H) * HD;
 
-    uint32_t load_iter = 0;  // chunk tiles requested so far
-    uint32_t mma_phase = 0;
-    int pending_stage = -1;  // thread 0: a requested tile not yet consumed
-    uint32_t pending_parity = 0;
-    bool failed = false, mma_pending = false;
-    float ga0 = 1.f, ga1 = 1.f, gb0 = 0.f, gb1 = 0.f;  // warp 0: gates of the chunk ahead
-
-    auto issue_loads = [&](uint32_t iter, int64_t tok, int h) {
-        const uint32_t st = iter & 1u;
-        uint64_t *bar = &bar_load[st];
-        uint8_t *kq = smem + OFF_KQ + st * KQ_STAGE;
-        uint8_t *vv = smem + OFF_V + st * V_STAGE;
-        mbar_arrive_expect_tx(bar, LOAD_BYTES);
-        const int t32 = static_cast<int>(tok);
-        tma_load_3d(kq, &tm_k, 0, h, t32, bar);
-        tma_load_3d(kq + 16384, &tm_k, 64, h, t32, bar);
-        tma_load_3d(kq + 8192, &tm_q, 0, h, t32, bar);
-        tma_load_3d(kq + 24576, &tm_q, 64, h, t32, bar);
-        tma_load_3d(vv, &tm_v, 0, h, t32, bar);
-        tma_load_3d(vv + 8192, &tm_v, 64, h, t32, bar);
-        pending_stage = static_cast<int>(st);
-        pending_parity = (iter >> 1) & 1u;
-    };
-    // Commit the issued MMAs and wait for them on every thread.
-    auto mma_sync = [&]() -> bool {
-        if (tid == 0) umma_commit(bar_mma);
-        mma_pending = true;
-        const bool ok = mbar_wait(bar_mma, mma_phase);
-        if (__syncthreads_or(!ok)) return false;
-        mma_phase ^= 1u;
-        mma_pending = false;
-        tc_fence_after();
-        return true;
-    };
-    // Make thread-written smem operands and TMEM stores visible to the MMA issuer.
-    auto operands_ready = [&]() {
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-    };
-
-    for (int64_t item = blockIdx.x; item < n_items && !failed; item += gridDim.x) {
+    // The chunks this CTA processes, in order: items blockIdx.x, +gridDim.x,
+    // ..., and within an item its chunks of CH positions from the sequence
+    // start. Chunk k of that order uses TMA stage k & 1 and gate tables k & 1.
+    auto bounds = [&](int64_t item, int64_t &t0, int64_t &t1) {
         const int64_t seq = item / H;
-        const int h = static_cast<int>(item - seq * H);
-        int64_t t0, t1;
         if (p.cu_seqlens) {
             // Offsets are caller data: clamp them to the packed stream.
             t0 = p.cu_seqlens[seq];
@@ -407,6 +348,150 @@ __global__ void __launch_bounds__(NT, 1)
             t0 = seq * p.seq_len;
             t1 = t0 + p.seq_len;
         }
+    };
+    struct Ref {
+        int64_t item, ts;  // item < 0: no chunk
+        int L, h;
+    };
+    // First chunk at or after item `it` (skipping empty sequences).
+    auto first_from = [&](int64_t it) -> Ref {
+        for (; it < n_items; it += gridDim.x) {
+            int64_t t0, t1;
+            bounds(it, t0, t1);
+            if (t1 > t0) {
+                const int64_t seq = it / H;
+                return Ref{it, t0, static_cast<int>((t1 - t0) < CH ? (t1 - t0) : CH),
+                           static_cast<int>(it - seq * H)};
+            }
+        }
+        return Ref{-1, 0, 0, 0};
+    };
+    auto next_of = [&](const Ref &r) -> Ref {
+        int64_t t0, t1;
+        bounds(r.item, t0, t1);
+        const int64_t tn = r.ts + CH;
+        if (tn < t1) return Ref{r.item, tn, static_cast<int>((t1 - tn) < CH ? (t1 - tn) : CH), r.h};
+        return first_from(r.item + gridDim.x);
+    };
+
+    uint32_t mma_phase = 0;
+    bool failed = false, mma_pending = false, d1_pending = false;
+    int loads_issued = 0, loads_waited = 0;  // thread 0 / all threads
+
+    auto issue_loads = [&](int k, const Ref &r) {
+        const uint32_t st = k & 1;
+        uint64_t *bar = &bar_load[st];
+        uint8_t *kq = smem + OFF_KQ + st * KQ_STAGE;
+        uint8_t *vv = smem + OFF_V + st * V_STAGE;
+        mbar_arrive_expect_tx(bar, LOAD_BYTES);
+        const int t32 = static_cast<int>(r.ts);
+        tma_load_3d(kq, &tm_k, 0, r.h, t32, bar);
+        tma_load_3d(kq + 16384, &tm_k, 64, r.h, t32, bar);
+        tma_load_3d(kq + 8192, &tm_q, 0, r.h, t32, bar);
+        tma_load_3d(kq + 24576, &tm_q, 64, r.h, t32, bar);
+        tma_load_3d(vv, &tm_v, 0, r.h, t32, bar);
+        tma_load_3d(vv + 8192, &tm_v, 64, r.h, t32, bar);
+    };
+    // Commit the issued state-chain MMAs and wait for them on every thread.
+    auto mma_wait = [&]() -> bool {
+        const bool ok = mbar_wait(bar_mma, mma_phase);
+        if (__syncthreads_or(!ok)) return false;
+        mma_phase ^= 1u;
+        mma_pending = false;
+        tc_fence_after();
+        return true;
+    };
+    auto mma_commit = [&]() {
+        if (tid == 0) umma_commit(bar_mma);
+        mma_pending = true;
+    };
+    // Make thread-written smem operands and TMEM stores visible to the MMA issuer.
+    auto operands_ready = [&]() {
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    };
+
+    // Gate tables of chunk k (warp 0, two positions per lane): prefix sums of
+    // log2 alpha over nonzero alphas and of zero-alpha counts; padded rows get
+    // alpha = 1, beta = 0 so they write nothing.
+    auto gate_tables = [&](int k, const Ref &r) {
+        float *g = reinterpret_cast<float *>(smem + OFF_SMALL) + (k & 1) * 384;
+        int *zz = reinterpret_cast<int *>(g + 64);
+        float *be = g + 128, *gm = g + 192, *pl = g + 256, *bg = g + 320;
+        const int p0 = 2 * lane, p1 = p0 + 1;
+        const float a0 = p0 < r.L ? p.alpha[(r.ts + p0) * H + r.h] : 1.f;
+        const float a1 = p1 < r.L ? p.alpha[(r.ts + p1) * H + r.h] : 1.f;
+        const float b0 = p0 < r.L ? p.beta[(r.ts + p0) * H + r.h] : 0.f;
+        const float b1 = p1 < r.L ? p.beta[(r.ts + p1) * H + r.h] : 0.f;
+        const bool nz0 = a0 >= 1.17549435e-38f, nz1 = a1 >= 1.17549435e-38f;
+        const float l0 = nz0 ? lg2(a0) : 0.f, l1 = nz1 ? lg2(a1) : 0.f;
+        const int z0 = nz0 ? 0 : 1, z1 = nz1 ? 0 : 1;
+        float ls = l0 + l1;
+        int zs = z0 + z1;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const float lo = __shfl_up_sync(0xffffffffu, ls, off);
+            const int zo = __shfl_up_sync(0xffffffffu, zs, off);
+            if (lane >= off) { ls += lo; zs += zo; }
+        }
+        const float g1 = ls, g0 = ls - l1;  // inclusive prefix at p1, p0
+        const int y1 = zs, y0 = zs - z1;
+        const float g63 = __shfl_sync(0xffffffffu, g1, 31);
+        const int y63 = __shfl_sync(0xffffffffu, y1, 31);
+        g[p0] = g0; g[p1] = g1;
+        zz[p0] = y0; zz[p1] = y1;
+        be[p0] = b0; be[p1] = b1;
+        const float gm0 = y0 == 0 ? ex2(g0) : 0.f, gm1 = y1 == 0 ? ex2(g1) : 0.f;
+        gm[p0] = gm0; gm[p1] = gm1;
+        bg[p0] = b0 * gm0; bg[p1] = b1 * gm1;
+        pl[p0] = y0 == y63 ? ex2(g63 - g0) : 0.f;
+        pl[p1] = y1 == y63 ? ex2(g63 - g1) : 0.f;
+    };
+    // D1 = [K; Q] K^T of chunk k on its (fp16) tiles, tracked by bar_d1.
+    auto issue_d1 = [&](int kc) {
+        const uint32_t kq = sbase + OFF_KQ + (kc & 1) * KQ_STAGE;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_f16(tmem + TM_D1, sdesc_sw128(kq + off, 16, 1024), sdesc_sw128(kq + off, 16, 1024),
+                     ID_D1, kk > 0);
+        }
+        umma_commit(bar_d1);
+    };
+    // Everything chunk k needs before its first SIMT phase: gate tables, its
+    // tiles landed and converted to fp16, and D1 = [K; Q] K^T issued.
+    auto prepare = [&](int k, const Ref &r) -> bool {
+        if (warp == 0) gate_tables(k, r);
+        const bool ok = mbar_wait(&bar_load[k & 1], (k >> 1) & 1);
+        if (__syncthreads_or(!ok)) return false;
+        ++loads_waited;
+        tiles_to_f16(smem + OFF_KQ + (k & 1) * KQ_STAGE, smem + OFF_V + (k & 1) * V_STAGE, tid, NT);
+        operands_ready();
+        if (tid == 0) issue_d1(k);
+        d1_pending = true;
+        return true;
+    };
+
+    // Prime: tiles of the first two chunks, then chunk 0's preparation.
+    Ref cur = first_from(blockIdx.x);
+    {
+        const Ref second = cur.item >= 0 ? next_of(cur) : cur;
+        if (tid == 0) {
+            if (cur.item >= 0) issue_loads(0, cur);
+            if (second.item >= 0) issue_loads(1, second);
+        }
+        loads_issued = (cur.item >= 0) + (second.item >= 0);
+        if (cur.item >= 0 && !prepare(0, cur)) failed = true;
+    }
+    int k = 0;  // index of the chunk being processed
+
+    for (int64_t item = blockIdx.x; item < n_items && !failed; item += gridDim.x) {
+        const int64_t seq = item / H;
+        const int h = static_cast<int>(item - seq * H);
+        int64_t t0, t1;
+        bounds(item, t0, t1);
         const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
 
         // ---- initial state: (row, half) -> TMEM (fp32) and the fp16 copy
@@ -429,81 +514,24 @@ __global__ void __launch_bounds__(NT, 1)
             }
             tmem_wait_st();
         }
-        if (tid == 0 && nch > 0) issue_loads(load_iter, t0, h);
         operands_ready();
 
-        for (int c = 0; c < nch; ++c) {
+        for (int c = 0; c < nch; ++c, ++k) {
             const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
             const int L = static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH);
-            const uint32_t st = load_iter & 1u;
-            const uint32_t lpar = (load_iter >> 1) & 1u;
-            const uint32_t kq = sbase + OFF_KQ + st * KQ_STAGE;
-            const uint32_t vb = sbase + OFF_V + st * V_STAGE;
+            const uint32_t kq = sbase + OFF_KQ + (k & 1) * KQ_STAGE;
+            const uint32_t vb = sbase + OFF_V + (k & 1) * V_STAGE;
+            const float *sgl = reinterpret_cast<const float *>(smem + OFF_SMALL) + (k & 1) * 384;
+            const int *sz = reinterpret_cast<const int *>(sgl + 64);
+            const float *sbeta = sgl + 128, *sgam = sgl + 192, *spl = sgl + 256, *sbg = sgl + 320;
 
-            // ---- gate tables (warp 0, two positions per lane): prefix sums of
-            // log2 alpha over nonzero alphas and of zero-alpha counts; padded
-            // rows get alpha = 1, beta = 0 so they write nothing. The gates of
-            // the next chunk of the same sequence are fetched here too, so
-            // their global-load latency is hidden behind this chunk.
-            if (warp == 0) {
-                const int p0 = 2 * lane, p1 = p0 + 1;
-                if (c == 0) {
-                    ga0 = p0 < L ? p.alpha[(ts + p0) * H + h] : 1.f;
-                    ga1 = p1 < L ? p.alpha[(ts + p1) * H + h] : 1.f;
-                    gb0 = p0 < L ? p.beta[(ts + p0) * H + h] : 0.f;
-                    gb1 = p1 < L ? p.beta[(ts + p1) * H + h] : 0.f;
-                }
-                const float a0 = ga0, a1 = ga1, b0 = gb0, b1 = gb1;
-                if (c + 1 < nch) {
-                    const int64_t tn = ts + CH;
-                    const int Ln = static_cast<int>((t1 - tn) < CH ? (t1 - tn) : CH);
-                    ga0 = p0 < Ln ? p.alpha[(tn + p0) * H + h] : 1.f;
-                    ga1 = p1 < Ln ? p.alpha[(tn + p1) * H + h] : 1.f;
-                    gb0 = p0 < Ln ? p.beta[(tn + p0) * H + h] : 0.f;
-                    gb1 = p1 < Ln ? p.beta[(tn + p1) * H + h] : 0.f;
-                }
-                const bool nz0 = a0 >= 1.17549435e-38f, nz1 = a1 >= 1.17549435e-38f;
-                const float l0 = nz0 ? lg2(a0) : 0.f, l1 = nz1 ? lg2(a1) : 0.f;
-                const int z0 = nz0 ? 0 : 1, z1 = nz1 ? 0 : 1;
-                float ls = l0 + l1;
-                int zs = z0 + z1;
-#pragma unroll
-                for (int off = 1; off < 32; off <<= 1) {
-                    const float lo = __shfl_up_sync(0xffffffffu, ls, off);
-                    const int zo = __shfl_up_sync(0xffffffffu, zs, off);
-                    if (lane >= off) { ls += lo; zs += zo; }
-                }
-                const float g1 = ls, g0 = ls - l1;   // inclusive prefix at p1, p0
-                const int y1 = zs, y0 = zs - z1;
-                const float g63 = __shfl_sync(0xffffffffu, g1, 31);
-                const int y63 = __shfl_sync(0xffffffffu, y1, 31);
-                sgl[p0] = g0; sgl[p1] = g1;
-                sz[p0] = y0; sz[p1] = y1;
-                sbeta[p0] = b0; sbeta[p1] = b1;
-                const float gm0 = y0 == 0 ? ex2(g0) : 0.f, gm1 = y1 == 0 ? ex2(g1) : 0.f;
-                sgam[p0] = gm0; sgam[p1] = gm1;
-                sbg[p0] = b0 * gm0; sbg[p1] = b1 * gm1;
-                spl[p0] = y0 == y63 ? ex2(g63 - g0) : 0.f;
-                spl[p1] = y1 == y63 ? ex2(g63 - g1) : 0.f;
+            // ---- D1 of this chunk (issued during the previous chunk's tail)
+            {
+                const bool ok = mbar_wait(bar_d1, k & 1);
+                if (__syncthreads_or(!ok)) { failed = true; break; }
+                d1_pending = false;
+                tc_fence_after();
             }
-            const bool ok = mbar_wait(&bar_load[st], lpar);
-            if (__syncthreads_or(!ok)) { failed = true; break; }
-            if (tid == 0) pending_stage = -1;
-            ++load_iter;
-            // Prefetch the next chunk into the other stage: its previous
-            // contents were last read by MMAs that have completed.
-            if (tid == 0 && c + 1 < nch) issue_loads(load_iter, ts + CH, h);
-
-            // ---- D1 = [K; Q] K^T
-            if (tid == 0) {
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_f16(tmem + TM_D1, sdesc_sw128(kq + off, 16, 1024),
-                             sdesc_sw128(kq + off, 16, 1024), ID_D1, kk > 0);
-                }
-            }
-            if (!mma_sync()) { failed = true; break; }
 
             // ---- A = beta P (K K^T) (fp32) and M = P (Q K^T) (fp16), 32 columns per thread
             {
@@ -546,8 +574,11 @@ __global__ void __launch_bounds__(NT, 1)
             }
             __syncthreads();
 
-            // ---- diagonal 16 x 16 tiles of T (warps 0-1) while warps 2-7
-            // convert this stage's tiles to fp16
+            // ---- diagonal 16 x 16 tiles of T (warps 0-1) while warps 2-7 zero
+            // tiles (0,1), (2,3) of T and prepare the next chunk: its gate
+            // tables (warp 2), its tiles converted to fp16
+            const Ref nxt = next_of(Ref{item, ts, L, h});
+            bool prep_fail = false;
             if (tid < 64) {
                 const int I = tid >> 4, j = tid & 15;
                 float x[16];
@@ -568,15 +599,25 @@ __global__ void __launch_bounds__(NT, 1)
                     Tf[(16 * I + r) * AST + 16 * I + j] = x[r];
                 }
             } else {
-                // Tiles (0,1) and (2,3) of T are zero (read by the 32 x 32 products).
                 for (int e = tid - 64; e < 512; e += NT - 64) {
                     const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
                     Tf[(32 * blk + rr) * AST + 32 * blk + 16 + cc] = 0.f;
                 }
-                tiles_to_f16(smem + OFF_KQ + st * KQ_STAGE, smem + OFF_V + st * V_STAGE, sgam,
-                             tid - 64, NT - 64);
+                if (nxt.item >= 0) {
+                    if (warp == 2) gate_tables(k + 1, nxt);
+                    prep_fail = !mbar_wait(&bar_load[(k + 1) & 1], ((k + 1) >> 1) & 1);
+                    if (!prep_fail)
+                        tiles_to_f16(smem + OFF_KQ + ((k + 1) & 1) * KQ_STAGE,
+                                     smem + OFF_V + ((k + 1) & 1) * V_STAGE, tid - 64, NT - 64);
+                    fence_proxy_async_smem();
+                }
             }
-            __syncthreads();
+            if (__syncthreads_or(prep_fail)) { failed = true; break; }
+            if (nxt.item >= 0) {
+                ++loads_waited;
+                if (tid == 0) issue_d1(k + 1);
+                d1_pending = true;
+            }
             solve_offdiag(Af, Tf, Xf, warp, lane);
 
             // ---- T diag(beta) and T diag(beta gamma) as fp16 operands
@@ -606,7 +647,7 @@ __global__ void __launch_bounds__(NT, 1)
             }
             operands_ready();
 
-            // ---- D_U = V^T (T diag b)^T, D_W = K^T (T diag bg)^T, D_O = Q~ S0^T
+            // ---- D_U = V^T (T diag b)^T, D_W = K^T (T diag bg)^T, D_O = Q S0^T
             if (tid == 0) {
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
@@ -625,7 +666,8 @@ __global__ void __launch_bounds__(NT, 1)
                              sdesc_sw128(sbase + OFF_S + off, 16, 1024), ID_O, kk > 0);
                 }
             }
-            if (!mma_sync()) { failed = true; break; }
+            mma_commit();
+            if (!mma_wait()) { failed = true; break; }
             {
                 float x[32];
                 tmem_ld32(trow + TM_W + 32 * half, x);  // W[t][j = row], t in this half
@@ -645,7 +687,8 @@ __global__ void __launch_bounds__(NT, 1)
                              sdesc_sw128(sbase + OFF_WT + kk * 2048, 8192, 1024), ID_KM64, 1);
                 }
             }
-            if (!mma_sync()) { failed = true; break; }
+            mma_commit();
+            if (!mma_wait()) { failed = true; break; }
             {
                 float x[32];
                 tmem_ld32(trow + TM_U + 32 * half, x);  // Delta[s][i = row], s in this half
@@ -668,6 +711,19 @@ __global__ void __launch_bounds__(NT, 1)
                     for (int e = 0; e < 32; ++e) v[e] *= gC;
                     tmem_st32(trow + TM_S + 64 * half + 32 * q2, v);
                 }
+                // D_O row t <- gamma_t (Q S0^T)[t] before M Delta accumulates
+                // (rows live in lanes 0..15 of each subpartition; the other
+                // lanes' columns here belong to no accumulator).
+                const float gt = sgam[(16 * (warp & 3) + lane) & 63];
+#pragma unroll
+                for (int q2 = 0; q2 < 2; ++q2) {
+                    float v[32];
+                    tmem_ld32(trow + TM_O + 64 * half + 32 * q2, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) v[e] *= gt;
+                    tmem_st32(trow + TM_O + 64 * half + 32 * q2, v);
+                }
                 tmem_wait_st();
             }
             operands_ready();
@@ -685,7 +741,17 @@ __global__ void __launch_bounds__(NT, 1)
                              sdesc_sw128(kq + kk * 2048, 16384, 1024), ID_KM128, 1);
                 }
             }
-            if (!mma_sync()) { failed = true; break; }
+            mma_commit();
+
+            if (!mma_wait()) { failed = true; break; }
+            // The stage of this chunk is free again: fetch the chunk after next.
+            if (nxt.item >= 0) {
+                const Ref nn = next_of(nxt);
+                if (nn.item >= 0) {
+                    if (tid == 0) issue_loads(k + 2, nn);
+                    ++loads_issued;
+                }
+            }
 
             // ---- epilogue: O rows (D_O row t sits in lane 32 (t / 16) + t % 16;
             // lanes 16..31 of each warp hold no row) go out as 16-byte stores;
@@ -748,8 +814,10 @@ __global__ void __launch_bounds__(NT, 1)
     if (failed) {
         // Drain what this CTA still has in flight (bounded), then report.
         if (tid == 0) {
-            if (pending_stage >= 0) mbar_wait(&bar_load[pending_stage], pending_parity, 200000000ull);
+            for (int kk = loads_waited; kk < loads_issued; ++kk)
+                mbar_wait(&bar_load[kk & 1], (kk >> 1) & 1, 200000000ull);
             if (mma_pending) mbar_wait(bar_mma, mma_phase, 200000000ull);
+            if (d1_pending) mbar_wait(bar_d1, k & 1, 200000000ull);
             atomicExch(&g_tc_status, 1);
         }
         __syncthreads();
