@@ -411,12 +411,101 @@ def run_ours(args):
     return 0
 
 
+def run_layer(args):
+    """--workload layer: the full Local-block layer, B=8, T=32768, H=64,
+    d=128, heads split evenly over the ranks, per-head outputs all-gathered
+    (NCCL) into [B, T, H*d] on every rank. Total work is fixed: strong scaling."""
+    import torch
+    from rhizome_b200 import capi
+    from rhizome_b200.layer import gdr_layer_sharded
+
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    capi.lib()
+    LB, LT, LH = 8, 32768, 64
+    if LH % world:
+        raise SystemExit(f"H = {LH} heads do not split over {world} ranks")
+    hs = LH // world
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    n = torch.nn.functional.normalize
+    q = torch.empty((LB, LT, hs, D), device=dev, dtype=torch.bfloat16)
+    k = torch.empty_like(q)
+    v = torch.empty_like(q)
+    for bb in range(LB):  # generate per sequence to bound temporaries
+        q[bb] = n(torch.randn(LT, hs, D, device=dev, generator=g), dim=-1).to(torch.bfloat16)
+        k[bb] = n(torch.randn(LT, hs, D, device=dev, generator=g), dim=-1).to(torch.bfloat16)
+        v[bb] = torch.randn(LT, hs, D, device=dev, generator=g).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn(LB, LT, hs, device=dev, generator=g))
+    alpha = torch.exp(-torch.nn.functional.softplus(torch.randn(LB, LT, hs, device=dev, generator=g) + 2))
+    stream = torch.cuda.current_stream(dev)
+    ev = []
+
+    def step(record):
+        if record:
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev.append((a0, a1))
+            a0.record(stream)
+            out = gdr_layer_sharded(q, k, v, alpha, beta,
+                                    compute=lambda *x: _timed_compute(x, a1, stream))
+        else:
+            out = gdr_layer_sharded(q, k, v, alpha, beta)
+        return out
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(args.steps):
+        step(True)
+    s1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    elapsed = max_over_ranks(s0.elapsed_time(s1), world)
+    comp = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) / args.steps, world)
+    tokens = LB * LT
+    gathered_bytes = (world - 1) * LB * LT * hs * D * 2
+    if rank == 0:
+        line = {
+            "metric": "GDR layer tokens/s", "value": tokens * args.steps / (elapsed / 1e3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "full Local-block GDR layer B=8 T=32768 H=64 d=128, heads "
+                                   "split over ranks, outputs all-gathered (NCCL)",
+                       "global_batch": LB, "seq_len": LT, "heads": LH, "head_dim": D,
+                       "parallelism": f"heads/{world}"},
+            "kernel_only": {"value": tokens / (comp / 1e3), "unit": "tokens/s",
+                            "ms_per_step": comp},
+            "allgather": {"bytes_received_per_rank": gathered_bytes,
+                          "ms_per_step": elapsed / args.steps - comp},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def _timed_compute(x, ev_done, stream):
+    from rhizome_b200 import ops
+    out = ops.gdr_scan_chunked(*x)
+    ev_done.record(stream)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="prefill", choices=["prefill", "layer"],
+                    help="prefill: the headline chunked-prefill batch (weak scaling over "
+                         "ranks); layer: the full head-sharded layer with its all-gather")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--traffic", type=float, default=None,
                     help="measured DRAM bytes per launch of the dominant kernel (ncu)")
@@ -425,6 +514,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "layer":
+        return run_layer(args)
     return run_ours(args)
 
 

@@ -211,6 +211,24 @@ int rhz_varlen_unpack_tokens(void *padded, const void *packed, const int32_t *cu
                              int64_t n, int64_t max_len, int64_t row_bytes, rhz_stream_t stream);
 
 /* --------------------------------------------------------------------- */
+/* Head sharding across GPUs (bit-exact moves)                             */
+/* --------------------------------------------------------------------- */
+
+/*
+ * rhz_heads_unshard / rhz_heads_shard -- the full Local-block layer splits
+ * its H heads evenly over G ranks (rank r owns heads [r H/G, (r+1) H/G)); the
+ * recurrence never mixes heads (delta.rs:93-127 is per head), so the only
+ * exchange is an all-gather of per-head outputs. A collective gathers the
+ * ranks' [tokens][H/G][d] outputs rank-major into gathered [G][tokens][H/G][d];
+ * unshard reorders that into out [tokens][H][d], shard does the reverse.
+ * elem_bytes is 2 (bf16) or 4 (f32).
+ */
+int rhz_heads_unshard(void *out, const void *gathered, int64_t G, int64_t tokens, int32_t H,
+                      int32_t d, int32_t elem_bytes, rhz_stream_t stream);
+int rhz_heads_shard(void *gathered, const void *full, int64_t G, int64_t tokens, int32_t H,
+                    int32_t d, int32_t elem_bytes, rhz_stream_t stream);
+
+/* --------------------------------------------------------------------- */
 /* No-allocation variant                                                  */
 /* --------------------------------------------------------------------- */
 

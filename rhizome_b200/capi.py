@@ -81,6 +81,8 @@ SIGNATURES = {
     "rhz_varlen_pack_tokens": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "rhz_varlen_unpack_tokens": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "rhz_varlen_segments_to_cu_seqlens_noalloc": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "rhz_heads_unshard": (C.c_int, [_vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp]),
+    "rhz_heads_shard": (C.c_int, [_vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp]),
 }
 
 # Largest B*T rhz_varlen_segments_to_cu_seqlens_noalloc accepts.

@@ -404,4 +404,32 @@ int rhz_varlen_unpack_tokens(void *padded, const void *packed, const int32_t *cu
     return launch_pack_tokens(padded, packed, cu_seqlens, n, max_len, row_bytes, true, as_cuda(stream));
 }
 
+int rhz_heads_unshard(void *out, const void *gathered, int64_t G, int64_t tokens, int32_t H,
+                      int32_t d, int32_t elem_bytes, rhz_stream_t stream) {
+    clear_error();
+    if (G < 1 || tokens < 0 || H < 1 || d < 1) return set_error(RHZ_ERR_SHAPE, "bad sizes (G %lld, tokens %lld, H %d, d %d)", (long long)G, (long long)tokens, H, d);
+    if (H % G) return set_error(RHZ_ERR_SHAPE, "H = %d heads do not split evenly over G = %lld ranks", H, (long long)G);
+    if (elem_bytes != 2 && elem_bytes != 4) return set_error(RHZ_ERR_DTYPE, "elem_bytes = %d (expected 2 or 4)", elem_bytes);
+    const int64_t row_bytes = static_cast<int64_t>(d) * elem_bytes;
+    if ((H / G) * row_bytes % 4) return set_error(RHZ_ERR_SHAPE, "a rank's rows (%lld bytes) are not a multiple of 4 bytes", (long long)((H / G) * row_bytes));
+    RHZ_TRY(check_ptr(out, "out", 16, tokens > 0));
+    RHZ_TRY(check_ptr(gathered, "gathered", 16, tokens > 0));
+    RHZ_TRY(require_sm100());
+    return launch_heads_unshard(out, gathered, G, tokens, H / G, row_bytes, false, as_cuda(stream));
+}
+
+int rhz_heads_shard(void *gathered, const void *full, int64_t G, int64_t tokens, int32_t H,
+                    int32_t d, int32_t elem_bytes, rhz_stream_t stream) {
+    clear_error();
+    if (G < 1 || tokens < 0 || H < 1 || d < 1) return set_error(RHZ_ERR_SHAPE, "bad sizes (G %lld, tokens %lld, H %d, d %d)", (long long)G, (long long)tokens, H, d);
+    if (H % G) return set_error(RHZ_ERR_SHAPE, "H = %d heads do not split evenly over G = %lld ranks", H, (long long)G);
+    if (elem_bytes != 2 && elem_bytes != 4) return set_error(RHZ_ERR_DTYPE, "elem_bytes = %d (expected 2 or 4)", elem_bytes);
+    const int64_t row_bytes = static_cast<int64_t>(d) * elem_bytes;
+    if ((H / G) * row_bytes % 4) return set_error(RHZ_ERR_SHAPE, "a rank's rows (%lld bytes) are not a multiple of 4 bytes", (long long)((H / G) * row_bytes));
+    RHZ_TRY(check_ptr(full, "full", 16, tokens > 0));
+    RHZ_TRY(check_ptr(gathered, "gathered", 16, tokens > 0));
+    RHZ_TRY(require_sm100());
+    return launch_heads_unshard(gathered, full, G, tokens, H / G, row_bytes, true, as_cuda(stream));
+}
+
 }  // extern "C"

@@ -60,6 +60,8 @@ int launch_chunk_map(int32_t *chunk_seq, int32_t *chunk_start, int32_t *n_chunks
                      size_t ws_bytes, cudaStream_t s);
 int launch_gather_states(float *dense, const float *pool, const int32_t *slots, int64_t n,
                          int64_t num_slots, int H, int d, bool scatter, cudaStream_t s);
+int launch_heads_unshard(void *dst, const void *src, int64_t G, int64_t tokens, int64_t Hs,
+                         int64_t row_bytes, bool shard, cudaStream_t s);
 int launch_pack_tokens(void *dst, const void *src, const int32_t *cu, int64_t n, int64_t max_len,
                        int64_t row_bytes, bool unpack, cudaStream_t s);
 

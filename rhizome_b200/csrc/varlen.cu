@@ -243,6 +243,30 @@ __global__ void pack_tokens_kernel(char *__restrict__ dst, const char *__restric
     }
 }
 
+// ---- head-sharded outputs: rank-major gather buffer <-> [tokens][H][d]
+
+// out[tok][r * Hs + hh][:] = gathered[r][tok][hh][:] (unshard), or the
+// reverse (shard), for rows of row_bytes; one CTA row loop per (r, tok).
+__global__ void heads_unshard_kernel(char *__restrict__ dst, const char *__restrict__ src,
+                                     int64_t G, int64_t tokens, int64_t Hs, int64_t row_bytes,
+                                     bool shard, bool vec16) {
+    const int64_t slab = Hs * row_bytes;  // one rank's rows of one token
+    for (int64_t u = blockIdx.x; u < G * tokens; u += gridDim.x) {
+        const int64_t r = u / tokens, tok = u - r * tokens;
+        const int64_t goff = (r * tokens + tok) * slab;           // gathered layout
+        const int64_t ooff = (tok * G + r) * slab;                // [tok][r][Hs][d] == [tok][H][d]
+        const char *s = src + (shard ? ooff : goff);
+        char *d = dst + (shard ? goff : ooff);
+        if (vec16) {
+            for (int64_t x = threadIdx.x; x < slab / 16; x += blockDim.x)
+                reinterpret_cast<int4 *>(d)[x] = reinterpret_cast<const int4 *>(s)[x];
+        } else {
+            for (int64_t x = threadIdx.x; x < slab / 4; x += blockDim.x)
+                reinterpret_cast<int32_t *>(d)[x] = reinterpret_cast<const int32_t *>(s)[x];
+        }
+    }
+}
+
 int64_t tiles_of(int64_t n) { return (n + SCAN_TILE - 1) / SCAN_TILE; }
 
 }  // namespace
@@ -309,6 +333,24 @@ int launch_gather_states(float *dense, const float *pool, const int32_t *slots, 
     gather_states_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(dense, pool, slots, n,
                                                                       num_slots, H, dd, scatter, vec);
     return check_launch(scatter ? "scatter_states" : "gather_states");
+}
+
+int launch_heads_unshard(void *dst, const void *src, int64_t G, int64_t tokens, int64_t Hs,
+                         int64_t row_bytes, bool shard, cudaStream_t s) {
+    if (G == 0 || tokens == 0 || Hs == 0 || row_bytes == 0) return RHZ_OK;
+    const int64_t slab = Hs * row_bytes;
+    const bool vec16 = slab % 16 == 0 && aligned(dst, 16) && aligned(src, 16);
+    int sms = 148;
+    bool sm100 = true;
+    device_info(&sms, &sm100);
+    int64_t grid = G * tokens;
+    if (grid > static_cast<int64_t>(sms) * 16) grid = static_cast<int64_t>(sms) * 16;
+    int threads = static_cast<int>(slab / (vec16 ? 16 : 4));
+    threads = threads < 32 ? 32 : (threads > 256 ? 256 : (threads + 31) / 32 * 32);
+    heads_unshard_kernel<<<static_cast<unsigned>(grid), threads, 0, s>>>(
+        static_cast<char *>(dst), static_cast<const char *>(src), G, tokens, Hs, row_bytes, shard,
+        vec16);
+    return check_launch(shard ? "heads_shard" : "heads_unshard");
 }
 
 int launch_pack_tokens(void *dst, const void *src, const int32_t *cu, int64_t n, int64_t max_len,
