@@ -141,6 +141,27 @@ int rhz_gdr_varlen_fwd(void *o, float *state_pool, const int32_t *slot_idx,
                        int32_t dtype, uint32_t flags, rhz_stream_t stream);
 
 /*
+ * rhz_gdr_multistep -- replaces gated_delta_multistep
+ * (crates/ops/src/delta.rs:201-230): n sequences x H heads of T positions
+ * (q, k, v [n][T][H][d]; alpha, beta [n][T][H]), of which the first
+ * Tn = min(T, max_positions) (at most 64) are processed. Writes outs
+ * [n][Tn][H][d] and the state after every position, states
+ * [n][Tn][H][d][d] f32. With state_pool == NULL it follows the reference:
+ * the state starts at zero (the reset at t = 0 discards any initial state)
+ * and resets where segment[b][t] != segment[b][t-1] (segment [n][T] int64 or
+ * NULL). With a state_pool, sequence i starts from state_pool[slot_idx[i]]
+ * (slot i when slot_idx is NULL), segments are ignored and the pool is not
+ * modified: speculative decoding scores draft positions and commits the
+ * state of the last accepted one afterwards (e.g. with
+ * rhz_varlen_scatter_states).
+ */
+int rhz_gdr_multistep(void *outs, float *states, const float *state_pool,
+                      const int32_t *slot_idx, const void *q, const void *k, const void *v,
+                      const float *alpha, const float *beta, const int64_t *segment, int64_t n,
+                      int64_t T, int64_t max_positions, int64_t num_slots, int32_t H, int32_t d,
+                      int32_t dtype, rhz_stream_t stream);
+
+/*
  * rhz_gdr_workspace_bytes -- scratch needed by rhz_gdr_sequential /
  * rhz_gdr_scan_chunked with a segment array of B x T positions.
  */

@@ -72,6 +72,8 @@ SIGNATURES = {
     "rhz_gdr_varlen_fwd": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
                                      _i64, _i32, _i32, _i32, _u32, _vp]),
     "rhz_gdr_workspace_bytes": (_sz, [_i64, _i64]),
+    "rhz_gdr_multistep": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
+                                    _i64, _i64, _i32, _i32, _i32, _vp]),
     "rhz_varlen_prefix_sum": (C.c_int, [_vp, _vp, _i64, _vp]),
     "rhz_varlen_segments_to_cu_seqlens": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _vp, _sz, _vp]),
     "rhz_varlen_chunk_map": (C.c_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i64, _vp, _sz, _vp]),

@@ -404,6 +404,39 @@ int rhz_varlen_unpack_tokens(void *padded, const void *packed, const int32_t *cu
     return launch_pack_tokens(padded, packed, cu_seqlens, n, max_len, row_bytes, true, as_cuda(stream));
 }
 
+int rhz_gdr_multistep(void *outs, float *states, const float *state_pool,
+                      const int32_t *slot_idx, const void *q, const void *k, const void *v,
+                      const float *alpha, const float *beta, const int64_t *segment, int64_t n,
+                      int64_t T, int64_t max_positions, int64_t num_slots, int32_t H, int32_t d,
+                      int32_t dtype, rhz_stream_t stream) {
+    clear_error();
+    RHZ_TRY(check_dtype(dtype));
+    RHZ_TRY(check_heads(H, d));
+    if (n < 0 || T < 0 || max_positions < 0 || num_slots < 0)
+        return set_error(RHZ_ERR_SHAPE, "negative size (n %lld, T %lld, max_positions %lld, num_slots %lld)",
+                         (long long)n, (long long)T, (long long)max_positions, (long long)num_slots);
+    const int64_t Tn = T < max_positions ? T : max_positions;
+    if (Tn > 64) return set_error(RHZ_ERR_SHAPE, "multistep handles at most 64 positions per call (got %lld)", (long long)Tn);
+    if (state_pool && slot_idx == nullptr && n > num_slots)
+        return set_error(RHZ_ERR_SHAPE, "n = %lld sequences but only %lld slots (slot_idx is NULL)", (long long)n, (long long)num_slots);
+    if (n * H > INT32_MAX) return set_error(RHZ_ERR_SHAPE, "n*H exceeds the grid");
+    if (n == 0 || Tn == 0) return RHZ_OK;
+    RHZ_TRY(check_ptr(q, "q", 16, true));
+    RHZ_TRY(check_ptr(k, "k", 16, true));
+    RHZ_TRY(check_ptr(v, "v", 16, true));
+    RHZ_TRY(check_ptr(outs, "outs", 16, true));
+    RHZ_TRY(check_ptr(states, "states", 16, true));
+    RHZ_TRY(check_ptr(alpha, "alpha", 4, true));
+    RHZ_TRY(check_ptr(beta, "beta", 4, true));
+    RHZ_TRY(check_ptr(state_pool, "state_pool", 16, state_pool != nullptr));
+    RHZ_TRY(check_ptr(slot_idx, "slot_idx", 4, slot_idx != nullptr));
+    RHZ_TRY(check_ptr(segment, "segment", 8, segment != nullptr));
+    RHZ_TRY(require_sm100());
+    MultistepArgs a{outs, states, state_pool, slot_idx, q, k, v, alpha, beta, segment, n, T,
+                    static_cast<int>(Tn), num_slots, H, d, dtype, as_cuda(stream)};
+    return launch_multistep(a);
+}
+
 int rhz_heads_unshard(void *out, const void *gathered, int64_t G, int64_t tokens, int32_t H,
                       int32_t d, int32_t elem_bytes, rhz_stream_t stream) {
     clear_error();

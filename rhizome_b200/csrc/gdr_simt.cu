@@ -170,6 +170,104 @@ __global__ void __launch_bounds__(WARPS * 32)
     if (writer) op[myrow] = from_f32<T>(mine);
 }
 
+// ------------------------------------------------------------------ multistep
+
+// gated_delta_multistep (delta.rs:201-230) for n sequences x H heads of up
+// to Tn positions: the state rows stay in registers across the positions and
+// the state after every position is written out (speculative decoding keeps
+// them to roll back to the last accepted draft token). With pool == nullptr
+// the state starts at zero and resets wherever the segment id changes (the
+// reference's semantics; its reset at t = 0 discards `init`); otherwise it
+// starts from pool[slot] and the pool is left untouched.
+template <typename T, int RPW, int NV, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32)
+    gdr_multistep_kernel(T *__restrict__ outs, float *__restrict__ states,
+                         const float *__restrict__ pool, const int32_t *__restrict__ slots,
+                         const T *__restrict__ q, const T *__restrict__ k, const T *__restrict__ v,
+                         const float *__restrict__ alpha, const float *__restrict__ beta,
+                         const int64_t *__restrict__ segment, int64_t Tin, int Tn,
+                         int64_t num_slots, int H, int d, bool vec) {
+    const int64_t item = blockIdx.x;  // sequence * H + head
+    const int64_t seq = item / H;
+    const int h = static_cast<int>(item - seq * H);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = blockIdx.y * (WARPS * RPW) + warp * RPW;
+    if (row0 >= d) return;
+    constexpr int SHIFT = 5 - Log2<RPW>::value;
+    const int myrow = row0 + (lane >> SHIFT);
+    const bool writer = (lane & ((1 << SHIFT) - 1)) == 0 && myrow < d;
+    const int64_t dd = static_cast<int64_t>(d) * d;
+
+    float s[RPW][NV][4];
+    bool valid = true;
+    if (pool) {
+        const int64_t slot = slots ? static_cast<int64_t>(slots[seq]) : seq;
+        valid = slot >= 0 && slot < num_slots;
+        const float *S = valid ? pool + (slot * H + h) * dd : nullptr;
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+            for (int c = 0; c < NV; ++c) {
+                const int j = 128 * c + 4 * lane;
+                if (valid && row0 + r < d) {
+                    load4(S + static_cast<int64_t>(row0 + r) * d + j, vec, nvalid(d, j), s[r][c]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) s[r][c][e] = 0.f;
+                }
+            }
+    } else {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+            for (int c = 0; c < NV; ++c)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) s[r][c][e] = 0.f;
+    }
+    const int64_t row_stride = static_cast<int64_t>(H) * d;
+    for (int t = 0; t < Tn; ++t) {
+        const int64_t tok = seq * Tin + t;
+        if (!pool && segment && t > 0 && segment[tok] != segment[tok - 1]) {
+#pragma unroll
+            for (int r = 0; r < RPW; ++r)
+#pragma unroll
+                for (int c = 0; c < NV; ++c)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) s[r][c][e] = 0.f;
+        }
+        const T *qp = q + tok * row_stride + static_cast<int64_t>(h) * d;
+        const T *kp = k + tok * row_stride + static_cast<int64_t>(h) * d;
+        const T *vp = v + tok * row_stride + static_cast<int64_t>(h) * d;
+        float kk[NV][4], qq[NV][4], vr[RPW];
+#pragma unroll
+        for (int c = 0; c < NV; ++c) {
+            const int j = 128 * c + 4 * lane;
+            load4(kp + j, vec, nvalid(d, j), kk[c]);
+            load4(qp + j, vec, nvalid(d, j), qq[c]);
+        }
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) vr[r] = row0 + r < d ? to_f32(vp[row0 + r]) : 0.f;
+        const float a = alpha[tok * H + h], b = beta[tok * H + h];
+        float sk[RPW], ov[RPW], mine;
+        row_dots<RPW, NV>(s, kk, lane, sk, mine);
+        rank1_update<RPW, NV>(s, kk, sk, vr, a, b);
+        row_dots<RPW, NV>(s, qq, lane, ov, mine);
+        T *op = outs + (seq * Tn + t) * row_stride + static_cast<int64_t>(h) * d;
+        if (writer) op[myrow] = valid ? from_f32<T>(mine) : from_f32<T>(nanf(""));
+        float *St = states + ((seq * Tn + t) * H + h) * dd;
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+            if (row0 + r < d) {
+#pragma unroll
+                for (int c = 0; c < NV; ++c) {
+                    const int j = 128 * c + 4 * lane;
+                    store4(St + static_cast<int64_t>(row0 + r) * d + j, vec, nvalid(d, j), s[r][c]);
+                }
+            }
+        }
+    }
+}
+
 // ------------------------------------------------------------------ sequential
 
 // Tile of TS positions staged in shared memory: k and q rows (all d
@@ -365,7 +463,28 @@ int launch_seq_t(const SeqArgs &a) {
     return check_launch("gdr_seq_kernel");
 }
 
+template <typename T, int RPW, int NV, int WARPS>
+int launch_multistep_t(const MultistepArgs &a) {
+    dim3 grid(static_cast<unsigned>(a.n * a.H), (a.d + WARPS * RPW - 1) / (WARPS * RPW));
+    const bool vec = (a.d % 4) == 0;
+    gdr_multistep_kernel<T, RPW, NV, WARPS><<<grid, WARPS * 32, 0, a.stream>>>(
+        static_cast<T *>(a.outs), a.states, a.pool, a.slots, static_cast<const T *>(a.q),
+        static_cast<const T *>(a.k), static_cast<const T *>(a.v), a.alpha, a.beta, a.segment,
+        a.T, a.Tn, a.num_slots, a.H, a.d, vec);
+    return check_launch("gdr_multistep_kernel");
+}
+
 }  // namespace
+
+int launch_multistep(const MultistepArgs &a) {
+    if (a.n == 0 || a.Tn == 0) return RHZ_OK;
+    if (a.dtype == RHZ_DTYPE_BF16) {
+        if (a.d <= 128) return launch_multistep_t<__nv_bfloat16, 8, 1, 8>(a);
+        return launch_multistep_t<__nv_bfloat16, 4, 2, 8>(a);
+    }
+    if (a.d <= 128) return launch_multistep_t<float, 8, 1, 8>(a);
+    return launch_multistep_t<float, 4, 2, 8>(a);
+}
 
 int launch_step(const StepArgs &a) {
     if (a.n == 0) return RHZ_OK;

@@ -43,7 +43,25 @@ struct SeqArgs {
     cudaStream_t stream;
 };
 
+// Up to Tn positions per sequence, state after each position written out
+// (gdr_simt.cu). pool == nullptr: zero start with segment resets.
+struct MultistepArgs {
+    void *outs;
+    float *states;
+    const float *pool;
+    const int32_t *slots;
+    const void *q, *k, *v;
+    const float *alpha, *beta;
+    const int64_t *segment;
+    int64_t n, T;
+    int Tn;
+    int64_t num_slots;
+    int H, d, dtype;
+    cudaStream_t stream;
+};
+
 int launch_step(const StepArgs &a);
+int launch_multistep(const MultistepArgs &a);
 int launch_seq(const SeqArgs &a);
 // Tensor-core chunked kernel (bf16, d == 128). Returns RHZ_ERR_SHAPE for
 // shapes it does not tile.

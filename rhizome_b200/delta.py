@@ -144,19 +144,15 @@ def _scan(inp, init, chunk, dtype, device):
 def gated_delta_multistep(inp: DeltaInputs, init: DeltaState, max_positions: int, *,
                           dtype="f32", device="cuda"):
     """delta.rs:201-230: at most max_positions steps; returns (outputs,
-    [state after each position]). Resets at t = 0 and segment changes."""
+    [state after each position]). Resets at t = 0 (so `init` is discarded,
+    as in the reference) and at segment changes."""
     _check(inp)
-    d = inp.head_dim
-    n = max(0, min(len(inp), int(max_positions)))
-    state = init.clone()
-    outs, states = [], []
-    prev = None
-    for t in range(n):
-        if prev != inp.segment[t]:
-            state.reset()
-            prev = inp.segment[t]
-        sl = slice(t * d, (t + 1) * d)
-        outs.append(gated_delta_step(state, inp.q[sl], inp.k[sl], inp.v[sl], inp.alpha[t],
-                                     inp.beta[t], dtype=dtype, device=device))
-        states.append(state.clone())
-    return (np.concatenate(outs) if outs else np.zeros(0)), states
+    d, t = inp.head_dim, len(inp)
+    n = max(0, min(t, int(max_positions)))
+    if n == 0:
+        return np.zeros(0), []
+    q, k, v, a, b, seg = _head_tensors(inp, dtype, device)
+    outs, states = ops.gdr_multistep(q, k, v, a, b, max_positions=n, segment=seg)
+    outs = outs.double().cpu().numpy().reshape(n * d)
+    st = states.double().cpu().numpy().reshape(n, d * d)
+    return outs, [DeltaState(d, st[i].copy()) for i in range(n)]

@@ -66,6 +66,32 @@ def gdr_step(q, k, v, alpha, beta, state_pool, slot_idx=None, out=None):
     return o
 
 
+def gdr_multistep(q, k, v, alpha, beta, max_positions=8, segment=None, state_pool=None,
+                  slot_idx=None):
+    """gated_delta_multistep (delta.rs:201-230) for n sequences: q/k/v
+    [n, T, H, d]. Returns (outs [n, Tn, H, d], states [n, Tn, H, d, d]) with
+    Tn = min(T, max_positions). Without a state_pool the state starts at zero
+    and resets at segment changes (the reference); with one, sequence i starts
+    from state_pool[slot_idx[i]] and the pool is left unchanged."""
+    n, T = q.shape[0], q.shape[1]
+    H, d = _qkv(q, k, v, alpha, beta, (n, T))
+    Tn = max(0, min(T, int(max_positions)))
+    if segment is not None:
+        _need(segment, "segment", torch.int64, (n, T))
+    num_slots = 0
+    if state_pool is not None:
+        _need(state_pool, "state_pool", torch.float32)
+        num_slots = state_pool.shape[0]
+    if slot_idx is not None:
+        _need(slot_idx, "slot_idx", torch.int32, (n,))
+    outs = torch.empty((n, Tn, H, d), device=q.device, dtype=q.dtype)
+    states = torch.empty((n, Tn, H, d, d), device=q.device, dtype=torch.float32)
+    capi.call("rhz_gdr_multistep", _p(outs), _p(states), _p(state_pool), _p(slot_idx), _p(q),
+              _p(k), _p(v), _p(alpha), _p(beta), _p(segment), n, T, int(max_positions), num_slots,
+              H, d, _dt(q), _stream(q.device))
+    return outs, states
+
+
 def workspace_bytes(B: int, T: int) -> int:
     return int(capi.lib().rhz_gdr_workspace_bytes(B, T))
 

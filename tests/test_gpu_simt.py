@@ -175,3 +175,51 @@ def test_shape_errors_raise_before_launch():
         ops.gdr_sequential(q, q, q, al, torch.zeros((2, 4, 1), device="cuda"))
     with pytest.raises(capi.DtypeError):
         ops.gdr_sequential(q.half(), q.half(), q.half(), al, al)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("d", [6, 32, 128])
+def test_multistep_reference_semantics(dtype, d):
+    """gated_delta_multistep (delta.rs:201-230): zero start, resets at segment
+    changes, every per-position state returned."""
+    n, T, H, maxp = 5, 10, 2, 8
+    q, k, v, a, b = make_inputs(40 + d, n * T, H, d, dtype)
+    rng = np.random.default_rng(d)
+    seg = np.cumsum(rng.random((n, T)) < 0.25, axis=1).astype(np.int64)
+    sh = lambda x: x.reshape(n, T, *x.shape[1:])  # noqa: E731
+    dq, dk, dv, da, db = (sh(x) for x in device_inputs(q, k, v, a, b, dtype))
+    outs, states = ops.gdr_multistep(dq, dk, dv, da, db, max_positions=maxp,
+                                     segment=to_dev(seg, torch.int64))
+    torch.cuda.synchronize()
+    check = assert_fp32 if dtype == "f32" else assert_bf16
+    qq, kk, vv, aa, bb = (sh(x) for x in (q, k, v, a, b))
+    for i in range(n):
+        for h in range(H):
+            inp = O.DeltaInputs(d, qq[i, :, h], kk[i, :, h], vv[i, :, h], aa[i, :, h],
+                                bb[i, :, h], seg[i])
+            ro, rst = O.gated_delta_multistep(inp, O.DeltaState.zeros(d), maxp)
+            check(host(outs[i, :, h]).ravel(), ro, f"multistep o {i} {h}")
+            for t, st in enumerate(rst):
+                check(host(states[i, t, h]).ravel(), st.s, f"multistep state {i} {h} {t}")
+
+
+def test_multistep_from_slots_leaves_pool_untouched():
+    n, T, H, d, S = 4, 6, 3, 128, 7
+    q, k, v, a, b = make_inputs(77, n * T, H, d, "bf16")
+    pool = O.make_normal(9, 22, (S, H, d, d), 0.02).astype(np.float32).astype(np.float64)
+    slots = np.array([6, 1, 4, 2], dtype=np.int32)
+    sh = lambda x: x.reshape(n, T, *x.shape[1:])  # noqa: E731
+    dq, dk, dv, da, db = (sh(x) for x in device_inputs(q, k, v, a, b, "bf16"))
+    dpool = to_dev(pool, torch.float32)
+    before = dpool.clone()
+    outs, states = ops.gdr_multistep(dq, dk, dv, da, db, max_positions=8, state_pool=dpool,
+                                     slot_idx=to_dev(slots, torch.int32))
+    torch.cuda.synchronize()
+    assert torch.equal(dpool, before)
+    cu = np.arange(0, n * T + 1, T)
+    ro, _ = O.gdr_varlen(cu, q, k, v, a, b, state_in=pool, state_in_index=slots)
+    assert_bf16(host(outs).reshape(n * T, H, d), ro, "multistep from slots")
+    # the last per-position state is the step loop's final state
+    _, rfin = O.gdr_varlen(cu, q, k, v, a, b, state_in=pool, state_in_index=slots,
+                           state_out_shape=(n, H, d, d))
+    assert_bf16(host(states[:, -1]), rfin, "multistep final state")
