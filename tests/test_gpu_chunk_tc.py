@@ -150,3 +150,28 @@ def test_batch_invariance_and_chunk_invariance():
     sl = slice(T, 2 * T)
     o1, fin1 = run_dense(q[sl], k[sl], v[sl], a[sl], b[sl], 1, T)
     assert torch.equal(o1[0], o[1]) and torch.equal(fin1[0], fin[1])
+
+
+def test_varlen_prefill_config_full_size():
+    """The varlen-prefill benchmark: 64 sequences with seeded lengths
+    U{1..8192} packed into one stream, H=16, d=128, bf16 inputs, each sequence
+    starting from its own N(0, 0.02^2) state in a permuted slot pool and
+    writing its final state back."""
+    H, n = 16, 64
+    rng = np.random.default_rng(8192)
+    lens = rng.integers(1, 8193, size=n)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    tokens = int(cu[-1])
+    q, k, v, a, b = make_inputs(64, tokens, H, D, "bf16")
+    S = 96
+    pool = O.make_normal(6, 22, (S, H, D, D), 0.02).astype(np.float32).astype(np.float64)
+    slots = rng.permutation(S)[:n].astype(np.int32)
+    dq, dk, dv, da, db = device_inputs(q, k, v, a, b, "bf16")
+    dpool = to_dev(pool, torch.float32)
+    o = ops.gdr_varlen_fwd(dq, dk, dv, da, db, to_dev(cu, torch.int32), dpool,
+                           to_dev(slots, torch.int32))
+    torch.cuda.synchronize()
+    ro, rpool = O.gdr_varlen(cu, q, k, v, a, b, state_in=pool, state_in_index=slots,
+                             state_out_index=slots)
+    assert_bf16(host(o), ro, "cfg3 o")
+    assert_bf16(host(dpool), rpool, "cfg3 pool")
