@@ -19,41 +19,42 @@
 // entry with no sequential product chain; only differences t >= s are ever
 // exponentiated (never above 1, no overflow).
 //
-// The state products put the d dimension on M (= 128), so every accumulator
-// row maps to one TMEM lane (thread pair: warps w and w+4 share lanes
-// 32 (w & 3) .. +31 and split the columns); the output is an M = 64 product
-// so each of its rows (one position) is a contiguous 256-byte store:
-//   D1   = [K; Q] K^T          (128 x 64, K = d)     -> A (fp32 smem) and masked M
-//   D_U  = V^T (T diag b)^T    (128 x 64, K = C)
-//   D_W  = K^T (T diag bg)^T   (128 x 64, K = C)     -> -W^T (fp16 smem)
-//   D_O  = Q~ S0^T             ( 64 x 128, K = d)    Q~ = diag(gamma) Q
-//   D_U += S0 (-W^T)           (128 x 64, K = d)     -> Delta^T (fp16 smem)
-//   D_O += M Delta             ( 64 x 128, K = C)
-//   D_S += (P[C-1] Delta)^T K  (128 x 128, K = C)    (D_S pre-scaled by gamma_{C-1})
-// Q, K, V tiles arrive by TMA (128-byte swizzle, double-buffered one chunk
-// ahead; no multicast). D1 consumes them as bf16; they are then converted to
-// fp16 in place and every later product takes fp16 operands (A and B of one
-// MMA always share a type): 3 more mantissa bits for T, W, Delta, M and the
-// state copy than bf16 would give. The state stays in TMEM in fp32 for the
-// whole sequence; an fp16 copy in shared memory feeds the MMAs. fp16
-// intermediates bound |q.k|, |v|, |S| to < 65504 (unit-norm keys, as the
-// reference specifies, keep them far below).
+// Work split. Everything that depends only on the chunk's keys and gates --
+// the decayed [K; Q] K^T, the unit-lower-triangular inverse T, T diag(beta)
+// and W -- is independent across chunks; only the products with S form the
+// sequential chain. Each (sequence, head) item therefore runs on a cluster of
+// two CTAs:
+//   rank 1, the producer: for every chunk, D1 = [K; Q] K^T (bf16 tiles),
+//     A (fp32) and M = P (Q K^T) (fp16), the inverse (diagonal 16 x 16 tiles
+//     by substitution, the rest by a 2 x 2 recursion on mma.sync), then
+//     D_W = K^T (T diag(beta gamma))^T on tcgen05. It writes a 32 KB record
+//     {-W^T, T diag(beta), M} as ready-made fp16 operand images (128-byte
+//     swizzle) and hands it to the chain CTA with one shared-memory-to-peer
+//     bulk copy, two records in flight.
+//   rank 0, the chain: S in TMEM (fp32) for the whole sequence, an fp16 copy
+//     in shared memory as the MMA operand, and two MMA rounds per chunk:
+//       R1: D_U  = V^T (T diag b)^T + S (-W^T)   (128 x 64, = Delta^T)
+//           D_O  = Q~ S^T                         ( 64 x 128), Q~ = diag(gamma) Q
+//       R2: D_O += M Delta                        ( 64 x 128)
+//           D_S += Delta^T K~                     (128 x 128), K~ = diag(P[C-1]) K
+//     with D_S pre-scaled by gamma_{C-1} when the previous chunk's state is
+//     refreshed. Its tiles arrive by TMA one chunk ahead and are converted to
+//     fp16 in place (Q and K rows scaled on the way) under the R1 products.
+// Every product takes fp16 operands except D1 (A and B of one MMA always
+// share a type); fp16 intermediates bound |q.k|, |v|, |S| to < 65504
+// (unit-norm keys, as the reference specifies, keep them far below).
 //
-// The 64 x 64 unit-lower-triangular inverse: the four diagonal 16 x 16 tiles
-// by fp32 forward substitution (overlapped with the fp16 conversion), the rest
-// by a 2 x 2 recursion whose tile products run on mma.sync (fp16 operands,
-// fp32 accumulate).
-//
-// One CTA (256 threads, two warpgroups) per SM, persistent over
-// (sequence, head) items. Every wait is bounded; a timeout sets a sticky
-// device flag, drains in-flight copies and MMAs (bounded), frees TMEM and
-// returns.
+// One CTA per SM (each needs ~212 KB of shared memory), clusters persistent
+// over items. Every wait is bounded; a timeout sets a sticky device flag,
+// drains what is in flight (bounded), frees TMEM and returns. No load uses
+// cluster multicast.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <climits>
 #include <cstdint>
 #include <mutex>
 
@@ -74,41 +75,58 @@ constexpr int HD = 128;   // head dim (d_k = d_v)
 constexpr int NT = 256;   // threads per CTA
 constexpr int AST = 68;   // fp32 row stride of the A / T tables (16-byte rows, bank spread)
 
-// Shared memory map (offsets from a 1024-byte aligned base).
-constexpr uint32_t OFF_KQ = 0;                     // 2 stages x 32 KB: [half][K rows | Q rows]
-constexpr uint32_t KQ_STAGE = 32768;
-constexpr uint32_t OFF_V = 65536;                  // 2 stages x 16 KB: [half][V rows]
-constexpr uint32_t V_STAGE = 16384;
-constexpr uint32_t OFF_S = 98304;                  // fp16 state [half][128 rows][64]
-constexpr uint32_t OFF_TT = 131072;                // fp16 (T diag beta)        [t][s]
-constexpr uint32_t OFF_TH = 139264;                // fp16 (T diag beta gamma)  [t][s]
-constexpr uint32_t OFF_M = 147456;                 // fp16 masked decayed Q K^T [t][s]
-constexpr uint32_t OFF_R = 155648;                 // 48 KB, phase-aliased region:
-constexpr uint32_t OFF_WT = OFF_R;                 //   -W^T [j][t] fp16 (16 KB)
-constexpr uint32_t OFF_DT = OFF_R + 16384;         //   Delta^T [i][s] fp16 (16 KB)
-constexpr uint32_t OFF_DTS = OFF_R + 32768;        //   (P[C-1] Delta)^T [i][s] fp16 (16 KB)
-constexpr uint32_t OFF_AF = OFF_R;                 //   A fp32 [64][AST]   (solve phase)
-constexpr uint32_t OFF_TF = OFF_AF + 64 * AST * 4; //   T fp32 [64][AST]
-constexpr uint32_t OFF_XF = OFF_TF + 64 * AST * 4; //   32 x 32 fp32 partial products
-constexpr uint32_t OFF_SMALL = OFF_R + 49152;      // 2 x {gl, z, beta, gamma, P[C-1][.], beta*gamma}
-constexpr uint32_t OFF_BAR = OFF_SMALL + 3072;     // 4 mbarriers + TMEM base address
-constexpr uint32_t SMEM_USED = OFF_BAR + 64;
-constexpr size_t SMEM_ALLOC = SMEM_USED + 1024;    // slack for 1024-byte alignment
-static_assert(OFF_XF + 4 * 256 * 4 <= OFF_R + 49152, "solve scratch overflows its region");
+constexpr uint32_t KQ_STAGE = 32768;  // [half][K rows | Q rows], 64 x 64 bf16 boxes
+constexpr uint32_t V_STAGE = 16384;   // [half][V rows]
+constexpr uint32_t KQ_BYTES = 4 * 8192;
+constexpr uint32_t KQV_BYTES = 6 * 8192;
+
+// Producer -> chain record: fp16 operand images, 128-byte swizzle.
+constexpr uint32_t REC_WT = 0;        // -W^T [j = 128 rows][t = 64]     (MN-major B of R1)
+constexpr uint32_t REC_TT = 16384;    // T diag(beta) [t = 64 rows][s]   (K-major B of R1)
+constexpr uint32_t REC_M = 24576;     // M = P (Q K^T) [t rows][s]        (K-major A of R2)
+constexpr uint32_t REC_BYTES = 32768;
+
+// Chain CTA (cluster rank 0) shared memory.
+constexpr uint32_t C_OFF_KQ = 0;             // 2 stages
+constexpr uint32_t C_OFF_V = 65536;          // 2 stages
+constexpr uint32_t C_OFF_REC = 98304;        // 2 records
+constexpr uint32_t C_OFF_S = 163840;         // fp16 state [half][128 rows i][64 j]
+constexpr uint32_t C_OFF_DT = 196608;        // fp16 Delta^T [i = 128 rows][s]
+constexpr uint32_t C_OFF_GATE = 212992;      // 2 x gate tables (384 floats)
+constexpr uint32_t C_OFF_BAR = 216064;       // load[2], full[2], mma, TMEM base
+constexpr uint32_t C_USED = C_OFF_BAR + 64;
+
+// Producer CTA (cluster rank 1) shared memory.
+constexpr uint32_t P_OFF_KQ = 0;             // 2 stages
+constexpr uint32_t P_OFF_STG = 65536;        // 2 records being built
+constexpr uint32_t P_OFF_TH = 131072;        // fp16 T diag(beta gamma) [t][s]
+constexpr uint32_t P_OFF_AF = 139264;        // A fp32 [64][AST]
+constexpr uint32_t P_OFF_TF = P_OFF_AF + 64 * AST * 4;  // T fp32 [64][AST]
+constexpr uint32_t P_OFF_XF = P_OFF_TF + 64 * AST * 4;  // 32 x 32 fp32 partial products
+constexpr uint32_t P_OFF_GATE = P_OFF_XF + 4096;        // 2 x gate tables
+constexpr uint32_t P_OFF_BAR = P_OFF_GATE + 3072;       // load[2], d1, mma, empty[2], TMEM base, count
+constexpr uint32_t P_USED = P_OFF_BAR + 64;
+
+constexpr uint32_t SMEM_USED = C_USED > P_USED ? C_USED : P_USED;
+constexpr size_t SMEM_ALLOC = SMEM_USED + 1024;  // slack for 1024-byte alignment
+static_assert(C_OFF_GATE >= C_OFF_DT + 16384, "chain map overlaps");
+static_assert(P_OFF_AF >= P_OFF_TH + 8192, "producer map overlaps");
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in shared memory");
 
-// TMEM columns (f32 accumulators). D_O is an M = 64 accumulator (row t in
-// lane 32 (t / 16) + t % 16) over 128 columns; the others use all 128 lanes.
-constexpr uint32_t TM_D1 = 0, TM_U = 64, TM_W = 128, TM_O = 192, TM_S = 320;
-constexpr uint32_t TM_COLS = 512;
+// TMEM columns (f32). Chain: D_U (128 lanes x 64), D_O (M = 64: row t in
+// lane 32 (t / 16) + t % 16, 128 columns), D_S (128 x 128). Producer: D1
+// (128 x 64) and D_W (128 x 64).
+constexpr uint32_t TM_U = 0, TM_O = 64, TM_S = 192, C_TM_COLS = 512;
+constexpr uint32_t TM_D1 = 0, TM_W = 64, P_TM_COLS = 128;
 
-// Every product runs on fp16 operands (the bf16 tiles are converted in place).
-constexpr uint32_t ID_D1 = idesc_f16(128, 64, false, false);
+constexpr uint32_t ID_D1 = idesc_bf16(128, 64, false, false);
 constexpr uint32_t ID_MK64 = idesc_f16(128, 64, true, false);
 constexpr uint32_t ID_KM64 = idesc_f16(128, 64, false, true);
 constexpr uint32_t ID_KM128 = idesc_f16(128, 128, false, true);
 constexpr uint32_t ID_O = idesc_f16(64, 128, false, false);
-constexpr uint32_t LOAD_BYTES = 6 * 8192;  // K, Q, V: two 64 x 64 bf16 boxes each
+
+// Gate table layout (floats): gl[64] z[64] (int) beta[64] gamma[64] P[C-1][.][64] beta*gamma[64].
+constexpr int G_GL = 0, G_Z = 64, G_BE = 128, G_GM = 192, G_PL = 256, G_BG = 320, G_SIZE = 384;
 
 struct TcParams {
     __nv_bfloat16 *o;
@@ -170,24 +188,34 @@ __device__ __forceinline__ void st_zero32(uint8_t *blk, uint32_t row, uint32_t c
         *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + c)) = make_uint4(0, 0, 0, 0);
 }
 
-__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x) {
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x, float s) {
     __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162 *>(&x);
-    return pack_f16x2(__low2float(b), __high2float(b));
+    return pack_f16x2(__low2float(b) * s, __high2float(b) * s);
 }
 
-// bf16 -> fp16 in place on 16-byte chunks [first, 3072) of one stage's K, Q
-// (32 KB) and V (16 KB) tiles, stepping by `stride`. The swizzled layout is
-// elementwise, so it is unchanged; bf16 values in the fp16 normal range
-// convert exactly.
-__device__ __forceinline__ void tiles_to_f16(uint8_t *kq, uint8_t *vv, int first, int stride) {
+__device__ __forceinline__ void chunk_to_f16(uint4 *ptr, float s) {
+    uint4 w = *ptr;
+    w.x = bf16x2_to_f16x2(w.x, s);
+    w.y = bf16x2_to_f16x2(w.y, s);
+    w.z = bf16x2_to_f16x2(w.z, s);
+    w.w = bf16x2_to_f16x2(w.w, s);
+    *ptr = w;
+}
+
+// Chain: one stage's K, Q (32 KB) and V (16 KB) tiles bf16 -> fp16 in place,
+// Q rows scaled by gamma_t and K rows by P[C-1][s]; 16-byte chunks
+// [first, 3072) stepping by `stride`. The swizzle permutes chunks within a
+// row only, so chunk i of a K/Q half lies in row (i / 8) % 128 (rows 0..63 K,
+// 64..127 Q).
+__device__ __forceinline__ void chain_tiles_to_f16(uint8_t *kq, uint8_t *vv, const float *gm,
+                                                   const float *pl, int first, int stride) {
     for (int i = first; i < 3072; i += stride) {
-        uint4 *ptr = reinterpret_cast<uint4 *>(i < 2048 ? kq + i * 16 : vv + (i - 2048) * 16);
-        uint4 w = *ptr;
-        w.x = bf16x2_to_f16x2(w.x);
-        w.y = bf16x2_to_f16x2(w.y);
-        w.z = bf16x2_to_f16x2(w.z);
-        w.w = bf16x2_to_f16x2(w.w);
-        *ptr = w;
+        if (i < 2048) {
+            const int r = (i >> 3) & 127;
+            chunk_to_f16(reinterpret_cast<uint4 *>(kq + i * 16), r < 64 ? pl[r] : gm[r - 64]);
+        } else {
+            chunk_to_f16(reinterpret_cast<uint4 *>(vv + (i - 2048) * 16), 1.f);
+        }
     }
 }
 
@@ -284,78 +312,36 @@ __device__ void solve_offdiag(const float *Af, float *Tf, float *Xf, int warp, i
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(NT, 1)
-    gdr_chunk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
-                        const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, const TcParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // TMEM lane (accumulator row) of this thread and the column half it owns.
-    const int row = 32 * (warp & 3) + lane;
-    const int half = warp >> 2;
-    uint64_t *bar_load = reinterpret_cast<uint64_t *>(smem + OFF_BAR);  // [2] TMA per stage
-    uint64_t *bar_mma = bar_load + 2;                                   // state-chain MMAs
-    uint64_t *bar_d1 = bar_load + 3;                                    // D1 of the next chunk
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_load + 4);
-    float *Af = reinterpret_cast<float *>(smem + OFF_AF);
-    float *Tf = reinterpret_cast<float *>(smem + OFF_TF);
-    float *Xf = reinterpret_cast<float *>(smem + OFF_XF);
-    const uint32_t sbase = smem_u32(smem);
+struct Ref {
+    int64_t item, ts;  // item < 0: no chunk
+    int L, h;
+};
 
-    if (tid == 0) {
-        mbar_init(&bar_load[0], 1);
-        mbar_init(&bar_load[1], 1);
-        mbar_init(bar_mma, 1);
-        mbar_init(bar_d1, 1);
-        mbar_fence_init();
-        prefetch_tmap(&tm_q);
-        prefetch_tmap(&tm_k);
-        prefetch_tmap(&tm_v);
-    }
-    if (warp == 0) {
-        tmem_alloc(tmem_slot, TM_COLS);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    const uint32_t trow = tmem + (static_cast<uint32_t>(warp & 3) << 21);  // lane (32 (w&3)) << 16
+// The chunks a cluster processes, in order: items start, start + stride, ...
+// and within an item its chunks of CH positions from the sequence start.
+// Both CTAs of a cluster walk the same sequence; chunk k of it uses tile
+// stage, record slot and gate table k & 1.
+struct Walk {
+    const TcParams *p;
+    int64_t n_items, stride;
+    int H;
 
-    const int H = p.H;
-    int64_t n_seq = p.n_seq;
-    if (p.n_seq_dev) {
-        const int64_t nd = *p.n_seq_dev;
-        n_seq = nd < n_seq ? nd : n_seq;
-    }
-    const int64_t n_items = n_seq * H;
-    const int64_t tok_stride = static_cast<int64_t>(H) * HD;
-
-    // The chunks this CTA processes, in order: items blockIdx.x, +gridDim.x,
-    // ..., and within an item its chunks of CH positions from the sequence
-    // start. Chunk k of that order uses TMA stage k & 1 and gate tables k & 1.
-    auto bounds = [&](int64_t item, int64_t &t0, int64_t &t1) {
+    __device__ void bounds(int64_t item, int64_t &t0, int64_t &t1) const {
         const int64_t seq = item / H;
-        if (p.cu_seqlens) {
+        if (p->cu_seqlens) {
             // Offsets are caller data: clamp them to the packed stream.
-            t0 = p.cu_seqlens[seq];
-            t1 = p.cu_seqlens[seq + 1];
-            t0 = t0 < 0 ? 0 : (t0 > p.total_tokens ? p.total_tokens : t0);
-            t1 = t1 < t0 ? t0 : (t1 > p.total_tokens ? p.total_tokens : t1);
+            t0 = p->cu_seqlens[seq];
+            t1 = p->cu_seqlens[seq + 1];
+            t0 = t0 < 0 ? 0 : (t0 > p->total_tokens ? p->total_tokens : t0);
+            t1 = t1 < t0 ? t0 : (t1 > p->total_tokens ? p->total_tokens : t1);
         } else {
-            t0 = seq * p.seq_len;
-            t1 = t0 + p.seq_len;
+            t0 = seq * p->seq_len;
+            t1 = t0 + p->seq_len;
         }
-    };
-    struct Ref {
-        int64_t item, ts;  // item < 0: no chunk
-        int L, h;
-    };
+    }
     // First chunk at or after item `it` (skipping empty sequences).
-    auto first_from = [&](int64_t it) -> Ref {
-        for (; it < n_items; it += gridDim.x) {
+    __device__ Ref first_from(int64_t it) const {
+        for (; it < n_items; it += stride) {
             int64_t t0, t1;
             bounds(it, t0, t1);
             if (t1 > t0) {
@@ -365,34 +351,110 @@ __global__ void __launch_bounds__(NT, 1)
             }
         }
         return Ref{-1, 0, 0, 0};
-    };
-    auto next_of = [&](const Ref &r) -> Ref {
+    }
+    __device__ Ref next_of(const Ref &r) const {
         int64_t t0, t1;
         bounds(r.item, t0, t1);
         const int64_t tn = r.ts + CH;
         if (tn < t1) return Ref{r.item, tn, static_cast<int>((t1 - tn) < CH ? (t1 - tn) : CH), r.h};
-        return first_from(r.item + gridDim.x);
-    };
+        return first_from(r.item + stride);
+    }
+};
+
+// Gate tables of one chunk (one warp, two positions per lane): prefix sums of
+// log2 alpha over nonzero alphas and of zero-alpha counts, then gamma_t,
+// P[C-1][s], beta, beta*gamma. Padded rows get alpha = 1, beta = 0 so they
+// write nothing.
+__device__ __forceinline__ void gate_tables(float *g, const TcParams &p, const Ref &r, int lane) {
+    const int H = p.H;
+    int *zz = reinterpret_cast<int *>(g + G_Z);
+    const int p0 = 2 * lane, p1 = p0 + 1;
+    const float a0 = p0 < r.L ? p.alpha[(r.ts + p0) * H + r.h] : 1.f;
+    const float a1 = p1 < r.L ? p.alpha[(r.ts + p1) * H + r.h] : 1.f;
+    const float b0 = p0 < r.L ? p.beta[(r.ts + p0) * H + r.h] : 0.f;
+    const float b1 = p1 < r.L ? p.beta[(r.ts + p1) * H + r.h] : 0.f;
+    const bool nz0 = a0 >= 1.17549435e-38f, nz1 = a1 >= 1.17549435e-38f;
+    const float l0 = nz0 ? lg2(a0) : 0.f, l1 = nz1 ? lg2(a1) : 0.f;
+    const int z0 = nz0 ? 0 : 1, z1 = nz1 ? 0 : 1;
+    float ls = l0 + l1;
+    int zs = z0 + z1;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const float lo = __shfl_up_sync(0xffffffffu, ls, off);
+        const int zo = __shfl_up_sync(0xffffffffu, zs, off);
+        if (lane >= off) { ls += lo; zs += zo; }
+    }
+    const float g1 = ls, g0 = ls - l1;  // inclusive prefix at p1, p0
+    const int y1 = zs, y0 = zs - z1;
+    const float g63 = __shfl_sync(0xffffffffu, g1, 31);
+    const int y63 = __shfl_sync(0xffffffffu, y1, 31);
+    g[G_GL + p0] = g0; g[G_GL + p1] = g1;
+    zz[p0] = y0; zz[p1] = y1;
+    g[G_BE + p0] = b0; g[G_BE + p1] = b1;
+    const float gm0 = y0 == 0 ? ex2(g0) : 0.f, gm1 = y1 == 0 ? ex2(g1) : 0.f;
+    g[G_GM + p0] = gm0; g[G_GM + p1] = gm1;
+    g[G_BG + p0] = b0 * gm0; g[G_BG + p1] = b1 * gm1;
+    g[G_PL + p0] = y0 == y63 ? ex2(g63 - g0) : 0.f;
+    g[G_PL + p1] = y1 == y63 ? ex2(g63 - g1) : 0.f;
+}
+
+struct RoleState {
+    bool failed;
+    int k;              // chunks finished (chain: records consumed)
+    int full_waited;    // chain: record barriers waited
+};
+
+// Make thread-written smem operands and TMEM stores visible to the MMA issuer.
+__device__ __forceinline__ void operands_ready() {
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+}
+
+// ------------------------------------------------------------------ chain CTA
+
+__device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k,
+                                                const CUtensorMap *tm_v, const TcParams &p,
+                                                uint8_t *smem, const Walk &wk, int64_t start,
+                                                uint32_t tmem) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // TMEM lane (accumulator row) of this thread and the column half it owns.
+    const int row = 32 * (warp & 3) + lane;
+    const int half = warp >> 2;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(warp & 3) << 21);  // lane (32 (w&3)) << 16
+    uint64_t *bar_load = reinterpret_cast<uint64_t *>(smem + C_OFF_BAR);
+    uint64_t *bar_full = bar_load + 2;
+    uint64_t *bar_mma = bar_load + 4;
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t peer_empty = mapa_shared(sbase + P_OFF_BAR + 32, 1);  // producer's empty[0]
+    const int H = p.H;
+    const int64_t tok_stride = static_cast<int64_t>(H) * HD;
 
     uint32_t mma_phase = 0;
-    bool failed = false, mma_pending = false, d1_pending = false;
-    int loads_issued = 0, loads_waited = 0;  // thread 0 / all threads
+    bool failed = false, mma_pending = false;
+    int loads_issued = 0, loads_waited = 0, full_waited = 0;
+    int k = 0;
 
-    auto issue_loads = [&](int k, const Ref &r) {
-        const uint32_t st = k & 1;
+    auto gates = [&](int kc) { return reinterpret_cast<float *>(smem + C_OFF_GATE) + (kc & 1) * G_SIZE; };
+    auto issue_loads = [&](int kc, const Ref &r) {
+        const uint32_t st = kc & 1;
         uint64_t *bar = &bar_load[st];
-        uint8_t *kq = smem + OFF_KQ + st * KQ_STAGE;
-        uint8_t *vv = smem + OFF_V + st * V_STAGE;
-        mbar_arrive_expect_tx(bar, LOAD_BYTES);
+        uint8_t *kq = smem + C_OFF_KQ + st * KQ_STAGE;
+        uint8_t *vv = smem + C_OFF_V + st * V_STAGE;
+        mbar_arrive_expect_tx(bar, KQV_BYTES);
         const int t32 = static_cast<int>(r.ts);
-        tma_load_3d(kq, &tm_k, 0, r.h, t32, bar);
-        tma_load_3d(kq + 16384, &tm_k, 64, r.h, t32, bar);
-        tma_load_3d(kq + 8192, &tm_q, 0, r.h, t32, bar);
-        tma_load_3d(kq + 24576, &tm_q, 64, r.h, t32, bar);
-        tma_load_3d(vv, &tm_v, 0, r.h, t32, bar);
-        tma_load_3d(vv + 8192, &tm_v, 64, r.h, t32, bar);
+        tma_load_3d(kq, tm_k, 0, r.h, t32, bar);
+        tma_load_3d(kq + 16384, tm_k, 64, r.h, t32, bar);
+        tma_load_3d(kq + 8192, tm_q, 0, r.h, t32, bar);
+        tma_load_3d(kq + 24576, tm_q, 64, r.h, t32, bar);
+        tma_load_3d(vv, tm_v, 0, r.h, t32, bar);
+        tma_load_3d(vv + 8192, tm_v, 64, r.h, t32, bar);
     };
-    // Commit the issued state-chain MMAs and wait for them on every thread.
+    auto mma_commit = [&]() {
+        if (tid == 0) umma_commit(bar_mma);
+        mma_pending = true;
+    };
     auto mma_wait = [&]() -> bool {
         const bool ok = mbar_wait(bar_mma, mma_phase);
         if (__syncthreads_or(!ok)) return false;
@@ -401,105 +463,59 @@ __global__ void __launch_bounds__(NT, 1)
         tc_fence_after();
         return true;
     };
-    auto mma_commit = [&]() {
-        if (tid == 0) umma_commit(bar_mma);
-        mma_pending = true;
-    };
-    // Make thread-written smem operands and TMEM stores visible to the MMA issuer.
-    auto operands_ready = [&]() {
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-    };
-
-    // Gate tables of chunk k (warp 0, two positions per lane): prefix sums of
-    // log2 alpha over nonzero alphas and of zero-alpha counts; padded rows get
-    // alpha = 1, beta = 0 so they write nothing.
-    auto gate_tables = [&](int k, const Ref &r) {
-        float *g = reinterpret_cast<float *>(smem + OFF_SMALL) + (k & 1) * 384;
-        int *zz = reinterpret_cast<int *>(g + 64);
-        float *be = g + 128, *gm = g + 192, *pl = g + 256, *bg = g + 320;
-        const int p0 = 2 * lane, p1 = p0 + 1;
-        const float a0 = p0 < r.L ? p.alpha[(r.ts + p0) * H + r.h] : 1.f;
-        const float a1 = p1 < r.L ? p.alpha[(r.ts + p1) * H + r.h] : 1.f;
-        const float b0 = p0 < r.L ? p.beta[(r.ts + p0) * H + r.h] : 0.f;
-        const float b1 = p1 < r.L ? p.beta[(r.ts + p1) * H + r.h] : 0.f;
-        const bool nz0 = a0 >= 1.17549435e-38f, nz1 = a1 >= 1.17549435e-38f;
-        const float l0 = nz0 ? lg2(a0) : 0.f, l1 = nz1 ? lg2(a1) : 0.f;
-        const int z0 = nz0 ? 0 : 1, z1 = nz1 ? 0 : 1;
-        float ls = l0 + l1;
-        int zs = z0 + z1;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const float lo = __shfl_up_sync(0xffffffffu, ls, off);
-            const int zo = __shfl_up_sync(0xffffffffu, zs, off);
-            if (lane >= off) { ls += lo; zs += zo; }
-        }
-        const float g1 = ls, g0 = ls - l1;  // inclusive prefix at p1, p0
-        const int y1 = zs, y0 = zs - z1;
-        const float g63 = __shfl_sync(0xffffffffu, g1, 31);
-        const int y63 = __shfl_sync(0xffffffffu, y1, 31);
-        g[p0] = g0; g[p1] = g1;
-        zz[p0] = y0; zz[p1] = y1;
-        be[p0] = b0; be[p1] = b1;
-        const float gm0 = y0 == 0 ? ex2(g0) : 0.f, gm1 = y1 == 0 ? ex2(g1) : 0.f;
-        gm[p0] = gm0; gm[p1] = gm1;
-        bg[p0] = b0 * gm0; bg[p1] = b1 * gm1;
-        pl[p0] = y0 == y63 ? ex2(g63 - g0) : 0.f;
-        pl[p1] = y1 == y63 ? ex2(g63 - g1) : 0.f;
-    };
-    // D1 = [K; Q] K^T of chunk k on its (fp16) tiles, tracked by bar_d1.
-    auto issue_d1 = [&](int kc) {
-        const uint32_t kq = sbase + OFF_KQ + (kc & 1) * KQ_STAGE;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_f16(tmem + TM_D1, sdesc_sw128(kq + off, 16, 1024), sdesc_sw128(kq + off, 16, 1024),
-                     ID_D1, kk > 0);
-        }
-        umma_commit(bar_d1);
-    };
-    // Everything chunk k needs before its first SIMT phase: gate tables, its
-    // tiles landed and converted to fp16, and D1 = [K; Q] K^T issued.
-    auto prepare = [&](int k, const Ref &r) -> bool {
-        if (warp == 0) gate_tables(k, r);
-        const bool ok = mbar_wait(&bar_load[k & 1], (k >> 1) & 1);
+    // Chunk kc's tiles landed -> fp16 with the gate scalings (its gate table
+    // must be written before the call; the barrier inside orders it).
+    auto convert = [&](int kc) -> bool {
+        const bool ok = mbar_wait(&bar_load[kc & 1], (kc >> 1) & 1);
         if (__syncthreads_or(!ok)) return false;
         ++loads_waited;
-        tiles_to_f16(smem + OFF_KQ + (k & 1) * KQ_STAGE, smem + OFF_V + (k & 1) * V_STAGE, tid, NT);
-        operands_ready();
-        if (tid == 0) issue_d1(k);
-        d1_pending = true;
+        const float *g = gates(kc);
+        chain_tiles_to_f16(smem + C_OFF_KQ + (kc & 1) * KQ_STAGE, smem + C_OFF_V + (kc & 1) * V_STAGE,
+                           g + G_GM, g + G_PL, tid, NT);
         return true;
     };
 
-    // Prime: tiles of the first two chunks, then chunk 0's preparation.
-    Ref cur = first_from(blockIdx.x);
     {
-        const Ref second = cur.item >= 0 ? next_of(cur) : cur;
+        const Ref cur = wk.first_from(start);
+        const Ref second = cur.item >= 0 ? wk.next_of(cur) : cur;
         if (tid == 0) {
             if (cur.item >= 0) issue_loads(0, cur);
             if (second.item >= 0) issue_loads(1, second);
         }
         loads_issued = (cur.item >= 0) + (second.item >= 0);
-        if (cur.item >= 0 && !prepare(0, cur)) failed = true;
+        if (cur.item >= 0) {
+            if (warp == 0) gate_tables(gates(0), p, cur, lane);
+            if (!convert(0)) failed = true;
+        }
     }
-    int k = 0;  // index of the chunk being processed
 
-    for (int64_t item = blockIdx.x; item < n_items && !failed; item += gridDim.x) {
+    for (int64_t item = start; item < wk.n_items && !failed; item += wk.stride) {
         const int64_t seq = item / H;
         const int h = static_cast<int>(item - seq * H);
         int64_t t0, t1;
-        bounds(item, t0, t1);
+        wk.bounds(item, t0, t1);
         const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
 
-        // ---- initial state: (row, half) -> TMEM (fp32) and the fp16 copy
+        // ---- initial state: fp16 copy (unscaled) and D_S = gamma_{C-1} S0
         {
             int64_t slot = -1;
             if (p.state_in) slot = p.in_slots ? static_cast<int64_t>(p.in_slots[seq]) : seq;
             const bool have = p.state_in && slot >= 0 && slot < p.num_slots;
             const float *src = have ? p.state_in + ((slot * H + h) * HD + row) * HD + 64 * half : nullptr;
+            if (nch == 0) {
+                // Empty sequence: the final state is the initial state.
+                if (p.state_out) {
+                    const int64_t so = p.out_slots ? static_cast<int64_t>(p.out_slots[seq]) : seq;
+                    if (so >= 0 && so < p.num_slots) {
+                        float *dst = p.state_out + ((so * H + h) * HD + row) * HD + 64 * half;
+                        for (int e = 0; e < 64; e += 4)
+                            *reinterpret_cast<float4 *>(dst + e) =
+                                have ? *reinterpret_cast<const float4 *>(src + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                }
+                continue;
+            }
+            const float gC = gates(k)[G_GM + 63];
 #pragma unroll
             for (int q2 = 0; q2 < 2; ++q2) {
                 float v[32];
@@ -509,8 +525,10 @@ __global__ void __launch_bounds__(NT, 1)
                                     : make_float4(0.f, 0.f, 0.f, 0.f);
                     v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
                 }
+                st_row32_f16(smem + C_OFF_S + half * 16384, row, 4 * q2, v);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) v[e] *= gC;
                 tmem_st32(trow + TM_S + 64 * half + 32 * q2, v);
-                st_row32_f16(smem + OFF_S + half * 16384, row, 4 * q2, v);
             }
             tmem_wait_st();
         }
@@ -519,13 +537,239 @@ __global__ void __launch_bounds__(NT, 1)
         for (int c = 0; c < nch; ++c, ++k) {
             const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
             const int L = static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH);
-            const uint32_t kq = sbase + OFF_KQ + (k & 1) * KQ_STAGE;
-            const uint32_t vb = sbase + OFF_V + (k & 1) * V_STAGE;
-            const float *sgl = reinterpret_cast<const float *>(smem + OFF_SMALL) + (k & 1) * 384;
-            const int *sz = reinterpret_cast<const int *>(sgl + 64);
-            const float *sbeta = sgl + 128, *sgam = sgl + 192, *spl = sgl + 256, *sbg = sgl + 320;
+            const uint32_t kq = sbase + C_OFF_KQ + (k & 1) * KQ_STAGE;
+            const uint32_t vb = sbase + C_OFF_V + (k & 1) * V_STAGE;
+            const uint32_t rec = sbase + C_OFF_REC + (k & 1) * REC_BYTES;
 
-            // ---- D1 of this chunk (issued during the previous chunk's tail)
+            // ---- the producer's record for this chunk
+            {
+                const bool ok = mbar_wait_cluster(&bar_full[k & 1], (k >> 1) & 1);
+                if (__syncthreads_or(!ok)) { failed = true; break; }
+                ++full_waited;
+            }
+
+            // ---- R1: D_U = V^T (T diag b)^T + S (-W^T) ; D_O = Q~ S^T
+            if (tid == 0) {
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_f16(tmem + TM_U, sdesc_sw128(vb + kk * 2048, 8192, 1024),
+                             sdesc_sw128(rec + REC_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                    umma_f16(tmem + TM_U, sdesc_sw128(sbase + C_OFF_S + off, 16, 1024),
+                             sdesc_sw128(rec + REC_WT + kk * 2048, 8192, 1024), ID_KM64, 1);
+                }
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                    umma_f16(tmem + TM_O, sdesc_sw128(kq + off + 8192, 16, 1024),
+                             sdesc_sw128(sbase + C_OFF_S + off, 16, 1024), ID_O, kk > 0);
+                }
+            }
+            mma_commit();
+
+            // ---- under R1: the next chunk's gate table and fp16 tiles
+            const Ref nxt = wk.next_of(Ref{item, ts, L, h});
+            if (nxt.item >= 0) {
+                if (warp == 0) gate_tables(gates(k + 1), p, nxt, lane);
+                if (!convert(k + 1)) { failed = true; break; }
+            }
+            if (!mma_wait()) { failed = true; break; }
+
+            // ---- Delta^T (fp16): thread (row i, half) holds Delta[s][i] for its 32 s
+            {
+                float x[32];
+                tmem_ld32(trow + TM_U + 32 * half, x);
+                tmem_wait_ld();
+                st_row32_f16(smem + C_OFF_DT, row, 4 * half, x);
+            }
+            operands_ready();
+
+            // ---- R2: D_O += M Delta ; D_S += Delta^T K~
+            if (tid == 0) {
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_f16(tmem + TM_O, sdesc_sw128(rec + REC_M + kk * 32, 16, 1024),
+                             sdesc_sw128(sbase + C_OFF_DT + kk * 32, 16, 1024), ID_O, 1);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_f16(tmem + TM_S, sdesc_sw128(sbase + C_OFF_DT + kk * 32, 16, 1024),
+                             sdesc_sw128(kq + kk * 2048, 16384, 1024), ID_KM128, 1);
+            }
+            mma_commit();
+            if (!mma_wait()) { failed = true; break; }
+
+            // Record slot and tile stage k & 1 are free again.
+            if (tid == 0) mbar_arrive_remote(peer_empty + 8 * (k & 1));
+            if (nxt.item >= 0) {
+                const Ref nn = wk.next_of(nxt);
+                if (nn.item >= 0) {
+                    if (tid == 0) issue_loads(k + 2, nn);
+                    ++loads_issued;
+                }
+            }
+
+            // ---- epilogue: O rows (D_O row t sits in lane 32 (t / 16) + t % 16;
+            // lanes 16..31 of each warp hold no row) go out as 16-byte stores;
+            // the state's fp16 copy is refreshed and D_S pre-scaled for the
+            // next chunk, or the final state is written out.
+            {
+                float o[32];
+                const int t = 16 * (warp & 3) + lane;
+                const bool has_row = lane < 16 && t < L;
+                __nv_bfloat16 *op = p.o + (ts + t) * tok_stride + static_cast<int64_t>(h) * HD + 64 * half;
+#pragma unroll
+                for (int q2 = 0; q2 < 2; ++q2) {
+                    tmem_ld32(trow + TM_O + 64 * half + 32 * q2, o);
+                    tmem_wait_ld();
+                    if (has_row) {
+#pragma unroll
+                        for (int c8 = 0; c8 < 4; ++c8) {
+                            uint4 w;
+                            w.x = pack_bf16x2(o[8 * c8 + 0], o[8 * c8 + 1]);
+                            w.y = pack_bf16x2(o[8 * c8 + 2], o[8 * c8 + 3]);
+                            w.z = pack_bf16x2(o[8 * c8 + 4], o[8 * c8 + 5]);
+                            w.w = pack_bf16x2(o[8 * c8 + 6], o[8 * c8 + 7]);
+                            *reinterpret_cast<uint4 *>(op + 32 * q2 + 8 * c8) = w;
+                        }
+                    }
+                }
+                const bool more = c + 1 < nch;
+                const float gn = more ? gates(k + 1)[G_GM + 63] : 1.f;
+                float *dst = nullptr;
+                if (!more && p.state_out) {
+                    const int64_t so = p.out_slots ? static_cast<int64_t>(p.out_slots[seq]) : seq;
+                    if (so >= 0 && so < p.num_slots) dst = p.state_out + ((so * H + h) * HD + row) * HD + 64 * half;
+                }
+#pragma unroll
+                for (int q2 = 0; q2 < 2; ++q2) {
+                    float v[32];
+                    tmem_ld32(trow + TM_S + 64 * half + 32 * q2, v);
+                    tmem_wait_ld();
+                    if (more) {
+                        st_row32_f16(smem + C_OFF_S + half * 16384, row, 4 * q2, v);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] *= gn;
+                        tmem_st32(trow + TM_S + 64 * half + 32 * q2, v);
+                    } else if (dst) {
+#pragma unroll
+                        for (int e = 0; e < 32; e += 4)
+                            *reinterpret_cast<float4 *>(dst + 32 * q2 + e) =
+                                make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+                    }
+                }
+                if (more) tmem_wait_st();
+            }
+            operands_ready();
+        }
+    }
+
+    if (failed && tid == 0) {
+        for (int kk = loads_waited; kk < loads_issued; ++kk)
+            mbar_wait(&bar_load[kk & 1], (kk >> 1) & 1, 200000000ull);
+        if (mma_pending) mbar_wait(bar_mma, mma_phase, 200000000ull);
+        atomicExch(&g_tc_status, 1);
+    }
+    __syncthreads();
+    return RoleState{failed, k, full_waited};
+}
+
+// ------------------------------------------------------------------ producer CTA
+
+__device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k,
+                                                   const TcParams &p, uint8_t *smem, const Walk &wk,
+                                                   int64_t start, uint32_t tmem) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int row = 32 * (warp & 3) + lane;
+    const int half = warp >> 2;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(warp & 3) << 21);
+    uint64_t *bar_load = reinterpret_cast<uint64_t *>(smem + P_OFF_BAR);
+    uint64_t *bar_d1 = bar_load + 2;
+    uint64_t *bar_mma = bar_load + 3;
+    uint64_t *bar_empty = bar_load + 4;
+    uint32_t *copies = reinterpret_cast<uint32_t *>(bar_load + 6) + 1;
+    float *Af = reinterpret_cast<float *>(smem + P_OFF_AF);
+    float *Tf = reinterpret_cast<float *>(smem + P_OFF_TF);
+    float *Xf = reinterpret_cast<float *>(smem + P_OFF_XF);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t peer_full = mapa_shared(sbase + C_OFF_BAR + 16, 0);  // chain's full[0]
+    const uint32_t peer_rec = mapa_shared(sbase + C_OFF_REC, 0);
+
+    uint32_t mma_phase = 0;
+    bool failed = false, mma_pending = false, d1_pending = false;
+    int loads_issued = 0, loads_waited = 0;
+    int k = 0;
+
+    auto gates = [&](int kc) { return reinterpret_cast<float *>(smem + P_OFF_GATE) + (kc & 1) * G_SIZE; };
+    auto issue_loads = [&](int kc, const Ref &r) {
+        const uint32_t st = kc & 1;
+        uint64_t *bar = &bar_load[st];
+        uint8_t *kq = smem + P_OFF_KQ + st * KQ_STAGE;
+        mbar_arrive_expect_tx(bar, KQ_BYTES);
+        const int t32 = static_cast<int>(r.ts);
+        tma_load_3d(kq, tm_k, 0, r.h, t32, bar);
+        tma_load_3d(kq + 16384, tm_k, 64, r.h, t32, bar);
+        tma_load_3d(kq + 8192, tm_q, 0, r.h, t32, bar);
+        tma_load_3d(kq + 24576, tm_q, 64, r.h, t32, bar);
+    };
+    // D1 = [K; Q] K^T of chunk kc on its bf16 tiles, tracked by bar_d1.
+    auto issue_d1 = [&](int kc) {
+        const uint32_t kq = sbase + P_OFF_KQ + (kc & 1) * KQ_STAGE;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_f16(tmem + TM_D1, sdesc_sw128(kq + off, 16, 1024), sdesc_sw128(kq + off, 16, 1024),
+                     ID_D1, kk > 0);
+        }
+        umma_commit(bar_d1);
+    };
+
+    {
+        const Ref cur = wk.first_from(start);
+        const Ref second = cur.item >= 0 ? wk.next_of(cur) : cur;
+        if (tid == 0) {
+            if (cur.item >= 0) issue_loads(0, cur);
+            if (second.item >= 0) issue_loads(1, second);
+        }
+        loads_issued = (cur.item >= 0) + (second.item >= 0);
+        if (cur.item >= 0) {
+            if (warp == 0) gate_tables(gates(0), p, cur, lane);
+            const bool ok = mbar_wait(&bar_load[0], 0);
+            if (__syncthreads_or(!ok)) {
+                failed = true;
+            } else {
+                ++loads_waited;
+                if (tid == 0) {
+                    tc_fence_after();
+                    issue_d1(0);
+                }
+                d1_pending = true;
+            }
+        }
+    }
+
+    for (int64_t item = start; item < wk.n_items && !failed; item += wk.stride) {
+        const int64_t seq = item / wk.H;
+        const int h = static_cast<int>(item - seq * wk.H);
+        int64_t t0, t1;
+        wk.bounds(item, t0, t1);
+        const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
+
+        for (int c = 0; c < nch; ++c, ++k) {
+            const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
+            const int L = static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH);
+            const uint32_t kq = sbase + P_OFF_KQ + (k & 1) * KQ_STAGE;
+            uint8_t *stg = smem + P_OFF_STG + (k & 1) * REC_BYTES;
+            const float *g = gates(k);
+            const int *gz = reinterpret_cast<const int *>(g + G_Z);
+
+            // ---- record slot k & 1 is free once the chain consumed chunk k - 2
+            if (k >= 2) {
+                const bool ok = mbar_wait_cluster(&bar_empty[k & 1], ((k >> 1) - 1) & 1);
+                if (__syncthreads_or(!ok)) { failed = true; break; }
+            }
+            // ---- D1 of this chunk (issued during the previous chunk)
             {
                 const bool ok = mbar_wait(bar_d1, k & 1);
                 if (__syncthreads_or(!ok)) { failed = true; break; }
@@ -533,25 +777,25 @@ __global__ void __launch_bounds__(NT, 1)
                 tc_fence_after();
             }
 
-            // ---- A = beta P (K K^T) (fp32) and M = P (Q K^T) (fp16), 32 columns per thread
+            // ---- A = beta P (K K^T) (fp32) and M = P (Q K^T) (fp16 record), 32 columns per thread
             {
                 const bool qk = row >= 64;
                 const int t = row & 63;
                 const int s0 = 32 * half;
                 // Warp-uniform: the whole 32 x 32 block lies above the diagonal.
                 if (half == 1 && (warp & 1) == 0) {
-                    if (qk) st_zero32(smem + OFF_M, t, 4);
+                    if (qk) st_zero32(stg + REC_M, t, 4);
                 } else {
                     float v[32];
                     tmem_ld32(trow + TM_D1 + s0, v);
                     tmem_wait_ld();
-                    const float glt = sgl[t];
-                    const int zt = sz[t];
-                    const float bt = qk ? 1.f : sbeta[t];
+                    const float glt = g[G_GL + t];
+                    const int zt = gz[t];
+                    const float bt = qk ? 1.f : g[G_BE + t];
 #pragma unroll
                     for (int j4 = 0; j4 < 8; ++j4) {
-                        const float4 g4 = *reinterpret_cast<const float4 *>(sgl + s0 + 4 * j4);
-                        const int4 z4 = *reinterpret_cast<const int4 *>(sz + s0 + 4 * j4);
+                        const float4 g4 = *reinterpret_cast<const float4 *>(g + G_GL + s0 + 4 * j4);
+                        const int4 z4 = *reinterpret_cast<const int4 *>(gz + s0 + 4 * j4);
                         const float gs[4] = {g4.x, g4.y, g4.z, g4.w};
                         const int zs[4] = {z4.x, z4.y, z4.z, z4.w};
 #pragma unroll
@@ -563,7 +807,7 @@ __global__ void __launch_bounds__(NT, 1)
                         }
                     }
                     if (qk) {
-                        st_row32_f16(smem + OFF_M, t, 4 * half, v);
+                        st_row32_f16(stg + REC_M, t, 4 * half, v);
                     } else {
 #pragma unroll
                         for (int j4 = 0; j4 < 8; ++j4)
@@ -572,12 +816,14 @@ __global__ void __launch_bounds__(NT, 1)
                     }
                 }
             }
+            tc_fence_before();
             __syncthreads();
 
             // ---- diagonal 16 x 16 tiles of T (warps 0-1) while warps 2-7 zero
-            // tiles (0,1), (2,3) of T and prepare the next chunk: its gate
-            // tables (warp 2), its tiles converted to fp16
-            const Ref nxt = next_of(Ref{item, ts, L, h});
+            // tiles (0,1), (2,3) of T, convert this chunk's K to fp16 in place
+            // (D1 is done with it) and prepare the next chunk (gate table,
+            // tiles landed)
+            const Ref nxt = wk.next_of(Ref{item, ts, L, h});
             bool prep_fail = false;
             if (tid < 64) {
                 const int I = tid >> 4, j = tid & 15;
@@ -603,34 +849,37 @@ __global__ void __launch_bounds__(NT, 1)
                     const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
                     Tf[(32 * blk + rr) * AST + 32 * blk + 16 + cc] = 0.f;
                 }
+                uint8_t *kt = smem + P_OFF_KQ + (k & 1) * KQ_STAGE;
+                for (int e = tid - 64; e < 1024; e += NT - 64)
+                    chunk_to_f16(reinterpret_cast<uint4 *>(kt + (e >> 9) * 16384 + (e & 511) * 16), 1.f);
+                fence_proxy_async_smem();
                 if (nxt.item >= 0) {
-                    if (warp == 2) gate_tables(k + 1, nxt);
+                    if (warp == 2) gate_tables(gates(k + 1), p, nxt, lane);
                     prep_fail = !mbar_wait(&bar_load[(k + 1) & 1], ((k + 1) >> 1) & 1);
-                    if (!prep_fail)
-                        tiles_to_f16(smem + OFF_KQ + ((k + 1) & 1) * KQ_STAGE,
-                                     smem + OFF_V + ((k + 1) & 1) * V_STAGE, tid - 64, NT - 64);
-                    fence_proxy_async_smem();
                 }
             }
             if (__syncthreads_or(prep_fail)) { failed = true; break; }
             if (nxt.item >= 0) {
                 ++loads_waited;
-                if (tid == 0) issue_d1(k + 1);
+                if (tid == 0) {
+                    tc_fence_after();
+                    issue_d1(k + 1);
+                }
                 d1_pending = true;
             }
             solve_offdiag(Af, Tf, Xf, warp, lane);
 
-            // ---- T diag(beta) and T diag(beta gamma) as fp16 operands
+            // ---- T diag(beta) (record) and T diag(beta gamma) (local) as fp16 operands
             {
                 const int t = tid & 63;
                 const bool hat = (tid >> 6) & 1;
                 const int hh = tid >> 7;
                 const int s0 = 32 * hh;
-                uint8_t *dst = smem + (hat ? OFF_TH : OFF_TT);
+                uint8_t *dst = hat ? smem + P_OFF_TH : stg + REC_TT;
                 if (hh == 1 && t < 32) {
                     st_zero32(dst, t, 4);
                 } else {
-                    const float *sc = hat ? sbg : sbeta;
+                    const float *sc = g + (hat ? G_BG : G_BE);
                     float v[32];
 #pragma unroll
                     for (int j4 = 0; j4 < 8; ++j4) {
@@ -647,184 +896,126 @@ __global__ void __launch_bounds__(NT, 1)
             }
             operands_ready();
 
-            // ---- D_U = V^T (T diag b)^T, D_W = K^T (T diag bg)^T, D_O = Q S0^T
+            // ---- D_W = K^T (T diag bg)^T  (lane j, column t: W[t][j])
             if (tid == 0) {
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    umma_f16(tmem + TM_U, sdesc_sw128(vb + kk * 2048, 8192, 1024),
-                             sdesc_sw128(sbase + OFF_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
-                }
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
+                for (int kk = 0; kk < 4; ++kk)
                     umma_f16(tmem + TM_W, sdesc_sw128(kq + kk * 2048, 16384, 1024),
-                             sdesc_sw128(sbase + OFF_TH + kk * 32, 16, 1024), ID_MK64, kk > 0);
-                }
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_f16(tmem + TM_O, sdesc_sw128(kq + off + 8192, 16, 1024),
-                             sdesc_sw128(sbase + OFF_S + off, 16, 1024), ID_O, kk > 0);
-                }
+                             sdesc_sw128(sbase + P_OFF_TH + kk * 32, 16, 1024), ID_MK64, kk > 0);
+                umma_commit(bar_mma);
             }
-            mma_commit();
-            if (!mma_wait()) { failed = true; break; }
+            mma_pending = true;
+            {
+                const bool ok = mbar_wait(bar_mma, mma_phase);
+                if (__syncthreads_or(!ok)) { failed = true; break; }
+                mma_phase ^= 1u;
+                mma_pending = false;
+                tc_fence_after();
+            }
             {
                 float x[32];
-                tmem_ld32(trow + TM_W + 32 * half, x);  // W[t][j = row], t in this half
+                tmem_ld32(trow + TM_W + 32 * half, x);
                 tmem_wait_ld();
 #pragma unroll
                 for (int t = 0; t < 32; ++t) x[t] = -x[t];
-                st_row32_f16(smem + OFF_WT, row, 4 * half, x);
+                st_row32_f16(stg + REC_WT, row, 4 * half, x);
             }
-            operands_ready();
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncthreads();
 
-            // ---- Delta^T = U^T - S0 W^T (accumulated onto D_U)
+            // ---- stage k & 1 is free (D1 and D_W are done): fetch chunk k + 2;
+            // hand the record to the chain CTA
+            const Ref nn = nxt.item >= 0 ? wk.next_of(nxt) : nxt;
+            if (nn.item >= 0) ++loads_issued;
             if (tid == 0) {
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_f16(tmem + TM_U, sdesc_sw128(sbase + OFF_S + off, 16, 1024),
-                             sdesc_sw128(sbase + OFF_WT + kk * 2048, 8192, 1024), ID_KM64, 1);
-                }
-            }
-            mma_commit();
-            if (!mma_wait()) { failed = true; break; }
-            {
-                float x[32];
-                tmem_ld32(trow + TM_U + 32 * half, x);  // Delta[s][i = row], s in this half
-                tmem_wait_ld();
-                st_row32_f16(smem + OFF_DT, row, 4 * half, x);
-#pragma unroll
-                for (int j4 = 0; j4 < 8; ++j4) {
-                    const float4 pl = *reinterpret_cast<const float4 *>(spl + 32 * half + 4 * j4);
-                    x[4 * j4] *= pl.x; x[4 * j4 + 1] *= pl.y; x[4 * j4 + 2] *= pl.z; x[4 * j4 + 3] *= pl.w;
-                }
-                st_row32_f16(smem + OFF_DTS, row, 4 * half, x);
-                // D_S <- gamma_{C-1} D_S before the rank-C update accumulates.
-                const float gC = sgam[63];
-#pragma unroll
-                for (int q2 = 0; q2 < 2; ++q2) {
-                    float v[32];
-                    tmem_ld32(trow + TM_S + 64 * half + 32 * q2, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) v[e] *= gC;
-                    tmem_st32(trow + TM_S + 64 * half + 32 * q2, v);
-                }
-                // D_O row t <- gamma_t (Q S0^T)[t] before M Delta accumulates
-                // (rows live in lanes 0..15 of each subpartition; the other
-                // lanes' columns here belong to no accumulator).
-                const float gt = sgam[(16 * (warp & 3) + lane) & 63];
-#pragma unroll
-                for (int q2 = 0; q2 < 2; ++q2) {
-                    float v[32];
-                    tmem_ld32(trow + TM_O + 64 * half + 32 * q2, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) v[e] *= gt;
-                    tmem_st32(trow + TM_O + 64 * half + 32 * q2, v);
-                }
-                tmem_wait_st();
-            }
-            operands_ready();
-
-            // ---- D_O += M Delta ; D_S += (P[C-1] Delta)^T K
-            if (tid == 0) {
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    umma_f16(tmem + TM_O, sdesc_sw128(sbase + OFF_M + kk * 32, 16, 1024),
-                             sdesc_sw128(sbase + OFF_DT + kk * 32, 16, 1024), ID_O, 1);
-                }
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    umma_f16(tmem + TM_S, sdesc_sw128(sbase + OFF_DTS + kk * 32, 16, 1024),
-                             sdesc_sw128(kq + kk * 2048, 16384, 1024), ID_KM128, 1);
-                }
-            }
-            mma_commit();
-
-            if (!mma_wait()) { failed = true; break; }
-            // The stage of this chunk is free again: fetch the chunk after next.
-            if (nxt.item >= 0) {
-                const Ref nn = next_of(nxt);
-                if (nn.item >= 0) {
-                    if (tid == 0) issue_loads(k + 2, nn);
-                    ++loads_issued;
-                }
-            }
-
-            // ---- epilogue: O rows (D_O row t sits in lane 32 (t / 16) + t % 16;
-            // lanes 16..31 of each warp hold no row) go out as 16-byte stores;
-            // refresh the fp16 state copy
-            {
-                float o[32];
-                const int t = 16 * (warp & 3) + lane;
-                const bool has_row = lane < 16 && t < L;
-                __nv_bfloat16 *op = p.o + (ts + t) * tok_stride + static_cast<int64_t>(h) * HD + 64 * half;
-#pragma unroll
-                for (int q2 = 0; q2 < 2; ++q2) {
-                    tmem_ld32(trow + TM_O + 64 * half + 32 * q2, o);
-                    tmem_wait_ld();
-                    if (has_row) {
-#pragma unroll
-                        for (int c8 = 0; c8 < 4; ++c8) {
-                            uint4 w;
-                            w.x = pack_bf16x2(o[8 * c8 + 0], o[8 * c8 + 1]);
-                            w.y = pack_bf16x2(o[8 * c8 + 2], o[8 * c8 + 3]);
-                            w.z = pack_bf16x2(o[8 * c8 + 4], o[8 * c8 + 5]);
-                            w.w = pack_bf16x2(o[8 * c8 + 6], o[8 * c8 + 7]);
-                            *reinterpret_cast<uint4 *>(op + 32 * q2 + 8 * c8) = w;
-                        }
-                    }
-                }
-#pragma unroll
-                for (int q2 = 0; q2 < 2; ++q2) {
-                    float v[32];
-                    tmem_ld32(trow + TM_S + 64 * half + 32 * q2, v);
-                    tmem_wait_ld();
-                    st_row32_f16(smem + OFF_S + half * 16384, row, 4 * q2, v);
-                }
-            }
-            operands_ready();
-        }
-        if (failed) break;
-
-        // ---- final state
-        if (p.state_out) {
-            const int64_t slot = p.out_slots ? static_cast<int64_t>(p.out_slots[seq]) : seq;
-            if (slot >= 0 && slot < p.num_slots) {
-                float *dst = p.state_out + ((slot * H + h) * HD + row) * HD + 64 * half;
-#pragma unroll
-                for (int q2 = 0; q2 < 2; ++q2) {
-                    float v[32];
-                    tmem_ld32(trow + TM_S + 64 * half + 32 * q2, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 32; e += 4)
-                        *reinterpret_cast<float4 *>(dst + 32 * q2 + e) =
-                            make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-                }
+                tc_fence_after();
+                if (nn.item >= 0) issue_loads(k + 2, nn);
+                const uint32_t slot = k & 1;
+                mbar_arrive_expect_tx_remote(peer_full + 8 * slot, REC_BYTES);
+                bulk_copy_to_peer(peer_rec + slot * REC_BYTES, stg, REC_BYTES, peer_full + 8 * slot);
+                *copies = static_cast<uint32_t>(k + 1);
             }
         }
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
     }
 
-    if (failed) {
-        // Drain what this CTA still has in flight (bounded), then report.
-        if (tid == 0) {
-            for (int kk = loads_waited; kk < loads_issued; ++kk)
-                mbar_wait(&bar_load[kk & 1], (kk >> 1) & 1, 200000000ull);
-            if (mma_pending) mbar_wait(bar_mma, mma_phase, 200000000ull);
-            if (d1_pending) mbar_wait(bar_d1, k & 1, 200000000ull);
-            atomicExch(&g_tc_status, 1);
+    if (failed && tid == 0) {
+        for (int kk = loads_waited; kk < loads_issued; ++kk)
+            mbar_wait(&bar_load[kk & 1], (kk >> 1) & 1, 200000000ull);
+        if (mma_pending) mbar_wait(bar_mma, mma_phase, 200000000ull);
+        if (d1_pending) mbar_wait(bar_d1, k & 1, 200000000ull);
+        atomicExch(&g_tc_status, 1);
+    }
+    __syncthreads();
+    return RoleState{failed, k, 0};
+}
+
+__global__ void __launch_bounds__(NT, 1)
+    gdr_chunk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+                        const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v,
+                        const __grid_constant__ TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const uint32_t rank = cluster_ctarank();
+    const bool chain = rank == 0;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (chain ? C_OFF_BAR : P_OFF_BAR));
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + (chain ? 5 : 6));
+    const uint32_t ncols = chain ? C_TM_COLS : P_TM_COLS;
+
+    if (tid == 0) {
+        if (chain) {
+            for (int i = 0; i < 5; ++i) mbar_init(&bars[i], 1);  // load[2], full[2], mma
+        } else {
+            for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);  // load[2], d1, mma, empty[2]
+            tmem_slot[1] = 0;                                     // records handed over
         }
-        __syncthreads();
+        mbar_fence_init();
+        prefetch_tmap(&tm_q);
+        prefetch_tmap(&tm_k);
+        if (chain) prefetch_tmap(&tm_v);
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, ncols);
+        tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, TM_COLS);
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // Both CTAs' barriers exist before either side touches the other's.
+    cluster_sync();
+
+    int64_t n_seq = p.n_seq;
+    if (p.n_seq_dev) {
+        const int64_t nd = *p.n_seq_dev;
+        n_seq = nd < n_seq ? nd : n_seq;
+    }
+    const Walk wk{&p, n_seq * p.H, static_cast<int64_t>(cluster_count_x()), p.H};
+    const int64_t start = cluster_id_x();
+    RoleState rs = chain ? chain_role(&tm_q, &tm_k, &tm_v, p, smem, wk, start, tmem)
+                         : producer_role(&tm_q, &tm_k, p, smem, wk, start, tmem);
+
+    // Teardown: the producer has issued its last copy once both sides pass the
+    // first cluster barrier; the chain then waits (bounded) for copies it never
+    // consumed, so nothing still lands in its shared memory when it exits.
+    cluster_sync();
+    if (chain) {
+        const uint32_t sbase = smem_u32(smem);
+        const uint32_t issued = ld_shared_cluster_u32(mapa_shared(sbase + P_OFF_BAR + 52, 1));
+        if (tid == 0) {
+            uint64_t *bar_full = bars + 2;
+            for (int kk = rs.full_waited; kk < static_cast<int>(issued); ++kk)
+                mbar_wait_cluster(&bar_full[kk & 1], (kk >> 1) & 1, 200000000ull);
+        }
+        __syncthreads();
+    }
+    cluster_sync();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, ncols);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -871,6 +1062,9 @@ int launch_chunk_tc(const SeqArgs &a) {
         SeqArgs b = a;
         return launch_seq(b);
     }
+    if (tokens > INT_MAX - CH)
+        return set_error(RHZ_ERR_SHAPE, "tensor-core kernel addresses at most %d token rows (got %lld)",
+                         INT_MAX - CH, static_cast<long long>(tokens));
     CUtensorMap tq, tk, tv;
     int st = make_tmap(&tq, a.q, tokens, a.H);
     if (st == RHZ_OK) st = make_tmap(&tk, a.k, tokens, a.H);
@@ -879,8 +1073,6 @@ int launch_chunk_tc(const SeqArgs &a) {
     int sms = 148;
     bool sm100 = true;
     device_info(&sms, &sm100);
-    const int64_t items = a.n_seq * a.H;
-    const int grid = static_cast<int>(items < sms ? items : sms);
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(attr_once, [] {
@@ -890,6 +1082,9 @@ int launch_chunk_tc(const SeqArgs &a) {
     });
     if (attr_err != cudaSuccess)
         return set_error(RHZ_ERR_DEVICE, "gdr_chunk_tc_kernel smem attribute: %s", cudaGetErrorString(attr_err));
+    const int64_t items = a.n_seq * a.H;
+    const int64_t max_clusters = sms / 2;
+    const int clusters = static_cast<int>(items < max_clusters ? items : max_clusters);
     TcParams p;
     p.o = static_cast<__nv_bfloat16 *>(a.o);
     p.alpha = a.alpha;
@@ -905,7 +1100,22 @@ int launch_chunk_tc(const SeqArgs &a) {
     p.out_slots = a.out_slots;
     p.num_slots = a.num_slots;
     p.H = a.H;
-    gdr_chunk_tc_kernel<<<grid, NT, SMEM_ALLOC, a.stream>>>(tq, tk, tv, p);
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(NT, 1, 1);
+    cfg.dynamicSmemBytes = SMEM_ALLOC;
+    cfg.stream = a.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gdr_chunk_tc_kernel, tq, tk, tv, p);
+    if (e != cudaSuccess)
+        return set_error(RHZ_ERR_DEVICE, "gdr_chunk_tc_kernel launch: %s", cudaGetErrorString(e));
     return check_launch("gdr_chunk_tc_kernel");
 }
 
