@@ -86,26 +86,38 @@ constexpr uint32_t REC_TT = 16384;    // T diag(beta) [t = 64 rows][s]   (K-majo
 constexpr uint32_t REC_M = 24576;     // M = P (Q K^T) [t rows][s]        (K-major A of R2)
 constexpr uint32_t REC_BYTES = 32768;
 
+// Gate table layout (floats): gl[64] z[64] (int) beta[64] gamma[64] P[C-1][.][64] beta*gamma[64].
+constexpr int G_GL = 0, G_Z = 64, G_BE = 128, G_GM = 192, G_PL = 256, G_BG = 320, G_SIZE = 384;
+constexpr uint32_t G_BYTES = G_SIZE * 4;
+
 // Chain CTA (cluster rank 0) shared memory.
 constexpr uint32_t C_OFF_KQ = 0;             // 2 stages
 constexpr uint32_t C_OFF_V = 65536;          // 2 stages
-constexpr uint32_t C_OFF_REC = 98304;        // 2 records
-constexpr uint32_t C_OFF_S = 163840;         // fp16 state [half][128 rows i][64 j]
+constexpr uint32_t C_OFF_REC = 98304;        // 2 record slots
+constexpr uint32_t C_OFF_S = 163840;         // fp16 state [half j][128 rows i][64 j]
 constexpr uint32_t C_OFF_DT = 196608;        // fp16 Delta^T [i = 128 rows][s]
-constexpr uint32_t C_OFF_GATE = 212992;      // 2 x gate tables (384 floats)
-constexpr uint32_t C_OFF_BAR = 216064;       // load[2], full[2], mma, TMEM base
-constexpr uint32_t C_USED = C_OFF_BAR + 64;
+constexpr uint32_t C_OFF_GATE = 212992;      // ring of 4 gate tables
+constexpr uint32_t C_OFF_BAR = C_OFF_GATE + 4 * G_BYTES;
+// Chain barriers: tiles landed [2], record landed [2], D_U done (R1), D_S
+// done (R2), all of a chunk's products done, tiles converted [2] (warpgroup
+// 1 -> 0), D_O buffer read out [2] (1 -> 0), and a barrier that only the
+// failure path uses to wait for every MMA issued.
+constexpr int CB_LOAD = 0, CB_FULL = 2, CB_R1 = 4, CB_R2S = 5, CB_R2 = 6, CB_CONV = 7, CB_OFREE = 9,
+              CB_DRAIN = 11, CB_NUM = 12;
+constexpr uint32_t C_USED = C_OFF_BAR + CB_NUM * 8 + 16;  // + TMEM base
 
 // Producer CTA (cluster rank 1) shared memory.
-constexpr uint32_t P_OFF_KQ = 0;             // 2 stages
+constexpr uint32_t P_OFF_KQ = 0;             // 2 stages of K, Q tiles
 constexpr uint32_t P_OFF_STG = 65536;        // 2 records being built
-constexpr uint32_t P_OFF_TH = 131072;        // fp16 T diag(beta gamma) [t][s]
+constexpr uint32_t P_OFF_TH = 131072;        // fp16 T diag(beta gamma) [t][s]; earlier the solve's scratch
 constexpr uint32_t P_OFF_AF = 139264;        // A fp32 [64][AST]
-constexpr uint32_t P_OFF_TF = P_OFF_AF + 64 * AST * 4;  // T fp32 [64][AST]
-constexpr uint32_t P_OFF_XF = P_OFF_TF + 64 * AST * 4;  // 32 x 32 fp32 partial products
-constexpr uint32_t P_OFF_GATE = P_OFF_XF + 4096;        // 2 x gate tables
-constexpr uint32_t P_OFF_BAR = P_OFF_GATE + 3072;       // load[2], d1, mma, empty[2], TMEM base, count
-constexpr uint32_t P_USED = P_OFF_BAR + 64;
+constexpr uint32_t P_OFF_TF = P_OFF_AF + 64 * AST * 4;   // T fp32 [64][AST]
+constexpr uint32_t P_OFF_GATE = P_OFF_TF + 64 * AST * 4; // 2 gate tables
+constexpr uint32_t P_OFF_BAR = P_OFF_GATE + 2 * G_BYTES;
+// Producer barriers: tiles landed [2], D1 done, D_W done, chain slot free [2],
+// failure-path drain of every MMA issued.
+constexpr int PB_LOAD = 0, PB_D1 = 2, PB_MMA = 3, PB_EMPTY = 4, PB_DRAIN = 6, PB_NUM = 7;
+constexpr uint32_t P_USED = P_OFF_BAR + PB_NUM * 8 + 16;  // + TMEM base
 
 constexpr uint32_t SMEM_USED = C_USED > P_USED ? C_USED : P_USED;
 constexpr size_t SMEM_ALLOC = SMEM_USED + 1024;  // slack for 1024-byte alignment
@@ -113,10 +125,10 @@ static_assert(C_OFF_GATE >= C_OFF_DT + 16384, "chain map overlaps");
 static_assert(P_OFF_AF >= P_OFF_TH + 8192, "producer map overlaps");
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in shared memory");
 
-// TMEM columns (f32). Chain: D_U (128 lanes x 64), D_O (M = 64: row t in
-// lane 32 (t / 16) + t % 16, 128 columns), D_S (128 x 128). Producer: D1
-// (128 x 64) and D_W (128 x 64).
-constexpr uint32_t TM_U = 0, TM_O = 64, TM_S = 192, C_TM_COLS = 512;
+// TMEM columns (f32). Chain: D_U (128 lanes x 64), D_S (128 x 128) and two
+// D_O buffers (M = 64: row t in lane 32 (t / 16) + t % 16, 128 columns).
+// Producer: D1 (128 x 64) and D_W (128 x 64).
+constexpr uint32_t TM_U = 0, TM_S = 64, TM_O = 192, C_TM_COLS = 512;
 constexpr uint32_t TM_D1 = 0, TM_W = 64, P_TM_COLS = 128;
 
 constexpr uint32_t ID_D1 = idesc_bf16(128, 64, false, false);
@@ -124,9 +136,6 @@ constexpr uint32_t ID_MK64 = idesc_f16(128, 64, true, false);
 constexpr uint32_t ID_KM64 = idesc_f16(128, 64, false, true);
 constexpr uint32_t ID_KM128 = idesc_f16(128, 128, false, true);
 constexpr uint32_t ID_O = idesc_f16(64, 128, false, false);
-
-// Gate table layout (floats): gl[64] z[64] (int) beta[64] gamma[64] P[C-1][.][64] beta*gamma[64].
-constexpr int G_GL = 0, G_Z = 64, G_BE = 128, G_GM = 192, G_PL = 256, G_BG = 320, G_SIZE = 384;
 
 struct TcParams {
     __nv_bfloat16 *o;
@@ -193,28 +202,51 @@ __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x, float s) {
     return pack_f16x2(__low2float(b) * s, __high2float(b) * s);
 }
 
-__device__ __forceinline__ void chunk_to_f16(uint4 *ptr, float s) {
-    uint4 w = *ptr;
-    w.x = bf16x2_to_f16x2(w.x, s);
-    w.y = bf16x2_to_f16x2(w.y, s);
-    w.z = bf16x2_to_f16x2(w.z, s);
-    w.w = bf16x2_to_f16x2(w.w, s);
-    *ptr = w;
-}
-
 // Chain: one stage's K, Q (32 KB) and V (16 KB) tiles bf16 -> fp16 in place,
-// Q rows scaled by gamma_t and K rows by P[C-1][s]; 16-byte chunks
-// [first, 3072) stepping by `stride`. The swizzle permutes chunks within a
-// row only, so chunk i of a K/Q half lies in row (i / 8) % 128 (rows 0..63 K,
-// 64..127 Q).
+// Q rows scaled by gamma_t and K rows by P[C-1][s]; this thread's 16-byte
+// chunks are first, first + STRIDE, ... of the K/Q stage (2048 chunks) and of
+// the V stage (1024). The swizzle permutes chunks within a row only, so chunk
+// i of a K/Q half lies in row (i / 8) % 128 (rows 0..63 K, 64..127 Q).
+template <int STRIDE>
 __device__ __forceinline__ void chain_tiles_to_f16(uint8_t *kq, uint8_t *vv, const float *gm,
-                                                   const float *pl, int first, int stride) {
-    for (int i = first; i < 3072; i += stride) {
-        if (i < 2048) {
+                                                   const float *pl, int first) {
+    static_assert(2048 % (8 * STRIDE) == 0 && 1024 % (8 * STRIDE) == 0, "batches of 8 chunks");
+    // Eight loads in flight, then eight converted stores.
+#pragma unroll
+    for (int b = 0; b < 2048 / STRIDE; b += 8) {
+        uint4 x[8];
+        float sc[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const int i = first + (b + m) * STRIDE;
             const int r = (i >> 3) & 127;
-            chunk_to_f16(reinterpret_cast<uint4 *>(kq + i * 16), r < 64 ? pl[r] : gm[r - 64]);
-        } else {
-            chunk_to_f16(reinterpret_cast<uint4 *>(vv + (i - 2048) * 16), 1.f);
+            x[m] = *reinterpret_cast<const uint4 *>(kq + i * 16);
+            sc[m] = r < 64 ? pl[r] : gm[r - 64];
+        }
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const int i = first + (b + m) * STRIDE;
+            uint4 w = x[m];
+            w.x = bf16x2_to_f16x2(w.x, sc[m]);
+            w.y = bf16x2_to_f16x2(w.y, sc[m]);
+            w.z = bf16x2_to_f16x2(w.z, sc[m]);
+            w.w = bf16x2_to_f16x2(w.w, sc[m]);
+            *reinterpret_cast<uint4 *>(kq + i * 16) = w;
+        }
+    }
+#pragma unroll
+    for (int b = 0; b < 1024 / STRIDE; b += 8) {
+        uint4 x[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) x[m] = *reinterpret_cast<const uint4 *>(vv + (first + (b + m) * STRIDE) * 16);
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            uint4 w = x[m];
+            w.x = bf16x2_to_f16x2(w.x, 1.f);
+            w.y = bf16x2_to_f16x2(w.y, 1.f);
+            w.z = bf16x2_to_f16x2(w.z, 1.f);
+            w.w = bf16x2_to_f16x2(w.w, 1.f);
+            *reinterpret_cast<uint4 *>(vv + (first + (b + m) * STRIDE) * 16) = w;
         }
     }
 }
@@ -259,12 +291,78 @@ __device__ __forceinline__ void st_frag_c(float *C, int cs, int lane, const floa
     *reinterpret_cast<float2 *>(C + (g + 8) * cs + 2 * t) = make_float2(sign * d[2], sign * d[3]);
 }
 
+// Transpose of one 8 x 8 fp16 block held in the mma fragment layout.
+__device__ __forceinline__ uint32_t movtrans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+// A fragment (fp16) of a 16 x 16 matrix from its two 16 x 8 accumulator halves.
+__device__ __forceinline__ void c_to_a(const float (&c0)[4], const float (&c1)[4], uint32_t (&a)[4]) {
+    a[0] = h2(c0[0], c0[1]);
+    a[1] = h2(c0[2], c0[3]);
+    a[2] = h2(c1[0], c1[1]);
+    a[3] = h2(c1[2], c1[3]);
+}
+
+// B fragments (both 16 x 8 column halves) of the matrix whose A fragment is
+// `a`: the B layout of X is the A layout of X^T, block by block.
+__device__ __forceinline__ void a_to_b(const uint32_t (&a)[4], uint32_t (&b0)[2], uint32_t (&b1)[2]) {
+    b0[0] = movtrans(a[0]);
+    b0[1] = movtrans(a[1]);
+    b1[0] = movtrans(a[2]);
+    b1[1] = movtrans(a[3]);
+}
+
+// Inverse of the unit-lower-triangular 16 x 16 block I + N (N strictly lower,
+// fp32 in A at row stride AST) written to T (same stride), by one warp:
+// (I + N)^-1 = (I - N)(I + N^2)(I + N^4)(I + N^8), exact for nilpotent N of
+// order 16, as 12 mma.sync products with fp16 operands and fp32 accumulation.
+__device__ __forceinline__ void diag_inverse16(const float *A, float *T, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    float n0[4], n1[4];
+    {
+        const float2 a0 = *reinterpret_cast<const float2 *>(A + g * AST + 2 * t);
+        const float2 a1 = *reinterpret_cast<const float2 *>(A + (g + 8) * AST + 2 * t);
+        const float2 a2 = *reinterpret_cast<const float2 *>(A + g * AST + 8 + 2 * t);
+        const float2 a3 = *reinterpret_cast<const float2 *>(A + (g + 8) * AST + 8 + 2 * t);
+        n0[0] = a0.x; n0[1] = a0.y; n0[2] = a1.x; n0[3] = a1.y;
+        n1[0] = a2.x; n1[1] = a2.y; n1[2] = a3.x; n1[3] = a3.y;
+    }
+    // X = I - N in the accumulator layout (row g / g + 8, columns 8h + 2t, +1).
+    float x0[4], x1[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int r = g + 8 * (e >> 1), c = 2 * t + (e & 1);
+        x0[e] = (r == c ? 1.f : 0.f) - n0[e];
+        x1[e] = (r == c + 8 ? 1.f : 0.f) - n1[e];
+    }
+    uint32_t aP[4], bP0[2], bP1[2], aX[4];
+    c_to_a(n0, n1, aP);
+    a_to_b(aP, bP0, bP1);
+#pragma unroll
+    for (int lvl = 0; lvl < 3; ++lvl) {
+        // P <- P^2 (N^2, N^4, N^8), then X <- X + X P.
+        float p0[4] = {0.f, 0.f, 0.f, 0.f}, p1[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(p0, aP, bP0);
+        mma16816(p1, aP, bP1);
+        c_to_a(p0, p1, aP);
+        a_to_b(aP, bP0, bP1);
+        c_to_a(x0, x1, aX);
+        mma16816(x0, aX, bP0);
+        mma16816(x1, aX, bP1);
+    }
+    st_frag_c(T, AST, lane, x0, 1.f);
+    st_frag_c(T + 8, AST, lane, x1, 1.f);
+}
+
 // Off-diagonal part of T = (I + A)^-1 once the four diagonal 16 x 16 inverses
 // D_I are in Tf (and Tf's tiles (0,1) and (2,3) are zero), by a 2 x 2
 // recursion: T_{2p+1,2p} = -D_{2p+1} (A_{2p+1,2p} D_{2p}) for p = 0, 1, then
 // T[32:64, 0:32] = -T[32:64, 32:64] (A[32:64, 0:32] T[0:32, 0:32]). The
 // products run on mma.sync with fp16 operands (T is rounded to fp16 for the
-// tcgen05 products anyway). Ends synchronised.
+// tcgen05 products anyway), on all eight warps. Ends synchronised.
 __device__ void solve_offdiag(const float *Af, float *Tf, float *Xf, int warp, int lane) {
     if (warp < 4) {
         const int pb = warp >> 1, nt = warp & 1;
@@ -284,8 +382,8 @@ __device__ void solve_offdiag(const float *Af, float *Tf, float *Xf, int warp, i
         st_frag_c(Tf + r0 * AST + c0 + 8 * nt, AST, lane, y, -1.f);
     }
     __syncthreads();
+    const int mt = warp >> 2, nt = warp & 3;
     {
-        const int mt = warp >> 2, nt = warp & 3;
         float y[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int ks = 0; ks < 2; ++ks) {
@@ -298,7 +396,6 @@ __device__ void solve_offdiag(const float *Af, float *Tf, float *Xf, int warp, i
     }
     __syncthreads();
     {
-        const int mt = warp >> 2, nt = warp & 3;
         float y[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int ks = 0; ks < 2; ++ks) {
@@ -310,6 +407,14 @@ __device__ void solve_offdiag(const float *Af, float *Tf, float *Xf, int warp, i
         st_frag_c(Tf + (32 + 16 * mt) * AST + 8 * nt, AST, lane, y, -1.f);
     }
     __syncthreads();
+}
+
+// Make thread-written smem operands and TMEM stores visible to the MMA issuer.
+__device__ __forceinline__ void operands_ready() {
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
 }
 
 struct Ref {
@@ -361,18 +466,35 @@ struct Walk {
     }
 };
 
-// Gate tables of one chunk (one warp, two positions per lane): prefix sums of
-// log2 alpha over nonzero alphas and of zero-alpha counts, then gamma_t,
-// P[C-1][s], beta, beta*gamma. Padded rows get alpha = 1, beta = 0 so they
-// write nothing.
-__device__ __forceinline__ void gate_tables(float *g, const TcParams &p, const Ref &r, int lane) {
+// Gate inputs of one chunk for one warp (two positions per lane), loaded a
+// chunk ahead of their use so the global latency stays off the critical
+// path. Padded positions get alpha = 1, beta = 0 so they write nothing.
+struct GateIn {
+    float a0, a1, b0, b1;
+};
+
+__device__ __forceinline__ GateIn gate_load(const TcParams &p, const Ref &r, int lane) {
+    GateIn g{1.f, 1.f, 0.f, 0.f};
+    if (r.item < 0) return g;
     const int H = p.H;
+    const int p0 = 2 * lane, p1 = p0 + 1;
+    if (p0 < r.L) {
+        g.a0 = p.alpha[(r.ts + p0) * H + r.h];
+        g.b0 = p.beta[(r.ts + p0) * H + r.h];
+    }
+    if (p1 < r.L) {
+        g.a1 = p.alpha[(r.ts + p1) * H + r.h];
+        g.b1 = p.beta[(r.ts + p1) * H + r.h];
+    }
+    return g;
+}
+
+// Gate tables of one chunk (one warp): prefix sums of log2 alpha over nonzero
+// alphas and of zero-alpha counts, then gamma_t, P[C-1][s], beta, beta*gamma.
+__device__ __forceinline__ void gate_tables(float *g, const GateIn &in, int lane) {
     int *zz = reinterpret_cast<int *>(g + G_Z);
     const int p0 = 2 * lane, p1 = p0 + 1;
-    const float a0 = p0 < r.L ? p.alpha[(r.ts + p0) * H + r.h] : 1.f;
-    const float a1 = p1 < r.L ? p.alpha[(r.ts + p1) * H + r.h] : 1.f;
-    const float b0 = p0 < r.L ? p.beta[(r.ts + p0) * H + r.h] : 0.f;
-    const float b1 = p1 < r.L ? p.beta[(r.ts + p1) * H + r.h] : 0.f;
+    const float a0 = in.a0, a1 = in.a1, b0 = in.b0, b1 = in.b1;
     const bool nz0 = a0 >= 1.17549435e-38f, nz1 = a1 >= 1.17549435e-38f;
     const float l0 = nz0 ? lg2(a0) : 0.f, l1 = nz1 ? lg2(a1) : 0.f;
     const int z0 = nz0 ? 0 : 1, z1 = nz1 ? 0 : 1;
@@ -400,312 +522,349 @@ __device__ __forceinline__ void gate_tables(float *g, const TcParams &p, const R
 
 struct RoleState {
     bool failed;
-    int k;              // chunks finished (chain: records consumed)
-    int full_waited;    // chain: record barriers waited
 };
 
-// Make thread-written smem operands and TMEM stores visible to the MMA issuer.
-__device__ __forceinline__ void operands_ready() {
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-}
-
 // ------------------------------------------------------------------ chain CTA
-
+//
+// Warpgroup 0 runs the serial state path of every chunk k: record k, tiles k
+// converted and D_O buffer k & 1 free -> R1 -> Delta^T -> R2 -> state
+// refresh. Warpgroup 1 works beside it: gate tables two chunks ahead, the
+// fp16 conversion of chunk k + 1's tiles under chunk k's products, and, once
+// R2(k) is done, the release of stage / record slot k & 1, the loads of chunk
+// k + 2 and the O rows of chunk k from D_O[k & 1]. Every barrier phase has a
+// single producer and is consumed before it can be reused, so parities never
+// alias.
 __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k,
                                                 const CUtensorMap *tm_v, const TcParams &p,
                                                 uint8_t *smem, const Walk &wk, int64_t start,
                                                 uint32_t tmem) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // TMEM lane (accumulator row) of this thread and the column half it owns.
-    const int row = 32 * (warp & 3) + lane;
-    const int half = warp >> 2;
-    const uint32_t trow = tmem + (static_cast<uint32_t>(warp & 3) << 21);  // lane (32 (w&3)) << 16
-    uint64_t *bar_load = reinterpret_cast<uint64_t *>(smem + C_OFF_BAR);
-    uint64_t *bar_full = bar_load + 2;
-    uint64_t *bar_mma = bar_load + 4;
+    const int ww = warp & 3;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(ww) << 21);  // lanes 32 ww .. 32 ww + 31
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C_OFF_BAR);
+    uint64_t *bar_load = bars + CB_LOAD, *bar_full = bars + CB_FULL, *bar_r1 = bars + CB_R1,
+             *bar_r2s = bars + CB_R2S, *bar_r2 = bars + CB_R2, *bar_conv = bars + CB_CONV,
+             *bar_ofree = bars + CB_OFREE;
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t peer_empty = mapa_shared(sbase + P_OFF_BAR + 32, 1);  // producer's empty[0]
     const int H = p.H;
     const int64_t tok_stride = static_cast<int64_t>(H) * HD;
+    auto gates = [&](int kc) { return reinterpret_cast<float *>(smem + C_OFF_GATE) + (kc & 3) * G_SIZE; };
+    RoleState rs{false};
 
-    uint32_t mma_phase = 0;
-    bool failed = false, mma_pending = false;
-    int loads_issued = 0, loads_waited = 0, full_waited = 0;
-    int k = 0;
-
-    auto gates = [&](int kc) { return reinterpret_cast<float *>(smem + C_OFF_GATE) + (kc & 1) * G_SIZE; };
-    auto issue_loads = [&](int kc, const Ref &r) {
-        const uint32_t st = kc & 1;
-        uint64_t *bar = &bar_load[st];
-        uint8_t *kq = smem + C_OFF_KQ + st * KQ_STAGE;
-        uint8_t *vv = smem + C_OFF_V + st * V_STAGE;
-        mbar_arrive_expect_tx(bar, KQV_BYTES);
-        const int t32 = static_cast<int>(r.ts);
-        tma_load_3d(kq, tm_k, 0, r.h, t32, bar);
-        tma_load_3d(kq + 16384, tm_k, 64, r.h, t32, bar);
-        tma_load_3d(kq + 8192, tm_q, 0, r.h, t32, bar);
-        tma_load_3d(kq + 24576, tm_q, 64, r.h, t32, bar);
-        tma_load_3d(vv, tm_v, 0, r.h, t32, bar);
-        tma_load_3d(vv + 8192, tm_v, 64, r.h, t32, bar);
-    };
-    auto mma_commit = [&]() {
-        if (tid == 0) umma_commit(bar_mma);
-        mma_pending = true;
-    };
-    auto mma_wait = [&]() -> bool {
-        const bool ok = mbar_wait(bar_mma, mma_phase);
-        if (__syncthreads_or(!ok)) return false;
-        mma_phase ^= 1u;
-        mma_pending = false;
-        tc_fence_after();
-        return true;
-    };
-    // Chunk kc's tiles landed -> fp16 with the gate scalings (its gate table
-    // must be written before the call; the barrier inside orders it).
-    auto convert = [&](int kc) -> bool {
-        const bool ok = mbar_wait(&bar_load[kc & 1], (kc >> 1) & 1);
-        if (__syncthreads_or(!ok)) return false;
-        ++loads_waited;
-        const float *g = gates(kc);
-        chain_tiles_to_f16(smem + C_OFF_KQ + (kc & 1) * KQ_STAGE, smem + C_OFF_V + (kc & 1) * V_STAGE,
-                           g + G_GM, g + G_PL, tid, NT);
-        return true;
-    };
-
-    {
-        const Ref cur = wk.first_from(start);
-        const Ref second = cur.item >= 0 ? wk.next_of(cur) : cur;
-        if (tid == 0) {
-            if (cur.item >= 0) issue_loads(0, cur);
-            if (second.item >= 0) issue_loads(1, second);
-        }
-        loads_issued = (cur.item >= 0) + (second.item >= 0);
-        if (cur.item >= 0) {
-            if (warp == 0) gate_tables(gates(0), p, cur, lane);
-            if (!convert(0)) failed = true;
-        }
-    }
-
-    for (int64_t item = start; item < wk.n_items && !failed; item += wk.stride) {
-        const int64_t seq = item / H;
-        const int h = static_cast<int>(item - seq * H);
-        int64_t t0, t1;
-        wk.bounds(item, t0, t1);
-        const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
-
-        // ---- initial state: fp16 copy (unscaled) and D_S = gamma_{C-1} S0
-        {
+    if (tid < 128) {
+        // ------------------------------------------------ warpgroup 0: state path
+        const int row = tid;  // state row i = TMEM lane
+        int k = 0;
+        for (int64_t item = start; item < wk.n_items && !rs.failed; item += wk.stride) {
+            const int64_t seq = item / H;
+            const int h = static_cast<int>(item - seq * H);
+            int64_t t0, t1;
+            wk.bounds(item, t0, t1);
+            const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
             int64_t slot = -1;
             if (p.state_in) slot = p.in_slots ? static_cast<int64_t>(p.in_slots[seq]) : seq;
             const bool have = p.state_in && slot >= 0 && slot < p.num_slots;
-            const float *src = have ? p.state_in + ((slot * H + h) * HD + row) * HD + 64 * half : nullptr;
+            const float *src = have ? p.state_in + ((slot * H + h) * HD + row) * HD : nullptr;
+            int64_t so = -1;
+            if (p.state_out) so = p.out_slots ? static_cast<int64_t>(p.out_slots[seq]) : seq;
+            float *dst = (p.state_out && so >= 0 && so < p.num_slots)
+                             ? p.state_out + ((so * H + h) * HD + row) * HD
+                             : nullptr;
             if (nch == 0) {
                 // Empty sequence: the final state is the initial state.
-                if (p.state_out) {
-                    const int64_t so = p.out_slots ? static_cast<int64_t>(p.out_slots[seq]) : seq;
-                    if (so >= 0 && so < p.num_slots) {
-                        float *dst = p.state_out + ((so * H + h) * HD + row) * HD + 64 * half;
-                        for (int e = 0; e < 64; e += 4)
-                            *reinterpret_cast<float4 *>(dst + e) =
-                                have ? *reinterpret_cast<const float4 *>(src + e) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-                }
+                if (dst)
+                    for (int e = 0; e < HD; e += 4)
+                        *reinterpret_cast<float4 *>(dst + e) =
+                            have ? *reinterpret_cast<const float4 *>(src + e) : make_float4(0.f, 0.f, 0.f, 0.f);
                 continue;
             }
-            const float gC = gates(k)[G_GM + 63];
+            for (int c = 0; c < nch; ++c, ++k) {
+                const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
+                (void)ts;
+                const uint32_t kq = sbase + C_OFF_KQ + (k & 1) * KQ_STAGE;
+                const uint32_t vb = sbase + C_OFF_V + (k & 1) * V_STAGE;
+                const uint32_t rec = sbase + C_OFF_REC + (k & 1) * REC_BYTES;
+                const uint32_t tO = tmem + TM_O + 128 * (k & 1);
+
+                // ---- R1's inputs: record k (its barrier armed here; the peer's
+                // copy may already have delivered its bytes), tiles k in fp16,
+                // D_O buffer k & 1 read out
+                if (tid == 0) mbar_arrive_expect_tx(&bar_full[k & 1], REC_BYTES);
+                bool ok = mbar_wait_cluster(&bar_full[k & 1], (k >> 1) & 1);
+                ok = ok && mbar_wait(&bar_conv[k & 1], (k >> 1) & 1);
+                if (k >= 2) ok = ok && mbar_wait(&bar_ofree[k & 1], ((k >> 1) + 1) & 1);
+                if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
+
+                // ---- first chunk of the item: fp16 copy of S0 (unscaled) and
+                // D_S = gamma_{C-1} S0
+                if (c == 0) {
+                    const float gC = gates(k)[G_GM + 63];
 #pragma unroll
-            for (int q2 = 0; q2 < 2; ++q2) {
-                float v[32];
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        float v[32];
 #pragma unroll
-                for (int e = 0; e < 32; e += 4) {
-                    float4 f = have ? *reinterpret_cast<const float4 *>(src + 32 * q2 + e)
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-                    v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
+                        for (int e = 0; e < 32; e += 4) {
+                            const float4 f = have ? *reinterpret_cast<const float4 *>(src + 32 * q4 + e)
+                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                            v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
+                        }
+                        st_row32_f16(smem + C_OFF_S + (q4 >> 1) * 16384, row, 4 * (q4 & 1), v);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] *= gC;
+                        tmem_st32(trow + TM_S + 32 * q4, v);
+                    }
+                    tmem_wait_st();
+                    fence_proxy_async_smem();
+                    tc_fence_before();
+                    wg_sync(1);
                 }
-                st_row32_f16(smem + C_OFF_S + half * 16384, row, 4 * q2, v);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) v[e] *= gC;
-                tmem_st32(trow + TM_S + 64 * half + 32 * q2, v);
-            }
-            tmem_wait_st();
-        }
-        operands_ready();
 
-        for (int c = 0; c < nch; ++c, ++k) {
-            const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
-            const int L = static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH);
-            const uint32_t kq = sbase + C_OFF_KQ + (k & 1) * KQ_STAGE;
-            const uint32_t vb = sbase + C_OFF_V + (k & 1) * V_STAGE;
-            const uint32_t rec = sbase + C_OFF_REC + (k & 1) * REC_BYTES;
-
-            // ---- the producer's record for this chunk
-            {
-                const bool ok = mbar_wait_cluster(&bar_full[k & 1], (k >> 1) & 1);
-                if (__syncthreads_or(!ok)) { failed = true; break; }
-                ++full_waited;
-            }
-
-            // ---- R1: D_U = V^T (T diag b)^T + S (-W^T) ; D_O = Q~ S^T
-            if (tid == 0) {
+                // ---- R1: D_U = V^T (T diag b)^T + S (-W^T) ; D_O[k & 1] = Q~ S^T
+                if (tid == 0) {
+                    tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    umma_f16(tmem + TM_U, sdesc_sw128(vb + kk * 2048, 8192, 1024),
-                             sdesc_sw128(rec + REC_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_f16(tmem + TM_U, sdesc_sw128(vb + kk * 2048, 8192, 1024),
+                                 sdesc_sw128(rec + REC_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_f16(tmem + TM_U, sdesc_sw128(sbase + C_OFF_S + off, 16, 1024),
-                             sdesc_sw128(rec + REC_WT + kk * 2048, 8192, 1024), ID_KM64, 1);
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                        umma_f16(tmem + TM_U, sdesc_sw128(sbase + C_OFF_S + off, 16, 1024),
+                                 sdesc_sw128(rec + REC_WT + kk * 2048, 8192, 1024), ID_KM64, 1);
+                    }
+                    umma_commit(bar_r1);  // Delta^T is ready; D_O runs on behind it
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                        umma_f16(tO, sdesc_sw128(kq + off + 8192, 16, 1024),
+                                 sdesc_sw128(sbase + C_OFF_S + off, 16, 1024), ID_O, kk > 0);
+                    }
                 }
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_f16(tmem + TM_O, sdesc_sw128(kq + off + 8192, 16, 1024),
-                             sdesc_sw128(sbase + C_OFF_S + off, 16, 1024), ID_O, kk > 0);
-                }
-            }
-            mma_commit();
+                ok = mbar_wait(bar_r1, k & 1);
+                if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
+                tc_fence_after();
 
-            // ---- under R1: the next chunk's gate table and fp16 tiles
-            const Ref nxt = wk.next_of(Ref{item, ts, L, h});
-            if (nxt.item >= 0) {
-                if (warp == 0) gate_tables(gates(k + 1), p, nxt, lane);
-                if (!convert(k + 1)) { failed = true; break; }
-            }
-            if (!mma_wait()) { failed = true; break; }
-
-            // ---- Delta^T (fp16): thread (row i, half) holds Delta[s][i] for its 32 s
-            {
-                float x[32];
-                tmem_ld32(trow + TM_U + 32 * half, x);
-                tmem_wait_ld();
-                st_row32_f16(smem + C_OFF_DT, row, 4 * half, x);
-            }
-            operands_ready();
-
-            // ---- R2: D_O += M Delta ; D_S += Delta^T K~
-            if (tid == 0) {
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    umma_f16(tmem + TM_O, sdesc_sw128(rec + REC_M + kk * 32, 16, 1024),
-                             sdesc_sw128(sbase + C_OFF_DT + kk * 32, 16, 1024), ID_O, 1);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    umma_f16(tmem + TM_S, sdesc_sw128(sbase + C_OFF_DT + kk * 32, 16, 1024),
-                             sdesc_sw128(kq + kk * 2048, 16384, 1024), ID_KM128, 1);
-            }
-            mma_commit();
-            if (!mma_wait()) { failed = true; break; }
-
-            // Record slot and tile stage k & 1 are free again.
-            if (tid == 0) mbar_arrive_remote(peer_empty + 8 * (k & 1));
-            if (nxt.item >= 0) {
-                const Ref nn = wk.next_of(nxt);
-                if (nn.item >= 0) {
-                    if (tid == 0) issue_loads(k + 2, nn);
-                    ++loads_issued;
-                }
-            }
-
-            // ---- epilogue: O rows (D_O row t sits in lane 32 (t / 16) + t % 16;
-            // lanes 16..31 of each warp hold no row) go out as 16-byte stores;
-            // the state's fp16 copy is refreshed and D_S pre-scaled for the
-            // next chunk, or the final state is written out.
-            {
-                float o[32];
-                const int t = 16 * (warp & 3) + lane;
-                const bool has_row = lane < 16 && t < L;
-                __nv_bfloat16 *op = p.o + (ts + t) * tok_stride + static_cast<int64_t>(h) * HD + 64 * half;
-#pragma unroll
-                for (int q2 = 0; q2 < 2; ++q2) {
-                    tmem_ld32(trow + TM_O + 64 * half + 32 * q2, o);
+                // ---- Delta^T (fp16): row i, all 64 positions
+                {
+                    float x[32], y[32];
+                    tmem_ld32(trow + TM_U, x);
+                    tmem_ld32(trow + TM_U + 32, y);
                     tmem_wait_ld();
-                    if (has_row) {
+                    st_row32_f16(smem + C_OFF_DT, row, 0, x);
+                    st_row32_f16(smem + C_OFF_DT, row, 4, y);
+                }
+                fence_proxy_async_smem();
+                tc_fence_before();
+                wg_sync(1);
+
+                // ---- R2: D_S += Delta^T K~ (the state refresh waits for this
+                // part only), then D_O[k & 1] += M Delta
+                if (tid == 0) {
+                    tc_fence_after();
 #pragma unroll
-                        for (int c8 = 0; c8 < 4; ++c8) {
-                            uint4 w;
-                            w.x = pack_bf16x2(o[8 * c8 + 0], o[8 * c8 + 1]);
-                            w.y = pack_bf16x2(o[8 * c8 + 2], o[8 * c8 + 3]);
-                            w.z = pack_bf16x2(o[8 * c8 + 4], o[8 * c8 + 5]);
-                            w.w = pack_bf16x2(o[8 * c8 + 6], o[8 * c8 + 7]);
-                            *reinterpret_cast<uint4 *>(op + 32 * q2 + 8 * c8) = w;
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_f16(tmem + TM_S, sdesc_sw128(sbase + C_OFF_DT + kk * 32, 16, 1024),
+                                 sdesc_sw128(kq + kk * 2048, 16384, 1024), ID_KM128, 1);
+                    umma_commit(bar_r2s);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_f16(tO, sdesc_sw128(rec + REC_M + kk * 32, 16, 1024),
+                                 sdesc_sw128(sbase + C_OFF_DT + kk * 32, 16, 1024), ID_O, 1);
+                    umma_commit(bar_r2);
+                }
+                ok = mbar_wait(bar_r2s, k & 1);
+                if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
+                tc_fence_after();
+
+                // ---- state: fp16 copy for the next chunk and D_S pre-scaled
+                // by its gamma_{C-1}, or the final state
+                {
+                    const bool more = c + 1 < nch;
+                    const float gn = more ? gates(k + 1)[G_GM + 63] : 1.f;
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        float v[32];
+                        tmem_ld32(trow + TM_S + 32 * q4, v);
+                        tmem_wait_ld();
+                        if (more) {
+                            st_row32_f16(smem + C_OFF_S + (q4 >> 1) * 16384, row, 4 * (q4 & 1), v);
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) v[e] *= gn;
+                            tmem_st32(trow + TM_S + 32 * q4, v);
+                        } else if (dst) {
+#pragma unroll
+                            for (int e = 0; e < 32; e += 4)
+                                *reinterpret_cast<float4 *>(dst + 32 * q4 + e) =
+                                    make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
                         }
                     }
+                    if (more) tmem_wait_st();
                 }
-                const bool more = c + 1 < nch;
-                const float gn = more ? gates(k + 1)[G_GM + 63] : 1.f;
-                float *dst = nullptr;
-                if (!more && p.state_out) {
-                    const int64_t so = p.out_slots ? static_cast<int64_t>(p.out_slots[seq]) : seq;
-                    if (so >= 0 && so < p.num_slots) dst = p.state_out + ((so * H + h) * HD + row) * HD + 64 * half;
-                }
-#pragma unroll
-                for (int q2 = 0; q2 < 2; ++q2) {
-                    float v[32];
-                    tmem_ld32(trow + TM_S + 64 * half + 32 * q2, v);
-                    tmem_wait_ld();
-                    if (more) {
-                        st_row32_f16(smem + C_OFF_S + half * 16384, row, 4 * q2, v);
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) v[e] *= gn;
-                        tmem_st32(trow + TM_S + 64 * half + 32 * q2, v);
-                    } else if (dst) {
-#pragma unroll
-                        for (int e = 0; e < 32; e += 4)
-                            *reinterpret_cast<float4 *>(dst + 32 * q2 + e) =
-                                make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-                    }
-                }
-                if (more) tmem_wait_st();
+                fence_proxy_async_smem();
+                tc_fence_before();
+                wg_sync(1);
             }
-            operands_ready();
         }
-    }
+        if (rs.failed && tid == 0) {
+            // Every MMA this thread issued (including D_O products that no
+            // commit covered yet) completes before TMEM is released.
+            umma_commit(bars + CB_DRAIN);
+            mbar_wait(bars + CB_DRAIN, 0, 200000000ull);
+        }
+    } else {
+        // ------------------------------------------------ warpgroup 1: tiles, epilogue
+        const int wt = tid - 128;
+        const uint32_t peer_empty = mapa_shared(sbase + P_OFF_BAR + 8 * PB_EMPTY, 1);
+        int loads_issued = 0, loads_waited = 0;
+        GateIn gin{1.f, 1.f, 0.f, 0.f};  // warp 4: inputs of the gate table two chunks ahead
+        auto issue_loads = [&](int kc, const Ref &r) {
+            const uint32_t st = kc & 1;
+            uint64_t *bar = &bar_load[st];
+            uint8_t *kqs = smem + C_OFF_KQ + st * KQ_STAGE;
+            uint8_t *vv = smem + C_OFF_V + st * V_STAGE;
+            mbar_arrive_expect_tx(bar, KQV_BYTES);
+            const int t32 = static_cast<int>(r.ts);
+            tma_load_3d(kqs, tm_k, 0, r.h, t32, bar);
+            tma_load_3d(kqs + 16384, tm_k, 64, r.h, t32, bar);
+            tma_load_3d(kqs + 8192, tm_q, 0, r.h, t32, bar);
+            tma_load_3d(kqs + 24576, tm_q, 64, r.h, t32, bar);
+            tma_load_3d(vv, tm_v, 0, r.h, t32, bar);
+            tma_load_3d(vv + 8192, tm_v, 64, r.h, t32, bar);
+        };
+        auto convert = [&](int kc) {
+            const float *g = gates(kc);
+            chain_tiles_to_f16<128>(smem + C_OFF_KQ + (kc & 1) * KQ_STAGE,
+                                    smem + C_OFF_V + (kc & 1) * V_STAGE, g + G_GM, g + G_PL, wt);
+            fence_proxy_async_smem();
+        };
 
-    if (failed && tid == 0) {
-        for (int kk = loads_waited; kk < loads_issued; ++kk)
-            mbar_wait(&bar_load[kk & 1], (kk >> 1) & 1, 200000000ull);
-        if (mma_pending) mbar_wait(bar_mma, mma_phase, 200000000ull);
-        atomicExch(&g_tc_status, 1);
+        {
+            const Ref r0 = wk.first_from(start);
+            const Ref r1 = r0.item >= 0 ? wk.next_of(r0) : r0;
+            const Ref r2 = r1.item >= 0 ? wk.next_of(r1) : r1;
+            if (wt == 0) {
+                if (r0.item >= 0) issue_loads(0, r0);
+                if (r1.item >= 0) issue_loads(1, r1);
+            }
+            loads_issued = (r0.item >= 0) + (r1.item >= 0);
+            if (ww == 0) {
+                gate_tables(gates(0), gate_load(p, r0, lane), lane);
+                gate_tables(gates(1), gate_load(p, r1, lane), lane);
+                gin = gate_load(p, r2, lane);
+            }
+            if (r0.item >= 0) {
+                const bool ok = mbar_wait(&bar_load[0], 0);
+                if (wg_sync_or(2, !ok)) {
+                    rs.failed = true;
+                } else {
+                    ++loads_waited;
+                    convert(0);
+                    mbar_arrive(&bar_conv[0]);
+                }
+            }
+        }
+
+        int k = 0;
+        for (int64_t item = start; item < wk.n_items && !rs.failed; item += wk.stride) {
+            const int64_t seq = item / H;
+            const int h = static_cast<int>(item - seq * H);
+            int64_t t0, t1;
+            wk.bounds(item, t0, t1);
+            const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
+            for (int c = 0; c < nch; ++c, ++k) {
+                const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
+                const int L = static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH);
+                const Ref nxt = wk.next_of(Ref{item, ts, L, h});
+                const Ref nn = nxt.item >= 0 ? wk.next_of(nxt) : nxt;
+
+                // ---- gate table of chunk k + 2, then the inputs of chunk k + 3
+                if (nn.item >= 0 && ww == 0) {
+                    gate_tables(gates(k + 2), gin, lane);
+                    gin = gate_load(p, wk.next_of(nn), lane);
+                }
+                // ---- chunk k + 1's tiles -> fp16 (under chunk k's products)
+                if (nxt.item >= 0) {
+                    const bool ok = mbar_wait(&bar_load[(k + 1) & 1], ((k + 1) >> 1) & 1);
+                    if (wg_sync_or(2, !ok)) { rs.failed = true; break; }
+                    ++loads_waited;
+                    convert(k + 1);
+                }
+                // ---- chunk k's products are done
+                {
+                    const bool ok = mbar_wait(bar_r2, k & 1);
+                    if (wg_sync_or(2, !ok)) { rs.failed = true; break; }
+                    tc_fence_after();
+                }
+                if (nxt.item >= 0) mbar_arrive(&bar_conv[(k + 1) & 1]);
+                // Stage and record slot k & 1 are free again.
+                if (wt == 0) {
+                    mbar_arrive_remote_relaxed(peer_empty + 8 * (k & 1));
+                    if (nn.item >= 0) issue_loads(k + 2, nn);
+                }
+                if (nn.item >= 0) ++loads_issued;
+
+                // ---- O rows of chunk k (D_O row t in lane 32 (t / 16) + t % 16)
+                {
+                    const uint32_t tO = trow + TM_O + 128 * (k & 1);
+                    const int t = 16 * ww + lane;
+                    const bool has_row = lane < 16 && t < L;
+                    __nv_bfloat16 *op = p.o + (ts + t) * tok_stride + static_cast<int64_t>(h) * HD;
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        float o[32];
+                        tmem_ld32(tO + 32 * q4, o);
+                        tmem_wait_ld();
+                        if (has_row) {
+#pragma unroll
+                            for (int c8 = 0; c8 < 4; ++c8) {
+                                uint4 w;
+                                w.x = pack_bf16x2(o[8 * c8 + 0], o[8 * c8 + 1]);
+                                w.y = pack_bf16x2(o[8 * c8 + 2], o[8 * c8 + 3]);
+                                w.z = pack_bf16x2(o[8 * c8 + 4], o[8 * c8 + 5]);
+                                w.w = pack_bf16x2(o[8 * c8 + 6], o[8 * c8 + 7]);
+                                *reinterpret_cast<uint4 *>(op + 32 * q4 + 8 * c8) = w;
+                            }
+                        }
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&bar_ofree[k & 1]);
+                }
+            }
+        }
+        if (rs.failed && wt == 0)
+            for (int kk = loads_waited; kk < loads_issued; ++kk)
+                mbar_wait(&bar_load[kk & 1], (kk >> 1) & 1, 200000000ull);
     }
-    __syncthreads();
-    return RoleState{failed, k, full_waited};
+    if (rs.failed) atomicExch(&g_tc_status, 1);
+    rs.failed = __syncthreads_or(rs.failed);
+    return rs;
 }
 
 // ------------------------------------------------------------------ producer CTA
-
+//
+// All eight warps build chunk k's record while the tiles of chunk k + 1 land
+// and its D1 runs; records alternate between two staging buffers, so building
+// never waits for the copy of the previous record.
 __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k,
                                                    const TcParams &p, uint8_t *smem, const Walk &wk,
                                                    int64_t start, uint32_t tmem) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int row = 32 * (warp & 3) + lane;
-    const int half = warp >> 2;
+    const int row = 32 * (warp & 3) + lane;  // TMEM lane
+    const int half = warp >> 2;              // column half of this thread
     const uint32_t trow = tmem + (static_cast<uint32_t>(warp & 3) << 21);
-    uint64_t *bar_load = reinterpret_cast<uint64_t *>(smem + P_OFF_BAR);
-    uint64_t *bar_d1 = bar_load + 2;
-    uint64_t *bar_mma = bar_load + 3;
-    uint64_t *bar_empty = bar_load + 4;
-    uint32_t *copies = reinterpret_cast<uint32_t *>(bar_load + 6) + 1;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P_OFF_BAR);
+    uint64_t *bar_load = bars + PB_LOAD, *bar_d1 = bars + PB_D1, *bar_mma = bars + PB_MMA,
+             *bar_empty = bars + PB_EMPTY;
     float *Af = reinterpret_cast<float *>(smem + P_OFF_AF);
     float *Tf = reinterpret_cast<float *>(smem + P_OFF_TF);
-    float *Xf = reinterpret_cast<float *>(smem + P_OFF_XF);
+    float *Xf = reinterpret_cast<float *>(smem + P_OFF_TH);  // scratch of the solve; T^ comes later
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t peer_full = mapa_shared(sbase + C_OFF_BAR + 16, 0);  // chain's full[0]
+    const uint32_t peer_full = mapa_shared(sbase + C_OFF_BAR + 8 * CB_FULL, 0);
     const uint32_t peer_rec = mapa_shared(sbase + C_OFF_REC, 0);
-
-    uint32_t mma_phase = 0;
-    bool failed = false, mma_pending = false, d1_pending = false;
-    int loads_issued = 0, loads_waited = 0;
-    int k = 0;
-
     auto gates = [&](int kc) { return reinterpret_cast<float *>(smem + P_OFF_GATE) + (kc & 1) * G_SIZE; };
     auto issue_loads = [&](int kc, const Ref &r) {
-        const uint32_t st = kc & 1;
-        uint64_t *bar = &bar_load[st];
-        uint8_t *kq = smem + P_OFF_KQ + st * KQ_STAGE;
+        uint64_t *bar = &bar_load[kc & 1];
+        uint8_t *kq = smem + P_OFF_KQ + (kc & 1) * KQ_STAGE;
         mbar_arrive_expect_tx(bar, KQ_BYTES);
         const int t32 = static_cast<int>(r.ts);
         tma_load_3d(kq, tm_k, 0, r.h, t32, bar);
@@ -713,7 +872,7 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         tma_load_3d(kq + 8192, tm_q, 0, r.h, t32, bar);
         tma_load_3d(kq + 24576, tm_q, 64, r.h, t32, bar);
     };
-    // D1 = [K; Q] K^T of chunk kc on its bf16 tiles, tracked by bar_d1.
+    // D1 = [K; Q] K^T of chunk kc on its bf16 tiles.
     auto issue_d1 = [&](int kc) {
         const uint32_t kq = sbase + P_OFF_KQ + (kc & 1) * KQ_STAGE;
 #pragma unroll
@@ -725,6 +884,11 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         umma_commit(bar_d1);
     };
 
+    RoleState rs{false};
+    uint32_t mma_phase = 0;
+    int loads_issued = 0, loads_waited = 0;
+    int k = 0;
+    GateIn gin{1.f, 1.f, 0.f, 0.f};  // warp 4: inputs of the next chunk's gate table
     {
         const Ref cur = wk.first_from(start);
         const Ref second = cur.item >= 0 ? wk.next_of(cur) : cur;
@@ -734,50 +898,46 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         }
         loads_issued = (cur.item >= 0) + (second.item >= 0);
         if (cur.item >= 0) {
-            if (warp == 0) gate_tables(gates(0), p, cur, lane);
+            if (warp == 0) gate_tables(gates(0), gate_load(p, cur, lane), lane);
+            if (warp == 4) gin = gate_load(p, second, lane);
             const bool ok = mbar_wait(&bar_load[0], 0);
             if (__syncthreads_or(!ok)) {
-                failed = true;
+                rs.failed = true;
             } else {
                 ++loads_waited;
                 if (tid == 0) {
                     tc_fence_after();
                     issue_d1(0);
                 }
-                d1_pending = true;
             }
         }
     }
 
-    for (int64_t item = start; item < wk.n_items && !failed; item += wk.stride) {
+    for (int64_t item = start; item < wk.n_items && !rs.failed; item += wk.stride) {
         const int64_t seq = item / wk.H;
         const int h = static_cast<int>(item - seq * wk.H);
         int64_t t0, t1;
         wk.bounds(item, t0, t1);
         const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
-
         for (int c = 0; c < nch; ++c, ++k) {
             const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
             const int L = static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH);
+            uint8_t *kqp = smem + P_OFF_KQ + (k & 1) * KQ_STAGE;
             const uint32_t kq = sbase + P_OFF_KQ + (k & 1) * KQ_STAGE;
             uint8_t *stg = smem + P_OFF_STG + (k & 1) * REC_BYTES;
             const float *g = gates(k);
             const int *gz = reinterpret_cast<const int *>(g + G_Z);
 
-            // ---- record slot k & 1 is free once the chain consumed chunk k - 2
-            if (k >= 2) {
-                const bool ok = mbar_wait_cluster(&bar_empty[k & 1], ((k >> 1) - 1) & 1);
-                if (__syncthreads_or(!ok)) { failed = true; break; }
-            }
-            // ---- D1 of this chunk (issued during the previous chunk)
+            // ---- staging buffer k & 1 is free once the chain consumed chunk k - 2;
+            // D1 of this chunk (issued during the previous one)
             {
-                const bool ok = mbar_wait(bar_d1, k & 1);
-                if (__syncthreads_or(!ok)) { failed = true; break; }
-                d1_pending = false;
+                bool ok = k < 2 || mbar_wait_cluster(&bar_empty[k & 1], ((k >> 1) + 1) & 1);
+                ok = ok && mbar_wait(bar_d1, k & 1);
+                if (__syncthreads_or(!ok)) { rs.failed = true; break; }
                 tc_fence_after();
             }
 
-            // ---- A = beta P (K K^T) (fp32) and M = P (Q K^T) (fp16 record), 32 columns per thread
+            // ---- A = beta P (K K^T) (fp32) and M = P (Q K^T) (record, fp16), 32 columns per thread
             {
                 const bool qk = row >= 64;
                 const int t = row & 63;
@@ -819,53 +979,53 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             tc_fence_before();
             __syncthreads();
 
-            // ---- diagonal 16 x 16 tiles of T (warps 0-1) while warps 2-7 zero
-            // tiles (0,1), (2,3) of T, convert this chunk's K to fp16 in place
-            // (D1 is done with it) and prepare the next chunk (gate table,
-            // tiles landed)
+            // ---- diagonal 16 x 16 tiles of T (warps 0-3, one each) while warps
+            // 4-7 zero tiles (0,1), (2,3) of T, convert this chunk's K to fp16 in
+            // place (D1 is done with it), build the next gate table and wait for
+            // the next chunk's tiles
             const Ref nxt = wk.next_of(Ref{item, ts, L, h});
+            const Ref nn = nxt.item >= 0 ? wk.next_of(nxt) : nxt;
             bool prep_fail = false;
-            if (tid < 64) {
-                const int I = tid >> 4, j = tid & 15;
-                float x[16];
-#pragma unroll
-                for (int r = 0; r < 16; ++r) {
-                    const float *arow = Af + (16 * I + r) * AST + 16 * I;
-                    float a[16];
-#pragma unroll
-                    for (int c4 = 0; c4 < 4; ++c4) {
-                        const float4 f = *reinterpret_cast<const float4 *>(arow + 4 * c4);
-                        a[4 * c4] = f.x; a[4 * c4 + 1] = f.y; a[4 * c4 + 2] = f.z; a[4 * c4 + 3] = f.w;
-                    }
-                    float acc = (r == j) ? 1.f : 0.f;
-#pragma unroll
-                    for (int cc = 0; cc < r; ++cc)
-                        if (cc >= j) acc = fmaf(-a[cc], x[cc], acc);
-                    x[r] = (r >= j) ? acc : 0.f;
-                    Tf[(16 * I + r) * AST + 16 * I + j] = x[r];
-                }
+            if (warp < 4) {
+                diag_inverse16(Af + (16 * warp) * AST + 16 * warp, Tf + (16 * warp) * AST + 16 * warp, lane);
             } else {
-                for (int e = tid - 64; e < 512; e += NT - 64) {
+                const int wt = tid - 128;
+                for (int e = wt; e < 512; e += 128) {
                     const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
                     Tf[(32 * blk + rr) * AST + 32 * blk + 16 + cc] = 0.f;
                 }
-                uint8_t *kt = smem + P_OFF_KQ + (k & 1) * KQ_STAGE;
-                for (int e = tid - 64; e < 1024; e += NT - 64)
-                    chunk_to_f16(reinterpret_cast<uint4 *>(kt + (e >> 9) * 16384 + (e & 511) * 16), 1.f);
+                uint4 x[8];
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    const int e = wt + 128 * m;
+                    x[m] = *reinterpret_cast<const uint4 *>(kqp + (e >> 9) * 16384 + (e & 511) * 16);
+                }
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    const int e = wt + 128 * m;
+                    uint4 w = x[m];
+                    w.x = bf16x2_to_f16x2(w.x, 1.f);
+                    w.y = bf16x2_to_f16x2(w.y, 1.f);
+                    w.z = bf16x2_to_f16x2(w.z, 1.f);
+                    w.w = bf16x2_to_f16x2(w.w, 1.f);
+                    *reinterpret_cast<uint4 *>(kqp + (e >> 9) * 16384 + (e & 511) * 16) = w;
+                }
                 fence_proxy_async_smem();
                 if (nxt.item >= 0) {
-                    if (warp == 2) gate_tables(gates(k + 1), p, nxt, lane);
+                    if (warp == 4) {
+                        gate_tables(gates(k + 1), gin, lane);
+                        gin = gate_load(p, nn, lane);
+                    }
                     prep_fail = !mbar_wait(&bar_load[(k + 1) & 1], ((k + 1) >> 1) & 1);
                 }
             }
-            if (__syncthreads_or(prep_fail)) { failed = true; break; }
+            if (__syncthreads_or(prep_fail)) { rs.failed = true; break; }
             if (nxt.item >= 0) {
                 ++loads_waited;
                 if (tid == 0) {
                     tc_fence_after();
                     issue_d1(k + 1);
                 }
-                d1_pending = true;
             }
             solve_offdiag(Af, Tf, Xf, warp, lane);
 
@@ -875,9 +1035,9 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                 const bool hat = (tid >> 6) & 1;
                 const int hh = tid >> 7;
                 const int s0 = 32 * hh;
-                uint8_t *dst = hat ? smem + P_OFF_TH : stg + REC_TT;
+                uint8_t *dstb = hat ? smem + P_OFF_TH : stg + REC_TT;
                 if (hh == 1 && t < 32) {
-                    st_zero32(dst, t, 4);
+                    st_zero32(dstb, t, 4);
                 } else {
                     const float *sc = g + (hat ? G_BG : G_BE);
                     float v[32];
@@ -891,7 +1051,7 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                         v[4 * j4 + 2] = s + 2 <= t ? tv.z * sv.z : 0.f;
                         v[4 * j4 + 3] = s + 3 <= t ? tv.w * sv.w : 0.f;
                     }
-                    st_row32_f16(dst, t, 4 * hh, v);
+                    st_row32_f16(dstb, t, 4 * hh, v);
                 }
             }
             operands_ready();
@@ -904,12 +1064,10 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                              sdesc_sw128(sbase + P_OFF_TH + kk * 32, 16, 1024), ID_MK64, kk > 0);
                 umma_commit(bar_mma);
             }
-            mma_pending = true;
             {
                 const bool ok = mbar_wait(bar_mma, mma_phase);
-                if (__syncthreads_or(!ok)) { failed = true; break; }
+                if (__syncthreads_or(!ok)) { rs.failed = true; break; }
                 mma_phase ^= 1u;
-                mma_pending = false;
                 tc_fence_after();
             }
             {
@@ -925,29 +1083,27 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             __syncthreads();
 
             // ---- stage k & 1 is free (D1 and D_W are done): fetch chunk k + 2;
-            // hand the record to the chain CTA
-            const Ref nn = nxt.item >= 0 ? wk.next_of(nxt) : nxt;
+            // hand the record to the chain CTA (its slot k & 1 is free: the
+            // chain consumed chunk k - 2 before this staging buffer was reused)
             if (nn.item >= 0) ++loads_issued;
             if (tid == 0) {
                 tc_fence_after();
                 if (nn.item >= 0) issue_loads(k + 2, nn);
                 const uint32_t slot = k & 1;
-                mbar_arrive_expect_tx_remote(peer_full + 8 * slot, REC_BYTES);
                 bulk_copy_to_peer(peer_rec + slot * REC_BYTES, stg, REC_BYTES, peer_full + 8 * slot);
-                *copies = static_cast<uint32_t>(k + 1);
             }
         }
     }
 
-    if (failed && tid == 0) {
+    if (rs.failed && tid == 0) {
         for (int kk = loads_waited; kk < loads_issued; ++kk)
             mbar_wait(&bar_load[kk & 1], (kk >> 1) & 1, 200000000ull);
-        if (mma_pending) mbar_wait(bar_mma, mma_phase, 200000000ull);
-        if (d1_pending) mbar_wait(bar_d1, k & 1, 200000000ull);
+        umma_commit(bars + PB_DRAIN);  // every MMA issued, D1 and D_W alike
+        mbar_wait(bars + PB_DRAIN, 0, 200000000ull);
         atomicExch(&g_tc_status, 1);
     }
-    __syncthreads();
-    return RoleState{failed, k, 0};
+    rs.failed = __syncthreads_or(rs.failed);
+    return rs;
 }
 
 __global__ void __launch_bounds__(NT, 1)
@@ -962,15 +1118,18 @@ __global__ void __launch_bounds__(NT, 1)
     const uint32_t rank = cluster_ctarank();
     const bool chain = rank == 0;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (chain ? C_OFF_BAR : P_OFF_BAR));
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + (chain ? 5 : 6));
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + (chain ? CB_NUM : PB_NUM));
     const uint32_t ncols = chain ? C_TM_COLS : P_TM_COLS;
 
     if (tid == 0) {
         if (chain) {
-            for (int i = 0; i < 5; ++i) mbar_init(&bars[i], 1);  // load[2], full[2], mma
+            for (int i = 0; i < CB_NUM; ++i) mbar_init(&bars[i], 1);  // loads, R1, R2
+            for (int i = 0; i < 2; ++i) {
+                mbar_init(&bars[CB_CONV + i], 128);   // warpgroup 1 signals
+                mbar_init(&bars[CB_OFREE + i], 128);
+            }
         } else {
-            for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);  // load[2], d1, mma, empty[2]
-            tmem_slot[1] = 0;                                     // records handed over
+            for (int i = 0; i < PB_NUM; ++i) mbar_init(&bars[i], 1);
         }
         mbar_fence_init();
         prefetch_tmap(&tm_q);
@@ -995,24 +1154,19 @@ __global__ void __launch_bounds__(NT, 1)
     }
     const Walk wk{&p, n_seq * p.H, static_cast<int64_t>(cluster_count_x()), p.H};
     const int64_t start = cluster_id_x();
-    RoleState rs = chain ? chain_role(&tm_q, &tm_k, &tm_v, p, smem, wk, start, tmem)
-                         : producer_role(&tm_q, &tm_k, p, smem, wk, start, tmem);
+    const RoleState rs = chain ? chain_role(&tm_q, &tm_k, &tm_v, p, smem, wk, start, tmem)
+                               : producer_role(&tm_q, &tm_k, p, smem, wk, start, tmem);
 
-    // Teardown: the producer has issued its last copy once both sides pass the
-    // first cluster barrier; the chain then waits (bounded) for copies it never
-    // consumed, so nothing still lands in its shared memory when it exits.
+    // Teardown: past this cluster barrier neither side issues anything to the
+    // other. Normally every record copy has been consumed; after a failure a
+    // copy may still be in flight, so the chain pauses (bounded) to let it land
+    // before its shared memory goes away.
     cluster_sync();
-    if (chain) {
-        const uint32_t sbase = smem_u32(smem);
-        const uint32_t issued = ld_shared_cluster_u32(mapa_shared(sbase + P_OFF_BAR + 52, 1));
-        if (tid == 0) {
-            uint64_t *bar_full = bars + 2;
-            for (int kk = rs.full_waited; kk < static_cast<int>(issued); ++kk)
-                mbar_wait_cluster(&bar_full[kk & 1], (kk >> 1) & 1, 200000000ull);
+    if (chain && rs.failed && tid == 0) {
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 200000ull) {
         }
-        __syncthreads();
     }
-    cluster_sync();
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, ncols);

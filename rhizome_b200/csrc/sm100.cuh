@@ -37,6 +37,30 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  : "memory");
 }
 
+// One arrival (release, CTA scope) on a local barrier.
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Named barrier over the 128 threads of one warpgroup (ids 1..15; 0 is
+// __syncthreads), and the same with an OR-reduction of a predicate.
+__device__ __forceinline__ void wg_sync(int id) {
+    asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory");
+}
+
+__device__ __forceinline__ bool wg_sync_or(int id, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(pred)), "r"(id)
+        : "memory");
+    return r != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -113,17 +137,31 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
     return r;
 }
 
-// Arrive (release, cluster scope) on a barrier in a peer CTA's shared memory.
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+// Relaxed arrive on a barrier in a peer CTA's shared memory: a pure signal
+// that publishes no data of this thread (e.g. "the MMAs that read this buffer
+// have completed"), so it skips the release fence.
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+                 : "memory");
+}
+
+// Release arrive (cluster scope) on a barrier in a peer CTA: publishes this
+// thread's earlier writes to the peer.
+__device__ __forceinline__ void mbar_arrive_remote_release(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                  : "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive_expect_tx_remote(uint32_t cluster_addr, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
-                     cluster_addr),
-                 "r"(bytes)
+// 16-byte store into a peer CTA's shared memory.
+__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint4 v) {
+    asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(v.x),
+                 "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
+}
+
+// Generic-proxy writes to cluster shared memory -> visible to the async proxy.
+__device__ __forceinline__ void fence_proxy_async_cluster() {
+    asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
 }
 
 // Bulk copy of `bytes` (multiple of 16, both ends 16-byte aligned) from this
