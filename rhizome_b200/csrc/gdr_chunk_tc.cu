@@ -211,8 +211,9 @@ template <int STRIDE>
 __device__ __forceinline__ void chain_tiles_to_f16(uint8_t *kq, uint8_t *vv, const float *gm,
                                                    const float *pl, int first) {
     static_assert(2048 % (8 * STRIDE) == 0 && 1024 % (8 * STRIDE) == 0, "batches of 8 chunks");
-    // Eight loads in flight, then eight converted stores.
-#pragma unroll
+    // Eight loads in flight, then eight converted stores (batches rolled to
+    // keep the code small).
+#pragma unroll 1
     for (int b = 0; b < 2048 / STRIDE; b += 8) {
         uint4 x[8];
         float sc[8];
@@ -234,7 +235,7 @@ __device__ __forceinline__ void chain_tiles_to_f16(uint8_t *kq, uint8_t *vv, con
             *reinterpret_cast<uint4 *>(kq + i * 16) = w;
         }
     }
-#pragma unroll
+#pragma unroll 1
     for (int b = 0; b < 1024 / STRIDE; b += 8) {
         uint4 x[8];
 #pragma unroll
@@ -599,7 +600,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 // D_S = gamma_{C-1} S0
                 if (c == 0) {
                     const float gC = gates(k)[G_GM + 63];
-#pragma unroll
+#pragma unroll 1
                     for (int q4 = 0; q4 < 4; ++q4) {
                         float v[32];
 #pragma unroll
@@ -681,7 +682,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 {
                     const bool more = c + 1 < nch;
                     const float gn = more ? gates(k + 1)[G_GM + 63] : 1.f;
-#pragma unroll
+#pragma unroll 1
                     for (int q4 = 0; q4 < 4; ++q4) {
                         float v[32];
                         tmem_ld32(trow + TM_S + 32 * q4, v);
@@ -809,7 +810,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     const int t = 16 * ww + lane;
                     const bool has_row = lane < 16 && t < L;
                     __nv_bfloat16 *op = p.o + (ts + t) * tok_stride + static_cast<int64_t>(h) * HD;
-#pragma unroll
+#pragma unroll 1
                     for (int q4 = 0; q4 < 4; ++q4) {
                         float o[32];
                         tmem_ld32(tO + 32 * q4, o);
