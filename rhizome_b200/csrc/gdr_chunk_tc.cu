@@ -109,8 +109,8 @@ constexpr uint32_t C_USED = C_OFF_BAR + CB_NUM * 8 + 16;  // + TMEM base
 // Producer CTA (cluster rank 1) shared memory.
 constexpr uint32_t P_OFF_KQ = 0;             // 2 stages of K, Q tiles
 constexpr uint32_t P_OFF_STG = 65536;        // 2 records being built
-constexpr uint32_t P_OFF_TH = 131072;        // fp16 T diag(beta gamma) [t][s]; earlier the solve's scratch
-constexpr uint32_t P_OFF_AF = 139264;        // A fp32 [64][AST]
+constexpr uint32_t P_OFF_TH = 131072;        // T diag(beta gamma) [t][s] as bf16 hi, lo (2 x 8 KB); earlier the solve's scratch
+constexpr uint32_t P_OFF_AF = 147456;        // A fp32 [64][AST]
 constexpr uint32_t P_OFF_TF = P_OFF_AF + 64 * AST * 4;   // T fp32 [64][AST]
 constexpr uint32_t P_OFF_GATE = P_OFF_TF + 64 * AST * 4; // 2 gate tables
 constexpr uint32_t P_OFF_BAR = P_OFF_GATE + 2 * G_BYTES;
@@ -122,7 +122,7 @@ constexpr uint32_t P_USED = P_OFF_BAR + PB_NUM * 8 + 16;  // + TMEM base
 constexpr uint32_t SMEM_USED = C_USED > P_USED ? C_USED : P_USED;
 constexpr size_t SMEM_ALLOC = SMEM_USED + 1024;  // slack for 1024-byte alignment
 static_assert(C_OFF_GATE >= C_OFF_DT + 16384, "chain map overlaps");
-static_assert(P_OFF_AF >= P_OFF_TH + 8192, "producer map overlaps");
+static_assert(P_OFF_AF >= P_OFF_TH + 16384, "producer map overlaps");
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in shared memory");
 
 // TMEM columns (f32). Chain: D_U (128 lanes x 64), D_S (128 x 128) and two
@@ -133,6 +133,7 @@ constexpr uint32_t TM_D1 = 0, TM_W = 64, P_TM_COLS = 128;
 
 constexpr uint32_t ID_D1 = idesc_bf16(128, 64, false, false);
 constexpr uint32_t ID_MK64 = idesc_f16(128, 64, true, false);
+constexpr uint32_t ID_MK64_BF = idesc_bf16(128, 64, true, false);
 constexpr uint32_t ID_KM64 = idesc_f16(128, 64, false, true);
 constexpr uint32_t ID_KM128 = idesc_f16(128, 128, false, true);
 constexpr uint32_t ID_O = idesc_f16(64, 128, false, false);
@@ -189,6 +190,26 @@ __device__ __forceinline__ void st_row32_f16(uint8_t *blk, uint32_t row, uint32_
 #pragma unroll
     for (int c = 0; c < 4; ++c)
         *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + c)) = pack8_f16(v + 8 * c);
+}
+
+// 32 values as a bf16 pair hi = bf16(v), lo = bf16(v - hi) into two blocks
+// of the same layout as st_row32_f16 (hi + lo carries ~16 mantissa bits).
+__device__ __forceinline__ void st_row32_bf16_split(uint8_t *hi_blk, uint8_t *lo_blk, uint32_t row,
+                                                    uint32_t c0, const float *v) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float a = v[8 * c + 2 * e], b = v[8 * c + 2 * e + 1];
+            const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+            const __nv_bfloat162 l = __floats2bfloat162_rn(a - __low2float(h), b - __high2float(h));
+            hi[e] = *reinterpret_cast<const uint32_t *>(&h);
+            lo[e] = *reinterpret_cast<const uint32_t *>(&l);
+        }
+        *reinterpret_cast<uint4 *>(hi_blk + sw128_offset(row, c0 + c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4 *>(lo_blk + sw128_offset(row, c0 + c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
 }
 
 __device__ __forceinline__ void st_zero32(uint8_t *blk, uint32_t row, uint32_t c0) {
@@ -923,7 +944,6 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         for (int c = 0; c < nch; ++c, ++k) {
             const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
             const int L = static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH);
-            uint8_t *kqp = smem + P_OFF_KQ + (k & 1) * KQ_STAGE;
             const uint32_t kq = sbase + P_OFF_KQ + (k & 1) * KQ_STAGE;
             uint8_t *stg = smem + P_OFF_STG + (k & 1) * REC_BYTES;
             const float *g = gates(k);
@@ -981,9 +1001,8 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             __syncthreads();
 
             // ---- diagonal 16 x 16 tiles of T (warps 0-3, one each) while warps
-            // 4-7 zero tiles (0,1), (2,3) of T, convert this chunk's K to fp16 in
-            // place (D1 is done with it), build the next gate table and wait for
-            // the next chunk's tiles
+            // 4-7 zero tiles (0,1), (2,3) of T, build the next gate table and
+            // wait for the next chunk's tiles
             const Ref nxt = wk.next_of(Ref{item, ts, L, h});
             const Ref nn = nxt.item >= 0 ? wk.next_of(nxt) : nxt;
             bool prep_fail = false;
@@ -995,23 +1014,6 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                     const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
                     Tf[(32 * blk + rr) * AST + 32 * blk + 16 + cc] = 0.f;
                 }
-                uint4 x[8];
-#pragma unroll
-                for (int m = 0; m < 8; ++m) {
-                    const int e = wt + 128 * m;
-                    x[m] = *reinterpret_cast<const uint4 *>(kqp + (e >> 9) * 16384 + (e & 511) * 16);
-                }
-#pragma unroll
-                for (int m = 0; m < 8; ++m) {
-                    const int e = wt + 128 * m;
-                    uint4 w = x[m];
-                    w.x = bf16x2_to_f16x2(w.x, 1.f);
-                    w.y = bf16x2_to_f16x2(w.y, 1.f);
-                    w.z = bf16x2_to_f16x2(w.z, 1.f);
-                    w.w = bf16x2_to_f16x2(w.w, 1.f);
-                    *reinterpret_cast<uint4 *>(kqp + (e >> 9) * 16384 + (e & 511) * 16) = w;
-                }
-                fence_proxy_async_smem();
                 if (nxt.item >= 0) {
                     if (warp == 4) {
                         gate_tables(gates(k + 1), gin, lane);
@@ -1030,7 +1032,8 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             }
             solve_offdiag(Af, Tf, Xf, warp, lane);
 
-            // ---- T diag(beta) (record) and T diag(beta gamma) (local) as fp16 operands
+            // ---- T diag(beta) (record, fp16) and T diag(beta gamma) (local, as a
+            // bf16 hi + lo pair so that D_W can read K's bf16 tile as it landed)
             {
                 const int t = tid & 63;
                 const bool hat = (tid >> 6) & 1;
@@ -1039,6 +1042,7 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                 uint8_t *dstb = hat ? smem + P_OFF_TH : stg + REC_TT;
                 if (hh == 1 && t < 32) {
                     st_zero32(dstb, t, 4);
+                    if (hat) st_zero32(dstb + 8192, t, 4);
                 } else {
                     const float *sc = g + (hat ? G_BG : G_BE);
                     float v[32];
@@ -1052,17 +1056,22 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                         v[4 * j4 + 2] = s + 2 <= t ? tv.z * sv.z : 0.f;
                         v[4 * j4 + 3] = s + 3 <= t ? tv.w * sv.w : 0.f;
                     }
-                    st_row32_f16(dstb, t, 4 * hh, v);
+                    if (hat)
+                        st_row32_bf16_split(dstb, dstb + 8192, t, 4 * hh, v);
+                    else
+                        st_row32_f16(dstb, t, 4 * hh, v);
                 }
             }
             operands_ready();
 
-            // ---- D_W = K^T (T diag bg)^T  (lane j, column t: W[t][j])
+            // ---- D_W = K^T (T diag bg)^T = K^T (hi + lo)^T on bf16 operands
+            // (lane j, column t: W[t][j])
             if (tid == 0) {
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    umma_f16(tmem + TM_W, sdesc_sw128(kq + kk * 2048, 16384, 1024),
-                             sdesc_sw128(sbase + P_OFF_TH + kk * 32, 16, 1024), ID_MK64, kk > 0);
+                for (int kk = 0; kk < 8; ++kk)
+                    umma_f16(tmem + TM_W, sdesc_sw128(kq + (kk & 3) * 2048, 16384, 1024),
+                             sdesc_sw128(sbase + P_OFF_TH + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
+                             ID_MK64_BF, kk > 0);
                 umma_commit(bar_mma);
             }
             {
