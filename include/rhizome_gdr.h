@@ -162,6 +162,35 @@ int rhz_gdr_multistep(void *outs, float *states, const float *state_pool,
                       int32_t dtype, rhz_stream_t stream);
 
 /*
+ * rhz_gdr_prep -- the Local block's input producer (SPEC.md:53-54, 61-63),
+ * the step in front of the recurrence, built from the reference's pieces:
+ * per channel the causal depthwise conv of kernel 4, causal_conv1d_step
+ * (crates/ops/src/delta.rs:236-243), carried across each sequence from its
+ * slot's 3-sample state; then q = l2norm(conv q) * q_scale,
+ * k = l2norm(conv k), v = conv v (l2norm, crates/ops/src/elementwise.rs:
+ * 125-129), beta = sigmoid(beta_logit) (:5-12), alpha =
+ * exp(-softplus(a_head[h]) * softplus(alpha_logit)) (:36-42).
+ * Layouts: xq/xk/xv and q/k/v [tokens][H][d] in `dtype`; beta_logit,
+ * alpha_logit, alpha, beta [tokens][H] f32; a_head [H]; conv_w [3][H][d][4]
+ * and conv_b [3][H][d] f32 for the q, k, v channels; conv_state
+ * [num_slots][3][H][d][3] f32, samples oldest first. Sequence i covers
+ * [cu_seqlens[i], cu_seqlens[i+1]) (cu_seqlens NULL: n_seq dense rows of
+ * seq_len tokens, total_tokens ignored) and uses conv-state slot
+ * slot_idx[i] (slot i when slot_idx is NULL). RHZ_FLAG_ZERO_INIT starts
+ * every sequence from a zero conv state (a segment start); its last three
+ * samples are written back unless RHZ_FLAG_NO_STATE_WRITE (or conv_state is
+ * NULL: zero start, nothing written). A slot index outside [0, num_slots)
+ * starts from zeros and writes nothing. d a multiple of 4, at most 512.
+ * Decode is the same call with one token per sequence.
+ */
+int rhz_gdr_prep(void *q, void *k, void *v, float *alpha, float *beta, const void *xq,
+                 const void *xk, const void *xv, const float *beta_logit, const float *alpha_logit,
+                 const float *a_head, const float *conv_w, const float *conv_b, float *conv_state,
+                 const int32_t *slot_idx, const int32_t *cu_seqlens, int64_t n_seq,
+                 int64_t seq_len, int64_t total_tokens, int64_t num_slots, int32_t H, int32_t d,
+                 float q_scale, int32_t dtype, uint32_t flags, rhz_stream_t stream);
+
+/*
  * rhz_gdr_workspace_bytes -- scratch needed by rhz_gdr_sequential /
  * rhz_gdr_scan_chunked with a segment array of B x T positions.
  */

@@ -515,3 +515,70 @@ void rhzo_make_normal(uint64_t seed, uint64_t stream, int64_t n, double sigma, d
     rhzo_philox_init(&p, seed, stream);
     for (int64_t i = 0; i < n; ++i) out[i] = sigma * rhzo_philox_next_normal(&p);
 }
+
+/* ------------------------------------------------------------------------ */
+/* The Local block's input producer (SPEC.md:53-54, 61-63), composed from the */
+/* reference's own pieces on the device layouts:                             */
+/*   per channel, causal_conv1d_step (delta.rs:236-243) carried across the   */
+/*   sequence from the slot's 3-sample state (zeros when zero_init or the     */
+/*   slot index is out of range; segment starts reset it);                    */
+/*   q = l2norm(conv_q, q_scale), k = l2norm(conv_k, 1) (elementwise.rs:      */
+/*   125-129), v = conv_v; beta = sigmoid(beta_logit) (elementwise.rs:5-12);  */
+/*   alpha = exp(-softplus(a_h) * softplus(alpha_logit)) (elementwise.rs:     */
+/*   36-42, the SPEC.md:54 form).                                             */
+/* Layouts: xq/xk/xv and q/k/v [tokens][H][d]; logits, alpha, beta          */
+/* [tokens][H]; a_head [H]; conv_w [3][H][d][4] and conv_b [3][H][d] for the  */
+/* q, k, v channels; conv_state [num_slots][3][H][d][3] (oldest first).       */
+/* Sequence i covers tokens [cu[i], cu[i+1]) and uses slot slots[i] (slot i   */
+/* when slots is NULL); its final conv state is written back when            */
+/* write_state and the slot is valid.                                         */
+/* ------------------------------------------------------------------------ */
+void rhzo_gdr_prep(int64_t n_seq, const int32_t *cu, int64_t H, int64_t d, const double *xq,
+                   const double *xk, const double *xv, const double *beta_logit,
+                   const double *alpha_logit, const double *a_head, const double *conv_w,
+                   const double *conv_b, double *conv_state, const int32_t *slots,
+                   int64_t num_slots, int zero_init, int write_state, double q_scale, double *q,
+                   double *k, double *v, double *alpha, double *beta) {
+    const double *xs[3] = {xq, xk, xv};
+    double *ys[3] = {q, k, v};
+    double *row = (double *)malloc((size_t)d * sizeof(double));
+    for (int64_t i = 0; i < n_seq; ++i) {
+        const int64_t t0 = cu[i], t1 = cu[i + 1];
+        const int64_t slot = slots ? (int64_t)slots[i] : i;
+        const int valid = conv_state != NULL && slot >= 0 && slot < num_slots;
+        for (int64_t h = 0; h < H; ++h) {
+            for (int a = 0; a < 3; ++a) {
+                for (int64_t c = 0; c < d; ++c) {
+                    double st[3] = {0.0, 0.0, 0.0};
+                    double *cs = valid ? conv_state + (((slot * 3 + a) * H + h) * d + c) * 3 : NULL;
+                    if (cs && !zero_init) {
+                        st[0] = cs[0];
+                        st[1] = cs[1];
+                        st[2] = cs[2];
+                    }
+                    const double *w = conv_w + ((a * H + h) * d + c) * 4;
+                    const double b = conv_b[(a * H + h) * d + c];
+                    for (int64_t t = t0; t < t1; ++t) {
+                        ys[a][(t * H + h) * d + c] =
+                            rhzo_causal_conv1d_step(st, w, xs[a][(t * H + h) * d + c], b);
+                    }
+                    if (cs && write_state) {
+                        cs[0] = st[0];
+                        cs[1] = st[1];
+                        cs[2] = st[2];
+                    }
+                }
+            }
+            for (int64_t t = t0; t < t1; ++t) {
+                for (int a = 0; a < 2; ++a) {
+                    double *y = ys[a] + (t * H + h) * d;
+                    rhzo_l2norm(y, d, a == 0 ? q_scale : 1.0, row);
+                    memcpy(y, row, (size_t)d * sizeof(double));
+                }
+                beta[t * H + h] = rhzo_sigmoid(beta_logit[t * H + h]);
+                alpha[t * H + h] = exp(-rhzo_softplus(a_head[h]) * rhzo_softplus(alpha_logit[t * H + h]));
+            }
+        }
+    }
+    free(row);
+}

@@ -59,6 +59,10 @@ def lib():
         L.rhzo_make_qkv_gates.argtypes = [u64, i64, i64, i64, _dp, _dp, _dp, _dp, _dp]
         L.rhzo_make_normal.argtypes = [u64, u64, i64, d64, _dp]
         L.rhzo_make_test_inputs.argtypes = [i64, i64, u64, _dp, _dp, _dp, _dp, _dp]
+        _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+        L.rhzo_gdr_prep.argtypes = [i64, _i32p, i64, i64, _dp, _dp, _dp, _dp, _dp, _dp, _dp,
+                                    _dp, vp, vp, i64, C.c_int, C.c_int, d64, _dp, _dp, _dp,
+                                    _dp, _dp]
         _lib = L
     return _lib
 
@@ -286,6 +290,30 @@ def gdr_dense(q, k, v, alpha, beta, state_in=None, nthreads=None):
     lib().rhzo_gdr_dense(B, T, H, d, q, k, v, alpha, beta, _ptr(si), o, _ptr(so),
                          _threads(nthreads))
     return o, so
+
+
+def gdr_prep(cu_seqlens, xq, xk, xv, beta_logit, alpha_logit, a_head, conv_w, conv_b,
+             conv_state=None, slots=None, zero_init=False, write_state=True, q_scale=1.0):
+    """The Local block's input producer on the device layouts (gdr_oracle.c).
+
+    xq/xk/xv: [tokens, H, d]; logits: [tokens, H]; a_head: [H];
+    conv_w: [3, H, d, 4]; conv_b: [3, H, d]; conv_state: [slots, 3, H, d, 3]
+    or None (zeros, nothing written). Returns (q, k, v, alpha, beta,
+    conv_state_after)."""
+    cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+    xq, xk, xv, bl, al, ah, w, b = map(_f64, (xq, xk, xv, beta_logit, alpha_logit, a_head,
+                                             conv_w, conv_b))
+    tokens, H, d = xq.shape
+    n_seq = cu.size - 1
+    q = np.zeros_like(xq); k = np.zeros_like(xq); v = np.zeros_like(xq)
+    alpha = np.zeros((tokens, H)); beta = np.zeros_like(alpha)
+    cs = None if conv_state is None else _f64(conv_state).copy()
+    num_slots = 0 if cs is None else cs.shape[0]
+    sl = None if slots is None else np.ascontiguousarray(slots, np.int32)
+    lib().rhzo_gdr_prep(n_seq, cu, H, d, xq, xk, xv, bl, al, ah, w, b, _ptr(cs), _ptr(sl),
+                        num_slots, int(zero_init), int(write_state), float(q_scale), q, k, v,
+                        alpha, beta)
+    return q, k, v, alpha, beta, cs
 
 
 def make_qkv_gates(seed: int, tokens: int, H: int, d: int):

@@ -437,6 +437,55 @@ int rhz_gdr_multistep(void *outs, float *states, const float *state_pool,
     return launch_multistep(a);
 }
 
+int rhz_gdr_prep(void *q, void *k, void *v, float *alpha, float *beta, const void *xq,
+                 const void *xk, const void *xv, const float *beta_logit, const float *alpha_logit,
+                 const float *a_head, const float *conv_w, const float *conv_b, float *conv_state,
+                 const int32_t *slot_idx, const int32_t *cu_seqlens, int64_t n_seq,
+                 int64_t seq_len, int64_t total_tokens, int64_t num_slots, int32_t H, int32_t d,
+                 float q_scale, int32_t dtype, uint32_t flags, rhz_stream_t stream) {
+    clear_error();
+    RHZ_TRY(check_dtype(dtype));
+    if (H < 1 || d < 4 || d > 512 || d % 4)
+        return set_error(RHZ_ERR_SHAPE, "prep needs H >= 1 and d a multiple of 4 in [4, 512] (got H %d, d %d)", H, d);
+    if (n_seq < 0 || seq_len < 0 || total_tokens < 0 || num_slots < 0)
+        return set_error(RHZ_ERR_SHAPE, "negative size (n_seq %lld, seq_len %lld, total_tokens %lld, num_slots %lld)",
+                         (long long)n_seq, (long long)seq_len, (long long)total_tokens, (long long)num_slots);
+    if (flags & ~(RHZ_FLAG_ZERO_INIT | RHZ_FLAG_NO_STATE_WRITE))
+        return set_error(RHZ_ERR_INVALID, "unknown flags 0x%x", flags);
+    if (cu_seqlens == nullptr) total_tokens = n_seq * seq_len;
+    if (conv_state && slot_idx == nullptr && n_seq > num_slots)
+        return set_error(RHZ_ERR_SHAPE, "n_seq = %lld sequences but only %lld conv-state slots (slot_idx is NULL)",
+                         (long long)n_seq, (long long)num_slots);
+    if (total_tokens * H > (int64_t)INT32_MAX * 8) return set_error(RHZ_ERR_SHAPE, "tokens*H exceeds the grid");
+    if (n_seq == 0 || total_tokens == 0) {
+        if (n_seq == 0 || conv_state == nullptr || (flags & RHZ_FLAG_NO_STATE_WRITE)) return RHZ_OK;
+    }
+    const size_t vec = dtype == RHZ_DTYPE_BF16 ? 8 : 16;
+    const bool rows = total_tokens > 0;
+    RHZ_TRY(check_ptr(q, "q", vec, rows));
+    RHZ_TRY(check_ptr(k, "k", vec, rows));
+    RHZ_TRY(check_ptr(v, "v", vec, rows));
+    RHZ_TRY(check_ptr(xq, "xq", vec, rows));
+    RHZ_TRY(check_ptr(xk, "xk", vec, rows));
+    RHZ_TRY(check_ptr(xv, "xv", vec, rows));
+    RHZ_TRY(check_ptr(alpha, "alpha", 4, rows));
+    RHZ_TRY(check_ptr(beta, "beta", 4, rows));
+    RHZ_TRY(check_ptr(beta_logit, "beta_logit", 4, rows));
+    RHZ_TRY(check_ptr(alpha_logit, "alpha_logit", 4, rows));
+    RHZ_TRY(check_ptr(a_head, "a_head", 4, rows));
+    RHZ_TRY(check_ptr(conv_w, "conv_w", 16, true));
+    RHZ_TRY(check_ptr(conv_b, "conv_b", 16, true));
+    RHZ_TRY(check_ptr(conv_state, "conv_state", 4, conv_state != nullptr));
+    RHZ_TRY(check_ptr(slot_idx, "slot_idx", 4, slot_idx != nullptr));
+    RHZ_TRY(check_ptr(cu_seqlens, "cu_seqlens", 4, cu_seqlens != nullptr));
+    RHZ_TRY(require_sm100());
+    PrepArgs a{q, k, v, alpha, beta, xq, xk, xv, beta_logit, alpha_logit, a_head, conv_w, conv_b,
+               conv_state, slot_idx, cu_seqlens, n_seq, seq_len, total_tokens, num_slots, H, d, dtype,
+               q_scale, (flags & RHZ_FLAG_ZERO_INIT) != 0, conv_state != nullptr && !(flags & RHZ_FLAG_NO_STATE_WRITE),
+               as_cuda(stream)};
+    return launch_prep(a);
+}
+
 int rhz_heads_unshard(void *out, const void *gathered, int64_t G, int64_t tokens, int32_t H,
                       int32_t d, int32_t elem_bytes, rhz_stream_t stream) {
     clear_error();

@@ -60,7 +60,25 @@ struct MultistepArgs {
     cudaStream_t stream;
 };
 
+// Input producer: conv + norms + gates in front of the recurrence (prep.cu).
+struct PrepArgs {
+    void *q, *k, *v;
+    float *alpha, *beta;
+    const void *xq, *xk, *xv;
+    const float *beta_logit, *alpha_logit, *a_head;
+    const float *conv_w, *conv_b;
+    float *conv_state;          // nullptr => zero carried state, nothing written
+    const int32_t *slots;       // nullptr => sequence i uses slot i
+    const int32_t *cu_seqlens;  // nullptr => dense n_seq x seq_len
+    int64_t n_seq, seq_len, total_tokens, num_slots;
+    int H, d, dtype;
+    float q_scale;
+    bool zero_init, write_state;
+    cudaStream_t stream;
+};
+
 int launch_step(const StepArgs &a);
+int launch_prep(const PrepArgs &a);
 int launch_multistep(const MultistepArgs &a);
 int launch_seq(const SeqArgs &a);
 // Tensor-core chunked kernel (bf16, d == 128). Returns RHZ_ERR_SHAPE for

@@ -92,6 +92,50 @@ def gdr_multistep(q, k, v, alpha, beta, max_positions=8, segment=None, state_poo
     return outs, states
 
 
+def gdr_prep(xq, xk, xv, beta_logit, alpha_logit, a_head, conv_w, conv_b, conv_state=None,
+             slot_idx=None, cu_seqlens=None, q_scale=1.0, zero_init=False, write_state=True):
+    """The Local block's input producer: causal depthwise conv of kernel 4
+    (delta.rs:236-243) carried per sequence in conv_state slots, then
+    q = l2norm(conv q) * q_scale, k = l2norm(conv k), v = conv v,
+    beta = sigmoid(beta_logit), alpha = exp(-softplus(a_head) softplus(alpha_logit)).
+
+    Dense: xq/xk/xv [B, T, H, d] (cu_seqlens None, one sequence per batch
+    row); packed: [tokens, H, d] with cu_seqlens [n_seq + 1] int32. Logits
+    [.., H] f32; a_head [H]; conv_w [3, H, d, 4]; conv_b [3, H, d];
+    conv_state [slots, 3, H, d, 3] f32 (updated in place unless
+    write_state is False). Returns (q, k, v, alpha, beta)."""
+    H, d = xq.shape[-2], xq.shape[-1]
+    for t, name in ((xk, "xk"), (xv, "xv")):
+        _need(t, name, xq.dtype, tuple(xq.shape))
+    if cu_seqlens is None:
+        B, T = xq.shape[0], xq.shape[1]
+        n_seq, seq_len, total = B, T, B * T
+    else:
+        _need(cu_seqlens, "cu_seqlens", torch.int32)
+        n_seq, seq_len, total = cu_seqlens.numel() - 1, 0, xq.shape[0]
+    for t, name in ((beta_logit, "beta_logit"), (alpha_logit, "alpha_logit")):
+        _need(t, name, torch.float32, tuple(xq.shape[:-1]))
+    _need(a_head, "a_head", torch.float32, (H,))
+    _need(conv_w, "conv_w", torch.float32, (3, H, d, 4))
+    _need(conv_b, "conv_b", torch.float32, (3, H, d))
+    num_slots = 0
+    if conv_state is not None:
+        _need(conv_state, "conv_state", torch.float32)
+        num_slots = conv_state.shape[0]
+    if slot_idx is not None:
+        _need(slot_idx, "slot_idx", torch.int32, (n_seq,))
+    q, k, v = torch.empty_like(xq), torch.empty_like(xq), torch.empty_like(xq)
+    alpha = torch.empty(xq.shape[:-1], device=xq.device, dtype=torch.float32)
+    beta = torch.empty_like(alpha)
+    flags = (capi.RHZ_FLAG_ZERO_INIT if zero_init else 0) | \
+            (0 if write_state else capi.RHZ_FLAG_NO_STATE_WRITE)
+    capi.call("rhz_gdr_prep", _p(q), _p(k), _p(v), _p(alpha), _p(beta), _p(xq), _p(xk), _p(xv),
+              _p(beta_logit), _p(alpha_logit), _p(a_head), _p(conv_w), _p(conv_b), _p(conv_state),
+              _p(slot_idx), _p(cu_seqlens), n_seq, seq_len, total, num_slots, H, d,
+              float(q_scale), _dt(xq), flags, _stream(xq.device))
+    return q, k, v, alpha, beta
+
+
 def workspace_bytes(B: int, T: int) -> int:
     return int(capi.lib().rhz_gdr_workspace_bytes(B, T))
 

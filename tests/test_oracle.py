@@ -247,3 +247,53 @@ def test_generator_distributions():
     assert np.all((al > 0) & (al < 1)) and np.all((be > 0) & (be < 1))
     # alpha = exp(-softplus(x + 2)) with x ~ N(0,1): median exp(-softplus(2))
     assert abs(np.median(al) - math.exp(-math.log1p(math.exp(2.0)))) < 0.05
+
+
+def _prep_python(cu, xq, xk, xv, bl, al, ah, w, b, cs, slots, zero_init, write_state, q_scale):
+    """Pure-Python restatement of the input producer, one channel at a time
+    with causal_conv1d_step (delta.rs:236-243) and l2norm/sigmoid/softplus
+    (elementwise.rs), to check the batched C driver."""
+    import math
+    T, H, d = xq.shape
+    outs = [np.zeros_like(xq) for _ in range(3)]
+    alpha = np.zeros((T, H)); beta = np.zeros((T, H))
+    cs = None if cs is None else cs.copy()
+    for i in range(len(cu) - 1):
+        slot = slots[i] if slots is not None else i
+        valid = cs is not None and 0 <= slot < cs.shape[0]
+        for h in range(H):
+            for a, x in enumerate((xq, xk, xv)):
+                for c in range(d):
+                    st = np.zeros(3)
+                    if valid and not zero_init:
+                        st[:] = cs[slot, a, h, c]
+                    for t in range(cu[i], cu[i + 1]):
+                        outs[a][t, h, c] = O.causal_conv1d_step(st, w[a, h, c], x[t, h, c], b[a, h, c])
+                    if valid and write_state:
+                        cs[slot, a, h, c] = st
+            for t in range(cu[i], cu[i + 1]):
+                outs[0][t, h] = O.l2norm(outs[0][t, h], q_scale)
+                outs[1][t, h] = O.l2norm(outs[1][t, h], 1.0)
+                beta[t, h] = O.sigmoid(bl[t, h])
+                alpha[t, h] = math.exp(-O.softplus(ah[h]) * O.softplus(al[t, h]))
+    return outs[0], outs[1], outs[2], alpha, beta, cs
+
+
+@pytest.mark.parametrize("zero_init,write_state", [(False, True), (True, True), (False, False)])
+def test_prep_driver_matches_python_restatement(zero_init, write_state):
+    rng = np.random.default_rng(5)
+    H, d = 2, 8
+    cu = np.array([0, 1, 3, 3, 9], dtype=np.int32)  # lengths 1, 2, 0, 6
+    T = int(cu[-1])
+    xq, xk, xv = (rng.normal(size=(T, H, d)) for _ in range(3))
+    bl, al = rng.normal(size=(T, H)), rng.normal(size=(T, H))
+    ah = rng.normal(size=H)
+    w, b = rng.normal(size=(3, H, d, 4)), rng.normal(size=(3, H, d))
+    cs = rng.normal(size=(6, 3, H, d, 3))
+    slots = np.array([4, 0, 2, 9], dtype=np.int32)  # slot 9 is out of range
+    got = O.gdr_prep(cu, xq, xk, xv, bl, al, ah, w, b, cs, slots, zero_init, write_state, 1.7)
+    ref = _prep_python(cu, xq, xk, xv, bl, al, ah, w, b, cs, slots, zero_init, write_state, 1.7)
+    for g, r in zip(got, ref):
+        np.testing.assert_array_equal(g, r)
+    if not write_state:
+        np.testing.assert_array_equal(got[5], cs)
