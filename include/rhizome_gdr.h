@@ -141,6 +141,32 @@ int rhz_gdr_varlen_fwd(void *o, float *state_pool, const int32_t *slot_idx,
                        int32_t dtype, uint32_t flags, rhz_stream_t stream);
 
 /*
+ * rhz_gdr_varlen_fwd_norm -- rhz_gdr_varlen_fwd followed by the Local
+ * block's per-head output norm, groupnorm_heads (crates/ops/src/norm.rs:
+ * 48-60): every (token, head) output row of d values becomes
+ * o / sqrt(mean(o^2) + norm_eps) * norm_scale[0..d) (the reference applies
+ * the first d scale entries to every head). On the bf16 d = 128 path the
+ * norm runs in the recurrence kernel's epilogue on the fp32 accumulator;
+ * otherwise the standalone rhz_groupnorm_heads follows on the same stream.
+ * norm_scale: d f32 (16-byte aligned); d a multiple of 4.
+ */
+int rhz_gdr_varlen_fwd_norm(void *o, float *state_pool, const int32_t *slot_idx,
+                            const int32_t *cu_seqlens, const void *q, const void *k, const void *v,
+                            const float *alpha, const float *beta, const float *norm_scale,
+                            float norm_eps, int64_t n_seq, int64_t total_tokens, int64_t num_slots,
+                            int32_t H, int32_t d, int32_t dtype, uint32_t flags, rhz_stream_t stream);
+
+/*
+ * rhz_groupnorm_heads -- replaces groupnorm_heads (crates/ops/src/norm.rs:
+ * 48-60) over `rows` rows of H heads x d values ([rows][H][d], f32 or
+ * bf16): each head is RMS-normalised on its own with scale[0..d) and eps
+ * (rmsnorm, norm.rs:8-13). out may equal x (in place). d a multiple of 4,
+ * at most 512.
+ */
+int rhz_groupnorm_heads(void *out, const void *x, const float *scale, int64_t rows, int32_t H,
+                        int32_t d, float eps, int32_t dtype, rhz_stream_t stream);
+
+/*
  * rhz_gdr_multistep -- replaces gated_delta_multistep
  * (crates/ops/src/delta.rs:201-230): n sequences x H heads of T positions
  * (q, k, v [n][T][H][d]; alpha, beta [n][T][H]), of which the first

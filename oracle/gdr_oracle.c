@@ -582,3 +582,23 @@ void rhzo_gdr_prep(int64_t n_seq, const int32_t *cu, int64_t H, int64_t d, const
     }
     free(row);
 }
+
+/* rmsnorm, crates/ops/src/norm.rs:8-13: x / sqrt(mean(x^2) + eps) * scale. */
+static void rmsnorm_row(const double *x, int64_t n, const double *scale, double eps, double *out) {
+    double acc = -0.0;
+    for (int64_t i = 0; i < n; ++i) acc = acc + x[i] * x[i];
+    const double ms = acc / (double)n;
+    const double inv = 1.0 / sqrt(ms + eps);
+    for (int64_t i = 0; i < n; ++i) out[i] = x[i] * inv * scale[i];
+}
+
+/* groupnorm_heads, norm.rs:48-60, over `rows` token rows of `heads` x `dh`
+ * values: every head of every row is RMS-normalised on its own with the
+ * first dh entries of `scale` (the reference slices scale[..dh] for each
+ * head). */
+void rhzo_groupnorm_heads(const double *x, int64_t rows, int64_t heads, int64_t dh,
+                          const double *scale, double eps, double *out) {
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t h = 0; h < heads; ++h)
+            rmsnorm_row(x + (r * heads + h) * dh, dh, scale, eps, out + (r * heads + h) * dh);
+}

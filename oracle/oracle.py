@@ -63,6 +63,7 @@ def lib():
         L.rhzo_gdr_prep.argtypes = [i64, _i32p, i64, i64, _dp, _dp, _dp, _dp, _dp, _dp, _dp,
                                     _dp, vp, vp, i64, C.c_int, C.c_int, d64, _dp, _dp, _dp,
                                     _dp, _dp]
+        L.rhzo_groupnorm_heads.argtypes = [_dp, i64, i64, i64, _dp, d64, _dp]
         _lib = L
     return _lib
 
@@ -314,6 +315,17 @@ def gdr_prep(cu_seqlens, xq, xk, xv, beta_logit, alpha_logit, a_head, conv_w, co
                         num_slots, int(zero_init), int(write_state), float(q_scale), q, k, v,
                         alpha, beta)
     return q, k, v, alpha, beta, cs
+
+
+def groupnorm_heads(x, scale, eps: float):
+    """norm.rs:48-60 on rows of [.., H, dh] values (x of any leading shape);
+    each head uses scale[:dh]."""
+    x = _f64(x)
+    H, dh = x.shape[-2], x.shape[-1]
+    rows = x.size // (H * dh)
+    out = np.zeros_like(x)
+    lib().rhzo_groupnorm_heads(x, rows, H, dh, _f64(scale), float(eps), out)
+    return out
 
 
 def make_qkv_gates(seed: int, tokens: int, H: int, d: int):

@@ -83,6 +83,10 @@ SIGNATURES = {
     "rhz_varlen_pack_tokens": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "rhz_varlen_unpack_tokens": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "rhz_varlen_segments_to_cu_seqlens_noalloc": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "rhz_gdr_varlen_fwd_norm": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                          C.c_float, _i64, _i64, _i64, _i32, _i32, _i32,
+                                          C.c_uint32, _vp]),
+    "rhz_groupnorm_heads": (C.c_int, [_vp, _vp, _vp, _i64, _i32, _i32, C.c_float, _i32, _vp]),
     "rhz_gdr_prep": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _i32, C.c_float, _i32,
                                C.c_uint32, _vp]),

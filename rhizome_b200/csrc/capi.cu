@@ -131,9 +131,14 @@ __global__ void final_slot_kernel(const int32_t *cu, const int32_t *n_seg, int64
     }
 }
 
+// The tensor-core kernel applies an output norm in its epilogue; the fp32
+// scan is followed by the standalone norm over the same rows.
 int run_seq(const SeqArgs &a) {
     if (chunk_tc_supports(a.d, a.dtype)) return launch_chunk_tc(a);
-    return launch_seq(a);
+    const int st = launch_seq(a);
+    if (st != RHZ_OK || a.norm_scale == nullptr) return st;
+    const int64_t rows = a.cu_seqlens ? a.total_tokens : a.n_seq * a.seq_len;
+    return launch_groupnorm_heads(a.o, a.o, a.norm_scale, rows, a.H, a.d, a.norm_eps, a.dtype, a.stream);
 }
 
 int sequential_impl(void *o, float *state_final, const void *q, const void *k, const void *v,
@@ -262,12 +267,14 @@ int rhz_gdr_scan_chunked(void *o, float *state_final, const void *q, const void 
                            dtype, workspace, workspace_bytes, stream);
 }
 
-int rhz_gdr_varlen_fwd(void *o, float *state_pool, const int32_t *slot_idx,
-                       const int32_t *cu_seqlens, const void *q, const void *k, const void *v,
-                       const float *alpha, const float *beta, int64_t n_seq,
-                       int64_t total_tokens, int64_t num_slots, int32_t H, int32_t d,
-                       int32_t dtype, uint32_t flags, rhz_stream_t stream) {
-    clear_error();
+}  // extern "C"
+
+namespace {
+int varlen_impl(void *o, float *state_pool, const int32_t *slot_idx, const int32_t *cu_seqlens,
+                const void *q, const void *k, const void *v, const float *alpha, const float *beta,
+                const float *norm_scale, float norm_eps, int64_t n_seq, int64_t total_tokens,
+                int64_t num_slots, int32_t H, int32_t d, int32_t dtype, uint32_t flags,
+                rhz_stream_t stream) {
     RHZ_TRY(check_dtype(dtype));
     RHZ_TRY(check_heads(H, d));
     if (flags & ~(RHZ_FLAG_ZERO_INIT | RHZ_FLAG_NO_STATE_WRITE))
@@ -302,7 +309,53 @@ int rhz_gdr_varlen_fwd(void *o, float *state_pool, const int32_t *slot_idx,
     a.out_slots = slot_idx;
     a.num_slots = num_slots;
     a.H = H; a.d = d; a.dtype = dtype; a.stream = as_cuda(stream);
+    a.norm_scale = norm_scale;
+    a.norm_eps = norm_eps;
     return run_seq(a);
+}
+}  // namespace
+
+extern "C" {
+
+int rhz_gdr_varlen_fwd(void *o, float *state_pool, const int32_t *slot_idx,
+                       const int32_t *cu_seqlens, const void *q, const void *k, const void *v,
+                       const float *alpha, const float *beta, int64_t n_seq,
+                       int64_t total_tokens, int64_t num_slots, int32_t H, int32_t d,
+                       int32_t dtype, uint32_t flags, rhz_stream_t stream) {
+    clear_error();
+    return varlen_impl(o, state_pool, slot_idx, cu_seqlens, q, k, v, alpha, beta, nullptr, 0.f,
+                       n_seq, total_tokens, num_slots, H, d, dtype, flags, stream);
+}
+
+int rhz_gdr_varlen_fwd_norm(void *o, float *state_pool, const int32_t *slot_idx,
+                            const int32_t *cu_seqlens, const void *q, const void *k, const void *v,
+                            const float *alpha, const float *beta, const float *norm_scale,
+                            float norm_eps, int64_t n_seq, int64_t total_tokens, int64_t num_slots,
+                            int32_t H, int32_t d, int32_t dtype, uint32_t flags, rhz_stream_t stream) {
+    clear_error();
+    if (!(norm_eps >= 0.f)) return set_error(RHZ_ERR_INVALID, "norm_eps must be >= 0");
+    RHZ_TRY(check_ptr(norm_scale, "norm_scale", 16, true));
+    if (d % 4) return set_error(RHZ_ERR_SHAPE, "the output norm needs d a multiple of 4 (got %d)", d);
+    return varlen_impl(o, state_pool, slot_idx, cu_seqlens, q, k, v, alpha, beta, norm_scale,
+                       norm_eps, n_seq, total_tokens, num_slots, H, d, dtype, flags, stream);
+}
+
+int rhz_groupnorm_heads(void *out, const void *x, const float *scale, int64_t rows, int32_t H,
+                        int32_t d, float eps, int32_t dtype, rhz_stream_t stream) {
+    clear_error();
+    RHZ_TRY(check_dtype(dtype));
+    if (rows < 0 || H < 1 || d < 4 || d > 512 || d % 4)
+        return set_error(RHZ_ERR_SHAPE, "groupnorm_heads needs rows >= 0, H >= 1, d a multiple of 4 in [4, 512] (got %lld, %d, %d)",
+                         (long long)rows, H, d);
+    if (!(eps >= 0.f)) return set_error(RHZ_ERR_INVALID, "eps must be >= 0");
+    if (rows * H > (int64_t)INT32_MAX * 8) return set_error(RHZ_ERR_SHAPE, "rows*H exceeds the grid");
+    if (rows == 0) return RHZ_OK;
+    const size_t vec = dtype == RHZ_DTYPE_BF16 ? 8 : 16;
+    RHZ_TRY(check_ptr(out, "out", vec, true));
+    RHZ_TRY(check_ptr(x, "x", vec, true));
+    RHZ_TRY(check_ptr(scale, "scale", 16, true));
+    RHZ_TRY(require_sm100());
+    return launch_groupnorm_heads(out, x, scale, rows, H, d, eps, dtype, as_cuda(stream));
 }
 
 size_t rhz_gdr_workspace_bytes(int64_t B, int64_t T) {

@@ -104,7 +104,9 @@ constexpr uint32_t C_OFF_BAR = C_OFF_GATE + 4 * G_BYTES;
 // failure path uses to wait for every MMA issued.
 constexpr int CB_LOAD = 0, CB_FULL = 2, CB_R1 = 4, CB_R2S = 5, CB_R2 = 6, CB_CONV = 7, CB_OFREE = 9,
               CB_DRAIN = 11, CB_NUM = 12;
-constexpr uint32_t C_USED = C_OFF_BAR + CB_NUM * 8 + 16;  // + TMEM base
+constexpr uint32_t C_OFF_NORM = C_OFF_BAR + 128;  // output-norm scale, HD floats
+constexpr uint32_t C_USED = C_OFF_NORM + HD * 4;
+static_assert(C_OFF_NORM >= C_OFF_BAR + CB_NUM * 8 + 16, "chain barriers overlap the norm scale");
 
 // Producer CTA (cluster rank 1) shared memory.
 constexpr uint32_t P_OFF_KQ = 0;             // 2 stages of K, Q tiles
@@ -149,6 +151,8 @@ struct TcParams {
     const int32_t *out_slots;
     int64_t num_slots;
     int H;
+    const float *norm_scale;  // non-null: groupnorm_heads on each O row in the epilogue
+    float norm_eps;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -760,6 +764,9 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
             fence_proxy_async_smem();
         };
 
+        float *nsc = reinterpret_cast<float *>(smem + C_OFF_NORM);
+        const bool norm = p.norm_scale != nullptr;
+        if (norm) nsc[wt] = p.norm_scale[wt];  // wt < 128 = HD
         {
             const Ref r0 = wk.first_from(start);
             const Ref r1 = r0.item >= 0 ? wk.next_of(r0) : r0;
@@ -825,17 +832,36 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 }
                 if (nn.item >= 0) ++loads_issued;
 
-                // ---- O rows of chunk k (D_O row t in lane 32 (t / 16) + t % 16)
+                // ---- O rows of chunk k (D_O row t in lane 32 (t / 16) + t % 16),
+                // optionally RMS-normalised per head first (groupnorm_heads,
+                // norm.rs:48-60, on the fp32 accumulator)
                 {
                     const uint32_t tO = trow + TM_O + 128 * (k & 1);
                     const int t = 16 * ww + lane;
                     const bool has_row = lane < 16 && t < L;
                     __nv_bfloat16 *op = p.o + (ts + t) * tok_stride + static_cast<int64_t>(h) * HD;
+                    float inv = 1.f;
+                    if (norm) {
+                        float ss = 0.f;
+#pragma unroll 1
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            float o[32];
+                            tmem_ld32(tO + 32 * q4, o);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) ss += o[e] * o[e];
+                        }
+                        inv = 1.f / sqrtf(ss / static_cast<float>(HD) + p.norm_eps);
+                    }
 #pragma unroll 1
                     for (int q4 = 0; q4 < 4; ++q4) {
                         float o[32];
                         tmem_ld32(tO + 32 * q4, o);
                         tmem_wait_ld();
+                        if (norm) {
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) o[e] = o[e] * inv * nsc[32 * q4 + e];
+                        }
                         if (has_row) {
 #pragma unroll
                             for (int c8 = 0; c8 < 4; ++c8) {
@@ -1264,6 +1290,8 @@ int launch_chunk_tc(const SeqArgs &a) {
     p.out_slots = a.out_slots;
     p.num_slots = a.num_slots;
     p.H = a.H;
+    p.norm_scale = a.norm_scale;
+    p.norm_eps = a.norm_eps;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);

@@ -41,6 +41,8 @@ struct SeqArgs {
     int64_t num_slots;
     int H, d, dtype;
     cudaStream_t stream;
+    const float *norm_scale;    // non-null: groupnorm_heads on o (scale[0..d), norm_eps)
+    float norm_eps;
 };
 
 // Up to Tn positions per sequence, state after each position written out
@@ -96,6 +98,9 @@ int launch_chunk_map(int32_t *chunk_seq, int32_t *chunk_start, int32_t *n_chunks
                      size_t ws_bytes, cudaStream_t s);
 int launch_gather_states(float *dense, const float *pool, const int32_t *slots, int64_t n,
                          int64_t num_slots, int H, int d, bool scatter, cudaStream_t s);
+// groupnorm_heads over rows x H slices of d values (norm.cu); out may be x.
+int launch_groupnorm_heads(void *out, const void *x, const float *scale, int64_t rows, int H, int d,
+                           float eps, int dtype, cudaStream_t s);
 int launch_heads_unshard(void *dst, const void *src, int64_t G, int64_t tokens, int64_t Hs,
                          int64_t row_bytes, bool shard, cudaStream_t s);
 int launch_pack_tokens(void *dst, const void *src, const int32_t *cu, int64_t n, int64_t max_len,

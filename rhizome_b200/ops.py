@@ -204,6 +204,48 @@ def gdr_varlen_fwd(q, k, v, alpha, beta, cu_seqlens, state_pool=None, slot_idx=N
     return o
 
 
+def gdr_varlen_fwd_norm(q, k, v, alpha, beta, cu_seqlens, norm_scale, norm_eps=1e-6,
+                        state_pool=None, slot_idx=None, zero_init=False, write_state=True):
+    """gdr_varlen_fwd followed by the per-head output norm groupnorm_heads
+    (norm.rs:48-60): each output row o[t, h] becomes
+    o / sqrt(mean(o^2) + norm_eps) * norm_scale[:d]. Fused into the
+    tensor-core kernel's epilogue on the bf16 d = 128 path."""
+    tokens = q.shape[0]
+    H, d = _qkv(q, k, v, alpha, beta, (tokens,))
+    _need(cu_seqlens, "cu_seqlens", torch.int32)
+    _need(norm_scale, "norm_scale", torch.float32)
+    if norm_scale.numel() < d:
+        raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"norm_scale has {norm_scale.numel()} entries, need at least d = {d}")
+    n_seq = cu_seqlens.numel() - 1
+    flags = (capi.RHZ_FLAG_ZERO_INIT if zero_init else 0) | (0 if write_state else capi.RHZ_FLAG_NO_STATE_WRITE)
+    num_slots = 0
+    if state_pool is not None:
+        _need(state_pool, "state_pool", torch.float32)
+        num_slots = state_pool.shape[0]
+    if slot_idx is not None:
+        _need(slot_idx, "slot_idx", torch.int32, (n_seq,))
+    o = torch.empty_like(q)
+    capi.call("rhz_gdr_varlen_fwd_norm", _p(o), _p(state_pool), _p(slot_idx), _p(cu_seqlens),
+              _p(q), _p(k), _p(v), _p(alpha), _p(beta), _p(norm_scale), float(norm_eps), n_seq,
+              tokens, num_slots, H, d, _dt(q), flags, _stream(q.device))
+    return o
+
+
+def groupnorm_heads(x, scale, eps=1e-6, out=None):
+    """groupnorm_heads (norm.rs:48-60) on x [..., H, d]: each head's d values
+    RMS-normalised with scale[:d]; out may be x (in place)."""
+    _need(x, "x")
+    _need(scale, "scale", torch.float32)
+    H, d = x.shape[-2], x.shape[-1]
+    if scale.numel() < d:
+        raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"scale has {scale.numel()} entries, need at least d = {d}")
+    rows = x.numel() // (H * d) if x.numel() else 0
+    o = torch.empty_like(x) if out is None else out
+    capi.call("rhz_groupnorm_heads", _p(o), _p(x), _p(scale), rows, H, d, float(eps), _dt(x),
+              _stream(x.device))
+    return o
+
+
 # ---------------------------------------------------------------- varlen helpers
 
 def prefix_sum(lengths: torch.Tensor) -> torch.Tensor:

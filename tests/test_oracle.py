@@ -297,3 +297,20 @@ def test_prep_driver_matches_python_restatement(zero_init, write_state):
         np.testing.assert_array_equal(g, r)
     if not write_state:
         np.testing.assert_array_equal(got[5], cs)
+
+
+def test_groupnorm_heads_reference_cases():  # norm.rs:65-77, 117-130
+    s = np.ones(4)
+    a = O.groupnorm_heads(np.array([1.0, -2.0, 3.0, 0.5]).reshape(1, 1, 4), s, 1e-12)
+    b = O.groupnorm_heads(np.array([10.0, -20.0, 30.0, 5.0]).reshape(1, 1, 4), s, 1e-12)
+    assert np.max(np.abs(a - b)) < 1e-9
+    y = O.groupnorm_heads(np.array([1.0, 1.0, 100.0, 100.0]).reshape(1, 2, 2), np.ones(2), 1e-12)
+    assert np.max(np.abs(y.ravel()[:2] - y.ravel()[2:])) < 1e-9  # heads normalised independently
+
+
+def test_groupnorm_heads_matches_numpy():
+    rng = np.random.default_rng(3)
+    x = rng.normal(size=(5, 3, 8))
+    scale = rng.normal(size=24)  # only the first dh entries are used
+    ref = x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + 1e-6) * scale[:8]
+    np.testing.assert_allclose(O.groupnorm_heads(x, scale, 1e-6), ref, rtol=1e-14, atol=1e-15)
