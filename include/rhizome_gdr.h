@@ -217,6 +217,30 @@ int rhz_gdr_prep(void *q, void *k, void *v, float *alpha, float *beta, const voi
                  float q_scale, int32_t dtype, uint32_t flags, rhz_stream_t stream);
 
 /*
+ * rhz_gdr_scan_chunked_bwd -- backward of rhz_gdr_sequential /
+ * rhz_gdr_scan_chunked (the adjoint the reference names, "reverse scan of
+ * the rank-1 update", docs/kernels.md:16, but does not implement; derived
+ * from delta.rs:93-127 and checked against f64 central differences). The
+ * state resets at t = 0 and where segment[b][t] != segment[b][t-1] (segment
+ * [B][T] int64 or NULL), exactly as in the forward. Given d_o [B][T][H][d]
+ * (the gradient of o) and d_state_final [B][H][d][d] (the gradient of the
+ * final state, or NULL for zero), writes dq, dk, dv [B][T][H][d] (dtype)
+ * and dalpha, dbeta [B][T][H] f32. fp32 arithmetic for f32 and bf16 inputs;
+ * d a multiple of 4, at most 128. Needs `workspace` of
+ * rhz_gdr_bwd_workspace_bytes(B, T, H, d) bytes (state checkpoints every 8
+ * positions and per-row-block partial sums; the result is deterministic).
+ */
+int rhz_gdr_scan_chunked_bwd(void *dq, void *dk, void *dv, float *dalpha, float *dbeta,
+                             const void *q, const void *k, const void *v, const float *alpha,
+                             const float *beta, const int64_t *segment, const void *d_o,
+                             const float *d_state_final, int64_t B, int64_t T, int32_t H,
+                             int32_t d, int32_t dtype, void *workspace, size_t workspace_bytes,
+                             rhz_stream_t stream);
+
+/* rhz_gdr_bwd_workspace_bytes -- scratch of rhz_gdr_scan_chunked_bwd (0 for unsupported shapes). */
+size_t rhz_gdr_bwd_workspace_bytes(int64_t B, int64_t T, int32_t H, int32_t d);
+
+/*
  * rhz_gdr_workspace_bytes -- scratch needed by rhz_gdr_sequential /
  * rhz_gdr_scan_chunked with a segment array of B x T positions.
  */

@@ -602,3 +602,89 @@ void rhzo_groupnorm_heads(const double *x, int64_t rows, int64_t heads, int64_t 
         for (int64_t h = 0; h < heads; ++h)
             rmsnorm_row(x + (r * heads + h) * dh, dh, scale, eps, out + (r * heads + h) * dh);
 }
+
+/* ------------------------------------------------------------------------ */
+/* Adjoint of the recurrence (the reference names it, docs/kernels.md:16,     */
+/* "reverse scan of the rank-1 update", but has no code: this is derived from */
+/* delta.rs:93-127 and pinned by central differences in the tests).          */
+/* Per position, with P = S_{t-1} (after any reset), M = alpha (I - beta k k^T) */
+/* (symmetric) and S_t = P M + beta v k^T, o_t = S_t q_t, and G the adjoint   */
+/* of S_t:                                                                   */
+/*   G += dO_t q_t^T;  dq_t = S_t^T dO_t;  g = G k_t;  p = P k_t               */
+/*   dv_t = beta g;  dbeta_t = v.g - alpha p.g;  dalpha_t = <P, G> - beta p.g  */
+/*   dk_t = beta G^T v - alpha beta (P^T g + G^T p)                          */
+/*   G <- G M = alpha (G - beta g k^T), and G <- 0 where the state was reset. */
+/* Resets: at t = 0 when reset_at_start, and wherever segment changes (the     */
+/* sequential semantics of delta.rs:137-141). With no reset at t = 0 the      */
+/* forward starts from `init` (NULL: zeros) and dinit receives G at the start. */
+/* dS_final (NULL: zero) is the adjoint of the final state.                   */
+/* ------------------------------------------------------------------------ */
+void rhzo_gated_delta_backward(int64_t d, int64_t t_len, const double *q, const double *k,
+                               const double *v, const double *alpha, const double *beta,
+                               const int64_t *segment, int reset_at_start, const double *init,
+                               const double *d_o, const double *d_s_final, double *dq,
+                               double *dk, double *dv, double *dalpha, double *dbeta,
+                               double *dinit) {
+    const int64_t dd = d * d;
+    double *prev = (double *)calloc((size_t)(t_len * dd + 1), sizeof(double));
+    double *post = (double *)calloc((size_t)(t_len * dd + 1), sizeof(double));
+    double *s = (double *)calloc((size_t)dd, sizeof(double));
+    double *sk = (double *)malloc((size_t)d * sizeof(double));
+    double *o = (double *)malloc((size_t)d * sizeof(double));
+    double *g = (double *)malloc((size_t)d * sizeof(double));
+    double *pk = (double *)malloc((size_t)d * sizeof(double));
+    double *G = (double *)calloc((size_t)dd, sizeof(double));
+    if (init && !reset_at_start) memcpy(s, init, (size_t)dd * sizeof(double));
+    /* forward, keeping the state before (after reset) and after every step */
+    for (int64_t t = 0; t < t_len; ++t) {
+        const int reset = (t == 0 && reset_at_start) || (t > 0 && segment && segment[t] != segment[t - 1]);
+        if (reset) memset(s, 0, (size_t)dd * sizeof(double));
+        memcpy(prev + t * dd, s, (size_t)dd * sizeof(double));
+        step_impl(s, d, q + t * d, k + t * d, v + t * d, alpha[t], beta[t], sk, o);
+        memcpy(post + t * dd, s, (size_t)dd * sizeof(double));
+    }
+    if (d_s_final) memcpy(G, d_s_final, (size_t)dd * sizeof(double));
+    for (int64_t t = t_len - 1; t >= 0; --t) {
+        const double *qt = q + t * d, *kt = k + t * d, *vt = v + t * d, *dot = d_o + t * d;
+        const double *P = prev + t * dd, *S = post + t * dd;
+        const double a = alpha[t], b = beta[t];
+        for (int64_t i = 0; i < d; ++i)
+            for (int64_t j = 0; j < d; ++j) G[i * d + j] += dot[i] * qt[j];
+        for (int64_t j = 0; j < d; ++j) {
+            double acc = 0.0;
+            for (int64_t i = 0; i < d; ++i) acc += S[i * d + j] * dot[i];
+            dq[t * d + j] = acc;
+        }
+        double pg = 0.0, vg = 0.0, pG = 0.0;
+        for (int64_t i = 0; i < d; ++i) {
+            double gi = 0.0, pi = 0.0;
+            for (int64_t j = 0; j < d; ++j) {
+                gi += G[i * d + j] * kt[j];
+                pi += P[i * d + j] * kt[j];
+                pG += P[i * d + j] * G[i * d + j];
+            }
+            g[i] = gi;
+            pk[i] = pi;
+            pg += pi * gi;
+            vg += vt[i] * gi;
+            dv[t * d + i] = b * gi;
+        }
+        dbeta[t] = vg - a * pg;
+        dalpha[t] = pG - b * pg;
+        for (int64_t j = 0; j < d; ++j) {
+            double gv = 0.0, pgj = 0.0, gp = 0.0;
+            for (int64_t i = 0; i < d; ++i) {
+                gv += G[i * d + j] * vt[i];
+                pgj += P[i * d + j] * g[i];
+                gp += G[i * d + j] * pk[i];
+            }
+            dk[t * d + j] = b * gv - a * b * (pgj + gp);
+        }
+        for (int64_t i = 0; i < d; ++i)
+            for (int64_t j = 0; j < d; ++j) G[i * d + j] = a * (G[i * d + j] - b * g[i] * kt[j]);
+        const int reset = (t == 0 && reset_at_start) || (t > 0 && segment && segment[t] != segment[t - 1]);
+        if (reset) memset(G, 0, (size_t)dd * sizeof(double));
+    }
+    if (dinit) memcpy(dinit, G, (size_t)dd * sizeof(double));
+    free(prev); free(post); free(s); free(sk); free(o); free(g); free(pk); free(G);
+}

@@ -64,6 +64,8 @@ def lib():
                                     _dp, vp, vp, i64, C.c_int, C.c_int, d64, _dp, _dp, _dp,
                                     _dp, _dp]
         L.rhzo_groupnorm_heads.argtypes = [_dp, i64, i64, i64, _dp, d64, _dp]
+        L.rhzo_gated_delta_backward.argtypes = [i64, i64, _dp, _dp, _dp, _dp, _dp, vp, C.c_int,
+                                                vp, _dp, vp, _dp, _dp, _dp, _dp, _dp, vp]
         _lib = L
     return _lib
 
@@ -326,6 +328,24 @@ def groupnorm_heads(x, scale, eps: float):
     out = np.zeros_like(x)
     lib().rhzo_groupnorm_heads(x, rows, H, dh, _f64(scale), float(eps), out)
     return out
+
+
+def gated_delta_backward(q, k, v, alpha, beta, d_o, segment=None, reset_at_start=True,
+                         init=None, d_state_final=None):
+    """Adjoint of the sequential recurrence for one head (gdr_oracle.c):
+    q/k/v/d_o [T, d]; alpha/beta [T]; segment [T] int64 or None. Returns
+    (dq, dk, dv, dalpha, dbeta, dinit)."""
+    q, k, v, alpha, beta, d_o = map(_f64, (q, k, v, alpha, beta, d_o))
+    T, d = q.shape
+    dq, dk, dv = np.zeros_like(q), np.zeros_like(q), np.zeros_like(q)
+    da, db = np.zeros(T), np.zeros(T)
+    dinit = np.zeros((d, d))
+    seg = None if segment is None else np.ascontiguousarray(segment, np.int64)
+    ini = None if init is None else _f64(init)
+    dsf = None if d_state_final is None else _f64(d_state_final)
+    lib().rhzo_gated_delta_backward(d, T, q, k, v, alpha, beta, _ptr(seg), int(reset_at_start),
+                                    _ptr(ini), d_o, _ptr(dsf), dq, dk, dv, da, db, _ptr(dinit))
+    return dq, dk, dv, da, db, dinit
 
 
 def make_qkv_gates(seed: int, tokens: int, H: int, d: int):

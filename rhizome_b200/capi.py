@@ -86,6 +86,10 @@ SIGNATURES = {
     "rhz_gdr_varlen_fwd_norm": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                           C.c_float, _i64, _i64, _i64, _i32, _i32, _i32,
                                           C.c_uint32, _vp]),
+    "rhz_gdr_scan_chunked_bwd": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                           _vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp, _sz,
+                                           _vp]),
+    "rhz_gdr_bwd_workspace_bytes": (_sz, [_i64, _i64, _i32, _i32]),
     "rhz_groupnorm_heads": (C.c_int, [_vp, _vp, _vp, _i64, _i32, _i32, C.c_float, _i32, _vp]),
     "rhz_gdr_prep": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _i32, C.c_float, _i32,

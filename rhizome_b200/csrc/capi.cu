@@ -340,6 +340,49 @@ int rhz_gdr_varlen_fwd_norm(void *o, float *state_pool, const int32_t *slot_idx,
                        norm_eps, n_seq, total_tokens, num_slots, H, d, dtype, flags, stream);
 }
 
+size_t rhz_gdr_bwd_workspace_bytes(int64_t B, int64_t T, int32_t H, int32_t d) {
+    if (B < 0 || T < 0 || H < 1 || d < 4 || d > 128 || d % 4) return 0;
+    return bwd_ws_bytes(B, T, H, d);
+}
+
+int rhz_gdr_scan_chunked_bwd(void *dq, void *dk, void *dv, float *dalpha, float *dbeta,
+                             const void *q, const void *k, const void *v, const float *alpha,
+                             const float *beta, const int64_t *segment, const void *d_o,
+                             const float *d_state_final, int64_t B, int64_t T, int32_t H,
+                             int32_t d, int32_t dtype, void *workspace, size_t workspace_bytes,
+                             rhz_stream_t stream) {
+    clear_error();
+    RHZ_TRY(check_dtype(dtype));
+    if (B < 0 || T < 0 || H < 1 || d < 4 || d > 128 || d % 4)
+        return set_error(RHZ_ERR_SHAPE, "backward needs B, T >= 0, H >= 1, d a multiple of 4 in [4, 128] (got %lld, %lld, %d, %d)",
+                         (long long)B, (long long)T, H, d);
+    if (B * H * ((d + 15) / 16) > INT32_MAX || B * H * T > INT32_MAX)
+        return set_error(RHZ_ERR_SHAPE, "B*H*T exceeds the grid");
+    if (B == 0 || T == 0) return RHZ_OK;
+    const size_t need = bwd_ws_bytes(B, T, H, d);
+    if (workspace == nullptr || workspace_bytes < need)
+        return set_error(RHZ_ERR_INVALID, "workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+    const size_t vec = dtype == RHZ_DTYPE_BF16 ? 8 : 16;
+    RHZ_TRY(check_ptr(workspace, "workspace", 256, true));
+    RHZ_TRY(check_ptr(q, "q", vec, true));
+    RHZ_TRY(check_ptr(k, "k", vec, true));
+    RHZ_TRY(check_ptr(v, "v", vec, true));
+    RHZ_TRY(check_ptr(d_o, "d_o", vec, true));
+    RHZ_TRY(check_ptr(dq, "dq", vec, true));
+    RHZ_TRY(check_ptr(dk, "dk", vec, true));
+    RHZ_TRY(check_ptr(dv, "dv", vec, true));
+    RHZ_TRY(check_ptr(alpha, "alpha", 4, true));
+    RHZ_TRY(check_ptr(beta, "beta", 4, true));
+    RHZ_TRY(check_ptr(dalpha, "dalpha", 4, true));
+    RHZ_TRY(check_ptr(dbeta, "dbeta", 4, true));
+    RHZ_TRY(check_ptr(segment, "segment", 8, segment != nullptr));
+    RHZ_TRY(check_ptr(d_state_final, "d_state_final", 16, d_state_final != nullptr));
+    RHZ_TRY(require_sm100());
+    BwdArgs a{dq, dk, dv, dalpha, dbeta, q, k, v, d_o, alpha, beta, segment, d_state_final,
+              workspace, B, T, H, d, dtype, as_cuda(stream)};
+    return launch_bwd(a);
+}
+
 int rhz_groupnorm_heads(void *out, const void *x, const float *scale, int64_t rows, int32_t H,
                         int32_t d, float eps, int32_t dtype, rhz_stream_t stream) {
     clear_error();

@@ -98,6 +98,23 @@ int launch_chunk_map(int32_t *chunk_seq, int32_t *chunk_start, int32_t *n_chunks
                      size_t ws_bytes, cudaStream_t s);
 int launch_gather_states(float *dense, const float *pool, const int32_t *slots, int64_t n,
                          int64_t num_slots, int H, int d, bool scatter, cudaStream_t s);
+// Backward of the sequential / chunked scan (gdr_bwd.cu): resets at t = 0
+// and at segment changes; dense [B][T][H][d] layouts.
+struct BwdArgs {
+    void *dq, *dk, *dv;
+    float *dalpha, *dbeta;
+    const void *q, *k, *v, *d_o;
+    const float *alpha, *beta;
+    const int64_t *segment;       // [B][T] or nullptr
+    const float *d_state_final;   // [B][H][d][d] or nullptr
+    void *workspace;
+    int64_t B, T;
+    int H, d, dtype;
+    cudaStream_t stream;
+};
+size_t bwd_ws_bytes(int64_t B, int64_t T, int H, int d);
+int launch_bwd(const BwdArgs &a);
+
 // groupnorm_heads over rows x H slices of d values (norm.cu); out may be x.
 int launch_groupnorm_heads(void *out, const void *x, const float *scale, int64_t rows, int H, int d,
                            float eps, int dtype, cudaStream_t s);

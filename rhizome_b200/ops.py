@@ -204,6 +204,28 @@ def gdr_varlen_fwd(q, k, v, alpha, beta, cu_seqlens, state_pool=None, slot_idx=N
     return o
 
 
+def gdr_scan_chunked_bwd(q, k, v, alpha, beta, d_o, segment=None, d_state_final=None,
+                         workspace=None):
+    """Backward of gdr_scan_chunked / gdr_sequential on [B, T, H, d] (resets
+    at t = 0 and at segment changes): returns (dq, dk, dv, dalpha, dbeta) for
+    the upstream gradients d_o [B, T, H, d] and d_state_final [B, H, d, d]."""
+    B, T = q.shape[0], q.shape[1]
+    H, d = _qkv(q, k, v, alpha, beta, (B, T))
+    _need(d_o, "d_o", q.dtype, tuple(q.shape))
+    if segment is not None:
+        _need(segment, "segment", torch.int64, (B, T))
+    if d_state_final is not None:
+        _need(d_state_final, "d_state_final", torch.float32, (B, H, d, d))
+    nbytes = int(capi.lib().rhz_gdr_bwd_workspace_bytes(B, T, H, d))
+    ws = workspace if workspace is not None else torch.empty(max(nbytes, 1), device=q.device, dtype=torch.uint8)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+    dalpha, dbeta = torch.empty_like(alpha), torch.empty_like(beta)
+    capi.call("rhz_gdr_scan_chunked_bwd", _p(dq), _p(dk), _p(dv), _p(dalpha), _p(dbeta), _p(q),
+              _p(k), _p(v), _p(alpha), _p(beta), _p(segment), _p(d_o), _p(d_state_final), B, T,
+              H, d, _dt(q), _p(ws), nbytes, _stream(q.device))
+    return dq, dk, dv, dalpha, dbeta
+
+
 def gdr_varlen_fwd_norm(q, k, v, alpha, beta, cu_seqlens, norm_scale, norm_eps=1e-6,
                         state_pool=None, slot_idx=None, zero_init=False, write_state=True):
     """gdr_varlen_fwd followed by the per-head output norm groupnorm_heads
