@@ -74,6 +74,29 @@ const char *rhz_last_error(void);
 /* ABI version of this header (major * 100 + minor). */
 int rhz_abi_version(void);
 
+/*
+ * Device-side failure status -- an addition of this library (the reference's
+ * ops run on the CPU and have no device waits). The tensor-core kernels
+ * bound every wait on a barrier or a copy; a wait that runs out makes the
+ * kernel drain its copies, release its resources and return early, leaving
+ * that launch's outputs undefined, and sets a sticky flag on the device.
+ * rhz_device_status reads the flags of the current device (synchronising
+ * with it) into *timed_out (1 if any wait ran out since the last clear, else
+ * 0) and clears them when clear != 0.
+ */
+int rhz_device_status(int32_t *timed_out, int clear);
+
+/*
+ * Which tensor-core form runs the bf16, d == 128 chunked scan
+ * (rhz_gdr_scan_chunked, rhz_gdr_varlen_fwd): a 2-CTA cluster per
+ * (sequence, head) item, or one CTA per item. AUTO (the default) picks by
+ * the item count against the SM count. Both give the same results within
+ * the bf16 tolerance. Process-wide; the previous setting goes to *previous
+ * unless it is NULL. A variant outside the enum returns RHZ_ERR_INVALID.
+ */
+enum rhz_chunk_kernel { RHZ_CHUNK_AUTO = 0, RHZ_CHUNK_PAIR = 1, RHZ_CHUNK_SOLO = 2 };
+int rhz_gdr_set_chunk_kernel(int32_t variant, int32_t *previous);
+
 /* --------------------------------------------------------------------- */
 /* GDR op family                                                          */
 /* --------------------------------------------------------------------- */

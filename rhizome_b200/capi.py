@@ -96,7 +96,12 @@ SIGNATURES = {
                                C.c_uint32, _vp]),
     "rhz_heads_unshard": (C.c_int, [_vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp]),
     "rhz_heads_shard": (C.c_int, [_vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp]),
+    "rhz_device_status": (C.c_int, [_vp, C.c_int]),
+    "rhz_gdr_set_chunk_kernel": (C.c_int, [_i32, _vp]),
 }
+
+# Forms of the tensor-core chunked scan (enum rhz_chunk_kernel).
+RHZ_CHUNK_AUTO, RHZ_CHUNK_PAIR, RHZ_CHUNK_SOLO = 0, 1, 2
 
 # Largest B*T rhz_varlen_segments_to_cu_seqlens_noalloc accepts.
 RHZ_NOALLOC_MAX_POSITIONS = 1 << 26

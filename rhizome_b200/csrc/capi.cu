@@ -222,6 +222,25 @@ const char *rhz_last_error(void) { return g_last_error; }
 
 int rhz_abi_version(void) { return 100; }
 
+int rhz_device_status(int32_t *timed_out, int clear) {
+    clear_error();
+    if (!timed_out) return set_error(RHZ_ERR_INVALID, "timed_out must not be NULL");
+    int a = 0, b = 0;
+    int st = chunk_pair_status(&a, clear != 0);
+    if (st == RHZ_OK) st = chunk_solo_status(&b, clear != 0);
+    if (st != RHZ_OK) return st;
+    *timed_out = (a | b) ? 1 : 0;
+    return RHZ_OK;
+}
+
+int rhz_gdr_set_chunk_kernel(int32_t variant, int32_t *previous) {
+    clear_error();
+    int prev = 0;
+    const int st = set_chunk_variant(variant, &prev);
+    if (st == RHZ_OK && previous) *previous = prev;
+    return st;
+}
+
 int rhz_gdr_step(void *o, float *state_pool, const int32_t *slot_idx, const void *q,
                  const void *k, const void *v, const float *alpha, const float *beta, int64_t n,
                  int64_t num_slots, int32_t H, int32_t d, int32_t dtype, rhz_stream_t stream) {

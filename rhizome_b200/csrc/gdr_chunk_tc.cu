@@ -54,6 +54,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <climits>
 #include <cstdint>
 #include <mutex>
@@ -1242,7 +1243,55 @@ int make_tmap(CUtensorMap *m, const void *base, int64_t tokens, int H) {
 
 bool chunk_tc_supports(int d, int dtype) { return d == HD && dtype == RHZ_DTYPE_BF16; }
 
+int chunk_pair_status(int *flag, bool clear) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_status, sizeof(int));
+    if (e == cudaSuccess && clear && v) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_tc_status, &zero, sizeof(int));
+    }
+    if (e != cudaSuccess) return set_error(RHZ_ERR_DEVICE, "reading the pair kernel's status: %s", cudaGetErrorString(e));
+    *flag = v;
+    return RHZ_OK;
+}
+
+namespace {
+std::atomic<int> g_chunk_variant{RHZ_CHUNK_AUTO};
+}
+
+int set_chunk_variant(int v, int *prev) {
+    if (v < RHZ_CHUNK_AUTO || v > RHZ_CHUNK_SOLO)
+        return set_error(RHZ_ERR_INVALID, "chunk kernel variant %d is not one of 0, 1, 2", v);
+    *prev = g_chunk_variant.exchange(v);
+    return RHZ_OK;
+}
+
+// Work per (sequence, head) item: the cluster pair finishes an item in
+// about 1/1.6 of the one-CTA kernel's time (measured on B200 at B=4, T=4096,
+// H=16) but holds two SMs, so once there are more items than pairs the
+// one-CTA kernel's doubled parallelism wins. Compare whole passes over the
+// SMs with that cost ratio.
+bool chunk_use_solo(int64_t items, int sms) {
+    const int64_t pairs = sms / 2 > 0 ? sms / 2 : 1;
+    const int64_t pair_passes = (items + pairs - 1) / pairs;
+    const int64_t solo_passes = (items + sms - 1) / sms;
+    return 10 * pair_passes > 16 * solo_passes;
+}
+
 int launch_chunk_tc(const SeqArgs &a) {
+    if (!chunk_tc_supports(a.d, a.dtype))
+        return set_error(RHZ_ERR_SHAPE, "tensor-core kernel needs bf16 and head_dim 128 (got %d)", a.d);
+    int v = g_chunk_variant.load();
+    if (v == RHZ_CHUNK_AUTO) {
+        int sms = 148;
+        bool sm100 = true;
+        device_info(&sms, &sm100);
+        v = chunk_use_solo(a.n_seq * a.H, sms) ? RHZ_CHUNK_SOLO : RHZ_CHUNK_PAIR;
+    }
+    return v == RHZ_CHUNK_SOLO ? launch_chunk_solo(a) : launch_chunk_pair(a);
+}
+
+int launch_chunk_pair(const SeqArgs &a) {
     if (!chunk_tc_supports(a.d, a.dtype))
         return set_error(RHZ_ERR_SHAPE, "tensor-core kernel needs bf16 and head_dim 128 (got %d)", a.d);
     const int64_t tokens = a.cu_seqlens ? a.total_tokens : a.n_seq * a.seq_len;

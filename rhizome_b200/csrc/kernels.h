@@ -87,6 +87,16 @@ int launch_seq(const SeqArgs &a);
 // shapes it does not tile.
 int launch_chunk_tc(const SeqArgs &a);
 bool chunk_tc_supports(int d, int dtype);
+// The two forms behind launch_chunk_tc: a 2-CTA cluster per (sequence, head)
+// item (gdr_chunk_tc.cu) and one CTA per item (gdr_chunk_solo.cu).
+int launch_chunk_pair(const SeqArgs &a);
+int launch_chunk_solo(const SeqArgs &a);
+bool chunk_use_solo(int64_t items, int sms);
+// Forces one form (RHZ_CHUNK_*), the previous setting to *prev.
+int set_chunk_variant(int v, int *prev);
+// Sticky device flags: 1 once a bounded wait of that kernel gave up.
+int chunk_pair_status(int *flag, bool clear);
+int chunk_solo_status(int *flag, bool clear);
 
 // Variable-length index work (varlen.cu).
 int launch_prefix_sum(int32_t *cu, const int32_t *lengths, int64_t n, cudaStream_t s);

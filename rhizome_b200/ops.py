@@ -7,6 +7,8 @@ f32, states [n, H, d, d] f32 with S[i][j], i the v index and j the k index.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import capi
@@ -347,3 +349,24 @@ def unpack_tokens(packed: torch.Tensor, cu_seqlens: torch.Tensor, max_len: int) 
     capi.call("rhz_varlen_unpack_tokens", _p(padded), _p(packed), _p(cu_seqlens), n, max_len,
               row_bytes, _stream(packed.device))
     return padded
+
+
+def device_status(clear: bool = False) -> bool:
+    """True if a bounded device-side wait of a tensor-core kernel ran out on
+    the current device since the last clear (that launch's outputs are
+    undefined); ``clear`` resets the flag."""
+    flag = ctypes.c_int32(0)
+    capi.call("rhz_device_status", ctypes.byref(flag), 1 if clear else 0)
+    return bool(flag.value)
+
+
+def set_chunk_kernel(variant: str) -> str:
+    """Pick the tensor-core chunked form process-wide: "auto" (by item count
+    against SM count), "pair" (2-CTA cluster per item) or "solo" (one CTA per
+    item). Returns the previous setting."""
+    names = {"auto": capi.RHZ_CHUNK_AUTO, "pair": capi.RHZ_CHUNK_PAIR, "solo": capi.RHZ_CHUNK_SOLO}
+    if variant not in names:
+        raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"unknown chunk kernel {variant!r}")
+    prev = ctypes.c_int32(0)
+    capi.call("rhz_gdr_set_chunk_kernel", names[variant], ctypes.byref(prev))
+    return {v: k for k, v in names.items()}[prev.value]

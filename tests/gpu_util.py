@@ -2,10 +2,13 @@
 Philox generator, rounded to exactly what the device kernels receive."""
 from __future__ import annotations
 
+import contextlib
+
 import numpy as np
 import torch
 
 from oracle import oracle as O
+from rhizome_b200 import ops
 from tests.tolerance import bf16_round
 
 
@@ -36,3 +39,14 @@ def device_inputs(q, k, v, a, b, dtype: str):
     td = TORCH_DT[dtype]
     return (to_dev(q, td), to_dev(k, td), to_dev(v, td), to_dev(a, torch.float32),
             to_dev(b, torch.float32))
+
+
+@contextlib.contextmanager
+def chunk_form(name: str):
+    """Pin the tensor-core chunked scan to one form ("pair", "solo", "auto")
+    for the duration of the block."""
+    prev = ops.set_chunk_kernel(name)
+    try:
+        yield
+    finally:
+        ops.set_chunk_kernel(prev)

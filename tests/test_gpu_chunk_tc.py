@@ -1,18 +1,26 @@
 """GPU parity of the tcgen05 chunked prefill (bf16 in, fp32 state) against
 the f64 oracle on the same (bf16-rounded) inputs, through the C ABI, at the
 bf16 tolerance (<= 2e-2 relative to max|ref|, <= 1e-2 absolute, and
-1e-2 RMS(ref) + 2e-2 |ref| elementwise)."""
+1e-2 RMS(ref) + 2e-2 |ref| elementwise). Every case runs on both forms of the
+kernel (the 2-CTA cluster per item and the one-CTA kernel), pinned through
+rhz_gdr_set_chunk_kernel."""
 import numpy as np
 import pytest
 import torch
 
 from oracle import oracle as O
 from rhizome_b200 import ops
-from tests.gpu_util import device_inputs, host, make_inputs, to_dev
+from tests.gpu_util import chunk_form, device_inputs, host, make_inputs, to_dev
 from tests.tolerance import assert_bf16
 
 pytestmark = pytest.mark.gpu
 D = 128
+
+
+@pytest.fixture(autouse=True, params=["pair", "solo"])
+def form(request):
+    with chunk_form(request.param):
+        yield request.param
 
 
 def dense_case(seed, B, T, H, scale_q=1.0, alpha=None, beta=None):
@@ -175,3 +183,40 @@ def test_varlen_prefill_config_full_size():
                              state_out_index=slots)
     assert_bf16(host(o), ro, "cfg3 o")
     assert_bf16(host(dpool), rpool, "cfg3 pool")
+
+
+def test_forms_agree_and_auto_dispatch():
+    """The two forms agree within the bf16 tolerance of each other's rounding
+    (they round at the same points but accumulate in different orders), and
+    the default picks the cluster pair for few items and the one-CTA kernel
+    for more items than the pairs cover at once."""
+    B, T, H = 2, 300, 4
+    q, k, v, a, b = dense_case(55, B, T, H)
+    with chunk_form("pair"):
+        op, sp = run_dense(q, k, v, a, b, B, T)
+    with chunk_form("solo"):
+        os_, ss = run_dense(q, k, v, a, b, B, T)
+    with chunk_form("auto"):
+        oa, sa = run_dense(q, k, v, a, b, B, T)
+    assert torch.equal(oa, op) and torch.equal(sa, sp)  # 8 items: pair
+    ro, rs = O.gdr_dense(*(x.reshape(B, T, *x.shape[1:]) for x in (q, k, v, a, b)))
+    assert_bf16(host(os_), ro, "solo o")
+    assert_bf16(host(os_), host(op), "solo vs pair o")
+    assert_bf16(host(ss), host(sp), "solo vs pair state")
+    # 2 x 128 heads = 256 items: four passes of 74 pairs against two of 148
+    # single CTAs, so the one-CTA kernel
+    B, T, H = 2, 70, 128
+    q, k, v, a, b = dense_case(56, B, T, H)
+    with chunk_form("solo"):
+        os_, ss = run_dense(q, k, v, a, b, B, T)
+    with chunk_form("auto"):
+        oa, sa = run_dense(q, k, v, a, b, B, T)
+    assert torch.equal(oa, os_) and torch.equal(sa, ss)
+
+
+def test_device_status_clear_after_runs():
+    assert not ops.device_status(clear=True)
+    B, T, H = 1, 130, 2
+    q, k, v, a, b = dense_case(57, B, T, H)
+    run_dense(q, k, v, a, b, B, T)
+    assert not ops.device_status()

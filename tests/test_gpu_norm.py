@@ -7,7 +7,7 @@ import torch
 
 from oracle import oracle as O
 from rhizome_b200 import ops
-from tests.gpu_util import host, make_inputs, to_dev
+from tests.gpu_util import chunk_form, host, make_inputs, to_dev
 from tests.tolerance import assert_bf16, assert_fp32, bf16_round, error_stats
 
 pytestmark = pytest.mark.gpu
@@ -53,8 +53,16 @@ def _varlen_case(dtype, seed):
     return cu, q, k, v, a, b, pool, slots, scale
 
 
+@pytest.mark.parametrize("form", ["pair", "solo"])
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
-def test_varlen_with_output_norm_matches_oracle(dtype):
+def test_varlen_with_output_norm_matches_oracle(dtype, form):
+    if dtype == "f32" and form == "solo":
+        pytest.skip("the f32 path does not use the tensor-core kernels")
+    with chunk_form(form):
+        _check_varlen_with_output_norm(dtype)
+
+
+def _check_varlen_with_output_norm(dtype):
     cu, q, k, v, a, b, pool, slots, scale = _varlen_case(dtype, 21)
     td = torch.bfloat16 if dtype == "bf16" else torch.float32
     dpool = to_dev(pool, torch.float32)
@@ -85,10 +93,16 @@ def test_varlen_with_output_norm_matches_oracle(dtype):
         assert_fp32(host(o), O.groupnorm_heads(host(plain), scale, 1e-6), "norm op")
 
 
-def test_fused_epilogue_equals_separate_norm():
+@pytest.mark.parametrize("form", ["pair", "solo"])
+def test_fused_epilogue_equals_separate_norm(form):
     """bf16: the norm in the recurrence epilogue (on the fp32 accumulator)
     against recurrence -> bf16 o -> standalone norm: within one extra bf16
     rounding of each other."""
+    with chunk_form(form):
+        _check_fused_epilogue()
+
+
+def _check_fused_epilogue():
     cu, q, k, v, a, b, pool, slots, scale = _varlen_case("bf16", 22)
     args = [to_dev(x, torch.bfloat16) for x in (q, k, v)] + \
         [to_dev(a, torch.float32), to_dev(b, torch.float32), to_dev(cu, torch.int32)]
