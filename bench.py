@@ -12,8 +12,8 @@ shards with no data-path collective, so scaling is weak.
 Keys beyond the driver contract: `roofline` (dominant kernel, HBM bound at
 this arithmetic intensity, with the tensor-core fraction beside it),
 `cpu_baseline` (the f64 oracle restating crates/ops/src/delta.rs, timed on
-this host's cores), `e2e` (same metric through the C-ABI call with host
-buffers and the copies inside the timed region), `decode` (ragged decode
+this host's cores), `e2e` (same metric through the host-buffer C-ABI call,
+rhz_gdr_scan_chunked_host, with the copies inside the timed region), `decode` (ragged decode
 step: 512 sequences x 16 heads from a 1024-slot fp32 pool), `clocks`.
 
 `--impl reference` times the reference's CPU implementation of the path (the
@@ -314,23 +314,24 @@ def run_ours(args):
                 "tensor": {"achieved": round(tflops, 1), "peak": peaks["bf16_tflops"],
                            "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4)}}
 
-    # End to end through the C ABI with host buffers: pinned inputs copied in,
-    # outputs and final states copied out, every step.
+    # End to end through the host-buffer C-ABI call (rhz_gdr_scan_chunked_host):
+    # pinned host inputs in, host outputs and final states out, every step;
+    # the library pipelines the copies against the scan over slabs of
+    # positions.
     hq, hk, hv, ha, hb = (x.cpu().pin_memory() for x in sets[0])
     ho = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
     hfin = torch.empty(fin.shape, dtype=fin.dtype, pin_memory=True)
-    dq, dk, dv, da, db = (torch.empty_like(x) for x in sets[0])
-    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, ha, hb))
+    ws_bytes = capi.lib().rhz_gdr_host_workspace_bytes(B, T, H, D, capi.RHZ_DTYPE_BF16, 0)
+    hws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    slab = min((T + 63) // 64 * 64, max(256, ((T + 7) // 8 + 63) // 64 * 64))
+    n_slabs = (T + slab - 1) // slab
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, ha, hb)) + n_slabs * (3 * B + 1) * 4
     d2h = ho.numel() * ho.element_size() + hfin.numel() * hfin.element_size()
 
     def e2e_step():
-        for dst, src in ((dq, hq), (dk, hk), (dv, hv), (da, ha), (db, hb)):
-            dst.copy_(src, non_blocking=True)
-        capi.call("rhz_gdr_scan_chunked", o.data_ptr(), fin.data_ptr(), dq.data_ptr(),
-                  dk.data_ptr(), dv.data_ptr(), da.data_ptr(), db.data_ptr(), None, None, CHUNK,
-                  B, T, H, D, capi.RHZ_DTYPE_BF16, None, 0, sptr)
-        ho.copy_(o, non_blocking=True)
-        hfin.copy_(fin, non_blocking=True)
+        capi.call("rhz_gdr_scan_chunked_host", ho.data_ptr(), hfin.data_ptr(), hq.data_ptr(),
+                  hk.data_ptr(), hv.data_ptr(), ha.data_ptr(), hb.data_ptr(), None, None, CHUNK,
+                  B, T, H, D, capi.RHZ_DTYPE_BF16, hws.data_ptr(), ws_bytes, sptr)
 
     e2e_steps = max(3, min(args.steps, 10))
     for _ in range(2):
@@ -458,7 +459,9 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (2 x 270 MB sets, alternated)"},
             "roofline": roofline, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / e2e_steps, 4),
+                    "call": f"rhz_gdr_scan_chunked_host, pinned host buffers, {n_slabs} slabs "
+                            f"of {slab} positions pipelined"},
             "gpu_launches": args.steps, "clocks": clock_info, "decode": decode,
             "producer": producer, "output_norm": outnorm,
         }

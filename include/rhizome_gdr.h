@@ -147,6 +147,34 @@ int rhz_gdr_scan_chunked(void *o, float *state_final, const void *q, const void 
                          void *workspace, size_t workspace_bytes, rhz_stream_t stream);
 
 /*
+ * rhz_gdr_scan_chunked_host -- rhz_gdr_scan_chunked with o, state_final, q,
+ * k, v, alpha, beta, segment and state_init in HOST memory (the reference
+ * op's own calling convention: slices in, vectors out), for callers whose
+ * data is not yet on the GPU. The call copies the inputs in and the outputs
+ * out itself, pipelined over slabs of positions (a multiple of 64, about
+ * T / 8, at least 256) on two copy streams of its own, so the copies of
+ * slab j+1 in, the scan of slab j and the copy of slab j-1 out overlap; the
+ * scan runs on `stream`, after the work already queued there. Returns when
+ * every output is in host memory. Host buffers should be page-locked
+ * (cudaHostAlloc / cudaHostRegister) for the copies to overlap; pageable
+ * memory works but serialises them. `workspace`: device memory of
+ * rhz_gdr_host_workspace_bytes(B, T, H, d, dtype, segment != NULL) bytes,
+ * 256-byte aligned (three slab buffer sets, two state pools, the whole
+ * alpha and beta arrays and the slab piece tables). B <= 65535. Results: without segments bitwise those of
+ * rhz_gdr_scan_chunked (slabs start on 64-position chunk boundaries and the
+ * fp32 state crosses slab boundaries unrounded); with segments a segment
+ * that spans a slab boundary is chunked from the boundary as well, which
+ * changes the bf16 kernel's rounding order within its tolerance.
+ */
+int rhz_gdr_scan_chunked_host(void *o, float *state_final, const void *q, const void *k,
+                              const void *v, const float *alpha, const float *beta,
+                              const int64_t *segment, const float *state_init, int64_t chunk,
+                              int64_t B, int64_t T, int32_t H, int32_t d, int32_t dtype,
+                              void *workspace, size_t workspace_bytes, rhz_stream_t stream);
+size_t rhz_gdr_host_workspace_bytes(int64_t B, int64_t T, int32_t H, int32_t d, int32_t dtype,
+                                    int has_segment);
+
+/*
  * rhz_gdr_varlen_fwd -- continuous-batching prefill over one packed stream.
  * Sequence i occupies token rows [cu_seqlens[i], cu_seqlens[i+1]) of
  * q/k/v/alpha/beta/o (cu_seqlens: n_seq + 1 int32, device, non-decreasing,

@@ -97,6 +97,9 @@ SIGNATURES = {
     "rhz_heads_unshard": (C.c_int, [_vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp]),
     "rhz_heads_shard": (C.c_int, [_vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp]),
     "rhz_device_status": (C.c_int, [_vp, C.c_int]),
+    "rhz_gdr_scan_chunked_host": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64,
+                                            _i64, _i64, _i32, _i32, _i32, _vp, _sz, _vp]),
+    "rhz_gdr_host_workspace_bytes": (_sz, [_i64, _i64, _i32, _i32, _i32, C.c_int]),
     "rhz_gdr_set_chunk_kernel": (C.c_int, [_i32, _vp]),
 }
 

@@ -1,13 +1,17 @@
 // C ABI of the GDR library: argument validation (the shape rules of
 // DeltaInputs::is_consistent, crates/ops/src/delta.rs:46-55, on the batched
 // layouts), status codes with a per-thread message, and dispatch to the
-// kernels. Nothing here allocates device memory.
+// kernels. Nothing here allocates device memory; the host-buffer entry point
+// keeps three copy streams and a few events per device.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
+#include <vector>
 
 #include "../../include/rhizome_gdr.h"
 #include "common.cuh"
@@ -627,6 +631,276 @@ int rhz_heads_shard(void *gathered, const void *full, int64_t G, int64_t tokens,
     RHZ_TRY(check_ptr(gathered, "gathered", 16, tokens > 0));
     RHZ_TRY(require_sm100());
     return launch_heads_unshard(gathered, full, G, tokens, H / G, row_bytes, true, as_cuda(stream));
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------------
+// Host-buffer chunked scan: the reference signature with every tensor in
+// host memory, pipelined over slabs of positions so that the host->device
+// copies of slab j+1, the scan of slab j and the device->host copy of slab
+// j-1 overlap.
+namespace {
+
+constexpr int kHostSets = 3;  // buffer sets in flight
+
+struct HostPlan {
+    int64_t slab;      // positions per slab (multiple of 64)
+    int64_t n_slabs;
+    int64_t max_pieces;
+    size_t tok_bytes, gate_bytes, state_bytes, set_bytes;
+    size_t q_off, k_off, v_off, o_off, a_off, b_off;  // within a set
+    size_t pools_off, gates_off, gates_bytes, meta_off, total;
+};
+
+HostPlan host_plan(int64_t B, int64_t T, int32_t H, int32_t d, int32_t dtype, bool has_segment) {
+    auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+    HostPlan p{};
+    const int64_t t64 = (T + 63) / 64 * 64;
+    const int64_t eighth = ((T + 7) / 8 + 63) / 64 * 64;
+    p.slab = std::min<int64_t>(t64, std::max<int64_t>(256, eighth));
+    if (p.slab < 64) p.slab = 64;
+    p.n_slabs = T > 0 ? (T + p.slab - 1) / p.slab : 0;
+    p.max_pieces = B * p.n_slabs + (has_segment ? B * T : 0);
+    const size_t esz = dtype == RHZ_DTYPE_BF16 ? 2 : 4;
+    const size_t rows = static_cast<size_t>(B) * p.slab * H;
+    p.tok_bytes = up(rows * d * esz);
+    p.gate_bytes = up(rows * sizeof(float));
+    p.q_off = 0;
+    p.k_off = p.tok_bytes;
+    p.v_off = 2 * p.tok_bytes;
+    p.o_off = 3 * p.tok_bytes;
+    p.a_off = 4 * p.tok_bytes;
+    p.b_off = 4 * p.tok_bytes + p.gate_bytes;
+    p.set_bytes = 4 * p.tok_bytes + 2 * p.gate_bytes;
+    p.state_bytes = up(static_cast<size_t>(B) * H * d * d * sizeof(float));
+    p.pools_off = kHostSets * p.set_bytes;
+    p.gates_bytes = up(static_cast<size_t>(B) * T * H * sizeof(float));
+    p.gates_off = p.pools_off + 2 * p.state_bytes;
+    p.meta_off = p.gates_off + 2 * p.gates_bytes;
+    // per slab: row offsets (B + 1), piece offsets (pieces + 1), in slots,
+    // out slots
+    p.total = p.meta_off + up((3 * static_cast<size_t>(p.max_pieces) +
+                               p.n_slabs * static_cast<size_t>(B + 2)) * sizeof(int32_t));
+    return p;
+}
+
+// One slab's pieces: batch row b's positions [t0, t0 + len) split where the
+// segment id changes. A piece continues row b's carried state when it starts
+// the slab inside the same segment as the previous slab's last position
+// (slot b of the previous pool), else starts from zero (slot -1: the reset
+// at t = 0 and at segment changes, delta.rs:139-141); the last piece of a
+// row writes slot b of the next pool.
+void slab_pieces(const int64_t *seg, int64_t B, int64_t T, int64_t t0, int64_t len,
+                 std::vector<int32_t> &cu, std::vector<int32_t> &in, std::vector<int32_t> &out) {
+    cu.push_back(0);
+    for (int64_t b = 0; b < B; ++b) {
+        const int64_t *sr = seg ? seg + b * T : nullptr;
+        const int32_t base = static_cast<int32_t>(b * len);
+        int64_t start = t0;
+        auto emit = [&](int64_t s, int64_t e) {
+            cu.push_back(base + static_cast<int32_t>(e - t0));
+            const bool carry = s == t0 && t0 > 0 && (sr == nullptr || sr[t0] == sr[t0 - 1]);
+            in.push_back(carry ? static_cast<int32_t>(b) : -1);
+            out.push_back(e == t0 + len ? static_cast<int32_t>(b) : -1);
+        };
+        if (sr) {
+            for (int64_t t = t0 + 1; t < t0 + len; ++t) {
+                if (sr[t] != sr[t - 1]) {
+                    emit(start, t);
+                    start = t;
+                }
+            }
+        }
+        emit(start, t0 + len);
+    }
+}
+
+// Copy streams and events of the host-buffer entry point, created on a
+// device's first call and kept for the process (creating and destroying them
+// per call cost ~0.2 ms). Calls on one device take the mutex in turn.
+struct HostStreams {
+    std::mutex m;
+    bool ready = false;
+    cudaStream_t up = nullptr, down = nullptr;
+    cudaEvent_t start = nullptr, in[kHostSets] = {}, comp[kHostSets] = {}, out[kHostSets] = {};
+    cudaError_t create() {
+        if (ready) return cudaSuccess;
+        cudaError_t e = cudaStreamCreateWithFlags(&up, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&down, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&start, cudaEventDisableTiming);
+        for (int i = 0; i < kHostSets && e == cudaSuccess; ++i) {
+            e = cudaEventCreateWithFlags(&in[i], cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&comp[i], cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&out[i], cudaEventDisableTiming);
+        }
+        ready = e == cudaSuccess;
+        return e;
+    }
+};
+HostStreams g_host[64];
+
+// Rows [t0, t0 + len) of every batch row of a [B][T][row_bytes] host array
+// into (or out of) a packed [B][len][row_bytes] device buffer.
+cudaError_t copy_slab(void *dst, const void *src, int64_t B, int64_t T, int64_t t0, int64_t len,
+                      size_t row_bytes, bool to_device, cudaStream_t s) {
+    if (to_device)
+        return cudaMemcpy2DAsync(dst, len * row_bytes,
+                                 static_cast<const char *>(src) + t0 * row_bytes, T * row_bytes,
+                                 len * row_bytes, B, cudaMemcpyHostToDevice, s);
+    return cudaMemcpy2DAsync(static_cast<char *>(dst) + t0 * row_bytes, T * row_bytes, src,
+                             len * row_bytes, len * row_bytes, B, cudaMemcpyDeviceToHost, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t rhz_gdr_host_workspace_bytes(int64_t B, int64_t T, int32_t H, int32_t d, int32_t dtype,
+                                    int has_segment) {
+    if (B < 0 || T < 0 || H < 1 || d < 1 || (dtype != RHZ_DTYPE_F32 && dtype != RHZ_DTYPE_BF16))
+        return 0;
+    return host_plan(B, T, H, d, dtype, has_segment != 0).total;
+}
+
+int rhz_gdr_scan_chunked_host(void *o, float *state_final, const void *q, const void *k,
+                              const void *v, const float *alpha, const float *beta,
+                              const int64_t *segment, const float *state_init, int64_t chunk,
+                              int64_t B, int64_t T, int32_t H, int32_t d, int32_t dtype,
+                              void *workspace, size_t workspace_bytes, rhz_stream_t stream) {
+    clear_error();
+    if (chunk < 0) return set_error(RHZ_ERR_SHAPE, "chunk = %lld: must be >= 0", (long long)chunk);
+    RHZ_TRY(check_dtype(dtype));
+    RHZ_TRY(check_heads(H, d));
+    if (B < 0 || T < 0) return set_error(RHZ_ERR_SHAPE, "B = %lld, T = %lld: must be >= 0", (long long)B, (long long)T);
+    if (B * T > INT32_MAX - 1) return set_error(RHZ_ERR_SHAPE, "B*T = %lld positions exceeds int32 indexing", (long long)(B * T));
+    const bool any = B * T > 0;
+    for (const void *p : {static_cast<const void *>(o), q, k, v, static_cast<const void *>(alpha),
+                          static_cast<const void *>(beta)})
+        if (any && p == nullptr) return set_error(RHZ_ERR_INVALID, "a host tensor (q, k, v, alpha, beta or o) is NULL");
+    const size_t state_elems = static_cast<size_t>(B) * H * d * d;
+    if (T == 0) {
+        // The loop never runs: the reference returns init.clone() (delta.rs:135).
+        if (state_final && state_elems) {
+            if (state_init) memcpy(state_final, state_init, state_elems * sizeof(float));
+            else memset(state_final, 0, state_elems * sizeof(float));
+        }
+        return RHZ_OK;
+    }
+    if (B == 0) return RHZ_OK;
+    if (B > 65535) return set_error(RHZ_ERR_SHAPE, "B = %lld: the host-buffer entry point takes at most 65535 batch rows", (long long)B);
+    const HostPlan pl = host_plan(B, T, H, d, dtype, segment != nullptr);
+    if (workspace == nullptr || workspace_bytes < pl.total)
+        return set_error(RHZ_ERR_INVALID, "workspace too small: need %zu bytes, got %zu", pl.total, workspace_bytes);
+    RHZ_TRY(check_ptr(workspace, "workspace", 256, true));
+    RHZ_TRY(require_sm100());
+
+    // Every slab's pieces, built on the host and sent in one copy.
+    std::vector<int32_t> meta;
+    std::vector<int64_t> rows_at(pl.n_slabs), cu_at(pl.n_slabs), in_at(pl.n_slabs),
+        out_at(pl.n_slabs), pieces(pl.n_slabs);
+    {
+        std::vector<int32_t> cu, in, out;
+        for (int64_t j = 0; j < pl.n_slabs; ++j) {
+            const int64_t t0 = j * pl.slab, len = std::min(pl.slab, T - t0);
+            rows_at[j] = static_cast<int64_t>(meta.size());
+            for (int64_t b = 0; b <= B; ++b) meta.push_back(static_cast<int32_t>(b * len));
+            cu.clear(); in.clear(); out.clear();
+            slab_pieces(segment, B, T, t0, len, cu, in, out);
+            pieces[j] = static_cast<int64_t>(in.size());
+            cu_at[j] = static_cast<int64_t>(meta.size());
+            meta.insert(meta.end(), cu.begin(), cu.end());
+            in_at[j] = static_cast<int64_t>(meta.size());
+            meta.insert(meta.end(), in.begin(), in.end());
+            out_at[j] = static_cast<int64_t>(meta.size());
+            meta.insert(meta.end(), out.begin(), out.end());
+        }
+    }
+    char *ws = static_cast<char *>(workspace);
+    int32_t *dmeta = reinterpret_cast<int32_t *>(ws + pl.meta_off);
+    float *pool[2] = {reinterpret_cast<float *>(ws + pl.pools_off),
+                      reinterpret_cast<float *>(ws + pl.pools_off + pl.state_bytes)};
+    float *galpha = reinterpret_cast<float *>(ws + pl.gates_off);
+    float *gbeta = reinterpret_cast<float *>(ws + pl.gates_off + pl.gates_bytes);
+    const size_t esz = dtype == RHZ_DTYPE_BF16 ? 2 : 4;
+    const size_t tok_row = static_cast<size_t>(H) * d * esz, gate_row = static_cast<size_t>(H) * sizeof(float);
+    cudaStream_t cs = as_cuda(stream);
+
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64)
+        return set_error(RHZ_ERR_DEVICE, "cudaGetDevice: %s", cudaGetErrorString(e));
+    HostStreams &hs = g_host[dev];
+    std::lock_guard<std::mutex> lock(hs.m);
+    e = hs.create();
+    if (e == cudaSuccess) e = cudaEventRecord(hs.start, cs);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(hs.up, hs.start, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(hs.down, hs.start, 0);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(dmeta, meta.data(), meta.size() * sizeof(int32_t), cudaMemcpyHostToDevice, hs.up);
+    // The gates are small: both whole arrays go in first, in two copies, and
+    // each slab's rows are packed on the device. (Per-slab gate copies either
+    // queued their fixed cost into the token stream or, on a copy stream of
+    // their own, waited up to a millisecond for the copy engine.)
+    const size_t gate_all = static_cast<size_t>(B) * T * H * sizeof(float);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(galpha, alpha, gate_all, cudaMemcpyHostToDevice, hs.up);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(gbeta, beta, gate_all, cudaMemcpyHostToDevice, hs.up);
+    int st = RHZ_OK;
+    for (int64_t j = 0; j < pl.n_slabs && e == cudaSuccess && st == RHZ_OK; ++j) {
+        const int set = static_cast<int>(j % kHostSets);
+        char *buf = ws + set * pl.set_bytes;
+        const int64_t t0 = j * pl.slab, len = std::min(pl.slab, T - t0);
+        // inputs of slab j (after the scan of slab j - kHostSets released the set)
+        if (j >= kHostSets) e = cudaStreamWaitEvent(hs.up, hs.comp[set], 0);
+        if (e == cudaSuccess) e = copy_slab(buf + pl.q_off, q, B, T, t0, len, tok_row, true, hs.up);
+        if (e == cudaSuccess) e = copy_slab(buf + pl.k_off, k, B, T, t0, len, tok_row, true, hs.up);
+        if (e == cudaSuccess) e = copy_slab(buf + pl.v_off, v, B, T, t0, len, tok_row, true, hs.up);
+        if (e == cudaSuccess) e = cudaEventRecord(hs.in[set], hs.up);
+        // the scan of slab j (after its inputs landed and slab j - kHostSets's
+        // output left the set)
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, hs.in[set], 0);
+        if (e == cudaSuccess && j >= kHostSets) e = cudaStreamWaitEvent(cs, hs.out[set], 0);
+        if (e != cudaSuccess) break;
+        st = launch_pack_tokens(buf + pl.a_off, galpha + t0 * H, dmeta + rows_at[j], B, T, gate_row,
+                                false, cs);
+        if (st == RHZ_OK)
+            st = launch_pack_tokens(buf + pl.b_off, gbeta + t0 * H, dmeta + rows_at[j], B, T,
+                                    gate_row, false, cs);
+        if (st != RHZ_OK) break;
+        SeqArgs a{};
+        a.o = buf + pl.o_off;
+        a.q = buf + pl.q_off; a.k = buf + pl.k_off; a.v = buf + pl.v_off;
+        a.alpha = reinterpret_cast<const float *>(buf + pl.a_off);
+        a.beta = reinterpret_cast<const float *>(buf + pl.b_off);
+        a.cu_seqlens = dmeta + cu_at[j];
+        a.n_seq = pieces[j];
+        a.total_tokens = B * len;
+        a.state_in = j > 0 ? pool[(j - 1) & 1] : nullptr;
+        a.in_slots = dmeta + in_at[j];
+        a.state_out = pool[j & 1];
+        a.out_slots = dmeta + out_at[j];
+        a.num_slots = B;
+        a.H = H; a.d = d; a.dtype = dtype; a.stream = cs;
+        st = run_seq(a);
+        if (st != RHZ_OK) break;
+        e = cudaEventRecord(hs.comp[set], cs);
+        // output of slab j
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(hs.down, hs.comp[set], 0);
+        if (e == cudaSuccess) e = copy_slab(o, buf + pl.o_off, B, T, t0, len, tok_row, false, hs.down);
+        if (e == cudaSuccess) e = cudaEventRecord(hs.out[set], hs.down);
+    }
+    if (e == cudaSuccess && st == RHZ_OK && state_final)
+        e = cudaMemcpyAsync(state_final, pool[(pl.n_slabs - 1) & 1], state_elems * sizeof(float),
+                            cudaMemcpyDeviceToHost, hs.down);
+    // The call returns with every output in host memory (and with the copy
+    // streams idle, also on an error path).
+    const cudaError_t e2 = cudaStreamSynchronize(hs.down);
+    const cudaError_t e3 = cudaStreamSynchronize(cs);
+    cudaStreamSynchronize(hs.up);
+    if (st != RHZ_OK) return st;
+    if (e == cudaSuccess) e = e2 != cudaSuccess ? e2 : e3;
+    if (e != cudaSuccess) return set_error(RHZ_ERR_DEVICE, "host-buffer scan: %s", cudaGetErrorString(e));
+    return RHZ_OK;
 }
 
 }  // extern "C"

@@ -182,6 +182,57 @@ def gdr_scan_chunked(q, k, v, alpha, beta, chunk=64, segment=None, state_init=No
                        with_state, workspace)
 
 
+def _need_host(x: torch.Tensor, name: str, dtype=None, shape=None):
+    if x.is_cuda:
+        raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"{name} must be a host (CPU) tensor")
+    if not x.is_contiguous():
+        raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"{name} must be contiguous")
+    if dtype is not None and x.dtype != dtype:
+        raise capi.DtypeError(capi.RHZ_ERR_DTYPE, f"{name} must be {dtype}, got {x.dtype}")
+    if shape is not None and tuple(x.shape) != tuple(shape):
+        raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"{name} has shape {tuple(x.shape)}, expected {tuple(shape)}")
+
+
+def host_workspace_bytes(B: int, T: int, H: int, d: int, dtype: torch.dtype,
+                         has_segment: bool = False) -> int:
+    return int(capi.lib().rhz_gdr_host_workspace_bytes(B, T, H, d, _DTYPES[dtype],
+                                                         1 if has_segment else 0))
+
+
+def gdr_scan_chunked_host(q, k, v, alpha, beta, chunk=64, segment=None, state_init=None,
+                          with_state=True, out=None, state_out=None, workspace=None,
+                          device=None):
+    """gated_delta_scan_chunked on HOST tensors [B, T, H, d] (pinned for the
+    copies to overlap): the library copies slabs in, scans them on `device`
+    and copies the outputs back, pipelined. Returns host (o, final|None)."""
+    B, T = q.shape[0], q.shape[1]
+    d, H = q.shape[-1], q.shape[-2]
+    for name, x in (("q", q), ("k", k), ("v", v)):
+        _need_host(x, name, q.dtype, (B, T, H, d))
+    _need_host(alpha, "alpha", torch.float32, (B, T, H))
+    _need_host(beta, "beta", torch.float32, (B, T, H))
+    if segment is not None:
+        _need_host(segment, "segment", torch.int64, (B, T))
+    if state_init is not None:
+        _need_host(state_init, "state_init", torch.float32, (B, H, d, d))
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    pin = q.is_pinned()
+    o = out if out is not None else torch.empty(q.shape, dtype=q.dtype, pin_memory=pin)
+    _need_host(o, "out", q.dtype, tuple(q.shape))
+    fin = None
+    if with_state:
+        fin = state_out if state_out is not None else torch.empty((B, H, d, d), dtype=torch.float32,
+                                                                  pin_memory=pin)
+        _need_host(fin, "state_out", torch.float32, (B, H, d, d))
+    nbytes = host_workspace_bytes(B, T, H, d, q.dtype, segment is not None)
+    ws = workspace if workspace is not None else torch.empty(nbytes, device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        capi.call("rhz_gdr_scan_chunked_host", _p(o), _p(fin), _p(q), _p(k), _p(v), _p(alpha),
+                  _p(beta), _p(segment), _p(state_init), chunk, B, T, H, d, _dt(q), _p(ws),
+                  ws.numel() * ws.element_size(), _stream(dev))
+    return o, fin
+
+
 def gdr_varlen_fwd(q, k, v, alpha, beta, cu_seqlens, state_pool=None, slot_idx=None,
                    zero_init=False, write_state=True, out=None):
     """Continuous-batching prefill over a packed stream q/k/v [tokens, H, d]:
