@@ -479,15 +479,34 @@ __global__ void __launch_bounds__(NT, 1)
     // Gate tables of chunk k (warp 0, two positions per lane): prefix sums of
     // log2 alpha over nonzero alphas and of zero-alpha counts; padded rows get
     // alpha = 1, beta = 0 so they write nothing.
-    auto gate_tables = [&](int k, const Ref &r) {
+    // Gate inputs of one chunk (two positions per lane of one warp), fetched
+    // a chunk ahead into registers; padded positions get alpha = 1, beta = 0.
+    struct GateIn {
+        float a0, a1, b0, b1;
+    };
+    auto gate_fetch = [&](const Ref &r) -> GateIn {
+        GateIn g{1.f, 1.f, 0.f, 0.f};
+        if (r.item < 0) return g;
+        const int p0 = 2 * lane, p1 = p0 + 1;
+        if (p0 < r.L) {
+            g.a0 = p.alpha[(r.ts + p0) * H + r.h];
+            g.b0 = p.beta[(r.ts + p0) * H + r.h];
+        }
+        if (p1 < r.L) {
+            g.a1 = p.alpha[(r.ts + p1) * H + r.h];
+            g.b1 = p.beta[(r.ts + p1) * H + r.h];
+        }
+        return g;
+    };
+    // Gate tables of chunk k (one warp): prefix sums of log2 alpha over
+    // nonzero alphas and of zero-alpha counts, then gamma_t, P[C-1][s], beta,
+    // beta*gamma.
+    auto gate_tables = [&](int k, const GateIn &in) {
         float *g = reinterpret_cast<float *>(smem + OFF_SMALL) + (k & 1) * 384;
         int *zz = reinterpret_cast<int *>(g + 64);
         float *be = g + 128, *gm = g + 192, *pl = g + 256, *bg = g + 320;
         const int p0 = 2 * lane, p1 = p0 + 1;
-        const float a0 = p0 < r.L ? p.alpha[(r.ts + p0) * H + r.h] : 1.f;
-        const float a1 = p1 < r.L ? p.alpha[(r.ts + p1) * H + r.h] : 1.f;
-        const float b0 = p0 < r.L ? p.beta[(r.ts + p0) * H + r.h] : 0.f;
-        const float b1 = p1 < r.L ? p.beta[(r.ts + p1) * H + r.h] : 0.f;
+        const float a0 = in.a0, a1 = in.a1, b0 = in.b0, b1 = in.b1;
         const bool nz0 = a0 >= 1.17549435e-38f, nz1 = a1 >= 1.17549435e-38f;
         const float l0 = nz0 ? lg2(a0) : 0.f, l1 = nz1 ? lg2(a1) : 0.f;
         const int z0 = nz0 ? 0 : 1, z1 = nz1 ? 0 : 1;
@@ -526,7 +545,7 @@ __global__ void __launch_bounds__(NT, 1)
     // Everything chunk k needs before its first SIMT phase: gate tables, its
     // tiles landed and converted to fp16, and D1 = [K; Q] K^T issued.
     auto prepare = [&](int k, const Ref &r) -> bool {
-        if (warp == 0) gate_tables(k, r);
+        if (warp == 0) gate_tables(k, gate_fetch(r));
         const bool ok = mbar_wait(&bar_load[k & 1], (k >> 1) & 1);
         if (__syncthreads_or(!ok)) return false;
         ++loads_waited;
@@ -539,12 +558,14 @@ __global__ void __launch_bounds__(NT, 1)
 
     // Prime: tiles of the first two chunks, then chunk 0's preparation.
     Ref cur = first_from(blockIdx.x);
+    GateIn gin{1.f, 1.f, 0.f, 0.f};  // warp 4: gate inputs of the next chunk
     {
         const Ref second = cur.item >= 0 ? next_of(cur) : cur;
         if (tid == 0) {
             if (cur.item >= 0) issue_loads(0, cur);
             if (second.item >= 0) issue_loads(1, second);
         }
+        if (warp == 4) gin = gate_fetch(second);
         loads_issued = (cur.item >= 0) + (second.item >= 0);
         if (cur.item >= 0 && !prepare(0, cur)) failed = true;
     }
@@ -638,8 +659,8 @@ __global__ void __launch_bounds__(NT, 1)
             __syncthreads();
 
             // ---- diagonal 16 x 16 tiles of T (warps 0-3, one each) while warps
-            // 4-7 zero tiles (0,1), (2,3) of T and prepare the next chunk: its
-            // gate tables (warp 4), its tiles converted to fp16
+            // 4-7 zero tiles (0,1), (2,3) of T and convert the next chunk's
+            // tiles to fp16
             const Ref nxt = next_of(Ref{item, ts, L, h});
             bool prep_fail = false;
             if (warp < 4) {
@@ -650,7 +671,6 @@ __global__ void __launch_bounds__(NT, 1)
                     Tf[(32 * blk + rr) * AST + 32 * blk + 16 + cc] = 0.f;
                 }
                 if (nxt.item >= 0) {
-                    if (warp == 4) gate_tables(k + 1, nxt);
                     prep_fail = !mbar_wait(&bar_load[(k + 1) & 1], ((k + 1) >> 1) & 1);
                     if (!prep_fail)
                         tiles_to_f16(smem + OFF_KQ + ((k + 1) & 1) * KQ_STAGE,
@@ -713,6 +733,12 @@ __global__ void __launch_bounds__(NT, 1)
                 }
             }
             mma_commit();
+            // The next chunk's gate table under these products (off the solve's
+            // path), and the gate inputs of the chunk after it.
+            if (warp == 4 && nxt.item >= 0) {
+                gate_tables(k + 1, gin);
+                gin = gate_fetch(next_of(nxt));
+            }
             if (!mma_wait()) { failed = true; break; }
             {
                 float x[32];

@@ -1028,8 +1028,8 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             __syncthreads();
 
             // ---- diagonal 16 x 16 tiles of T (warps 0-3, one each) while warps
-            // 4-7 zero tiles (0,1), (2,3) of T, build the next gate table and
-            // wait for the next chunk's tiles
+            // 4-7 zero tiles (0,1), (2,3) of T and wait for the next chunk's
+            // tiles
             const Ref nxt = wk.next_of(Ref{item, ts, L, h});
             const Ref nn = nxt.item >= 0 ? wk.next_of(nxt) : nxt;
             bool prep_fail = false;
@@ -1041,13 +1041,7 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                     const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
                     Tf[(32 * blk + rr) * AST + 32 * blk + 16 + cc] = 0.f;
                 }
-                if (nxt.item >= 0) {
-                    if (warp == 4) {
-                        gate_tables(gates(k + 1), gin, lane);
-                        gin = gate_load(p, nn, lane);
-                    }
-                    prep_fail = !mbar_wait(&bar_load[(k + 1) & 1], ((k + 1) >> 1) & 1);
-                }
+                if (nxt.item >= 0) prep_fail = !mbar_wait(&bar_load[(k + 1) & 1], ((k + 1) >> 1) & 1);
             }
             if (__syncthreads_or(prep_fail)) { rs.failed = true; break; }
             if (nxt.item >= 0) {
@@ -1100,6 +1094,13 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                              sdesc_sw128(sbase + P_OFF_TH + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
                              ID_MK64_BF, kk > 0);
                 umma_commit(bar_mma);
+            }
+            // The next chunk's gate table, under D_W (off the solve's path:
+            // executed once per chunk by one warp, it ran mostly on
+            // instruction-fetch stalls)
+            if (warp == 4 && nxt.item >= 0) {
+                gate_tables(gates(k + 1), gin, lane);
+                gin = gate_load(p, nn, lane);
             }
             {
                 const bool ok = mbar_wait(bar_mma, mma_phase);
