@@ -36,6 +36,7 @@ sys.path.insert(0, ROOT)
 B, T, H, D, CHUNK = 4, 4096, 16, 128, 64
 FLOP_PER_TOKEN_HEAD = 6 * D * D + 2 * CHUNK * (3 * D + 2 * D) + (2 / 3) * CHUNK * CHUNK  # 182,955
 DEC_N, DEC_SLOTS = 512, 1024
+VL_N, VL_SLOTS = 64, 96
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
 # the chunked kernel on this workload, from an ncu capture of that launch.
@@ -57,6 +58,12 @@ def algorithmic_bytes(b, t, h, d, with_state_in=False):
     per = 3 * d * 2 + d * 2 + 8  # q, k, v, o (bf16) + alpha, beta (f32)
     states = b * h * d * d * 4 * (2 if with_state_in else 1)
     return tok_heads * per + states
+
+
+def solo_form(items, sms):
+    """The library's choice between its two chunked forms (launch_chunk_tc)."""
+    pairs = max(sms // 2, 1)
+    return 10 * -(-items // pairs) > 16 * -(-items // sms)
 
 
 def decode_bytes(n, h, d):
@@ -439,6 +446,86 @@ def run_ours(args):
                             "unit": "GB/s", "frac": round(ggbs / peaks["hbm_gbs"], 4),
                             "kernel": "groupnorm_heads_kernel", "algorithmic_bytes": gbytes}}
 
+    # Varlen packed prefill: 64 sequences with seeded lengths
+    # U{1..8192} in one packed stream, H=16, each from its own N(0, 0.02^2)
+    # slot state, final states written back. Timed per launch.
+    import numpy as np
+    vl = np.random.default_rng(8192 + rank).integers(1, 8193, size=VL_N)
+    vcu = torch.tensor(np.concatenate([[0], np.cumsum(vl)]), dtype=torch.int32, device=dev)
+    vtok = int(vl.sum())
+    gv = torch.Generator(device=dev).manual_seed(31 + rank)
+    nrm = torch.nn.functional.normalize
+    vq = nrm(torch.randn((vtok, H, D), device=dev, generator=gv), dim=-1).to(torch.bfloat16)
+    vk = nrm(torch.randn((vtok, H, D), device=dev, generator=gv), dim=-1).to(torch.bfloat16)
+    vv = torch.randn((vtok, H, D), device=dev, generator=gv).to(torch.bfloat16)
+    vb = torch.sigmoid(torch.randn((vtok, H), device=dev, generator=gv))
+    va = torch.exp(-torch.nn.functional.softplus(torch.randn((vtok, H), device=dev, generator=gv) + 2))
+    vpool = torch.randn((VL_SLOTS, H, D, D), device=dev, generator=gv) * 0.02
+    vslots = torch.randperm(VL_SLOTS, device=dev, generator=gv)[:VL_N].to(torch.int32)
+    vo = torch.empty_like(vq)
+
+    def varlen():
+        capi.call("rhz_gdr_varlen_fwd", vo.data_ptr(), vpool.data_ptr(), vslots.data_ptr(),
+                  vcu.data_ptr(), vq.data_ptr(), vk.data_ptr(), vv.data_ptr(), va.data_ptr(),
+                  vb.data_ptr(), VL_N, vtok, VL_SLOTS, H, D, capi.RHZ_DTYPE_BF16, 0, sptr)
+
+    vl_ms = timed(varlen, 5)
+    vbytes = vtok * H * (3 * D * 2 + D * 2 + 8) + VL_N * H * D * D * 4 * 2
+    vflops = FLOP_PER_TOKEN_HEAD * vtok * H
+    vgbs = vbytes / (vl_ms / 1e3) / 1e9
+    vtf = vflops / (vl_ms / 1e3) / 1e12
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    varlen_line = {
+        "metric": "GDR varlen prefill tokens/s", "value": vtok * world / (vl_ms / 1e3),
+        "unit": "tokens/s", "ms_per_step": round(vl_ms, 4),
+        "config": {"sequences": VL_N, "tokens": vtok, "lengths": "U{1..8192}, seeded",
+                   "heads": H, "head_dim": D, "slots": VL_SLOTS,
+                   "kernel_form": "one CTA per item" if solo_form(VL_N * H, sms) else "2-CTA cluster"},
+        "roofline": {"bound": "hbm", "achieved": round(vgbs, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(vgbs / peaks["hbm_gbs"], 4),
+                     "algorithmic_bytes": vbytes, "algorithmic_flops": vflops,
+                     "tensor": {"achieved": round(vtf, 1), "peak": peaks["bf16_tflops"],
+                                "unit": "TFLOP/s", "frac": round(vtf / peaks["bf16_tflops"], 4)}}}
+    del vq, vk, vv, vo
+
+    # Varlen packing (the index/byte work beside the recurrence): slot states
+    # gathered into a dense batch (the decode pool's shape), and padded token
+    # rows packed by cu_seqlens (the varlen prefill's stream).
+    gdense = torch.empty((DEC_N, H, D, D), device=dev)
+
+    def gather():
+        capi.call("rhz_varlen_gather_states", gdense.data_ptr(), pool.data_ptr(), slots.data_ptr(),
+                  DEC_N, DEC_SLOTS, H, D, sptr)
+
+    ga_ms = timed(gather, 20)
+    gabytes = 2 * DEC_N * H * D * D * 4
+    row_bytes = H * D * 2
+    padded = torch.empty((VL_N, 8192, H, D), device=dev, dtype=torch.bfloat16)
+    packed = torch.empty((vtok, H, D), device=dev, dtype=torch.bfloat16)
+
+    def pack():
+        capi.call("rhz_varlen_pack_tokens", packed.data_ptr(), padded.data_ptr(), vcu.data_ptr(),
+                  VL_N, 8192, row_bytes, sptr)
+
+    pk_ms = timed(pack, 20)
+    pkbytes = 2 * vtok * row_bytes
+    del padded, packed, gdense
+    ga_gbs = gabytes / (ga_ms / 1e3) / 1e9
+    pk_gbs = pkbytes / (pk_ms / 1e3) / 1e9
+    packing = {
+        "gather_states": {"ms": round(ga_ms, 4), "config": f"{DEC_N} x {H} states of {D}x{D} f32 "
+                          f"from a {DEC_SLOTS}-slot pool", "algorithmic_bytes": gabytes,
+                          "roofline": {"bound": "hbm", "achieved": round(ga_gbs, 1),
+                                       "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                       "frac": round(ga_gbs / peaks["hbm_gbs"], 4),
+                                       "kernel": "gather_states_kernel"}},
+        "pack_tokens": {"ms": round(pk_ms, 4), "config": f"{vtok} rows of {row_bytes} B from "
+                        f"[{VL_N}, 8192] padded", "algorithmic_bytes": pkbytes,
+                        "roofline": {"bound": "hbm", "achieved": round(pk_gbs, 1),
+                                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                     "frac": round(pk_gbs / peaks["hbm_gbs"], 4),
+                                     "kernel": "pack_tokens_kernel"}}}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
@@ -463,7 +550,8 @@ def run_ours(args):
                     "call": f"rhz_gdr_scan_chunked_host, pinned host buffers, {n_slabs} slabs "
                             f"of {slab} positions pipelined"},
             "gpu_launches": args.steps, "clocks": clock_info, "decode": decode,
-            "producer": producer, "output_norm": outnorm,
+            "producer": producer, "output_norm": outnorm, "varlen_prefill": varlen_line,
+            "packing": packing,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -558,6 +646,77 @@ def _timed_compute(x, ev_done, stream):
     return out
 
 
+def run_case(args):
+    """--case NAME: warm-up + --steps launches of one kernel at a size meant
+    for an ncu capture (inputs above L2, a few GB at most), timed with CUDA
+    events. Not a benchmark line: a fixed launch sequence to profile."""
+    import torch
+    from rhizome_b200 import capi, ops
+    dev = torch.device("cuda", 0)
+    capi.lib()
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    g = torch.Generator(device=dev).manual_seed(77)
+    nrm = torch.nn.functional.normalize
+
+    def qkv(*shape):
+        q = nrm(torch.randn(shape, device=dev, generator=g), dim=-1).to(torch.bfloat16)
+        k = nrm(torch.randn(shape, device=dev, generator=g), dim=-1).to(torch.bfloat16)
+        v = torch.randn(shape, device=dev, generator=g).to(torch.bfloat16)
+        b = torch.sigmoid(torch.randn(shape[:-1], device=dev, generator=g))
+        a = torch.exp(-torch.nn.functional.softplus(torch.randn(shape[:-1], device=dev, generator=g) + 2))
+        return q, k, v, a, b
+
+    if args.case == "decode":  # configs[2]: 512 sequences x 16 heads, 1024-slot pool
+        q, k, v, a, b = qkv(DEC_N, H, D)
+        pool = torch.randn((DEC_SLOTS, H, D, D), device=dev, generator=g) * 0.02
+        slots = torch.randperm(DEC_SLOTS, device=dev, generator=g)[:DEC_N].to(torch.int32)
+        o = torch.empty_like(q)
+
+        def fn():
+            capi.call("rhz_gdr_step", o.data_ptr(), pool.data_ptr(), slots.data_ptr(), q.data_ptr(),
+                      k.data_ptr(), v.data_ptr(), a.data_ptr(), b.data_ptr(), DEC_N, DEC_SLOTS, H, D,
+                      capi.RHZ_DTYPE_BF16, sptr)
+    elif args.case == "gather":  # 512 x 16 states out of the 1024-slot pool
+        pool = torch.randn((DEC_SLOTS, H, D, D), device=dev, generator=g)
+        slots = torch.randperm(DEC_SLOTS, device=dev, generator=g)[:DEC_N].to(torch.int32)
+        dense = torch.empty((DEC_N, H, D, D), device=dev)
+
+        def fn():
+            capi.call("rhz_varlen_gather_states", dense.data_ptr(), pool.data_ptr(),
+                      slots.data_ptr(), DEC_N, DEC_SLOTS, H, D, sptr)
+    elif args.case == "pack":  # 16 sequences, lengths U{1..8192}, rows of H x d bf16
+        import numpy as np
+        lens = np.random.default_rng(5).integers(1, 8193, size=16)
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
+        padded = torch.randn((16, 8192, H, D), device=dev, generator=g).to(torch.bfloat16)
+        packed = torch.empty((int(lens.sum()), H, D), device=dev, dtype=torch.bfloat16)
+
+        def fn():
+            capi.call("rhz_varlen_pack_tokens", packed.data_ptr(), padded.data_ptr(), cu.data_ptr(),
+                      16, 8192, H * D * 2, sptr)
+    elif args.case in ("pair", "solo"):  # the two forms of the chunked kernel
+        Bc, Tc, Hc = (4, 4096, 16) if args.case == "pair" else (8, 1024, 64)
+        q, k, v, a, b = qkv(Bc, Tc, Hc, D)
+        ops.set_chunk_kernel(args.case)
+
+        def fn():
+            ops.gdr_scan_chunked(q, k, v, a, b)
+    else:
+        raise SystemExit(f"unknown case {args.case}")
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(args.steps):
+        fn()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    print(json.dumps({"case": args.case, "ms_per_launch": s0.elapsed_time(s1) / args.steps}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -568,11 +727,15 @@ def main():
                     help="prefill: the headline chunked-prefill batch (weak scaling over "
                          "ranks); layer: the full head-sharded layer with its all-gather")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--case", default=None, choices=["decode", "gather", "pack", "pair", "solo"],
+                    help="launch one kernel at a profiling size instead of the benchmark")
     ap.add_argument("--traffic", type=float, default=None,
                     help="measured DRAM bytes per launch of the dominant kernel (ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.case:
+        return run_case(args)
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "layer":
