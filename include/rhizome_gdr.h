@@ -71,7 +71,9 @@ enum rhz_dtype { RHZ_DTYPE_F32 = 0, RHZ_DTYPE_BF16 = 1 };
 /* Message of this thread's last failing call ("" if none). Never NULL. */
 const char *rhz_last_error(void);
 
-/* ABI version of this header (major * 100 + minor). */
+/* ABI version of this header (major * 100 + minor). 1.1 added the
+ * host-buffer scan, the device status query and the chunked-form setting. */
+#define RHZ_ABI_VERSION 101
 int rhz_abi_version(void);
 
 /*

@@ -224,7 +224,7 @@ extern "C" {
 
 const char *rhz_last_error(void) { return g_last_error; }
 
-int rhz_abi_version(void) { return 100; }
+int rhz_abi_version(void) { return RHZ_ABI_VERSION; }
 
 int rhz_device_status(int32_t *timed_out, int clear) {
     clear_error();

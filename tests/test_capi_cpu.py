@@ -48,7 +48,61 @@ def test_library_does_not_depend_on_torch_or_libcuda():
 
 
 def test_abi_version(lib):
-    assert lib.rhz_abi_version() == 100
+    hdr = open(os.path.join(ROOT, "include", "rhizome_gdr.h")).read()
+    declared = int(re.search(r"#define RHZ_ABI_VERSION (\d+)", hdr).group(1))
+    assert lib.rhz_abi_version() == declared == 101
+
+
+def test_chunk_form_setting_without_gpu(lib):
+    prev = C.c_int32(-1)
+    assert lib.rhz_gdr_set_chunk_kernel(7, C.byref(prev)) == capi.RHZ_ERR_INVALID
+    assert b"variant 7" in lib.rhz_last_error()
+    assert lib.rhz_gdr_set_chunk_kernel(capi.RHZ_CHUNK_SOLO, C.byref(prev)) == capi.RHZ_OK
+    assert prev.value == capi.RHZ_CHUNK_AUTO
+    assert lib.rhz_gdr_set_chunk_kernel(capi.RHZ_CHUNK_AUTO, C.byref(prev)) == capi.RHZ_OK
+    assert prev.value == capi.RHZ_CHUNK_SOLO
+    assert lib.rhz_gdr_set_chunk_kernel(capi.RHZ_CHUNK_AUTO, None) == capi.RHZ_OK
+
+
+def test_device_status_without_gpu(lib):
+    assert lib.rhz_device_status(None, 0) == capi.RHZ_ERR_INVALID
+    flag = C.c_int32(0)
+    assert lib.rhz_device_status(C.byref(flag), 0) == capi.RHZ_ERR_DEVICE
+
+
+def test_host_entry_without_gpu(lib):
+    """The host-buffer scan validates on the host; T = 0 is answered there
+    (the reference returns the initial state, delta.rs:135)."""
+    import numpy as np
+    B, H, d = 2, 3, 8
+    init = np.arange(B * H * d * d, dtype=np.float32)
+    fin = np.zeros_like(init)
+    ptr = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
+    st = lib.rhz_gdr_scan_chunked_host(FAKE, ptr(fin), FAKE, FAKE, FAKE, FAKE, FAKE, None,
+                                       ptr(init), 64, B, 0, H, d, capi.RHZ_DTYPE_F32, None, 0,
+                                       None)
+    assert st == capi.RHZ_OK and np.array_equal(fin, init)
+    st = lib.rhz_gdr_scan_chunked_host(FAKE, ptr(fin), FAKE, FAKE, FAKE, FAKE, FAKE, None, None,
+                                       64, B, 0, H, d, capi.RHZ_DTYPE_F32, None, 0, None)
+    assert st == capi.RHZ_OK and not fin.any()
+    # sizes and arguments checked before any device work
+    args = lambda B, T, ws, nb: (FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, None, None, 64, B, T,  # noqa: E731
+                                 H, d, capi.RHZ_DTYPE_BF16, ws, nb, None)
+    assert lib.rhz_gdr_scan_chunked_host(*args(70000, 4, FAKE, 1 << 40)) == capi.RHZ_ERR_SHAPE
+    assert lib.rhz_gdr_scan_chunked_host(*args(2, 300, FAKE, 16)) == capi.RHZ_ERR_INVALID
+    assert b"workspace too small" in lib.rhz_last_error()
+    assert lib.rhz_gdr_scan_chunked_host(*args(-1, 4, FAKE, 16)) == capi.RHZ_ERR_SHAPE
+    assert lib.rhz_gdr_scan_chunked_host(None, *args(2, 4, FAKE, 16)[1:]) == capi.RHZ_ERR_INVALID
+    # workspace: 3 slab sets + 2 pools + whole gates + piece tables
+    w = lib.rhz_gdr_host_workspace_bytes
+    assert w(-1, 4, H, d, 1, 0) == 0 and w(2, 4, H, d, 9, 0) == 0
+    b0, b1 = w(4, 4096, 16, 128, 1, 0), w(4, 4096, 16, 128, 1, 1)
+    slab = 512
+    sets = 3 * (4 * 4 * slab * 16 * 128 * 2 + 2 * 4 * slab * 16 * 4)
+    assert b0 >= sets + 2 * 4 * 16 * 128 * 128 * 4 + 2 * 4 * 4096 * 16 * 4
+    assert b1 > b0  # a segment change can split a slab row into more pieces
+    # with a valid workspace size the call needs a device
+    assert lib.rhz_gdr_scan_chunked_host(*args(2, 300, FAKE, w(2, 300, H, d, 1, 0))) == capi.RHZ_ERR_DEVICE
 
 
 FAKE = 1 << 20  # an aligned non-null address; never dereferenced by validation
