@@ -526,6 +526,30 @@ def run_ours(args):
                                      "frac": round(pk_gbs / peaks["hbm_gbs"], 4),
                                      "kernel": "pack_tokens_kernel"}}}
 
+    # Backward of the scan at the prefill shape (fp32 reverse scan with state
+    # checkpoints every 8 positions): latency-bound, reported for its time.
+    dO = torch.randn((B, T, H, D), device=dev, generator=gp).to(torch.bfloat16)
+    bws_bytes = int(capi.lib().rhz_gdr_bwd_workspace_bytes(B, T, H, D))
+    bws = torch.empty(bws_bytes, device=dev, dtype=torch.uint8)
+    gq, gk, gv = torch.empty_like(xq), torch.empty_like(xq), torch.empty_like(xq)
+    ga, gb = torch.empty_like(bl), torch.empty_like(bl)
+    q0, k0, v0, a0, b0 = sets[0]
+
+    def bwd():
+        capi.call("rhz_gdr_scan_chunked_bwd", gq.data_ptr(), gk.data_ptr(), gv.data_ptr(),
+                  ga.data_ptr(), gb.data_ptr(), q0.data_ptr(), k0.data_ptr(), v0.data_ptr(),
+                  a0.data_ptr(), b0.data_ptr(), None, dO.data_ptr(), None, B, T, H, D,
+                  capi.RHZ_DTYPE_BF16, bws.data_ptr(), bws_bytes, sptr)
+
+    bw_ms = timed(bwd, 3)
+    backward = {"metric": "GDR backward tokens/s", "value": B * T * world / (bw_ms / 1e3),
+                "unit": "tokens/s", "ms_per_step": round(bw_ms, 4),
+                "config": {"workload": f"backward of the chunked prefill B={B} T={T} H={H} d={D}",
+                           "dtype": "bf16 inputs and gradients, fp32 arithmetic"},
+                "bound": "latency (a sequential reverse scan per (sequence, head) row block)",
+                "kernel": "gdr_bwd_kernel"}
+    del dO, bws, gq, gk, gv
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
@@ -551,7 +575,7 @@ def run_ours(args):
                             f"of {slab} positions pipelined"},
             "gpu_launches": args.steps, "clocks": clock_info, "decode": decode,
             "producer": producer, "output_norm": outnorm, "varlen_prefill": varlen_line,
-            "packing": packing,
+            "packing": packing, "backward": backward,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
