@@ -305,76 +305,96 @@ __global__ void __launch_bounds__(32 * TWARPS, 3) gdr_prep_tile_kernel(const Pre
         int64_t t0 = 0, t1 = -1, slot = -1;
         bool have = false, covered = false;
         float win[3][4];  // [sample, oldest first][channel]
+        // In groups of HB tokens: pass 1, the conv outputs (the window slides
+        // along them); pass 2, their L2 norms, HB shuffle trees side by side;
+        // pass 3, the stores. (One token at a time, each norm's five dependent
+        // shuffles sat on the path of every row.)
+        constexpr int HB = 4;
+#pragma unroll 1
+        for (int jb = 0; jb < PER; jb += HB) {
+            float y[HB][4];
+            float ss[HB];
+            bool ok[HB];
 #pragma unroll
-        for (int j = 0; j < PER; ++j) {
-            if (j >= nt) break;
-            const int64_t tok = ta + j;
-            if (j == 0 || tok >= t1 || !covered) {  // the sequence holding this row
-                int64_t seq;
-                if (p.cu_seqlens) {
-                    int64_t lo = 0, hi = p.n_seq - 1;
-                    while (lo < hi) {
-                        const int64_t mid = (lo + hi + 1) >> 1;
-                        if (static_cast<int64_t>(p.cu_seqlens[mid]) <= tok) lo = mid;
-                        else hi = mid - 1;
+            for (int jj = 0; jj < HB; ++jj) {
+                const int j = jb + jj;
+                ok[jj] = false;
+                ss[jj] = 0.f;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) y[jj][e] = 0.f;
+                if (j >= nt) continue;
+                const int64_t tok = ta + j;
+                if (j == 0 || tok >= t1 || !covered) {  // the sequence holding this row
+                    int64_t seq;
+                    if (p.cu_seqlens) {
+                        int64_t lo = 0, hi = p.n_seq - 1;
+                        while (lo < hi) {
+                            const int64_t mid = (lo + hi + 1) >> 1;
+                            if (static_cast<int64_t>(p.cu_seqlens[mid]) <= tok) lo = mid;
+                            else hi = mid - 1;
+                        }
+                        seq = lo;
+                        t0 = p.cu_seqlens[lo];
+                        t1 = p.cu_seqlens[lo + 1];
+                        t0 = t0 < 0 ? 0 : t0;  // offsets are caller data
+                        covered = tok >= t0 && tok < t1;
+                    } else {
+                        seq = tok / p.seq_len;
+                        t0 = seq * p.seq_len;
+                        t1 = t0 + p.seq_len;
+                        covered = true;
                     }
-                    seq = lo;
-                    t0 = p.cu_seqlens[lo];
-                    t1 = p.cu_seqlens[lo + 1];
-                    t0 = t0 < 0 ? 0 : t0;  // offsets are caller data
-                    covered = tok >= t0 && tok < t1;
-                } else {
-                    seq = tok / p.seq_len;
-                    t0 = seq * p.seq_len;
-                    t1 = t0 + p.seq_len;
-                    covered = true;
-                }
-                slot = p.slots ? static_cast<int64_t>(p.slots[seq]) : seq;
-                have = p.conv_state && !p.zero_init && slot >= 0 && slot < p.num_slots;
-                if (covered && active) {
+                    slot = p.slots ? static_cast<int64_t>(p.slots[seq]) : seq;
+                    have = p.conv_state && !p.zero_init && slot >= 0 && slot < p.num_slots;
+                    if (covered && active) {
 #pragma unroll
-                    for (int m = 0; m < 3; ++m) {
-                        const int64_t t = tok - 3 + m;
-                        if (t >= t0) {
-                            load4(rows + (a * (TT + 3) + static_cast<int>(t - tok0 + 3)) * d + c0, true, 4, win[m]);
-                        } else if (have) {
-                            const float *st = p.conv_state + (((slot * 3 + a) * H + h) * d + c0) * 3;
+                        for (int m = 0; m < 3; ++m) {
+                            const int64_t t = tok - 3 + m;
+                            if (t >= t0) {
+                                load4(rows + (a * (TT + 3) + static_cast<int>(t - tok0 + 3)) * d + c0, true, 4, win[m]);
+                            } else if (have) {
+                                const float *st = p.conv_state + (((slot * 3 + a) * H + h) * d + c0) * 3;
 #pragma unroll
-                            for (int e = 0; e < 4; ++e) win[m][e] = st[3 * e + 3 + (t - t0)];
-                        } else {
+                                for (int e = 0; e < 4; ++e) win[m][e] = st[3 * e + 3 + (t - t0)];
+                            } else {
 #pragma unroll
-                            for (int e = 0; e < 4; ++e) win[m][e] = 0.f;
+                                for (int e = 0; e < 4; ++e) win[m][e] = 0.f;
+                            }
                         }
                     }
                 }
-            }
-            if (!covered) continue;  // a row that no sequence covers
-            float y[4] = {0.f, 0.f, 0.f, 0.f};
-            float ss = 0.f;
-            if (active) {
-                float x[4];
-                load4(rows + (a * (TT + 3) + static_cast<int>(tok - tok0) + 3) * d + c0, true, 4, x);
+                if (!covered) continue;  // a row that no sequence covers
+                ok[jj] = true;
+                if (active) {
+                    float x[4];
+                    load4(rows + (a * (TT + 3) + static_cast<int>(tok - tok0) + 3) * d + c0, true, 4, x);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    // weight[0] state[0] + weight[1] state[1] + weight[2] state[2] + weight[3] x + bias
-                    y[e] = w[e][0] * win[0][e] + w[e][1] * win[1][e] + w[e][2] * win[2][e] +
-                           w[e][3] * x[e] + bias[e];
-                    win[0][e] = win[1][e];
-                    win[1][e] = win[2][e];
-                    win[2][e] = x[e];
-                    ss += y[e] * y[e];
+                    for (int e = 0; e < 4; ++e) {
+                        // weight[0] state[0] + weight[1] state[1] + weight[2] state[2] + weight[3] x + bias
+                        y[jj][e] = w[e][0] * win[0][e] + w[e][1] * win[1][e] + w[e][2] * win[2][e] +
+                                   w[e][3] * x[e] + bias[e];
+                        win[0][e] = win[1][e];
+                        win[1][e] = win[2][e];
+                        win[2][e] = x[e];
+                        ss[jj] += y[jj][e] * y[jj][e];
+                    }
                 }
             }
-            float mul = 1.f;
             if (a < 2) {
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-                mul = (a == 0 ? p.q_scale : 1.f) / fmaxf(sqrtf(ss), 1e-12f);
+                for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+                    for (int jj = 0; jj < HB; ++jj) ss[jj] += __shfl_xor_sync(0xffffffffu, ss[jj], off);
+                }
             }
-            if (active) {
+#pragma unroll
+            for (int jj = 0; jj < HB; ++jj) {
+                if (!ok[jj] || !active) continue;
+                const int64_t tok = ta + jb + jj;
+                const float mul = a < 2 ? (a == 0 ? p.q_scale : 1.f) / fmaxf(sqrtf(ss[jj]), 1e-12f) : 1.f;
                 float o[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) o[e] = a < 2 ? y[e] * mul : y[e];
+                for (int e = 0; e < 4; ++e) o[e] = y[jj][e] * mul;
                 store4(ysel(a) + tok * rs + static_cast<int64_t>(h) * d + c0, o);
             }
         }
