@@ -649,18 +649,18 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 // ---- R1: D_U = V^T (T diag b)^T + S (-W^T) ; D_O[k & 1] = Q~ S^T
                 if (tid == 0) {
                     tc_fence_after();
-#pragma unroll
+#pragma unroll 1
                     for (int kk = 0; kk < 4; ++kk)
                         umma_f16(tmem + TM_U, sdesc_sw128(vb + kk * 2048, 8192, 1024),
                                  sdesc_sw128(rec + REC_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
-#pragma unroll
+#pragma unroll 1
                     for (int kk = 0; kk < 8; ++kk) {
                         const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
                         umma_f16(tmem + TM_U, sdesc_sw128(sbase + C_OFF_S + off, 16, 1024),
                                  sdesc_sw128(rec + REC_WT + kk * 2048, 8192, 1024), ID_KM64, 1);
                     }
                     umma_commit(bar_r1);  // Delta^T is ready; D_O runs on behind it
-#pragma unroll
+#pragma unroll 1
                     for (int kk = 0; kk < 8; ++kk) {
                         const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
                         umma_f16(tO, sdesc_sw128(kq + off + 8192, 16, 1024),
@@ -688,12 +688,12 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 // part only), then D_O[k & 1] += M Delta
                 if (tid == 0) {
                     tc_fence_after();
-#pragma unroll
+#pragma unroll 1
                     for (int kk = 0; kk < 4; ++kk)
                         umma_f16(tmem + TM_S, sdesc_sw128(sbase + C_OFF_DT + kk * 32, 16, 1024),
                                  sdesc_sw128(kq + kk * 2048, 16384, 1024), ID_KM128, 1);
                     umma_commit(bar_r2s);
-#pragma unroll
+#pragma unroll 1
                     for (int kk = 0; kk < 4; ++kk)
                         umma_f16(tO, sdesc_sw128(rec + REC_M + kk * 32, 16, 1024),
                                  sdesc_sw128(sbase + C_OFF_DT + kk * 32, 16, 1024), ID_O, 1);
@@ -922,9 +922,14 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         tma_load_3d(kq + 24576, tm_q, 64, r.h, t32, bar);
     };
     // D1 = [K; Q] K^T of chunk kc on its bf16 tiles.
+    // The MMA-issue loops of both roles stay rolled: the per-chunk code of a
+    // role is larger than the instruction cache keeps warm, and a rolled issue
+    // loop (one thread, eight MMAs) costs nothing on the critical path while
+    // the unrolled copies cost instruction-fetch stalls (4.5% of the kernel on
+    // one box; the one-CTA kernel, with a different footprint, did not gain).
     auto issue_d1 = [&](int kc) {
         const uint32_t kq = sbase + P_OFF_KQ + (kc & 1) * KQ_STAGE;
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < 8; ++kk) {
             const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
             umma_f16(tmem + TM_D1, sdesc_sw128(kq + off, 16, 1024), sdesc_sw128(kq + off, 16, 1024),
@@ -1088,7 +1093,7 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             // ---- D_W = K^T (T diag bg)^T = K^T (hi + lo)^T on bf16 operands
             // (lane j, column t: W[t][j])
             if (tid == 0) {
-#pragma unroll
+#pragma unroll 1
                 for (int kk = 0; kk < 8; ++kk)
                     umma_f16(tmem + TM_W, sdesc_sw128(kq + (kk & 3) * 2048, 16384, 1024),
                              sdesc_sw128(sbase + P_OFF_TH + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
