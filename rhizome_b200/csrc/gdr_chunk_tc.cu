@@ -197,12 +197,19 @@ __device__ __forceinline__ void st_row32_f16(uint8_t *blk, uint32_t row, uint32_
         *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + c)) = pack8_f16(v + 8 * c);
 }
 
-// 32 values as a bf16 pair hi = bf16(v), lo = bf16(v - hi) into two blocks
-// of the same layout as st_row32_f16 (hi + lo carries ~16 mantissa bits).
-__device__ __forceinline__ void st_row32_bf16_split(uint8_t *hi_blk, uint8_t *lo_blk, uint32_t row,
+// 16 values as fp16 into 16-byte chunks c0, c0+1 (same layout as st_row32_f16).
+__device__ __forceinline__ void st_row16_f16(uint8_t *blk, uint32_t row, uint32_t c0, const float *v) {
+    *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0)) = pack8_f16(v);
+    *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + 1)) = pack8_f16(v + 8);
+}
+
+// 16 values as a bf16 pair hi = bf16(v), lo = bf16(v - hi) into chunks c0,
+// c0+1 of row `row` of two blocks of the st_row32_f16 layout (hi + lo
+// carries ~16 mantissa bits).
+__device__ __forceinline__ void st_row16_bf16_split(uint8_t *hi_blk, uint8_t *lo_blk, uint32_t row,
                                                     uint32_t c0, const float *v) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
         uint32_t hi[4], lo[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -999,33 +1006,37 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                 if (half == 1 && (warp & 1) == 0) {
                     if (qk) st_zero32(stg + REC_M, t, 4);
                 } else {
-                    float v[32];
-                    tmem_ld32(trow + TM_D1 + s0, v);
-                    tmem_wait_ld();
                     const float glt = g[G_GL + t];
                     const int zt = gz[t];
                     const float bt = qk ? 1.f : g[G_BE + t];
+#pragma unroll 1
+                    for (int hp = 0; hp < 2; ++hp) {
+                        const int sb = s0 + 16 * hp;
+                        float v[16];
+                        tmem_ld16(trow + TM_D1 + sb, v);
+                        tmem_wait_ld();
 #pragma unroll
-                    for (int j4 = 0; j4 < 8; ++j4) {
-                        const float4 g4 = *reinterpret_cast<const float4 *>(g + G_GL + s0 + 4 * j4);
-                        const int4 z4 = *reinterpret_cast<const int4 *>(gz + s0 + 4 * j4);
-                        const float gs[4] = {g4.x, g4.y, g4.z, g4.w};
-                        const int zs[4] = {z4.x, z4.y, z4.z, z4.w};
+                        for (int j4 = 0; j4 < 4; ++j4) {
+                            const float4 g4 = *reinterpret_cast<const float4 *>(g + G_GL + sb + 4 * j4);
+                            const int4 z4 = *reinterpret_cast<const int4 *>(gz + sb + 4 * j4);
+                            const float gs[4] = {g4.x, g4.y, g4.z, g4.w};
+                            const int zs[4] = {z4.x, z4.y, z4.z, z4.w};
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int j = 4 * j4 + e, s = s0 + j;
-                            const float pv = zs[e] == zt ? ex2(glt - gs[e]) : 0.f;
-                            const bool keep = qk ? (s <= t) : (s < t);
-                            v[j] = keep ? bt * pv * v[j] : 0.f;
+                            for (int e = 0; e < 4; ++e) {
+                                const int j = 4 * j4 + e, s = sb + j;
+                                const float pv = zs[e] == zt ? ex2(glt - gs[e]) : 0.f;
+                                const bool keep = qk ? (s <= t) : (s < t);
+                                v[j] = keep ? bt * pv * v[j] : 0.f;
+                            }
                         }
-                    }
-                    if (qk) {
-                        st_row32_f16(stg + REC_M, t, 4 * half, v);
-                    } else {
+                        if (qk) {
+                            st_row16_f16(stg + REC_M, t, 4 * half + 2 * hp, v);
+                        } else {
 #pragma unroll
-                        for (int j4 = 0; j4 < 8; ++j4)
-                            *reinterpret_cast<float4 *>(Af + t * AST + s0 + 4 * j4) =
-                                make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+                            for (int j4 = 0; j4 < 4; ++j4)
+                                *reinterpret_cast<float4 *>(Af + t * AST + sb + 4 * j4) =
+                                    make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+                        }
                     }
                 }
             }
@@ -1071,21 +1082,25 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                     if (hat) st_zero32(dstb + 8192, t, 4);
                 } else {
                     const float *sc = g + (hat ? G_BG : G_BE);
-                    float v[32];
+#pragma unroll 1
+                    for (int hp = 0; hp < 2; ++hp) {
+                        const int sb = s0 + 16 * hp;
+                        float v[16];
 #pragma unroll
-                    for (int j4 = 0; j4 < 8; ++j4) {
-                        const float4 tv = *reinterpret_cast<const float4 *>(Tf + t * AST + s0 + 4 * j4);
-                        const float4 sv = *reinterpret_cast<const float4 *>(sc + s0 + 4 * j4);
-                        const int s = s0 + 4 * j4;
-                        v[4 * j4 + 0] = s + 0 <= t ? tv.x * sv.x : 0.f;
-                        v[4 * j4 + 1] = s + 1 <= t ? tv.y * sv.y : 0.f;
-                        v[4 * j4 + 2] = s + 2 <= t ? tv.z * sv.z : 0.f;
-                        v[4 * j4 + 3] = s + 3 <= t ? tv.w * sv.w : 0.f;
+                        for (int j4 = 0; j4 < 4; ++j4) {
+                            const float4 tv = *reinterpret_cast<const float4 *>(Tf + t * AST + sb + 4 * j4);
+                            const float4 sv = *reinterpret_cast<const float4 *>(sc + sb + 4 * j4);
+                            const int s = sb + 4 * j4;
+                            v[4 * j4 + 0] = s + 0 <= t ? tv.x * sv.x : 0.f;
+                            v[4 * j4 + 1] = s + 1 <= t ? tv.y * sv.y : 0.f;
+                            v[4 * j4 + 2] = s + 2 <= t ? tv.z * sv.z : 0.f;
+                            v[4 * j4 + 3] = s + 3 <= t ? tv.w * sv.w : 0.f;
+                        }
+                        if (hat)
+                            st_row16_bf16_split(dstb, dstb + 8192, t, 4 * hh + 2 * hp, v);
+                        else
+                            st_row16_f16(dstb, t, 4 * hh + 2 * hp, v);
                     }
-                    if (hat)
-                        st_row32_bf16_split(dstb, dstb + 8192, t, 4 * hh, v);
-                    else
-                        st_row32_f16(dstb, t, 4 * hh, v);
                 }
             }
             operands_ready();
