@@ -436,6 +436,18 @@ __global__ void __launch_bounds__(NT, 1)
         if (tn < t1) return Ref{r.item, tn, static_cast<int>((t1 - tn) < CH ? (t1 - tn) : CH), r.h};
         return first_from(r.item + gridDim.x);
     };
+    // The chunk n steps after chunk c of `item` (bounds [t0, t1), nch chunks,
+    // head h): arithmetic inside the item, the walk only past its end.
+    auto after = [&](int64_t item, int h, int64_t t0, int64_t t1, int nch, int c, int n) -> Ref {
+        const int cc = c + n;
+        if (cc < nch) {
+            const int64_t ts = t0 + static_cast<int64_t>(cc) * CH;
+            return Ref{item, ts, static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH), h};
+        }
+        Ref r = first_from(item + gridDim.x);
+        for (int i = nch; i < cc && r.item >= 0; ++i) r = next_of(r);
+        return r;
+    };
 
     uint32_t mma_phase = 0;
     bool failed = false, mma_pending = false, d1_pending = false;
@@ -661,7 +673,7 @@ __global__ void __launch_bounds__(NT, 1)
             // ---- diagonal 16 x 16 tiles of T (warps 0-3, one each) while warps
             // 4-7 zero tiles (0,1), (2,3) of T and convert the next chunk's
             // tiles to fp16
-            const Ref nxt = next_of(Ref{item, ts, L, h});
+            const Ref nxt = after(item, h, t0, t1, nch, c, 1);
             bool prep_fail = false;
             if (warp < 4) {
                 diag_inverse16(Af + (16 * warp) * AST + 16 * warp, Tf + (16 * warp) * AST + 16 * warp, lane);
@@ -737,7 +749,7 @@ __global__ void __launch_bounds__(NT, 1)
             // path), and the gate inputs of the chunk after it.
             if (warp == 4 && nxt.item >= 0) {
                 gate_tables(k + 1, gin);
-                gin = gate_fetch(next_of(nxt));
+                gin = gate_fetch(after(item, h, t0, t1, nch, c, 2));
             }
             if (!mma_wait()) { failed = true; break; }
             {
@@ -818,7 +830,7 @@ __global__ void __launch_bounds__(NT, 1)
             if (!mma_wait()) { failed = true; break; }
             // The stage of this chunk is free again: fetch the chunk after next.
             if (nxt.item >= 0) {
-                const Ref nn = next_of(nxt);
+                const Ref nn = after(item, h, t0, t1, nch, c, 2);
                 if (nn.item >= 0) {
                     if (tid == 0) issue_loads(k + 2, nn);
                     ++loads_issued;

@@ -498,6 +498,19 @@ struct Walk {
         if (tn < t1) return Ref{r.item, tn, static_cast<int>((t1 - tn) < CH ? (t1 - tn) : CH), r.h};
         return first_from(r.item + stride);
     }
+    // The chunk n steps after chunk c of `item` (bounds [t0, t1), nch chunks,
+    // head h): arithmetic inside the item, the walk only past its end (once
+    // per item rather than once per chunk).
+    __device__ Ref after(int64_t item, int h, int64_t t0, int64_t t1, int nch, int c, int n) const {
+        const int cc = c + n;
+        if (cc < nch) {
+            const int64_t ts = t0 + static_cast<int64_t>(cc) * CH;
+            return Ref{item, ts, static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH), h};
+        }
+        Ref r = first_from(item + stride);
+        for (int i = nch; i < cc && r.item >= 0; ++i) r = next_of(r);
+        return r;
+    }
 };
 
 // Gate inputs of one chunk for one warp (two positions per lane), loaded a
@@ -811,13 +824,13 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
             for (int c = 0; c < nch; ++c, ++k) {
                 const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
                 const int L = static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH);
-                const Ref nxt = wk.next_of(Ref{item, ts, L, h});
-                const Ref nn = nxt.item >= 0 ? wk.next_of(nxt) : nxt;
+                const Ref nxt = wk.after(item, h, t0, t1, nch, c, 1);
+                const Ref nn = wk.after(item, h, t0, t1, nch, c, 2);
 
                 // ---- gate table of chunk k + 2, then the inputs of chunk k + 3
                 if (nn.item >= 0 && ww == 0) {
                     gate_tables(gates(k + 2), gin, lane);
-                    gin = gate_load(p, wk.next_of(nn), lane);
+                    gin = gate_load(p, wk.after(item, h, t0, t1, nch, c, 3), lane);
                 }
                 // ---- chunk k + 1's tiles -> fp16 (under chunk k's products)
                 if (nxt.item >= 0) {
@@ -981,8 +994,6 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         wk.bounds(item, t0, t1);
         const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
         for (int c = 0; c < nch; ++c, ++k) {
-            const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
-            const int L = static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH);
             const uint32_t kq = sbase + P_OFF_KQ + (k & 1) * KQ_STAGE;
             uint8_t *stg = smem + P_OFF_STG + (k & 1) * REC_BYTES;
             const float *g = gates(k);
@@ -1046,8 +1057,8 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             // ---- diagonal 16 x 16 tiles of T (warps 0-3, one each) while warps
             // 4-7 zero tiles (0,1), (2,3) of T and wait for the next chunk's
             // tiles
-            const Ref nxt = wk.next_of(Ref{item, ts, L, h});
-            const Ref nn = nxt.item >= 0 ? wk.next_of(nxt) : nxt;
+            const Ref nxt = wk.after(item, h, t0, t1, nch, c, 1);
+            const Ref nn = wk.after(item, h, t0, t1, nch, c, 2);
             bool prep_fail = false;
             if (warp < 4) {
                 diag_inverse16(Af + (16 * warp) * AST + 16 * warp, Tf + (16 * warp) * AST + 16 * warp, lane);
