@@ -156,6 +156,12 @@ __device__ __forceinline__ void st_row32_f16(uint8_t *blk, uint32_t row, uint32_
         *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + c)) = pack8_f16(v + 8 * c);
 }
 
+// 16 values as fp16 into 16-byte chunks c0, c0+1 (same layout as st_row32_f16).
+__device__ __forceinline__ void st_row16_f16(uint8_t *blk, uint32_t row, uint32_t c0, const float *v) {
+    *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0)) = pack8_f16(v);
+    *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + 1)) = pack8_f16(v + 8);
+}
+
 __device__ __forceinline__ void st_zero32(uint8_t *blk, uint32_t row, uint32_t c0) {
 #pragma unroll
     for (int c = 0; c < 4; ++c)
@@ -638,33 +644,37 @@ __global__ void __launch_bounds__(NT, 1)
                 if (half == 1 && (warp & 1) == 0) {
                     if (qk) st_zero32(smem + OFF_M, t, 4);
                 } else {
-                    float v[32];
-                    tmem_ld32(trow + TM_D1 + s0, v);
-                    tmem_wait_ld();
                     const float glt = sgl[t];
                     const int zt = sz[t];
                     const float bt = qk ? 1.f : sbeta[t];
+#pragma unroll 1
+                    for (int hp = 0; hp < 2; ++hp) {
+                        const int sb = s0 + 16 * hp;
+                        float v[16];
+                        tmem_ld16(trow + TM_D1 + sb, v);
+                        tmem_wait_ld();
 #pragma unroll
-                    for (int j4 = 0; j4 < 8; ++j4) {
-                        const float4 g4 = *reinterpret_cast<const float4 *>(sgl + s0 + 4 * j4);
-                        const int4 z4 = *reinterpret_cast<const int4 *>(sz + s0 + 4 * j4);
-                        const float gs[4] = {g4.x, g4.y, g4.z, g4.w};
-                        const int zs[4] = {z4.x, z4.y, z4.z, z4.w};
+                        for (int j4 = 0; j4 < 4; ++j4) {
+                            const float4 g4 = *reinterpret_cast<const float4 *>(sgl + sb + 4 * j4);
+                            const int4 z4 = *reinterpret_cast<const int4 *>(sz + sb + 4 * j4);
+                            const float gs[4] = {g4.x, g4.y, g4.z, g4.w};
+                            const int zs[4] = {z4.x, z4.y, z4.z, z4.w};
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int j = 4 * j4 + e, s = s0 + j;
-                            const float pv = zs[e] == zt ? ex2(glt - gs[e]) : 0.f;
-                            const bool keep = qk ? (s <= t) : (s < t);
-                            v[j] = keep ? bt * pv * v[j] : 0.f;
+                            for (int e = 0; e < 4; ++e) {
+                                const int j = 4 * j4 + e, s = sb + j;
+                                const float pv = zs[e] == zt ? ex2(glt - gs[e]) : 0.f;
+                                const bool keep = qk ? (s <= t) : (s < t);
+                                v[j] = keep ? bt * pv * v[j] : 0.f;
+                            }
                         }
-                    }
-                    if (qk) {
-                        st_row32_f16(smem + OFF_M, t, 4 * half, v);
-                    } else {
+                        if (qk) {
+                            st_row16_f16(smem + OFF_M, t, 4 * half + 2 * hp, v);
+                        } else {
 #pragma unroll
-                        for (int j4 = 0; j4 < 8; ++j4)
-                            *reinterpret_cast<float4 *>(Af + t * AST + s0 + 4 * j4) =
-                                make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+                            for (int j4 = 0; j4 < 4; ++j4)
+                                *reinterpret_cast<float4 *>(Af + t * AST + sb + 4 * j4) =
+                                    make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+                        }
                     }
                 }
             }
@@ -709,18 +719,22 @@ __global__ void __launch_bounds__(NT, 1)
                     st_zero32(dst, t, 4);
                 } else {
                     const float *sc = hat ? sbg : sbeta;
-                    float v[32];
+#pragma unroll 1
+                    for (int hp = 0; hp < 2; ++hp) {
+                        const int sb = s0 + 16 * hp;
+                        float v[16];
 #pragma unroll
-                    for (int j4 = 0; j4 < 8; ++j4) {
-                        const float4 tv = *reinterpret_cast<const float4 *>(Tf + t * AST + s0 + 4 * j4);
-                        const float4 sv = *reinterpret_cast<const float4 *>(sc + s0 + 4 * j4);
-                        const int s = s0 + 4 * j4;
-                        v[4 * j4 + 0] = s + 0 <= t ? tv.x * sv.x : 0.f;
-                        v[4 * j4 + 1] = s + 1 <= t ? tv.y * sv.y : 0.f;
-                        v[4 * j4 + 2] = s + 2 <= t ? tv.z * sv.z : 0.f;
-                        v[4 * j4 + 3] = s + 3 <= t ? tv.w * sv.w : 0.f;
+                        for (int j4 = 0; j4 < 4; ++j4) {
+                            const float4 tv = *reinterpret_cast<const float4 *>(Tf + t * AST + sb + 4 * j4);
+                            const float4 sv = *reinterpret_cast<const float4 *>(sc + sb + 4 * j4);
+                            const int s = sb + 4 * j4;
+                            v[4 * j4 + 0] = s + 0 <= t ? tv.x * sv.x : 0.f;
+                            v[4 * j4 + 1] = s + 1 <= t ? tv.y * sv.y : 0.f;
+                            v[4 * j4 + 2] = s + 2 <= t ? tv.z * sv.z : 0.f;
+                            v[4 * j4 + 3] = s + 3 <= t ? tv.w * sv.w : 0.f;
+                        }
+                        st_row16_f16(dst, t, 4 * hh + 2 * hp, v);
                     }
-                    st_row32_f16(dst, t, 4 * hh, v);
                 }
             }
             operands_ready();
@@ -753,12 +767,15 @@ __global__ void __launch_bounds__(NT, 1)
             }
             if (!mma_wait()) { failed = true; break; }
             {
-                float x[32];
-                tmem_ld32(trow + TM_W + 32 * half, x);  // W[t][j = row], t in this half
-                tmem_wait_ld();
+#pragma unroll 1
+                for (int hp = 0; hp < 2; ++hp) {
+                    float x[16];
+                    tmem_ld16(trow + TM_W + 32 * half + 16 * hp, x);  // W[t][j = row], t in this half
+                    tmem_wait_ld();
 #pragma unroll
-                for (int t = 0; t < 32; ++t) x[t] = -x[t];
-                st_row32_f16(smem + OFF_WT, row, 4 * half, x);
+                    for (int t = 0; t < 16; ++t) x[t] = -x[t];
+                    st_row16_f16(smem + OFF_WT, row, 4 * half + 2 * hp, x);
+                }
             }
             operands_ready();
 
@@ -774,16 +791,19 @@ __global__ void __launch_bounds__(NT, 1)
             mma_commit();
             if (!mma_wait()) { failed = true; break; }
             {
-                float x[32];
-                tmem_ld32(trow + TM_U + 32 * half, x);  // Delta[s][i = row], s in this half
-                tmem_wait_ld();
-                st_row32_f16(smem + OFF_DT, row, 4 * half, x);
+#pragma unroll 1
+                for (int hp = 0; hp < 2; ++hp) {
+                    float x[16];
+                    tmem_ld16(trow + TM_U + 32 * half + 16 * hp, x);  // Delta[s][i = row]
+                    tmem_wait_ld();
+                    st_row16_f16(smem + OFF_DT, row, 4 * half + 2 * hp, x);
 #pragma unroll
-                for (int j4 = 0; j4 < 8; ++j4) {
-                    const float4 pl = *reinterpret_cast<const float4 *>(spl + 32 * half + 4 * j4);
-                    x[4 * j4] *= pl.x; x[4 * j4 + 1] *= pl.y; x[4 * j4 + 2] *= pl.z; x[4 * j4 + 3] *= pl.w;
+                    for (int j4 = 0; j4 < 4; ++j4) {
+                        const float4 pl = *reinterpret_cast<const float4 *>(spl + 32 * half + 16 * hp + 4 * j4);
+                        x[4 * j4] *= pl.x; x[4 * j4 + 1] *= pl.y; x[4 * j4 + 2] *= pl.z; x[4 * j4 + 3] *= pl.w;
+                    }
+                    st_row16_f16(smem + OFF_DTS, row, 4 * half + 2 * hp, x);
                 }
-                st_row32_f16(smem + OFF_DTS, row, 4 * half, x);
                 // D_S <- gamma_{C-1} D_S before the rank-C update accumulates.
                 const float gC = sgam[63];
 #pragma unroll
