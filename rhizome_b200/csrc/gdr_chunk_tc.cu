@@ -119,7 +119,8 @@ constexpr uint32_t P_OFF_GATE = P_OFF_TF + 64 * AST * 4; // 2 gate tables
 constexpr uint32_t P_OFF_BAR = P_OFF_GATE + 2 * G_BYTES;
 // Producer barriers: tiles landed [2], D1 done, D_W done, chain slot free [2],
 // failure-path drain of every MMA issued.
-constexpr int PB_LOAD = 0, PB_D1 = 2, PB_MMA = 3, PB_EMPTY = 4, PB_DRAIN = 6, PB_NUM = 7;
+constexpr int PB_LOAD = 0, PB_D1 = 2, PB_MMA = 3, PB_EMPTY = 4, PB_DRAIN = 6, PB_DRAIN2 = 7,
+              PB_NUM = 8;
 constexpr uint32_t P_USED = P_OFF_BAR + PB_NUM * 8 + 16;  // + TMEM base
 
 constexpr uint32_t SMEM_USED = C_USED > P_USED ? C_USED : P_USED;
@@ -1071,9 +1072,11 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                 if (nxt.item >= 0) prep_fail = !mbar_wait(&bar_load[(k + 1) & 1], ((k + 1) >> 1) & 1);
             }
             if (__syncthreads_or(prep_fail)) { rs.failed = true; break; }
+            // The next D1 comes from thread 128 (warps 4-7 have no part in the
+            // solve's first step; from thread 0 it delayed warp 0's).
             if (nxt.item >= 0) {
                 ++loads_waited;
-                if (tid == 0) {
+                if (tid == 128) {
                     tc_fence_after();
                     issue_d1(k + 1);
                 }
@@ -1167,9 +1170,13 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
     if (rs.failed && tid == 0) {
         for (int kk = loads_waited; kk < loads_issued; ++kk)
             mbar_wait(&bar_load[kk & 1], (kk >> 1) & 1, 200000000ull);
-        umma_commit(bars + PB_DRAIN);  // every MMA issued, D1 and D_W alike
+        umma_commit(bars + PB_DRAIN);  // every MMA thread 0 issued: D_W and the first D1
         mbar_wait(bars + PB_DRAIN, 0, 200000000ull);
         atomicExch(&g_tc_status, 1);
+    }
+    if (rs.failed && tid == 128) {
+        umma_commit(bars + PB_DRAIN2);  // the later D1s (issued by this thread)
+        mbar_wait(bars + PB_DRAIN2, 0, 200000000ull);
     }
     rs.failed = __syncthreads_or(rs.failed);
     return rs;
