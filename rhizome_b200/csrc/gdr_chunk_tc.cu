@@ -962,6 +962,22 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
     RoleState rs{false};
     uint32_t mma_phase = 0;
     int loads_issued = 0, loads_waited = 0;
+    // Record hand-over of the previous chunk, deferred into this chunk's
+    // first phase (thread 128, whose warp has no table block there).
+    bool ho_pending = false;
+    Ref ho_nn{-1, 0, 0, 0};
+    int ho_k = 0;
+    auto handover = [&]() {
+        if (tid == 128) {
+            tc_fence_after();
+            if (ho_nn.item >= 0) issue_loads(ho_k + 2, ho_nn);
+            const uint32_t slot = ho_k & 1;
+            bulk_copy_to_peer(peer_rec + slot * REC_BYTES, smem + P_OFF_STG + slot * REC_BYTES, REC_BYTES,
+                              peer_full + 8 * slot);
+        }
+        if (ho_nn.item >= 0) ++loads_issued;
+        ho_pending = false;
+    };
     int k = 0;
     GateIn gin{1.f, 1.f, 0.f, 0.f};  // warp 4: inputs of the next chunk's gate table
     {
@@ -1008,6 +1024,7 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                 if (__syncthreads_or(!ok)) { rs.failed = true; break; }
                 tc_fence_after();
             }
+            if (ho_pending) handover();
 
             // ---- A = beta P (K K^T) (fp32) and M = P (Q K^T) (record, fp16), 32 columns per thread
             {
@@ -1157,15 +1174,12 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             // ---- stage k & 1 is free (D1 and D_W are done): fetch chunk k + 2;
             // hand the record to the chain CTA (its slot k & 1 is free: the
             // chain consumed chunk k - 2 before this staging buffer was reused)
-            if (nn.item >= 0) ++loads_issued;
-            if (tid == 0) {
-                tc_fence_after();
-                if (nn.item >= 0) issue_loads(k + 2, nn);
-                const uint32_t slot = k & 1;
-                bulk_copy_to_peer(peer_rec + slot * REC_BYTES, stg, REC_BYTES, peer_full + 8 * slot);
-            }
+            ho_pending = true;
+            ho_nn = nn;
+            ho_k = k;
         }
     }
+    if (!rs.failed && ho_pending) handover();
 
     if (rs.failed && tid == 0) {
         for (int kk = loads_waited; kk < loads_issued; ++kk)
