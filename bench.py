@@ -72,8 +72,9 @@ def decode_bytes(n, h, d):
 
 
 class ClockSampler:
-    """SM clocks and clock-event (throttle) reasons during the timed region,
-    polled through NVML every 5 ms (the timed region can be tens of ms)."""
+    """SM clocks and clock-event (throttle) reasons, polled through NVML
+    every 2 ms while `active` is set: inside the headline timed region and
+    every timed sub-measurement (the headline region alone lasts a few ms)."""
 
     REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown", 0x8),
                ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
@@ -84,6 +85,7 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.samples = []
+        self.active = False
         self._stop = threading.Event()
         self.thread = None
         self.max_mhz = None
@@ -118,13 +120,15 @@ class ClockSampler:
     def _run(self):
         N = self.N
         while not self._stop.is_set():
-            try:
-                mhz = N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)
-                reasons = self.getreasons(self.h)
-                self.samples.append((mhz, reasons))
-            except Exception:
-                pass
-            time.sleep(0.005)
+            if self.active:
+                try:
+                    mhz = N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)
+                    reasons = self.getreasons(self.h)
+                    if self.active:
+                        self.samples.append((mhz, reasons))
+                except Exception:
+                    pass
+            time.sleep(0.002)
 
     def stop(self):
         if self.thread is None:
@@ -140,7 +144,9 @@ class ClockSampler:
                     names.add(nm)
         return {"sm_mhz": statistics.median(m for m, _ in self.samples),
                 "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
-                "reasons": sorted(names), "source": "NVML, 5 ms polling"}
+                "sm_min_mhz": min(m for m, _ in self.samples),
+                "reasons": sorted(names),
+                "source": "NVML, 2 ms polling inside the timed regions"}
 
 
 def dist_setup():
@@ -291,6 +297,7 @@ def run_ours(args):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.active = True
     start.record(stream)
     for i in range(args.steps):
         ev[i][0].record(stream)
@@ -298,9 +305,9 @@ def run_ours(args):
         ev[i][1].record(stream)
     end.record(stream)
     torch.cuda.synchronize()
+    clocks.active = False
     barrier(world)
     torch.cuda.synchronize()
-    clock_info = clocks.stop()
     elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
     kernel_ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
     kernel_ms = max_over_ranks(kernel_ms, world)
@@ -347,11 +354,13 @@ def run_ours(args):
     barrier(world)
     torch.cuda.synchronize()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.active = True
     s2.record(stream)
     for _ in range(e2e_steps):
         e2e_step()
     e2.record(stream)
     torch.cuda.synchronize()
+    clocks.active = False
     e2e_ms = max_over_ranks(s2.elapsed_time(e2), world)
     e2e_value = B * T * world * e2e_steps / (e2e_ms / 1e3)
 
@@ -373,11 +382,13 @@ def run_ours(args):
     torch.cuda.synchronize()
     dsteps = 50
     s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.active = True
     s3.record(stream)
     for _ in range(dsteps):
         dec()
     e3.record(stream)
     torch.cuda.synchronize()
+    clocks.active = False
     dec_ms = max_over_ranks(s3.elapsed_time(e3) / dsteps, world)
     dbytes = decode_bytes(DEC_N, H, D)
     dgbs = dbytes / (dec_ms / 1e3) / 1e9
@@ -396,11 +407,13 @@ def run_ours(args):
             fn()
         torch.cuda.synchronize()
         sa, sb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks.active = True
         sa.record(stream)
         for _ in range(n):
             fn()
         sb.record(stream)
         torch.cuda.synchronize()
+        clocks.active = False
         return max_over_ranks(sa.elapsed_time(sb) / n, world)
 
     xq, xk, xv = sets[0][0], sets[0][1], sets[0][2]
@@ -555,6 +568,9 @@ def run_ours(args):
                 "bound": "latency (a sequential reverse scan per (sequence, head) row block)",
                 "kernel": "gdr_bwd_kernel"}
     del dO, bws, gq, gk, gv
+    # Clock samples from inside the headline timed region and every timed
+    # sub-measurement above (the headline region alone lasts a few ms).
+    clock_info = clocks.stop()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
