@@ -612,7 +612,7 @@ def run_layer(args):
     (NCCL) into [B, T, H*d] on every rank. Total work is fixed: strong scaling."""
     import torch
     from rhizome_b200 import capi
-    from rhizome_b200.layer import gdr_layer_sharded
+    from rhizome_b200.layer import gdr_layer_sharded, gdr_layer_sharded_slabs
 
     world, rank, local = dist_setup()
     dev = torch.device("cuda", local)
@@ -640,8 +640,14 @@ def run_layer(args):
             a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev.append((a0, a1))
             a0.record(stream)
-            out = gdr_layer_sharded(q, k, v, alpha, beta,
-                                    compute=lambda *x: _timed_compute(x, a1, stream))
+            if args.slab:
+                out = gdr_layer_sharded_slabs(q, k, v, alpha, beta, slab=args.slab)
+                a1.record(stream)  # compute and gathers interleave: no split
+            else:
+                out = gdr_layer_sharded(q, k, v, alpha, beta,
+                                        compute=lambda *x: _timed_compute(x, a1, stream))
+        elif args.slab:
+            out = gdr_layer_sharded_slabs(q, k, v, alpha, beta, slab=args.slab)
         else:
             out = gdr_layer_sharded(q, k, v, alpha, beta)
         return out
@@ -670,13 +676,16 @@ def run_layer(args):
             "ms_per_step": elapsed / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "full Local-block GDR layer B=8 T=32768 H=64 d=128, heads "
-                                   "split over ranks, outputs all-gathered (NCCL)",
+                                   "split over ranks, outputs all-gathered (NCCL)"
+                                   + (f", all-gather overlapped in slabs of {args.slab} positions"
+                                      if args.slab else ""),
                        "global_batch": LB, "seq_len": LT, "heads": LH, "head_dim": D,
                        "parallelism": f"heads/{world}"},
-            "kernel_only": {"value": tokens / (comp / 1e3), "unit": "tokens/s",
-                            "ms_per_step": comp},
+            "kernel_only": None if args.slab else {"value": tokens / (comp / 1e3),
+                                                   "unit": "tokens/s", "ms_per_step": comp},
             "allgather": {"bytes_received_per_rank": gathered_bytes,
-                          "ms_per_step": elapsed / args.steps - comp},
+                          "ms_per_step": None if args.slab else elapsed / args.steps - comp,
+                          "overlapped_in_slabs": args.slab or None},
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -780,6 +789,9 @@ def main():
                     help="prefill: the headline chunked-prefill batch (weak scaling over "
                          "ranks); layer: the full head-sharded layer with its all-gather")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--slab", type=int, default=0,
+                    help="--workload layer: overlap the all-gather with compute in slabs of this "
+                         "many positions (a multiple of 64; 0 = one call, then one all-gather)")
     ap.add_argument("--case", default=None, choices=["decode", "gather", "pack", "norm", "pair", "solo"],
                     help="launch one kernel at a profiling size instead of the benchmark")
     ap.add_argument("--traffic", type=float, default=None,

@@ -73,3 +73,99 @@ def gdr_layer_sharded(q, k, v, alpha, beta, group=None, chunk: int = 64,
                            dtype=o_shard.dtype)
     dist.all_gather_into_tensor(gathered, o_shard, group=group)
     return unshard(gathered.view(world, *o_shard.shape)), fin
+
+
+class CudaSlabOps:
+    """Device side of gdr_layer_sharded_slabs: slab rows packed by
+    rhz_varlen_pack_tokens, the scan by rhz_gdr_varlen_fwd with the state
+    carried in a [B, H/G, d, d] pool, outputs unsharded by rhz_heads_unshard
+    and unpacked into the layer output by rhz_varlen_unpack_tokens."""
+
+    def __init__(self, B: int, device):
+        self.device = device
+        self.B = B
+        self._cu = {}
+
+    def rows(self, length: int) -> torch.Tensor:
+        """cu_seqlens of a slab: batch row b holds packed rows [b L, (b+1) L)."""
+        if length not in self._cu:
+            self._cu[length] = torch.arange(0, (self.B + 1) * length, length, device=self.device,
+                                            dtype=torch.int32)
+        return self._cu[length]
+
+    def pack(self, x: torch.Tensor, t0: int, t1: int) -> torch.Tensor:
+        B, T = x.shape[0], x.shape[1]
+        row = x[0, 0].numel() * x.element_size()
+        out = torch.empty((B * (t1 - t0), *x.shape[2:]), device=x.device, dtype=x.dtype)
+        capi.call("rhz_varlen_pack_tokens", out.data_ptr(), x.data_ptr() + t0 * row,
+                  self.rows(t1 - t0).data_ptr(), B, T, row, ops._stream(x.device))
+        return out
+
+    def compute(self, q, k, v, a, b, pool, first: bool, length: int) -> torch.Tensor:
+        o = torch.empty_like(q)
+        H, d = q.shape[1], q.shape[2]
+        flags = 1 if first else 0  # RHZ_FLAG_ZERO_INIT: the reset at t = 0
+        capi.call("rhz_gdr_varlen_fwd", o.data_ptr(), pool.data_ptr(), None,
+                  self.rows(length).data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                  a.data_ptr(), b.data_ptr(), self.B, self.B * length, self.B, H, d,
+                  ops._dt(q), flags, ops._stream(q.device))
+        return o
+
+    def unshard(self, gathered: torch.Tensor) -> torch.Tensor:
+        G, tok, Hs, d = gathered.shape
+        out = torch.empty((tok, G * Hs, d), device=gathered.device, dtype=gathered.dtype)
+        capi.call("rhz_heads_unshard", out.data_ptr(), gathered.data_ptr(), G, tok, G * Hs, d,
+                  gathered.element_size(), ops._stream(gathered.device))
+        return out
+
+    def unpack(self, out: torch.Tensor, slab: torch.Tensor, t0: int, t1: int) -> None:
+        B, T = out.shape[0], out.shape[1]
+        row = out[0, 0].numel() * out.element_size()
+        capi.call("rhz_varlen_unpack_tokens", out.data_ptr() + t0 * row, slab.data_ptr(),
+                  self.rows(t1 - t0).data_ptr(), B, T, row, ops._stream(out.device))
+
+
+def gdr_layer_sharded_slabs(q, k, v, alpha, beta, slab: int = 4096, group=None,
+                            slab_ops=None):
+    """gdr_layer_sharded with the all-gather overlapped: T is cut into slabs
+    (multiples of 64 positions, so the chunking and the result are those of
+    the one-call layer, bitwise on the bf16 kernels), each rank scans slab j
+    of its heads with the state carried from slab j-1, and slab j's outputs
+    are all-gathered while slab j+1 computes. Returns (o [B, T, H, d] on
+    every rank, this rank's final states [B, H/G, d, d]). `slab_ops` defaults
+    to the CUDA kernels (CudaSlabOps); it is a parameter so the host-side
+    orchestration can be checked against the f64 oracle on CPU process groups.
+    """
+    import torch.distributed as dist
+
+    if slab <= 0 or slab % 64:
+        raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"slab = {slab}: a positive multiple of 64")
+    B, T, Hs, d = q.shape
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    so = slab_ops or CudaSlabOps(B, q.device)
+    out = torch.empty((B, T, world * Hs, d), device=q.device, dtype=q.dtype)
+    pool = torch.zeros((B, Hs, d, d), device=q.device, dtype=torch.float32)
+    pending = None  # (work, gathered, t0, t1) of the slab whose gather is in flight
+
+    def finish(item):
+        work, gathered, t0, t1 = item
+        if work is not None:
+            work.wait()
+        so.unpack(out, so.unshard(gathered) if world > 1 else gathered[0], t0, t1)
+
+    for t0 in range(0, T, slab):
+        t1 = min(T, t0 + slab)
+        parts = [so.pack(x, t0, t1) for x in (q, k, v, alpha, beta)]
+        o_s = so.compute(*parts, pool, t0 == 0, t1 - t0)
+        if world > 1:
+            gathered = torch.empty((world, *o_s.shape), device=o_s.device, dtype=o_s.dtype)
+            work = dist.all_gather_into_tensor(gathered.view(world * o_s.shape[0], *o_s.shape[1:]),
+                                               o_s, group=group, async_op=True)
+        else:
+            gathered, work = o_s.unsqueeze(0), None
+        if pending is not None:
+            finish(pending)
+        pending = (work, gathered, t0, t1)
+    if pending is not None:
+        finish(pending)
+    return out, pool

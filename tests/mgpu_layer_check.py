@@ -9,7 +9,7 @@ import torch.distributed as dist
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 from rhizome_b200 import ops  # noqa: E402
-from rhizome_b200.layer import gdr_layer_sharded, head_range  # noqa: E402
+from rhizome_b200.layer import gdr_layer_sharded, gdr_layer_sharded_slabs, head_range  # noqa: E402
 
 
 def main():
@@ -32,6 +32,10 @@ def main():
     ref_o, ref_s = ops.gdr_scan_chunked(q, k, v, a, b)
     torch.cuda.synchronize()
     ok = torch.equal(o, ref_o) and torch.equal(fin, ref_s[:, h0:h1])
+    # the all-gather-overlapped form, three slabs (128, 128, 44 positions)
+    o2, fin2 = gdr_layer_sharded_slabs(*sh, slab=128)
+    torch.cuda.synchronize()
+    ok = ok and torch.equal(o2, ref_o) and torch.equal(fin2, ref_s[:, h0:h1])
     flag = torch.tensor([0 if ok else 1], device="cuda")
     dist.all_reduce(flag)
     dist.destroy_process_group()

@@ -10,7 +10,7 @@ import pytest
 import torch
 
 from rhizome_b200 import ops
-from rhizome_b200.layer import head_range, heads_shard, heads_unshard
+from rhizome_b200.layer import gdr_layer_sharded_slabs, head_range, heads_shard, heads_unshard
 
 pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -44,6 +44,24 @@ def test_sharded_computes_reassemble_the_full_layer_bitwise():
         assert torch.equal(s, ref_s[:, h0:h1])
         outs.append(o)
     assert torch.equal(heads_unshard(torch.stack(outs)), ref_o)
+
+
+@pytest.mark.parametrize("T,slab", [(300, 128), (64, 64), (130, 4096)])
+def test_slab_pipelined_layer_one_gpu_is_bitwise_the_one_call_layer(T, slab):
+    """Slabs of 64-multiples with the state carried in fp32 between them give
+    the one-call chunked result bit for bit (one rank: no all-gather)."""
+    B, H, D = 2, 4, 128
+    g = torch.Generator(device="cuda").manual_seed(T)
+    n = torch.nn.functional.normalize
+    q = n(torch.randn(B, T, H, D, device="cuda", generator=g), dim=-1).bfloat16()
+    k = n(torch.randn(B, T, H, D, device="cuda", generator=g), dim=-1).bfloat16()
+    v = torch.randn(B, T, H, D, device="cuda", generator=g).bfloat16()
+    b = torch.sigmoid(torch.randn(B, T, H, device="cuda", generator=g))
+    a = torch.exp(-torch.nn.functional.softplus(torch.randn(B, T, H, device="cuda", generator=g) + 2))
+    o, fin = gdr_layer_sharded_slabs(q, k, v, a, b, slab=slab)
+    ref_o, ref_s = ops.gdr_scan_chunked(q, k, v, a, b)
+    torch.cuda.synchronize()
+    assert torch.equal(o, ref_o) and torch.equal(fin, ref_s)
 
 
 def _free_port():

@@ -12,7 +12,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from rhizome_b200 import capi
-from rhizome_b200.layer import gdr_layer_sharded, head_range
+from rhizome_b200.layer import gdr_layer_sharded, gdr_layer_sharded_slabs, head_range
 
 B, T, H, D = 2, 70, 4, 8
 
@@ -51,6 +51,50 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
+class _OracleSlabOps:
+    """CPU stand-in for CudaSlabOps: torch packing and the f64 oracle's
+    varlen scan, the state carried in f64 between slabs (the layer's f32
+    pool receives a copy, as the device pool holds the kernels' f32 state)."""
+
+    def __init__(self, b):
+        self.B = b
+        self.state = None
+
+    def pack(self, x, t0, t1):
+        return x[:, t0:t1].reshape(self.B * (t1 - t0), *x.shape[2:]).contiguous()
+
+    def compute(self, q, k, v, a, b, pool, first, length):
+        from oracle import oracle as O
+        cu = np.arange(0, (self.B + 1) * length, length)
+        o, self.state = O.gdr_varlen(cu, q.numpy(), k.numpy(), v.numpy(), a.numpy(), b.numpy(),
+                                     state_in=None if first else self.state, nthreads=1)
+        pool.copy_(torch.from_numpy(self.state))
+        return torch.from_numpy(o)
+
+    def unshard(self, gathered):
+        G, tok, hs, d = gathered.shape
+        return gathered.permute(1, 0, 2, 3).reshape(tok, G * hs, d)
+
+    def unpack(self, out, slab, t0, t1):
+        out[:, t0:t1] = slab.reshape(self.B, t1 - t0, *out.shape[2:])
+
+
+def _slab_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        full = [torch.from_numpy(x) for x in _problem()]
+        h0, h1 = head_range(H, world, rank)
+        shard = [x[:, :, h0:h1].contiguous() for x in full]
+        o, fin = gdr_layer_sharded_slabs(*shard, slab=64, slab_ops=_OracleSlabOps(B))
+        ref_o, ref_s = _oracle_compute(*full)
+        ok = torch.equal(o, ref_o) and torch.equal(fin, ref_s[:, h0:h1].float())
+        q.put((rank, ok, (h0, h1)))
+    finally:
+        dist.destroy_process_group()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -69,6 +113,29 @@ def test_head_sharded_layer_matches_unsharded_on_two_gloo_ranks():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert sorted(results) == [(0, True, (0, 2)), (1, True, (2, 4))]
+
+
+def test_slab_pipelined_layer_matches_unsharded_on_two_gloo_ranks():
+    """The all-gather-overlapped form: T = 70 in slabs of 64 (a full slab
+    and a ragged one), the state carried between them."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_slab_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert sorted(results) == [(0, True, (0, 2)), (1, True, (2, 4))]
+
+
+def test_slab_must_be_a_multiple_of_64():
+    x = torch.zeros(1, 64, 1, 8)
+    a = torch.zeros(1, 64, 1)
+    with pytest.raises(capi.InvalidArgument):
+        gdr_layer_sharded_slabs(x, x, x, a, a, slab=100, slab_ops=_OracleSlabOps(1))
 
 
 def test_head_range_rules():
