@@ -10,7 +10,7 @@ import torch
 
 from oracle import oracle as O
 from rhizome_b200 import ops
-from tests.gpu_util import host, make_inputs, to_dev
+from tests.gpu_util import make_inputs
 from tests.tolerance import assert_bf16, assert_fp32
 
 pytestmark = pytest.mark.gpu
