@@ -177,3 +177,23 @@ def test_python_errors_map_status_codes(lib):
         capi.check(_step(lib, d=0))
     with pytest.raises(capi.DtypeError):
         capi.check(_step(lib, dtype=9))
+
+
+def test_torch_wrappers_validate_before_the_library():
+    """rhizome_b200.ops checks device, layout, dtype and shape of its torch
+    arguments before any C-ABI call (so these run without a GPU)."""
+    import torch
+    from rhizome_b200 import ops
+    q = torch.zeros(1, 64, 2, 128, dtype=torch.bfloat16)
+    a = torch.zeros(1, 64, 2)
+    with pytest.raises(capi.InvalidArgument, match="CUDA tensor"):
+        ops.gdr_scan_chunked(q, q, q, a, a)
+    # the host-buffer entry wants host tensors of matching shapes and dtypes
+    with pytest.raises(capi.ShapeError):
+        ops.gdr_scan_chunked_host(q, q[:, :32].contiguous(), q, a, a)
+    with pytest.raises(capi.DtypeError):
+        ops.gdr_scan_chunked_host(q, q, q, a.double(), a)
+    with pytest.raises(capi.InvalidArgument, match="contiguous"):
+        ops.gdr_scan_chunked_host(q.transpose(1, 2), q, q, a, a)
+    with pytest.raises(capi.InvalidArgument):
+        ops.set_chunk_kernel("fastest")
