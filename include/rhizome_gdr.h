@@ -394,11 +394,11 @@ int rhz_heads_shard(void *gathered, const void *full, int64_t G, int64_t tokens,
  * rhz_varlen_segments_to_cu_seqlens minus the workspace: the scan's scratch
  * lives in a 64 KiB array inside the library (on every GPU that loads it,
  * until the process exits), so the call allocates no device memory at all.
- * It is for callers that cannot allocate: a plan executor that only owns the
- * arena its planner sized ahead of time (crates/plan/src/arena.rs, every
- * offset fixed before the step) and has no slot for an op's private
- * scratch, or a serving process that reserved all device memory up front
- * for its state slots, where a cudaMalloc in the middle of a step can fail.
+ * It is for callers that cannot allocate: a plan executor that only owns one
+ * buffer, sized and laid out before the step runs, with no room set aside
+ * for an op's private scratch, or a serving process that reserved all
+ * device memory up front for its state slots, where a cudaMalloc in the
+ * middle of a step can fail.
  * Limits and rules:
  *   - B*T must not exceed RHZ_NOALLOC_MAX_POSITIONS (2^26); larger inputs
  *     return RHZ_ERR_SHAPE (use the workspace entry point instead);

@@ -141,6 +141,18 @@ def gdr_layer_sharded_slabs(q, k, v, alpha, beta, slab: int = 4096, group=None,
     if slab <= 0 or slab % 64:
         raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"slab = {slab}: a positive multiple of 64")
     B, T, Hs, d = q.shape
+    if slab_ops is None:
+        # The CUDA slab moves address rows by raw pointer arithmetic: every
+        # input must be a contiguous device tensor of this rank's [B, T, Hs]
+        # shape (a head-slice view such as x[:, :, h0:h1] is not).
+        ops._qkv(q, k, v, alpha, beta, (B, T))
+    else:
+        for name, x in (("k", k), ("v", v)):
+            if tuple(x.shape) != tuple(q.shape) or x.dtype != q.dtype:
+                raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"{name} must match q's shape and dtype")
+        for name, x in (("alpha", alpha), ("beta", beta)):
+            if tuple(x.shape) != (B, T, Hs) or x.dtype != torch.float32:
+                raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"{name} must be f32 [{B}, {T}, {Hs}]")
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     so = slab_ops or CudaSlabOps(B, q.device)
     out = torch.empty((B, T, world * Hs, d), device=q.device, dtype=q.dtype)

@@ -32,14 +32,34 @@ def _stream(dev: torch.device) -> int:
 
 
 def _need(x: torch.Tensor, name: str, dtype=None, shape=None):
-    if not x.is_cuda:
-        raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"{name} must be a CUDA tensor")
-    if not x.is_contiguous():
-        raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"{name} must be contiguous")
-    if dtype is not None and x.dtype != dtype:
-        raise capi.DtypeError(capi.RHZ_ERR_DTYPE, f"{name} must be {dtype}, got {x.dtype}")
+    # Shape and dtype first (the most specific message), then layout and device.
     if shape is not None and tuple(x.shape) != tuple(shape):
         raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"{name} has shape {tuple(x.shape)}, expected {tuple(shape)}")
+    if dtype is not None and x.dtype != dtype:
+        raise capi.DtypeError(capi.RHZ_ERR_DTYPE, f"{name} must be {dtype}, got {x.dtype}")
+    if not x.is_contiguous():
+        raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"{name} must be contiguous")
+    if not x.is_cuda:
+        raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"{name} must be a CUDA tensor")
+
+
+def _pool(state_pool, name, H, d):
+    """A state pool [slots, H, d, d] f32; returns its slot count."""
+    if state_pool.dim() != 4 or tuple(state_pool.shape[1:]) != (H, d, d):
+        raise capi.ShapeError(capi.RHZ_ERR_SHAPE,
+                              f"{name} shape {tuple(state_pool.shape)} != [slots, {H}, {d}, {d}]")
+    _need(state_pool, name, torch.float32)
+    return state_pool.shape[0]
+
+
+def _workspace(ws, nbytes, dev):
+    """The caller's workspace (or a new one of nbytes) and its real size in bytes."""
+    if ws is None:
+        ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
+    _need(ws, "workspace")
+    if ws.device != dev:
+        raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"workspace is on {ws.device}, q on {dev}")
+    return ws, ws.numel() * ws.element_size()
 
 
 def _qkv(q, k, v, alpha, beta, lead):
@@ -57,9 +77,9 @@ def gdr_step(q, k, v, alpha, beta, state_pool, slot_idx=None, out=None):
     on state_pool[slot_idx[i]]. q/k/v [n, H, d]; returns o [n, H, d]."""
     n = q.shape[0]
     H, d = _qkv(q, k, v, alpha, beta, (n,))
-    _need(state_pool, "state_pool", torch.float32)
-    if state_pool.dim() != 4 or tuple(state_pool.shape[1:]) != (H, d, d):
-        raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"state_pool shape {tuple(state_pool.shape)} != [slots, {H}, {d}, {d}]")
+    if out is not None:
+        _need(out, "out", q.dtype, tuple(q.shape))
+    _pool(state_pool, "state_pool", H, d)
     if slot_idx is not None:
         _need(slot_idx, "slot_idx", torch.int32, (n,))
     o = torch.empty_like(q) if out is None else out
@@ -80,10 +100,7 @@ def gdr_multistep(q, k, v, alpha, beta, max_positions=8, segment=None, state_poo
     Tn = max(0, min(T, int(max_positions)))
     if segment is not None:
         _need(segment, "segment", torch.int64, (n, T))
-    num_slots = 0
-    if state_pool is not None:
-        _need(state_pool, "state_pool", torch.float32)
-        num_slots = state_pool.shape[0]
+    num_slots = 0 if state_pool is None else _pool(state_pool, "state_pool", H, d)
     if slot_idx is not None:
         _need(slot_idx, "slot_idx", torch.int32, (n,))
     outs = torch.empty((n, Tn, H, d), device=q.device, dtype=q.dtype)
@@ -151,16 +168,14 @@ def _seq_common(name, q, k, v, alpha, beta, segment, state_init, chunk, with_sta
         _need(state_init, "state_init", torch.float32, (B, H, d, d))
     o = torch.empty_like(q)
     fin = torch.empty((B, H, d, d), device=q.device, dtype=torch.float32) if with_state else None
-    ws = workspace
-    nbytes = 0
-    if segment is not None:
-        nbytes = workspace_bytes(B, T)
-        if ws is None:
-            ws = torch.empty(nbytes, device=q.device, dtype=torch.uint8)
+    ws, nbytes = None, 0
+    if segment is not None or workspace is not None:
+        ws, nbytes = _workspace(workspace, workspace_bytes(B, T) if segment is not None else 0,
+                                q.device)
     args = [_p(o), _p(fin), _p(q), _p(k), _p(v), _p(alpha), _p(beta), _p(segment), _p(state_init)]
     if name == "rhz_gdr_scan_chunked":
         args.append(chunk)
-    args += [B, T, H, d, _dt(q), _p(ws), nbytes if ws is not None else 0, _stream(q.device)]
+    args += [B, T, H, d, _dt(q), _p(ws), nbytes, _stream(q.device)]
     capi.call(name, *args)
     return o, fin
 
@@ -244,12 +259,11 @@ def gdr_varlen_fwd(q, k, v, alpha, beta, cu_seqlens, state_pool=None, slot_idx=N
     _need(cu_seqlens, "cu_seqlens", torch.int32)
     n_seq = cu_seqlens.numel() - 1
     flags = (capi.RHZ_FLAG_ZERO_INIT if zero_init else 0) | (0 if write_state else capi.RHZ_FLAG_NO_STATE_WRITE)
-    num_slots = 0
-    if state_pool is not None:
-        _need(state_pool, "state_pool", torch.float32)
-        num_slots = state_pool.shape[0]
+    num_slots = 0 if state_pool is None else _pool(state_pool, "state_pool", H, d)
     if slot_idx is not None:
         _need(slot_idx, "slot_idx", torch.int32, (n_seq,))
+    if out is not None:
+        _need(out, "out", q.dtype, tuple(q.shape))
     o = torch.empty_like(q) if out is None else out
     capi.call("rhz_gdr_varlen_fwd", _p(o), _p(state_pool), _p(slot_idx), _p(cu_seqlens), _p(q),
               _p(k), _p(v), _p(alpha), _p(beta), n_seq, tokens, num_slots, H, d, _dt(q), flags,
@@ -269,8 +283,8 @@ def gdr_scan_chunked_bwd(q, k, v, alpha, beta, d_o, segment=None, d_state_final=
         _need(segment, "segment", torch.int64, (B, T))
     if d_state_final is not None:
         _need(d_state_final, "d_state_final", torch.float32, (B, H, d, d))
-    nbytes = int(capi.lib().rhz_gdr_bwd_workspace_bytes(B, T, H, d))
-    ws = workspace if workspace is not None else torch.empty(max(nbytes, 1), device=q.device, dtype=torch.uint8)
+    ws, nbytes = _workspace(workspace, int(capi.lib().rhz_gdr_bwd_workspace_bytes(B, T, H, d)),
+                            q.device)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
     dalpha, dbeta = torch.empty_like(alpha), torch.empty_like(beta)
     capi.call("rhz_gdr_scan_chunked_bwd", _p(dq), _p(dk), _p(dv), _p(dalpha), _p(dbeta), _p(q),
@@ -293,10 +307,7 @@ def gdr_varlen_fwd_norm(q, k, v, alpha, beta, cu_seqlens, norm_scale, norm_eps=1
         raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"norm_scale has {norm_scale.numel()} entries, need at least d = {d}")
     n_seq = cu_seqlens.numel() - 1
     flags = (capi.RHZ_FLAG_ZERO_INIT if zero_init else 0) | (0 if write_state else capi.RHZ_FLAG_NO_STATE_WRITE)
-    num_slots = 0
-    if state_pool is not None:
-        _need(state_pool, "state_pool", torch.float32)
-        num_slots = state_pool.shape[0]
+    num_slots = 0 if state_pool is None else _pool(state_pool, "state_pool", H, d)
     if slot_idx is not None:
         _need(slot_idx, "slot_idx", torch.int32, (n_seq,))
     o = torch.empty_like(q)
@@ -315,6 +326,8 @@ def groupnorm_heads(x, scale, eps=1e-6, out=None):
     if scale.numel() < d:
         raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"scale has {scale.numel()} entries, need at least d = {d}")
     rows = x.numel() // (H * d) if x.numel() else 0
+    if out is not None:
+        _need(out, "out", x.dtype, tuple(x.shape))
     o = torch.empty_like(x) if out is None else out
     capi.call("rhz_groupnorm_heads", _p(o), _p(x), _p(scale), rows, H, d, float(eps), _dt(x),
               _stream(x.device))

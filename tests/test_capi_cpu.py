@@ -197,3 +197,29 @@ def test_torch_wrappers_validate_before_the_library():
         ops.gdr_scan_chunked_host(q.transpose(1, 2), q, q, a, a)
     with pytest.raises(capi.InvalidArgument):
         ops.set_chunk_kernel("fastest")
+
+
+def test_torch_wrappers_check_out_pool_and_workspace():
+    """`out=`, state pools and caller workspaces are checked against the op's
+    own shapes before the library sees them (a smaller buffer would be
+    written past its end on the device)."""
+    import torch
+    from rhizome_b200 import ops
+    q = torch.zeros(4, 2, 128)
+    with pytest.raises(capi.InvalidArgument, match="CUDA tensor"):
+        ops._need(q, "out", q.dtype, tuple(q.shape))
+    with pytest.raises(capi.ShapeError, match="expected"):
+        ops._need(q[:2].contiguous(), "out", q.dtype, tuple(q.shape))
+    with pytest.raises(capi.DtypeError):
+        ops._need(q.bfloat16(), "out", q.dtype, tuple(q.shape))
+    # state pools: trailing dims must be (H, d, d)
+    pool = torch.zeros(3, 2, 64, 64)
+    with pytest.raises(capi.ShapeError, match="slots"):
+        ops._pool(pool, "state_pool", 2, 128)
+    with pytest.raises(capi.DtypeError):
+        ops._pool(torch.zeros(3, 2, 128, 128, dtype=torch.float64), "state_pool", 2, 128)
+    ok = torch.zeros(3, 2, 128, 128)
+    with pytest.raises(capi.InvalidArgument):
+        ops._pool(ok, "state_pool", 2, 128)  # right shape, but still a host tensor
+    with pytest.raises(capi.InvalidArgument, match="CUDA tensor"):
+        ops._workspace(torch.zeros(16, dtype=torch.uint8), 16, torch.device("cpu"))

@@ -177,6 +177,31 @@ def test_shape_errors_raise_before_launch():
         ops.gdr_sequential(q.half(), q.half(), q.half(), al, al)
 
 
+def test_wrappers_check_out_pools_and_workspaces():
+    """A too-small `out`, a state pool of the wrong head count or width, or a
+    too-small caller workspace is rejected before the library writes past its
+    end."""
+    n, H, d = 4, 2, 32
+    q = torch.zeros((n, H, d), device="cuda")
+    g = torch.zeros((n, H), device="cuda")
+    pool = torch.zeros((n, H, d, d), device="cuda")
+    with pytest.raises(capi.ShapeError):
+        ops.gdr_step(q, q, q, g, g, pool, out=q[:2].clone())
+    with pytest.raises(capi.DtypeError):
+        ops.gdr_step(q, q, q, g, g, pool, out=q.bfloat16())
+    cu = torch.tensor([0, 2, 4], device="cuda", dtype=torch.int32)
+    with pytest.raises(capi.ShapeError, match="slots"):
+        ops.gdr_varlen_fwd(q, q, q, g, g, cu, state_pool=torch.zeros((n, 1, d, d), device="cuda"))
+    with pytest.raises(capi.ShapeError):
+        ops.gdr_varlen_fwd(q, q, q, g, g, cu, state_pool=pool, out=q[:, :1].clone())
+    x = torch.zeros((2, 8, H, d), device="cuda")
+    a = torch.zeros((2, 8, H), device="cuda")
+    seg = torch.zeros((2, 8), device="cuda", dtype=torch.int64)
+    small = torch.empty(8, device="cuda", dtype=torch.uint8)
+    with pytest.raises(capi.InvalidArgument, match="workspace"):
+        ops.gdr_sequential(x, x, x, a, a, segment=seg, workspace=small)
+
+
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 @pytest.mark.parametrize("d", [6, 32, 128])
 def test_multistep_reference_semantics(dtype, d):
