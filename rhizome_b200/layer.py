@@ -147,12 +147,14 @@ def gdr_layer_sharded_slabs(q, k, v, alpha, beta, slab: int = 4096, group=None,
         # shape (a head-slice view such as x[:, :, h0:h1] is not).
         ops._qkv(q, k, v, alpha, beta, (B, T))
     else:
+        # Caller-supplied slab moves (the host-side check of the
+        # orchestration) may use other dtypes; the shapes must still agree.
         for name, x in (("k", k), ("v", v)):
-            if tuple(x.shape) != tuple(q.shape) or x.dtype != q.dtype:
-                raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"{name} must match q's shape and dtype")
+            if tuple(x.shape) != tuple(q.shape):
+                raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"{name} must match q's shape")
         for name, x in (("alpha", alpha), ("beta", beta)):
-            if tuple(x.shape) != (B, T, Hs) or x.dtype != torch.float32:
-                raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"{name} must be f32 [{B}, {T}, {Hs}]")
+            if tuple(x.shape) != (B, T, Hs):
+                raise capi.ShapeError(capi.RHZ_ERR_SHAPE, f"{name} must be [{B}, {T}, {Hs}]")
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     so = slab_ops or CudaSlabOps(B, q.device)
     out = torch.empty((B, T, world * Hs, d), device=q.device, dtype=q.dtype)
