@@ -14,7 +14,9 @@ this arithmetic intensity, with the tensor-core fraction beside it),
 `cpu_baseline` (the f64 oracle restating crates/ops/src/delta.rs, timed on
 this host's cores), `e2e` (same metric through the host-buffer C-ABI call,
 rhz_gdr_scan_chunked_host, with the copies inside the timed region), `decode` (ragged decode
-step: 512 sequences x 16 heads from a 1024-slot fp32 pool), `clocks`.
+step: 512 sequences x 16 heads from a 1024-slot fp32 pool), `layer` (the
+head-sharded full layer of configs[4] at this N, with its NCCL all-gather),
+`clocks`.
 
 `--impl reference` times the reference's CPU implementation of the path (the
 oracle port, all host threads) on a bounded sample of the same workload.
@@ -218,6 +220,14 @@ def cpu_reference_rate(sample_b: int, min_seconds: float, threads: int):
     return reps * sample_b * T / el, reps, el
 
 
+def prefill_config(world):
+    """The headline workload's config, identical in both arms."""
+    return {"workload": "chunked GDR prefill B=4 T=4096 H=16 d=128 chunk=64",
+            "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": D,
+            "chunk": CHUNK, "parallelism": f"shard{world} over (sequence, head)",
+            "l2": "inputs larger than L2 (2 x 270 MB sets, alternated)"}
+
+
 def run_reference(args):
     """--impl reference: the reference's CPU implementation (oracle port)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -252,9 +262,7 @@ def run_reference(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": "chunked GDR prefill B=4 T=4096 H=16 d=128 chunk=64",
-                   "global_batch": B, "seq_len": T, "heads": H, "head_dim": D,
-                   "parallelism": "host threads over (sequence, head)"},
+        "config": prefill_config(world),
         "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -279,12 +287,14 @@ def run_ours(args):
     sets = [make_inputs(1000 * rank + s, dev) for s in range(2)]
     o = torch.empty((B, T, H, D), device=dev, dtype=torch.bfloat16)
     fin = torch.empty((B, H, D, D), device=dev, dtype=torch.float32)
+    ws_n = int(capi.lib().rhz_gdr_workspace_bytes(B, T, H, D, capi.RHZ_DTYPE_BF16, 0))
+    ws = torch.empty(max(ws_n, 1), device=dev, dtype=torch.uint8)
 
     def launch(i):
         q, k, v, a, b = sets[i % 2]
         capi.call("rhz_gdr_scan_chunked", o.data_ptr(), fin.data_ptr(), q.data_ptr(),
                   k.data_ptr(), v.data_ptr(), a.data_ptr(), b.data_ptr(), None, None, CHUNK, B, T,
-                  H, D, capi.RHZ_DTYPE_BF16, None, 0, sptr)
+                  H, D, capi.RHZ_DTYPE_BF16, ws.data_ptr(), ws_n, sptr)
 
     for i in range(args.warmup):
         launch(i)
@@ -481,11 +491,14 @@ def run_ours(args):
     vpool = torch.randn((VL_SLOTS, H, D, D), device=dev, generator=gv) * 0.02
     vslots = torch.randperm(VL_SLOTS, device=dev, generator=gv)[:VL_N].to(torch.int32)
     vo = torch.empty_like(vq)
+    vws_n = int(capi.lib().rhz_gdr_varlen_workspace_bytes(VL_N, H, D, capi.RHZ_DTYPE_BF16))
+    vws = torch.empty(max(vws_n, 1), device=dev, dtype=torch.uint8)
 
     def varlen():
         capi.call("rhz_gdr_varlen_fwd", vo.data_ptr(), vpool.data_ptr(), vslots.data_ptr(),
                   vcu.data_ptr(), vq.data_ptr(), vk.data_ptr(), vv.data_ptr(), va.data_ptr(),
-                  vb.data_ptr(), VL_N, vtok, VL_SLOTS, H, D, capi.RHZ_DTYPE_BF16, 0, sptr)
+                  vb.data_ptr(), VL_N, vtok, VL_SLOTS, H, D, capi.RHZ_DTYPE_BF16, 0,
+                  vws.data_ptr(), vws_n, sptr)
 
     vl_ms = timed(varlen, 5)
     vbytes = vtok * H * (3 * D * 2 + D * 2 + 8) + VL_N * H * D * D * 4 * 2
@@ -571,6 +584,10 @@ def run_ours(args):
     # sub-measurement above (the headline region alone lasts a few ms).
     clock_info = clocks.stop()
 
+    # The head-sharded full layer at this N: the NCCL all-gather
+    # of per-head outputs is the one collective of the path.
+    layer = None if args.no_layer else layer_measure(args, world, rank, local, 3, 1)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
@@ -585,10 +602,7 @@ def run_ours(args):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "chunked GDR prefill B=4 T=4096 H=16 d=128 chunk=64",
-                       "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": D,
-                       "chunk": CHUNK, "parallelism": f"shard{world} over (sequence, head)",
-                       "l2": "inputs larger than L2 (2 x 270 MB sets, alternated)"},
+            "config": prefill_config(world),
             "roofline": roofline, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / e2e_steps, 4),
@@ -596,7 +610,7 @@ def run_ours(args):
                             f"of {slab} positions pipelined"},
             "gpu_launches": args.steps, "clocks": clock_info, "decode": decode,
             "producer": producer, "output_norm": outnorm, "varlen_prefill": varlen_line,
-            "packing": packing, "backward": backward,
+            "packing": packing, "backward": backward, "layer": layer,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -605,17 +619,16 @@ def run_ours(args):
     return 0
 
 
-def run_layer(args):
-    """--workload layer: the full Local-block layer, B=8, T=32768, H=64,
-    d=128, heads split evenly over the ranks, per-head outputs all-gathered
-    (NCCL) into [B, T, H*d] on every rank. Total work is fixed: strong scaling."""
+def layer_measure(args, world, rank, local, steps, warmup):
+    """The full Local-block layer: B=8, T=32768, H=64, d=128,
+    heads split evenly over the ranks, per-head outputs all-gathered (NCCL)
+    into [B, T, H*d] on every rank. Total work is fixed (strong scaling).
+    Every rank runs the same collectives in the same order; returns the
+    measurement dict (meaningful on rank 0)."""
     import torch
-    from rhizome_b200 import capi
     from rhizome_b200.layer import gdr_layer_sharded, gdr_layer_sharded_slabs
 
-    world, rank, local = dist_setup()
     dev = torch.device("cuda", local)
-    capi.lib()
     LB, LT, LH = 8, 32768, 64
     if LH % world:
         raise SystemExit(f"H = {LH} heads do not split over {world} ranks")
@@ -651,41 +664,59 @@ def run_layer(args):
             out = gdr_layer_sharded(q, k, v, alpha, beta)
         return out
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step(False)
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         step(True)
     s1.record(stream)
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     elapsed = max_over_ranks(s0.elapsed_time(s1), world)
-    comp = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) / args.steps, world)
+    comp = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) / steps, world)
+    del q, k, v, alpha, beta
+    torch.cuda.empty_cache()
     tokens = LB * LT
-    gathered_bytes = (world - 1) * LB * LT * hs * D * 2
+    received = (world - 1) * LB * LT * hs * D * 2
+    per_step = elapsed / steps
+    gather_ms = None if args.slab else max(per_step - comp, 0.0)
+    return {
+        "metric": "GDR layer tokens/s", "value": tokens * steps / (elapsed / 1e3),
+        "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": per_step, "scaling": "strong",
+        "config": {"workload": "full Local-block GDR layer B=8 T=32768 H=64 d=128, heads "
+                               "split over ranks, outputs all-gathered (NCCL) into [8, 32768, 8192]"
+                               + (f", all-gather overlapped in slabs of {args.slab} positions"
+                                  if args.slab else ""),
+                   "global_batch": LB, "seq_len": LT, "heads": LH, "head_dim": D,
+                   "parallelism": f"heads/{world}"},
+        "kernel_only": None if args.slab else {"value": tokens / (comp / 1e3), "unit": "tokens/s",
+                                               "ms_per_gpu": round(comp, 4)},
+        "allgather": {"bytes_received_per_rank": received,
+                      "ms_per_step": None if gather_ms is None else round(gather_ms, 4),
+                      "GBps_received_per_rank": (round(received / (gather_ms / 1e3) / 1e9, 1)
+                                                 if gather_ms else None),
+                      "includes": "NCCL all-gather into rank-major staging + unshard permute",
+                      "overlapped_in_slabs": args.slab or None},
+    }
+
+
+def run_layer(args):
+    """--workload layer: only the full-layer measurement, as its own line."""
+    import torch  # noqa: F401
+    from rhizome_b200 import capi
+
+    world, rank, local = dist_setup()
+    capi.lib()
+    line = layer_measure(args, world, rank, local, args.steps, args.warmup)
     if rank == 0:
-        line = {
-            "metric": "GDR layer tokens/s", "value": tokens * args.steps / (elapsed / 1e3),
-            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": elapsed / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "full Local-block GDR layer B=8 T=32768 H=64 d=128, heads "
-                                   "split over ranks, outputs all-gathered (NCCL)"
-                                   + (f", all-gather overlapped in slabs of {args.slab} positions"
-                                      if args.slab else ""),
-                       "global_batch": LB, "seq_len": LT, "heads": LH, "head_dim": D,
-                       "parallelism": f"heads/{world}"},
-            "kernel_only": None if args.slab else {"value": tokens / (comp / 1e3),
-                                                   "unit": "tokens/s", "ms_per_step": comp},
-            "allgather": {"bytes_received_per_rank": gathered_bytes,
-                          "ms_per_step": None if args.slab else elapsed / args.steps - comp,
-                          "overlapped_in_slabs": args.slab or None},
-        }
+        line.update({"higher_is_better": True, "vs_baseline": None, "dtype": "bf16",
+                     "data": "synthetic"})
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -788,6 +819,8 @@ def main():
                     help="prefill: the headline chunked-prefill batch (weak scaling over "
                          "ranks); layer: the full head-sharded layer with its all-gather")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-layer", action="store_true",
+                    help="skip the head-sharded full-layer sub-measurement")
     ap.add_argument("--slab", type=int, default=0,
                     help="--workload layer: overlap the all-gather with compute in slabs of this "
                          "many positions (a multiple of 64; 0 = one call, then one all-gather)")

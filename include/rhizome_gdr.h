@@ -72,8 +72,11 @@ enum rhz_dtype { RHZ_DTYPE_F32 = 0, RHZ_DTYPE_BF16 = 1 };
 const char *rhz_last_error(void);
 
 /* ABI version of this header (major * 100 + minor). 1.1 added the
- * host-buffer scan, the device status query and the chunked-form setting. */
-#define RHZ_ABI_VERSION 101
+ * host-buffer scan, the device status query and the chunked-form setting;
+ * 2.0 gives the bf16 tensor-core path caller-owned scratch: a workspace
+ * argument on rhz_gdr_varlen_fwd(_norm), and rhz_gdr_workspace_bytes takes
+ * the head count, width and dtype. */
+#define RHZ_ABI_VERSION 200
 int rhz_abi_version(void);
 
 /*
@@ -90,13 +93,15 @@ int rhz_device_status(int32_t *timed_out, int clear);
 
 /*
  * Which tensor-core form runs the bf16, d == 128 chunked scan
- * (rhz_gdr_scan_chunked, rhz_gdr_varlen_fwd): a 2-CTA cluster per
- * (sequence, head) item, or one CTA per item. AUTO (the default) picks by
- * the item count against the SM count. Both give the same results within
- * the bf16 tolerance. Process-wide; the previous setting goes to *previous
- * unless it is NULL. A variant outside the enum returns RHZ_ERR_INVALID.
+ * (rhz_gdr_scan_chunked, rhz_gdr_varlen_fwd): GRID (the default, AUTO) is
+ * one launch over every SM in which chain CTAs carry each (sequence, head)
+ * item's state and producer CTAs build the per-chunk records; PAIR (a 2-CTA
+ * cluster per item) and SOLO (one CTA per item) are the earlier forms. All
+ * give the same results within the bf16 tolerance; GRID and PAIR bitwise.
+ * Process-wide; the previous setting goes to *previous unless it is NULL.
+ * A variant outside the enum returns RHZ_ERR_INVALID.
  */
-enum rhz_chunk_kernel { RHZ_CHUNK_AUTO = 0, RHZ_CHUNK_PAIR = 1, RHZ_CHUNK_SOLO = 2 };
+enum rhz_chunk_kernel { RHZ_CHUNK_AUTO = 0, RHZ_CHUNK_PAIR = 1, RHZ_CHUNK_SOLO = 2, RHZ_CHUNK_GRID = 3 };
 int rhz_gdr_set_chunk_kernel(int32_t variant, int32_t *previous);
 
 /* --------------------------------------------------------------------- */
@@ -125,8 +130,10 @@ int rhz_gdr_step(void *o, float *state_pool, const int32_t *slot_idx, const void
  * (segment: [B][T] int64, or NULL for one segment per batch row). As in the
  * reference, the reset at t = 0 means `state_init` never reaches the
  * result: it is accepted (may be NULL) and ignored. state_final: [B][H][d][d]
- * (may be NULL). Needs `workspace` of rhz_gdr_workspace_bytes(B, T) bytes
- * when segment != NULL (NULL/0 otherwise).
+ * (may be NULL). `workspace`: device memory of
+ * rhz_gdr_workspace_bytes(B, T, H, d, dtype, segment != NULL) bytes,
+ * 256-byte aligned (NULL/0 when that is 0: the f32 path without segments).
+ * Calls that share a workspace must not overlap on the GPU.
  */
 int rhz_gdr_sequential(void *o, float *state_final, const void *q, const void *k,
                        const void *v, const float *alpha, const float *beta,
@@ -186,12 +193,18 @@ size_t rhz_gdr_host_workspace_bytes(int64_t B, int64_t T, int32_t H, int32_t d, 
  * gated_delta_step applied over the sequence from the slot's state -- the
  * reference's scan with the segment-start reset replaced by the slot's
  * contents. slot_idx == NULL means slot i. Slots must be distinct.
+ * `workspace`: device memory of rhz_gdr_varlen_workspace_bytes(n_seq, H, d,
+ * dtype) bytes, 256-byte aligned (NULL/0 when that is 0); calls that share
+ * a workspace must not overlap on the GPU.
  */
 int rhz_gdr_varlen_fwd(void *o, float *state_pool, const int32_t *slot_idx,
                        const int32_t *cu_seqlens, const void *q, const void *k, const void *v,
                        const float *alpha, const float *beta, int64_t n_seq,
                        int64_t total_tokens, int64_t num_slots, int32_t H, int32_t d,
-                       int32_t dtype, uint32_t flags, rhz_stream_t stream);
+                       int32_t dtype, uint32_t flags, void *workspace, size_t workspace_bytes,
+                       rhz_stream_t stream);
+/* Scratch of rhz_gdr_varlen_fwd(_norm) for n_seq sequences (0: none needed). */
+size_t rhz_gdr_varlen_workspace_bytes(int64_t n_seq, int32_t H, int32_t d, int32_t dtype);
 
 /*
  * rhz_gdr_varlen_fwd_norm -- rhz_gdr_varlen_fwd followed by the Local
@@ -207,7 +220,8 @@ int rhz_gdr_varlen_fwd_norm(void *o, float *state_pool, const int32_t *slot_idx,
                             const int32_t *cu_seqlens, const void *q, const void *k, const void *v,
                             const float *alpha, const float *beta, const float *norm_scale,
                             float norm_eps, int64_t n_seq, int64_t total_tokens, int64_t num_slots,
-                            int32_t H, int32_t d, int32_t dtype, uint32_t flags, rhz_stream_t stream);
+                            int32_t H, int32_t d, int32_t dtype, uint32_t flags, void *workspace,
+                            size_t workspace_bytes, rhz_stream_t stream);
 
 /*
  * rhz_groupnorm_heads -- replaces groupnorm_heads (crates/ops/src/norm.rs:
@@ -295,9 +309,13 @@ size_t rhz_gdr_bwd_workspace_bytes(int64_t B, int64_t T, int32_t H, int32_t d);
 
 /*
  * rhz_gdr_workspace_bytes -- scratch needed by rhz_gdr_sequential /
- * rhz_gdr_scan_chunked with a segment array of B x T positions.
+ * rhz_gdr_scan_chunked for B x T positions of H heads of width d in
+ * `dtype`, with or without a segment array: the tensor-core kernel's
+ * record rings and schedule (bf16, d == 128: about 17 MB) plus, with
+ * segments, the segment-boundary tables. 0 when nothing is needed.
  */
-size_t rhz_gdr_workspace_bytes(int64_t B, int64_t T);
+size_t rhz_gdr_workspace_bytes(int64_t B, int64_t T, int32_t H, int32_t d, int32_t dtype,
+                               int has_segment);
 
 /* --------------------------------------------------------------------- */
 /* Variable-length packing (bit-exact index work)                         */

@@ -70,8 +70,9 @@ SIGNATURES = {
     "rhz_gdr_scan_chunked": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
                                        _i64, _i32, _i32, _i32, _vp, _sz, _vp]),
     "rhz_gdr_varlen_fwd": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
-                                     _i64, _i32, _i32, _i32, _u32, _vp]),
-    "rhz_gdr_workspace_bytes": (_sz, [_i64, _i64]),
+                                     _i64, _i32, _i32, _i32, _u32, _vp, _sz, _vp]),
+    "rhz_gdr_varlen_workspace_bytes": (_sz, [_i64, _i32, _i32, _i32]),
+    "rhz_gdr_workspace_bytes": (_sz, [_i64, _i64, _i32, _i32, _i32, C.c_int]),
     "rhz_gdr_multistep": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
                                     _i64, _i64, _i32, _i32, _i32, _vp]),
     "rhz_varlen_prefix_sum": (C.c_int, [_vp, _vp, _i64, _vp]),
@@ -85,7 +86,7 @@ SIGNATURES = {
     "rhz_varlen_segments_to_cu_seqlens_noalloc": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "rhz_gdr_varlen_fwd_norm": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                           C.c_float, _i64, _i64, _i64, _i32, _i32, _i32,
-                                          C.c_uint32, _vp]),
+                                          C.c_uint32, _vp, _sz, _vp]),
     "rhz_gdr_scan_chunked_bwd": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                            _vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp, _sz,
                                            _vp]),
@@ -104,7 +105,7 @@ SIGNATURES = {
 }
 
 # Forms of the tensor-core chunked scan (enum rhz_chunk_kernel).
-RHZ_CHUNK_AUTO, RHZ_CHUNK_PAIR, RHZ_CHUNK_SOLO = 0, 1, 2
+RHZ_CHUNK_AUTO, RHZ_CHUNK_PAIR, RHZ_CHUNK_SOLO, RHZ_CHUNK_GRID = 0, 1, 2, 3
 
 # Largest B*T rhz_varlen_segments_to_cu_seqlens_noalloc accepts.
 RHZ_NOALLOC_MAX_POSITIONS = 1 << 26

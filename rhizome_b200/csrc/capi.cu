@@ -107,15 +107,24 @@ int check_ptr(const void *p, const char *name, size_t align, bool needed) {
     } while (0)
 
 // Offsets of the sequential/chunked entry points' workspace.
+// The tensor-core kernel's scratch (record rings, schedule) comes first,
+// then, with segments, the segment-to-cu_seqlens tables.
 struct SegWs {
-    size_t cu_off, nseg_off, slot_off, scan_off, total;
+    size_t grid_bytes, cu_off, nseg_off, slot_off, scan_off, total;
 };
 
-SegWs seg_ws(int64_t B, int64_t T) {
+SegWs seg_ws(int64_t B, int64_t T, int32_t H, int32_t d, int32_t dtype, bool has_segment) {
     auto up = [](size_t x) { return (x + 255) / 256 * 256; };
-    SegWs w;
+    SegWs w{};
     const size_t N = static_cast<size_t>(B * T);
-    w.cu_off = 0;
+    w.grid_bytes = chunk_tc_supports(d, dtype)
+                       ? up(chunk_grid_ws_bytes((has_segment ? B * T : B) * H, has_segment))
+                       : 0;
+    w.cu_off = w.grid_bytes;
+    if (!has_segment) {
+        w.nseg_off = w.slot_off = w.scan_off = w.total = w.grid_bytes;
+        return w;
+    }
     w.nseg_off = up(w.cu_off + (N + 1) * sizeof(int32_t));
     w.slot_off = up(w.nseg_off + sizeof(int32_t));
     w.scan_off = up(w.slot_off + (N + 1) * sizeof(int32_t));
@@ -163,6 +172,12 @@ int sequential_impl(void *o, float *state_final, const void *q, const void *k, c
     RHZ_TRY(check_ptr(beta, "beta", 4, any));
     RHZ_TRY(check_ptr(state_final, "state_final", 16, state_final != nullptr));
     RHZ_TRY(check_ptr(segment, "segment", 8, segment != nullptr));
+    const SegWs w = seg_ws(B, T, H, d, dtype, segment != nullptr);
+    if (any && w.total > 0) {
+        if (workspace == nullptr || workspace_bytes < w.total)
+            return set_error(RHZ_ERR_INVALID, "workspace too small: need %zu bytes, got %zu", w.total, workspace_bytes);
+        RHZ_TRY(check_ptr(workspace, "workspace", 256, true));
+    }
     RHZ_TRY(require_sm100());
     cudaStream_t s = as_cuda(stream);
     const size_t state_bytes = static_cast<size_t>(B) * H * d * d * sizeof(float);
@@ -179,11 +194,14 @@ int sequential_impl(void *o, float *state_final, const void *q, const void *k, c
     }
     if (B == 0) return RHZ_OK;
 
+    char *ws = static_cast<char *>(workspace);
     SeqArgs a{};
     a.o = o; a.q = q; a.k = k; a.v = v; a.alpha = alpha; a.beta = beta;
     a.total_tokens = B * T;
     a.H = H; a.d = d; a.dtype = dtype; a.stream = s;
     a.state_in = nullptr;  // reset at t = 0: the initial state never contributes
+    a.ws = w.grid_bytes ? ws : nullptr;
+    a.ws_bytes = w.grid_bytes;
     if (segment == nullptr) {
         a.cu_seqlens = nullptr;
         a.n_seq = B;
@@ -192,11 +210,6 @@ int sequential_impl(void *o, float *state_final, const void *q, const void *k, c
         a.num_slots = B;
         return run_seq(a);
     }
-    const SegWs w = seg_ws(B, T);
-    if (workspace == nullptr || workspace_bytes < w.total)
-        return set_error(RHZ_ERR_INVALID, "workspace too small: need %zu bytes, got %zu", w.total, workspace_bytes);
-    RHZ_TRY(check_ptr(workspace, "workspace", 256, true));
-    char *ws = static_cast<char *>(workspace);
     int32_t *cu = reinterpret_cast<int32_t *>(ws + w.cu_off);
     int32_t *nseg = reinterpret_cast<int32_t *>(ws + w.nseg_off);
     int32_t *slots = reinterpret_cast<int32_t *>(ws + w.slot_off);
@@ -229,11 +242,12 @@ int rhz_abi_version(void) { return RHZ_ABI_VERSION; }
 int rhz_device_status(int32_t *timed_out, int clear) {
     clear_error();
     if (!timed_out) return set_error(RHZ_ERR_INVALID, "timed_out must not be NULL");
-    int a = 0, b = 0;
+    int a = 0, b = 0, c = 0;
     int st = chunk_pair_status(&a, clear != 0);
     if (st == RHZ_OK) st = chunk_solo_status(&b, clear != 0);
+    if (st == RHZ_OK) st = chunk_grid_status(&c, clear != 0);
     if (st != RHZ_OK) return st;
-    *timed_out = (a | b) ? 1 : 0;
+    *timed_out = (a | b | c) ? 1 : 0;
     return RHZ_OK;
 }
 
@@ -297,7 +311,7 @@ int varlen_impl(void *o, float *state_pool, const int32_t *slot_idx, const int32
                 const void *q, const void *k, const void *v, const float *alpha, const float *beta,
                 const float *norm_scale, float norm_eps, int64_t n_seq, int64_t total_tokens,
                 int64_t num_slots, int32_t H, int32_t d, int32_t dtype, uint32_t flags,
-                rhz_stream_t stream) {
+                void *workspace, size_t workspace_bytes, rhz_stream_t stream) {
     RHZ_TRY(check_dtype(dtype));
     RHZ_TRY(check_heads(H, d));
     if (flags & ~(RHZ_FLAG_ZERO_INIT | RHZ_FLAG_NO_STATE_WRITE))
@@ -309,6 +323,12 @@ int varlen_impl(void *o, float *state_pool, const int32_t *slot_idx, const int32
     if (slot_idx == nullptr && n_seq > num_slots)
         return set_error(RHZ_ERR_SHAPE, "n_seq = %lld but only %lld slots (slot_idx is NULL)", (long long)n_seq, (long long)num_slots);
     if (n_seq == 0) return RHZ_OK;
+    const size_t need = chunk_tc_supports(d, dtype) ? chunk_grid_ws_bytes(n_seq * H, true) : 0;
+    if (need > 0) {
+        if (workspace == nullptr || workspace_bytes < need)
+            return set_error(RHZ_ERR_INVALID, "workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+        RHZ_TRY(check_ptr(workspace, "workspace", 256, true));
+    }
     const bool any = total_tokens > 0;
     RHZ_TRY(check_ptr(cu_seqlens, "cu_seqlens", 4, true));
     RHZ_TRY(check_ptr(q, "q", 16, any));
@@ -334,6 +354,8 @@ int varlen_impl(void *o, float *state_pool, const int32_t *slot_idx, const int32
     a.H = H; a.d = d; a.dtype = dtype; a.stream = as_cuda(stream);
     a.norm_scale = norm_scale;
     a.norm_eps = norm_eps;
+    a.ws = need ? workspace : nullptr;
+    a.ws_bytes = need;
     return run_seq(a);
 }
 }  // namespace
@@ -344,23 +366,32 @@ int rhz_gdr_varlen_fwd(void *o, float *state_pool, const int32_t *slot_idx,
                        const int32_t *cu_seqlens, const void *q, const void *k, const void *v,
                        const float *alpha, const float *beta, int64_t n_seq,
                        int64_t total_tokens, int64_t num_slots, int32_t H, int32_t d,
-                       int32_t dtype, uint32_t flags, rhz_stream_t stream) {
+                       int32_t dtype, uint32_t flags, void *workspace, size_t workspace_bytes,
+                       rhz_stream_t stream) {
     clear_error();
     return varlen_impl(o, state_pool, slot_idx, cu_seqlens, q, k, v, alpha, beta, nullptr, 0.f,
-                       n_seq, total_tokens, num_slots, H, d, dtype, flags, stream);
+                       n_seq, total_tokens, num_slots, H, d, dtype, flags, workspace,
+                       workspace_bytes, stream);
+}
+
+size_t rhz_gdr_varlen_workspace_bytes(int64_t n_seq, int32_t H, int32_t d, int32_t dtype) {
+    if (n_seq < 0 || H < 1 || d < 1) return 0;
+    return chunk_tc_supports(d, dtype) ? chunk_grid_ws_bytes(n_seq * H, true) : 0;
 }
 
 int rhz_gdr_varlen_fwd_norm(void *o, float *state_pool, const int32_t *slot_idx,
                             const int32_t *cu_seqlens, const void *q, const void *k, const void *v,
                             const float *alpha, const float *beta, const float *norm_scale,
                             float norm_eps, int64_t n_seq, int64_t total_tokens, int64_t num_slots,
-                            int32_t H, int32_t d, int32_t dtype, uint32_t flags, rhz_stream_t stream) {
+                            int32_t H, int32_t d, int32_t dtype, uint32_t flags, void *workspace,
+                            size_t workspace_bytes, rhz_stream_t stream) {
     clear_error();
     if (!(norm_eps >= 0.f)) return set_error(RHZ_ERR_INVALID, "norm_eps must be >= 0");
     RHZ_TRY(check_ptr(norm_scale, "norm_scale", 16, true));
     if (d % 4) return set_error(RHZ_ERR_SHAPE, "the output norm needs d a multiple of 4 (got %d)", d);
     return varlen_impl(o, state_pool, slot_idx, cu_seqlens, q, k, v, alpha, beta, norm_scale,
-                       norm_eps, n_seq, total_tokens, num_slots, H, d, dtype, flags, stream);
+                       norm_eps, n_seq, total_tokens, num_slots, H, d, dtype, flags, workspace,
+                       workspace_bytes, stream);
 }
 
 size_t rhz_gdr_bwd_workspace_bytes(int64_t B, int64_t T, int32_t H, int32_t d) {
@@ -424,9 +455,10 @@ int rhz_groupnorm_heads(void *out, const void *x, const float *scale, int64_t ro
     return launch_groupnorm_heads(out, x, scale, rows, H, d, eps, dtype, as_cuda(stream));
 }
 
-size_t rhz_gdr_workspace_bytes(int64_t B, int64_t T) {
-    if (B < 0 || T < 0) return 0;
-    return seg_ws(B, T).total;
+size_t rhz_gdr_workspace_bytes(int64_t B, int64_t T, int32_t H, int32_t d, int32_t dtype,
+                               int has_segment) {
+    if (B < 0 || T < 0 || H < 1 || d < 1) return 0;
+    return seg_ws(B, T, H, d, dtype, has_segment != 0).total;
 }
 
 int rhz_varlen_prefix_sum(int32_t *cu_seqlens, const int32_t *lengths, int64_t n,
@@ -650,7 +682,7 @@ struct HostPlan {
     int64_t max_pieces;
     size_t tok_bytes, gate_bytes, state_bytes, set_bytes;
     size_t q_off, k_off, v_off, o_off, a_off, b_off;  // within a set
-    size_t pools_off, gates_off, gates_bytes, meta_off, total;
+    size_t pools_off, gates_off, gates_bytes, meta_off, grid_off, grid_bytes, total;
 };
 
 HostPlan host_plan(int64_t B, int64_t T, int32_t H, int32_t d, int32_t dtype, bool has_segment) {
@@ -680,8 +712,11 @@ HostPlan host_plan(int64_t B, int64_t T, int32_t H, int32_t d, int32_t dtype, bo
     p.meta_off = p.gates_off + 2 * p.gates_bytes;
     // per slab: row offsets (B + 1), piece offsets (pieces + 1), in slots,
     // out slots
-    p.total = p.meta_off + up((3 * static_cast<size_t>(p.max_pieces) +
-                               p.n_slabs * static_cast<size_t>(B + 2)) * sizeof(int32_t));
+    p.grid_off = p.meta_off + up((3 * static_cast<size_t>(p.max_pieces) +
+                                  p.n_slabs * static_cast<size_t>(B + 2)) * sizeof(int32_t));
+    // the tensor-core kernel's scratch, shared by the slabs (one scan at a time)
+    p.grid_bytes = chunk_tc_supports(d, dtype) ? up(chunk_grid_ws_bytes(p.max_pieces * H, true)) : 0;
+    p.total = p.grid_off + p.grid_bytes;
     return p;
 }
 
@@ -881,6 +916,8 @@ int rhz_gdr_scan_chunked_host(void *o, float *state_final, const void *q, const 
         a.out_slots = dmeta + out_at[j];
         a.num_slots = B;
         a.H = H; a.d = d; a.dtype = dtype; a.stream = cs;
+        a.ws = pl.grid_bytes ? ws + pl.grid_off : nullptr;
+        a.ws_bytes = pl.grid_bytes;
         st = run_seq(a);
         if (st != RHZ_OK) break;
         e = cudaEventRecord(hs.comp[set], cs);

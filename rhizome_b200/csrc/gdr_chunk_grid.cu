@@ -1,0 +1,1615 @@
+// Chunked gated delta-rule prefill on the sm_100a tensor cores (bf16 inputs,
+// fp32 state and accumulation), d_k = d_v = 128, chunk C = 64.
+//
+// Math (per sequence and head; S is d_v x d_k, row i = v index): inside a
+// chunk of positions t = 0..C-1 that starts from state S0,
+//   P[t][s] = prod_{r=s+1..t} alpha_r (s <= t),  gamma_t = prod_{r=0..t} alpha_r
+//   A[t][s] = beta_t P[t][s] (k_t . k_s) for s < t, T = (I + A)^-1
+//   U = T diag(beta) V,  W = T diag(beta gamma) K,  Delta = U - W S0^T
+//   O[t] = gamma_t S0 q_t + sum_{s<=t} P[t][s] (q_t . k_s) Delta_s
+//   S_C = gamma_{C-1} S0 + sum_s P[C-1][s] Delta_s k_s^T
+// which equals C applications of gated_delta_step (crates/ops/src/delta.rs:
+// 93-127): S_t = alpha_t S_{t-1} + Delta_t k_t^T with
+// Delta_t = beta_t (v_t - alpha_t S_{t-1} k_t).
+//
+// Decays: with gl_t the prefix sum of log2(alpha) over the chunk's nonzero
+// alphas and z_t the number of zero alphas so far,
+//   P[t][s] = (z_t == z_s) ? exp2(gl_t - gl_s) : 0,
+// so alpha = 0 (a reset) gives exactly zero and the table costs one exp2 per
+// entry with no sequential product chain; only differences t >= s are ever
+// exponentiated (never above 1, no overflow).
+//
+// Work split. Everything that depends only on one chunk's keys and gates --
+// the decayed [K; Q] K^T, the unit-lower-triangular inverse T, T diag(beta)
+// and W -- is independent across chunks; only the products with S form the
+// sequential chain of each (sequence, head) item. The kernel is one
+// cooperative launch of one CTA per SM in two roles:
+//   chains (the first n_chains CTAs): item j, j + n_chains, ... one after
+//     the other, S in TMEM (fp32) for the whole sequence, an fp16 copy in
+//     shared memory as the MMA operand, and two MMA rounds per chunk:
+//       R1: D_U  = V^T (T diag b)^T + S (-W^T)   (128 x 64, = Delta^T)
+//           D_O  = Q~ S^T                         ( 64 x 128), Q~ = diag(gamma) Q
+//       R2: D_O += M Delta                        ( 64 x 128)
+//           D_S += Delta^T K~                     (128 x 128), K~ = diag(P[C-1]) K
+//     with D_S pre-scaled by gamma_{C-1} when the previous chunk's state is
+//     refreshed. Its tiles arrive by TMA one chunk ahead and are converted to
+//     fp16 in place (Q and K rows scaled on the way) under the R1 products.
+//   producers (the other CTAs): chunk records for every chain, in
+//     round-major order (round r of every chain before round r + 1 of any),
+//     so all chains are fed evenly. A record is the 32 KB {-W^T, T diag(beta),
+//     M = P (Q K^T)} as ready-made fp16 operand images (128-byte swizzle):
+//     D1 = [K; Q] K^T (bf16 tiles), A (fp32) and M, the inverse (diagonal
+//     16 x 16 tiles by the product formula, the rest by a 2 x 2 recursion on
+//     mma.sync), D_W = K^T (T diag(beta gamma))^T on tcgen05.
+// Records travel through a ring of RING slots per chain in the caller's
+// workspace (L2-resident: a few MB): the producer bulk-stores the record and
+// publishes the slot with a release flag; the chain acquires the flag, bulk-
+// loads the record into shared memory and releases the slot. Every product
+// takes fp16 operands except D1 (A and B of one MMA always share a type);
+// fp16 intermediates bound |q.k|, |v|, |S| to < 65504 (unit-norm keys, as
+// the reference specifies, keep them far below).
+//
+// Each chain's result depends only on its own item's inputs and every
+// record is computed the same way whichever producer builds it, so outputs
+// are batch invariant and bitwise deterministic. Every wait is bounded; a
+// timeout sets a sticky device flag and a workspace abort flag that ends the
+// other CTAs' waits, drains what is in flight (bounded), frees TMEM and
+// returns. No load uses multicast.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <climits>
+#include <cstdint>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace rhz {
+
+// Sticky per-device flag: set when a bounded device-side wait ran out.
+__device__ int g_grid_status = 0;
+
+namespace {
+using namespace sm100;
+
+constexpr int CH = 64;    // chunk length
+constexpr int HD = 128;   // head dim (d_k = d_v)
+constexpr int NT = 256;   // threads per CTA
+constexpr int AST = 68;   // fp32 row stride of the A / T tables (16-byte rows, bank spread)
+
+constexpr uint32_t KQ_STAGE = 32768;  // [half][K rows | Q rows], 64 x 64 bf16 boxes
+constexpr uint32_t V_STAGE = 16384;   // [half][V rows]
+constexpr uint32_t KQ_BYTES = 4 * 8192;
+constexpr uint32_t KQV_BYTES = 6 * 8192;
+
+// Producer -> chain record: fp16 operand images, 128-byte swizzle.
+constexpr uint32_t REC_WT = 0;        // -W^T [j = 128 rows][t = 64]     (MN-major B of R1)
+constexpr uint32_t REC_TT = 16384;    // T diag(beta) [t = 64 rows][s]   (K-major B of R1)
+constexpr uint32_t REC_M = 24576;     // M = P (Q K^T) [t rows][s]        (K-major A of R2)
+constexpr uint32_t REC_BYTES = 32768;
+
+// Gate table layout (floats): gl[64] z[64] (int) beta[64] gamma[64] P[C-1][.][64] beta*gamma[64].
+constexpr int G_GL = 0, G_Z = 64, G_BE = 128, G_GM = 192, G_PL = 256, G_BG = 320, G_SIZE = 384;
+constexpr uint32_t G_BYTES = G_SIZE * 4;
+
+// Chain CTA shared memory.
+constexpr uint32_t C_OFF_KQ = 0;             // 2 stages
+constexpr uint32_t C_OFF_V = 65536;          // 2 stages
+constexpr uint32_t C_OFF_REC = 98304;        // 2 record slots
+constexpr uint32_t C_OFF_S = 163840;         // fp16 state [half j][128 rows i][64 j]
+constexpr uint32_t C_OFF_DT = 196608;        // fp16 Delta^T [i = 128 rows][s]
+constexpr uint32_t C_OFF_GATE = 212992;      // ring of 4 gate tables
+constexpr uint32_t C_OFF_BAR = C_OFF_GATE + 4 * G_BYTES;
+// Chain barriers: tiles landed [2], record landed [2] (bulk load from the
+// ring), D_U done (R1), D_S
+// done (R2), all of a chunk's products done, tiles converted [2] (warpgroup
+// 1 -> 0), D_O buffer read out [2] (1 -> 0), and a barrier that only the
+// failure path uses to wait for every MMA issued.
+constexpr int CB_LOAD = 0, CB_FULL = 2, CB_R1 = 4, CB_R2S = 5, CB_R2 = 6, CB_CONV = 7, CB_OFREE = 9,
+              CB_DRAIN = 11, CB_NUM = 12;
+constexpr uint32_t C_OFF_NORM = C_OFF_BAR + 128;  // output-norm scale, HD floats
+constexpr uint32_t C_USED = C_OFF_NORM + HD * 4;
+static_assert(C_OFF_NORM >= C_OFF_BAR + CB_NUM * 8 + 16, "chain barriers overlap the norm scale");
+
+// Producer CTA shared memory.
+constexpr uint32_t P_OFF_KQ = 0;             // 2 stages of K, Q tiles
+constexpr uint32_t P_OFF_STG = 65536;        // 2 records being built
+constexpr uint32_t P_OFF_TH = 131072;        // T diag(beta gamma) [t][s] as bf16 hi, lo (2 x 8 KB); earlier the solve's scratch
+constexpr uint32_t P_OFF_AF = 147456;        // A fp32 [64][AST]
+constexpr uint32_t P_OFF_TF = P_OFF_AF + 64 * AST * 4;   // T fp32 [64][AST]
+constexpr uint32_t P_OFF_GATE = P_OFF_TF + 64 * AST * 4; // 2 gate tables
+constexpr uint32_t P_OFF_BAR = P_OFF_GATE + 2 * G_BYTES;
+// Producer barriers: tiles landed [2], D1 done, D_W done, failure-path drain
+// of every MMA issued (one per issuing thread).
+constexpr int PB_LOAD = 0, PB_D1 = 2, PB_MMA = 3, PB_DRAIN = 4, PB_DRAIN2 = 5, PB_NUM = 6;
+constexpr uint32_t P_USED = P_OFF_BAR + PB_NUM * 8 + 16;  // + TMEM base
+
+constexpr uint32_t SMEM_USED = C_USED > P_USED ? C_USED : P_USED;
+constexpr size_t SMEM_ALLOC = SMEM_USED + 1024;  // slack for 1024-byte alignment
+static_assert(C_OFF_GATE >= C_OFF_DT + 16384, "chain map overlaps");
+static_assert(P_OFF_AF >= P_OFF_TH + 16384, "producer map overlaps");
+static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in shared memory");
+
+// TMEM columns (f32). Chain: D_U (128 lanes x 64), D_S (128 x 128) and two
+// D_O buffers (M = 64: row t in lane 32 (t / 16) + t % 16, 128 columns).
+// Producer: D1 (128 x 64) and D_W (128 x 64).
+constexpr uint32_t TM_U = 0, TM_S = 64, TM_O = 192, C_TM_COLS = 512;
+constexpr uint32_t TM_D1 = 0, TM_W = 64, P_TM_COLS = 128;
+
+constexpr uint32_t ID_D1 = idesc_bf16(128, 64, false, false);
+constexpr uint32_t ID_MK64 = idesc_f16(128, 64, true, false);
+constexpr uint32_t ID_MK64_BF = idesc_bf16(128, 64, true, false);
+constexpr uint32_t ID_KM64 = idesc_f16(128, 64, false, true);
+constexpr uint32_t ID_KM128 = idesc_f16(128, 128, false, true);
+constexpr uint32_t ID_O = idesc_f16(64, 128, false, false);
+
+// Record ring: RING slots of REC_BYTES per chain; flags in the workspace.
+constexpr int RING = 4;
+constexpr int MAX_CHAINS = 128;
+
+struct GParams {
+    __nv_bfloat16 *o;
+    const float *alpha, *beta;
+    const int32_t *cu_seqlens, *n_seq_dev;
+    int64_t n_seq, seq_len, total_tokens;
+    const float *state_in;
+    const int32_t *in_slots;
+    float *state_out;
+    const int32_t *out_slots;
+    int64_t num_slots;
+    int H;
+    const float *norm_scale;  // non-null: groupnorm_heads on each O row in the epilogue
+    float norm_eps;
+    // grid
+    uint8_t *ring;        // [n_chains][RING][REC_BYTES]
+    int *ready;           // [n_chains][RING]: round + 1 of the record the slot holds
+    int *consumed;        // [n_chains]: rounds the chain has taken out of its ring
+    int *abort_flag;      // set by any CTA whose bounded wait ran out
+    const int32_t *off;   // packed streams: [items] first round of each item in its chain
+    const int32_t *sched; // packed streams: [0] rounds of the longest chain, [1 + j] rounds of chain j
+    int n_chains;
+    int n_prod;           // producer CTAs
+};
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float lg2(float x) {
+    float y;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// 8 consecutive values as one 16-byte fp16 chunk.
+__device__ __forceinline__ uint4 pack8_f16(const float *v) {
+    uint4 w;
+    w.x = pack_f16x2(v[0], v[1]);
+    w.y = pack_f16x2(v[2], v[3]);
+    w.z = pack_f16x2(v[4], v[5]);
+    w.w = pack_f16x2(v[6], v[7]);
+    return w;
+}
+
+// 32 values as fp16 into 16-byte chunks c0 .. c0+3 of row `row` of a
+// 128-byte-swizzled block of 128-byte rows (canonical SWIZZLE_128B layout).
+__device__ __forceinline__ void st_row32_f16(uint8_t *blk, uint32_t row, uint32_t c0,
+                                             const float *v) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + c)) = pack8_f16(v + 8 * c);
+}
+
+// 16 values as fp16 into 16-byte chunks c0, c0+1 (same layout as st_row32_f16).
+__device__ __forceinline__ void st_row16_f16(uint8_t *blk, uint32_t row, uint32_t c0, const float *v) {
+    *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0)) = pack8_f16(v);
+    *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + 1)) = pack8_f16(v + 8);
+}
+
+// 16 values as a bf16 pair hi = bf16(v), lo = bf16(v - hi) into chunks c0,
+// c0+1 of row `row` of two blocks of the st_row32_f16 layout (hi + lo
+// carries ~16 mantissa bits).
+__device__ __forceinline__ void st_row16_bf16_split(uint8_t *hi_blk, uint8_t *lo_blk, uint32_t row,
+                                                    uint32_t c0, const float *v) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float a = v[8 * c + 2 * e], b = v[8 * c + 2 * e + 1];
+            const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+            const __nv_bfloat162 l = __floats2bfloat162_rn(a - __low2float(h), b - __high2float(h));
+            hi[e] = *reinterpret_cast<const uint32_t *>(&h);
+            lo[e] = *reinterpret_cast<const uint32_t *>(&l);
+        }
+        *reinterpret_cast<uint4 *>(hi_blk + sw128_offset(row, c0 + c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4 *>(lo_blk + sw128_offset(row, c0 + c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+
+__device__ __forceinline__ void st_zero32(uint8_t *blk, uint32_t row, uint32_t c0) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + c)) = make_uint4(0, 0, 0, 0);
+}
+
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x, float s) {
+    __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162 *>(&x);
+    return pack_f16x2(__low2float(b) * s, __high2float(b) * s);
+}
+
+// Chain: one stage's K, Q (32 KB) and V (16 KB) tiles bf16 -> fp16 in place,
+// Q rows scaled by gamma_t and K rows by P[C-1][s]; this thread's 16-byte
+// chunks are first, first + STRIDE, ... of the K/Q stage (2048 chunks) and of
+// the V stage (1024). The swizzle permutes chunks within a row only, so chunk
+// i of a K/Q half lies in row (i / 8) % 128 (rows 0..63 K, 64..127 Q).
+template <int STRIDE>
+__device__ __forceinline__ void chain_tiles_to_f16(uint8_t *kq, uint8_t *vv, const float *gm,
+                                                   const float *pl, int first) {
+    static_assert(2048 % (8 * STRIDE) == 0 && 1024 % (8 * STRIDE) == 0, "batches of 8 chunks");
+    // Eight loads in flight, then eight converted stores (batches rolled to
+    // keep the code small).
+#pragma unroll 1
+    for (int b = 0; b < 2048 / STRIDE; b += 8) {
+        uint4 x[8];
+        float sc[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const int i = first + (b + m) * STRIDE;
+            const int r = (i >> 3) & 127;
+            x[m] = *reinterpret_cast<const uint4 *>(kq + i * 16);
+            sc[m] = r < 64 ? pl[r] : gm[r - 64];
+        }
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const int i = first + (b + m) * STRIDE;
+            uint4 w = x[m];
+            w.x = bf16x2_to_f16x2(w.x, sc[m]);
+            w.y = bf16x2_to_f16x2(w.y, sc[m]);
+            w.z = bf16x2_to_f16x2(w.z, sc[m]);
+            w.w = bf16x2_to_f16x2(w.w, sc[m]);
+            *reinterpret_cast<uint4 *>(kq + i * 16) = w;
+        }
+    }
+#pragma unroll 1
+    for (int b = 0; b < 1024 / STRIDE; b += 8) {
+        uint4 x[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) x[m] = *reinterpret_cast<const uint4 *>(vv + (first + (b + m) * STRIDE) * 16);
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            uint4 w = x[m];
+            w.x = bf16x2_to_f16x2(w.x, 1.f);
+            w.y = bf16x2_to_f16x2(w.y, 1.f);
+            w.z = bf16x2_to_f16x2(w.z, 1.f);
+            w.w = bf16x2_to_f16x2(w.w, 1.f);
+            *reinterpret_cast<uint4 *>(vv + (first + (b + m) * STRIDE) * 16) = w;
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t h2(float a, float b) { return pack_f16x2(a, b); }
+
+// D (16 x 8, fp32) += A (16 x 16, fp16) * B (16 x 8, fp16) on the warp's
+// legacy tensor-core path (mma.sync m16n8k16); fragments per the PTX layout
+// with g = lane / 4, t = lane % 4.
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// A fragment of the 16 x 16 fp32 tile at L (row stride ls), rounded to fp16.
+__device__ __forceinline__ void frag_a(const float *L, int ls, int lane, uint32_t (&a)[4]) {
+    const int g = lane >> 2, t = lane & 3;
+    const float2 x0 = *reinterpret_cast<const float2 *>(L + g * ls + 2 * t);
+    const float2 x1 = *reinterpret_cast<const float2 *>(L + (g + 8) * ls + 2 * t);
+    const float2 x2 = *reinterpret_cast<const float2 *>(L + g * ls + 2 * t + 8);
+    const float2 x3 = *reinterpret_cast<const float2 *>(L + (g + 8) * ls + 2 * t + 8);
+    a[0] = h2(x0.x, x0.y);
+    a[1] = h2(x1.x, x1.y);
+    a[2] = h2(x2.x, x2.y);
+    a[3] = h2(x3.x, x3.y);
+}
+
+// B fragment of the 16 x 8 fp32 tile at R (row-major [k][n], row stride rs).
+__device__ __forceinline__ void frag_b(const float *R, int rs, int lane, uint32_t (&b)[2]) {
+    const int g = lane >> 2, t = lane & 3;
+    b[0] = h2(R[(2 * t) * rs + g], R[(2 * t + 1) * rs + g]);
+    b[1] = h2(R[(2 * t + 8) * rs + g], R[(2 * t + 9) * rs + g]);
+}
+
+// Store the 16 x 8 accumulator (times `sign`) into fp32 rows at C (stride cs).
+__device__ __forceinline__ void st_frag_c(float *C, int cs, int lane, const float (&d)[4], float sign) {
+    const int g = lane >> 2, t = lane & 3;
+    *reinterpret_cast<float2 *>(C + g * cs + 2 * t) = make_float2(sign * d[0], sign * d[1]);
+    *reinterpret_cast<float2 *>(C + (g + 8) * cs + 2 * t) = make_float2(sign * d[2], sign * d[3]);
+}
+
+// Transpose of one 8 x 8 fp16 block held in the mma fragment layout.
+__device__ __forceinline__ uint32_t movtrans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+// A fragment (fp16) of a 16 x 16 matrix from its two 16 x 8 accumulator halves.
+__device__ __forceinline__ void c_to_a(const float (&c0)[4], const float (&c1)[4], uint32_t (&a)[4]) {
+    a[0] = h2(c0[0], c0[1]);
+    a[1] = h2(c0[2], c0[3]);
+    a[2] = h2(c1[0], c1[1]);
+    a[3] = h2(c1[2], c1[3]);
+}
+
+// B fragments (both 16 x 8 column halves) of the matrix whose A fragment is
+// `a`: the B layout of X is the A layout of X^T, block by block.
+__device__ __forceinline__ void a_to_b(const uint32_t (&a)[4], uint32_t (&b0)[2], uint32_t (&b1)[2]) {
+    b0[0] = movtrans(a[0]);
+    b0[1] = movtrans(a[1]);
+    b1[0] = movtrans(a[2]);
+    b1[1] = movtrans(a[3]);
+}
+
+// Inverse of the unit-lower-triangular 16 x 16 block I + N (N strictly lower,
+// fp32 in A at row stride AST) written to T (same stride), by one warp:
+// (I + N)^-1 = (I - N)(I + N^2)(I + N^4)(I + N^8), exact for nilpotent N of
+// order 16, as 12 mma.sync products with fp16 operands and fp32 accumulation.
+__device__ __forceinline__ void diag_inverse16(const float *A, float *T, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    float n0[4], n1[4];
+    {
+        const float2 a0 = *reinterpret_cast<const float2 *>(A + g * AST + 2 * t);
+        const float2 a1 = *reinterpret_cast<const float2 *>(A + (g + 8) * AST + 2 * t);
+        const float2 a2 = *reinterpret_cast<const float2 *>(A + g * AST + 8 + 2 * t);
+        const float2 a3 = *reinterpret_cast<const float2 *>(A + (g + 8) * AST + 8 + 2 * t);
+        n0[0] = a0.x; n0[1] = a0.y; n0[2] = a1.x; n0[3] = a1.y;
+        n1[0] = a2.x; n1[1] = a2.y; n1[2] = a3.x; n1[3] = a3.y;
+    }
+    // X = I - N in the accumulator layout (row g / g + 8, columns 8h + 2t, +1).
+    float x0[4], x1[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int r = g + 8 * (e >> 1), c = 2 * t + (e & 1);
+        x0[e] = (r == c ? 1.f : 0.f) - n0[e];
+        x1[e] = (r == c + 8 ? 1.f : 0.f) - n1[e];
+    }
+    uint32_t aP[4], bP0[2], bP1[2], aX[4];
+    c_to_a(n0, n1, aP);
+    a_to_b(aP, bP0, bP1);
+#pragma unroll
+    for (int lvl = 0; lvl < 3; ++lvl) {
+        // P <- P^2 (N^2, N^4, N^8), then X <- X + X P.
+        float p0[4] = {0.f, 0.f, 0.f, 0.f}, p1[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(p0, aP, bP0);
+        mma16816(p1, aP, bP1);
+        c_to_a(p0, p1, aP);
+        a_to_b(aP, bP0, bP1);
+        c_to_a(x0, x1, aX);
+        mma16816(x0, aX, bP0);
+        mma16816(x1, aX, bP1);
+    }
+    st_frag_c(T, AST, lane, x0, 1.f);
+    st_frag_c(T + 8, AST, lane, x1, 1.f);
+}
+
+// Off-diagonal part of T = (I + A)^-1 once the four diagonal 16 x 16 inverses
+// D_I are in Tf (and Tf's tiles (0,1) and (2,3) are zero), by a 2 x 2
+// recursion: T_{2p+1,2p} = -D_{2p+1} (A_{2p+1,2p} D_{2p}) for p = 0, 1, then
+// T[32:64, 0:32] = -T[32:64, 32:64] (A[32:64, 0:32] T[0:32, 0:32]). The
+// products run on mma.sync with fp16 operands (T is rounded to fp16 for the
+// tcgen05 products anyway), on all eight warps. Ends synchronised.
+__device__ void solve_offdiag(const float *Af, float *Tf, float *Xf, int warp, int lane) {
+    if (warp < 4) {
+        const int pb = warp >> 1, nt = warp & 1;
+        const int r0 = 32 * pb + 16, c0 = 32 * pb;  // tile (2p+1, 2p)
+        uint32_t a[4], b[2];
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        frag_a(Af + r0 * AST + c0, AST, lane, a);
+        frag_b(Tf + c0 * AST + c0 + 8 * nt, AST, lane, b);
+        mma16816(x, a, b);
+        float *X = Xf + pb * 256 + 8 * nt;  // [16][16]
+        st_frag_c(X, 16, lane, x, 1.f);
+        __syncwarp();
+        float y[4] = {0.f, 0.f, 0.f, 0.f};
+        frag_a(Tf + r0 * AST + r0, AST, lane, a);
+        frag_b(X, 16, lane, b);
+        mma16816(y, a, b);
+        st_frag_c(Tf + r0 * AST + c0 + 8 * nt, AST, lane, y, -1.f);
+    }
+    __syncthreads();
+    const int mt = warp >> 2, nt = warp & 3;
+    {
+        float y[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+            uint32_t a[4], b[2];
+            frag_a(Af + (32 + 16 * mt) * AST + 16 * ks, AST, lane, a);
+            frag_b(Tf + (16 * ks) * AST + 8 * nt, AST, lane, b);
+            mma16816(y, a, b);
+        }
+        st_frag_c(Xf + (16 * mt) * 32 + 8 * nt, 32, lane, y, 1.f);  // Y [32][32]
+    }
+    __syncthreads();
+    {
+        float y[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+            uint32_t a[4], b[2];
+            frag_a(Tf + (32 + 16 * mt) * AST + 32 + 16 * ks, AST, lane, a);
+            frag_b(Xf + (16 * ks) * 32 + 8 * nt, 32, lane, b);
+            mma16816(y, a, b);
+        }
+        st_frag_c(Tf + (32 + 16 * mt) * AST + 8 * nt, AST, lane, y, -1.f);
+    }
+    __syncthreads();
+}
+
+// Make thread-written smem operands and TMEM stores visible to the MMA issuer.
+__device__ __forceinline__ void operands_ready() {
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+}
+
+struct Ref {
+    int64_t item, ts;  // item < 0: no chunk
+    int L, h;
+    int r, j;          // producer tasks: round and chain
+};
+
+// The chunks a chain processes, in order: items start, start + stride, ...
+// (stride = number of chains) and within an item its chunks of CH positions
+// from the sequence start; the k-th chunk is the chain's round k and uses
+// tile stage, record slot and gate table k & 1 (k & 3 for gate tables).
+struct Walk {
+    const GParams *p;
+    int64_t n_items, stride;
+    int H;
+
+    __device__ void bounds(int64_t item, int64_t &t0, int64_t &t1) const {
+        const int64_t seq = item / H;
+        if (p->cu_seqlens) {
+            // Offsets are caller data: clamp them to the packed stream.
+            t0 = p->cu_seqlens[seq];
+            t1 = p->cu_seqlens[seq + 1];
+            t0 = t0 < 0 ? 0 : (t0 > p->total_tokens ? p->total_tokens : t0);
+            t1 = t1 < t0 ? t0 : (t1 > p->total_tokens ? p->total_tokens : t1);
+        } else {
+            t0 = seq * p->seq_len;
+            t1 = t0 + p->seq_len;
+        }
+    }
+    // First chunk at or after item `it` (skipping empty sequences).
+    __device__ Ref first_from(int64_t it) const {
+        for (; it < n_items; it += stride) {
+            int64_t t0, t1;
+            bounds(it, t0, t1);
+            if (t1 > t0) {
+                const int64_t seq = it / H;
+                return Ref{it, t0, static_cast<int>((t1 - t0) < CH ? (t1 - t0) : CH),
+                           static_cast<int>(it - seq * H), 0, 0};
+            }
+        }
+        return Ref{-1, 0, 0, 0, 0, 0};
+    }
+    __device__ Ref next_of(const Ref &r) const {
+        int64_t t0, t1;
+        bounds(r.item, t0, t1);
+        const int64_t tn = r.ts + CH;
+        if (tn < t1) return Ref{r.item, tn, static_cast<int>((t1 - tn) < CH ? (t1 - tn) : CH), r.h, 0, 0};
+        return first_from(r.item + stride);
+    }
+    // The chunk n steps after chunk c of `item` (bounds [t0, t1), nch chunks,
+    // head h): arithmetic inside the item, the walk only past its end (once
+    // per item rather than once per chunk).
+    __device__ Ref after(int64_t item, int h, int64_t t0, int64_t t1, int nch, int c, int n) const {
+        const int cc = c + n;
+        if (cc < nch) {
+            const int64_t ts = t0 + static_cast<int64_t>(cc) * CH;
+            return Ref{item, ts, static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH), h, 0, 0};
+        }
+        Ref r = first_from(item + stride);
+        for (int i = nch; i < cc && r.item >= 0; ++i) r = next_of(r);
+        return r;
+    }
+};
+
+// Producer tasks in round-major order: task t is round t / n_chains of chain
+// t % n_chains. Dense batches (every item has nch chunks) map a round to its
+// item by arithmetic; packed streams use the per-item round offsets `off`
+// that gdr_grid_sched_kernel computed (the item is the last one of its chain
+// whose offset is <= r; an empty item shares its offset with the next item,
+// which comes later in the chain, so the search never lands on it).
+struct Sched {
+    const GParams *p;
+    const Walk *wk;
+    int64_t n_items;
+    int NC;
+    int nch;       // dense: chunks per item; 0: packed stream (tables)
+    int64_t n_tasks;
+
+    __device__ int rounds(int j) const {
+        if (nch > 0) {
+            const int64_t m = (n_items - j + NC - 1) / NC;
+            return m > 0 ? static_cast<int>(m * nch) : 0;
+        }
+        return p->sched[1 + j];
+    }
+    // Task t, or item < 0 if that chain has no round t / NC.
+    __device__ Ref at(int64_t t) const {
+        const int r = static_cast<int>(t / NC), j = static_cast<int>(t - static_cast<int64_t>(r) * NC);
+        Ref out{-1, 0, 0, 0, r, j};
+        if (r >= rounds(j)) return out;
+        int64_t item;
+        int c;
+        if (nch > 0) {
+            const int m = r / nch;
+            c = r - m * nch;
+            item = j + static_cast<int64_t>(m) * NC;
+        } else {
+            int64_t lo = 0, hi = (n_items - j + NC - 1) / NC - 1;  // largest m with off <= r
+            while (lo < hi) {
+                const int64_t mid = (lo + hi + 1) >> 1;
+                if (p->off[j + mid * NC] <= r) lo = mid; else hi = mid - 1;
+            }
+            item = j + lo * NC;
+            c = r - p->off[item];
+        }
+        int64_t t0, t1;
+        wk->bounds(item, t0, t1);
+        const int64_t seq = item / p->H;
+        out.item = item;
+        out.ts = t0 + static_cast<int64_t>(c) * CH;
+        out.L = static_cast<int>((t1 - out.ts) < CH ? (t1 - out.ts) : CH);
+        out.h = static_cast<int>(item - seq * p->H);
+        return out;
+    }
+    // The first non-empty task at or after t among t, t + step, ...
+    __device__ Ref first_from(int64_t t, int64_t step) const {
+        for (; t < n_tasks; t += step) {
+            const Ref r = at(t);
+            if (r.item >= 0) return r;
+        }
+        return Ref{-1, 0, 0, 0, 0, 0};
+    }
+};
+
+// Gate inputs of one chunk for one warp (two positions per lane), loaded a
+// chunk ahead of their use so the global latency stays off the critical
+// path. Padded positions get alpha = 1, beta = 0 so they write nothing.
+struct GateIn {
+    float a0, a1, b0, b1;
+};
+
+__device__ __forceinline__ GateIn gate_load(const GParams &p, const Ref &r, int lane) {
+    GateIn g{1.f, 1.f, 0.f, 0.f};
+    if (r.item < 0) return g;
+    const int H = p.H;
+    const int p0 = 2 * lane, p1 = p0 + 1;
+    if (p0 < r.L) {
+        g.a0 = p.alpha[(r.ts + p0) * H + r.h];
+        g.b0 = p.beta[(r.ts + p0) * H + r.h];
+    }
+    if (p1 < r.L) {
+        g.a1 = p.alpha[(r.ts + p1) * H + r.h];
+        g.b1 = p.beta[(r.ts + p1) * H + r.h];
+    }
+    return g;
+}
+
+// Gate tables of one chunk (one warp): prefix sums of log2 alpha over nonzero
+// alphas and of zero-alpha counts, then gamma_t, P[C-1][s], beta, beta*gamma.
+__device__ __forceinline__ void gate_tables(float *g, const GateIn &in, int lane) {
+    int *zz = reinterpret_cast<int *>(g + G_Z);
+    const int p0 = 2 * lane, p1 = p0 + 1;
+    const float a0 = in.a0, a1 = in.a1, b0 = in.b0, b1 = in.b1;
+    const bool nz0 = a0 >= 1.17549435e-38f, nz1 = a1 >= 1.17549435e-38f;
+    const float l0 = nz0 ? lg2(a0) : 0.f, l1 = nz1 ? lg2(a1) : 0.f;
+    const int z0 = nz0 ? 0 : 1, z1 = nz1 ? 0 : 1;
+    float ls = l0 + l1;
+    int zs = z0 + z1;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const float lo = __shfl_up_sync(0xffffffffu, ls, off);
+        const int zo = __shfl_up_sync(0xffffffffu, zs, off);
+        if (lane >= off) { ls += lo; zs += zo; }
+    }
+    const float g1 = ls, g0 = ls - l1;  // inclusive prefix at p1, p0
+    const int y1 = zs, y0 = zs - z1;
+    const float g63 = __shfl_sync(0xffffffffu, g1, 31);
+    const int y63 = __shfl_sync(0xffffffffu, y1, 31);
+    g[G_GL + p0] = g0; g[G_GL + p1] = g1;
+    zz[p0] = y0; zz[p1] = y1;
+    g[G_BE + p0] = b0; g[G_BE + p1] = b1;
+    const float gm0 = y0 == 0 ? ex2(g0) : 0.f, gm1 = y1 == 0 ? ex2(g1) : 0.f;
+    g[G_GM + p0] = gm0; g[G_GM + p1] = gm1;
+    g[G_BG + p0] = b0 * gm0; g[G_BG + p1] = b1 * gm1;
+    g[G_PL + p0] = y0 == y63 ? ex2(g63 - g0) : 0.f;
+    g[G_PL + p1] = y1 == y63 ? ex2(g63 - g1) : 0.f;
+}
+
+struct RoleState {
+    bool failed;
+};
+
+// ------------------------------------------------------------------ chain CTA
+//
+// Warpgroup 0 runs the serial state path of every chunk k: record k, tiles k
+// converted and D_O buffer k & 1 free -> R1 -> Delta^T -> R2 -> state
+// refresh. Warpgroup 1 works beside it: gate tables two chunks ahead, the
+// fp16 conversion of chunk k + 1's tiles under chunk k's products, and, once
+// R2(k) is done, the release of stage / record slot k & 1, the loads of chunk
+// k + 2 and the O rows of chunk k from D_O[k & 1]. Every barrier phase has a
+// single producer and is consumed before it can be reused, so parities never
+// alias.
+__device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k,
+                                                const CUtensorMap *tm_v, const GParams &p,
+                                                uint8_t *smem, const Walk &wk, int64_t start,
+                                                uint32_t tmem) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ww = warp & 3;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(ww) << 21);  // lanes 32 ww .. 32 ww + 31
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C_OFF_BAR);
+    uint64_t *bar_load = bars + CB_LOAD, *bar_full = bars + CB_FULL, *bar_r1 = bars + CB_R1,
+             *bar_r2s = bars + CB_R2S, *bar_r2 = bars + CB_R2, *bar_conv = bars + CB_CONV,
+             *bar_ofree = bars + CB_OFREE;
+    const uint32_t sbase = smem_u32(smem);
+    const int H = p.H;
+    const int64_t tok_stride = static_cast<int64_t>(H) * HD;
+    auto gates = [&](int kc) { return reinterpret_cast<float *>(smem + C_OFF_GATE) + (kc & 3) * G_SIZE; };
+    const int chain = static_cast<int>(start);
+    int *consumed = p.consumed + chain;
+    RoleState rs{false};
+
+    if (tid < 128) {
+        // ------------------------------------------------ warpgroup 0: state path
+        const int row = tid;  // state row i = TMEM lane
+        int k = 0;
+        for (int64_t item = start; item < wk.n_items && !rs.failed; item += wk.stride) {
+            const int64_t seq = item / H;
+            const int h = static_cast<int>(item - seq * H);
+            int64_t t0, t1;
+            wk.bounds(item, t0, t1);
+            const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
+            int64_t slot = -1;
+            if (p.state_in) slot = p.in_slots ? static_cast<int64_t>(p.in_slots[seq]) : seq;
+            const bool have = p.state_in && slot >= 0 && slot < p.num_slots;
+            const float *src = have ? p.state_in + ((slot * H + h) * HD + row) * HD : nullptr;
+            int64_t so = -1;
+            if (p.state_out) so = p.out_slots ? static_cast<int64_t>(p.out_slots[seq]) : seq;
+            float *dst = (p.state_out && so >= 0 && so < p.num_slots)
+                             ? p.state_out + ((so * H + h) * HD + row) * HD
+                             : nullptr;
+            if (nch == 0) {
+                // Empty sequence: the final state is the initial state.
+                if (dst)
+                    for (int e = 0; e < HD; e += 4)
+                        *reinterpret_cast<float4 *>(dst + e) =
+                            have ? *reinterpret_cast<const float4 *>(src + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+                continue;
+            }
+            for (int c = 0; c < nch; ++c, ++k) {
+                const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
+                (void)ts;
+                const uint32_t kq = sbase + C_OFF_KQ + (k & 1) * KQ_STAGE;
+                const uint32_t vb = sbase + C_OFF_V + (k & 1) * V_STAGE;
+                const uint32_t rec = sbase + C_OFF_REC + (k & 1) * REC_BYTES;
+                const uint32_t tO = tmem + TM_O + 128 * (k & 1);
+
+                // ---- R1's inputs: record k (bulk-loaded from the ring by
+                // warpgroup 1; once it has landed the ring slot is free again),
+                // tiles k in fp16, D_O buffer k & 1 read out
+                bool ok = mbar_wait(&bar_full[k & 1], (k >> 1) & 1);
+                if (ok && tid == 0) st_release_gpu(consumed, k + 1);
+                ok = ok && mbar_wait(&bar_conv[k & 1], (k >> 1) & 1);
+                if (k >= 2) ok = ok && mbar_wait(&bar_ofree[k & 1], ((k >> 1) + 1) & 1);
+                if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
+
+                // ---- first chunk of the item: fp16 copy of S0 (unscaled) and
+                // D_S = gamma_{C-1} S0
+                if (c == 0) {
+                    const float gC = gates(k)[G_GM + 63];
+#pragma unroll 1
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        float v[32];
+#pragma unroll
+                        for (int e = 0; e < 32; e += 4) {
+                            const float4 f = have ? *reinterpret_cast<const float4 *>(src + 32 * q4 + e)
+                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                            v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
+                        }
+                        st_row32_f16(smem + C_OFF_S + (q4 >> 1) * 16384, row, 4 * (q4 & 1), v);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] *= gC;
+                        tmem_st32(trow + TM_S + 32 * q4, v);
+                    }
+                    tmem_wait_st();
+                    fence_proxy_async_smem();
+                    tc_fence_before();
+                    wg_sync(1);
+                }
+
+                // ---- R1: D_U = V^T (T diag b)^T + S (-W^T) ; D_O[k & 1] = Q~ S^T
+                if (tid == 0) {
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_f16(tmem + TM_U, sdesc_sw128(vb + kk * 2048, 8192, 1024),
+                                 sdesc_sw128(rec + REC_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
+#pragma unroll 1
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                        umma_f16(tmem + TM_U, sdesc_sw128(sbase + C_OFF_S + off, 16, 1024),
+                                 sdesc_sw128(rec + REC_WT + kk * 2048, 8192, 1024), ID_KM64, 1);
+                    }
+                    umma_commit(bar_r1);  // Delta^T is ready; D_O runs on behind it
+#pragma unroll 1
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                        umma_f16(tO, sdesc_sw128(kq + off + 8192, 16, 1024),
+                                 sdesc_sw128(sbase + C_OFF_S + off, 16, 1024), ID_O, kk > 0);
+                    }
+                }
+                ok = mbar_wait(bar_r1, k & 1);
+                if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
+                tc_fence_after();
+
+                // ---- Delta^T (fp16): row i, all 64 positions
+                {
+                    float x[32], y[32];
+                    tmem_ld32(trow + TM_U, x);
+                    tmem_ld32(trow + TM_U + 32, y);
+                    tmem_wait_ld();
+                    st_row32_f16(smem + C_OFF_DT, row, 0, x);
+                    st_row32_f16(smem + C_OFF_DT, row, 4, y);
+                }
+                fence_proxy_async_smem();
+                tc_fence_before();
+                wg_sync(1);
+
+                // ---- R2: D_S += Delta^T K~ (the state refresh waits for this
+                // part only), then D_O[k & 1] += M Delta
+                if (tid == 0) {
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_f16(tmem + TM_S, sdesc_sw128(sbase + C_OFF_DT + kk * 32, 16, 1024),
+                                 sdesc_sw128(kq + kk * 2048, 16384, 1024), ID_KM128, 1);
+                    umma_commit(bar_r2s);
+#pragma unroll 1
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_f16(tO, sdesc_sw128(rec + REC_M + kk * 32, 16, 1024),
+                                 sdesc_sw128(sbase + C_OFF_DT + kk * 32, 16, 1024), ID_O, 1);
+                    umma_commit(bar_r2);
+                }
+                ok = mbar_wait(bar_r2s, k & 1);
+                if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
+                tc_fence_after();
+
+                // ---- state: fp16 copy for the next chunk and D_S pre-scaled
+                // by its gamma_{C-1}, or the final state
+                {
+                    const bool more = c + 1 < nch;
+                    const float gn = more ? gates(k + 1)[G_GM + 63] : 1.f;
+#pragma unroll 1
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        float v[32];
+                        tmem_ld32(trow + TM_S + 32 * q4, v);
+                        tmem_wait_ld();
+                        if (more) {
+                            st_row32_f16(smem + C_OFF_S + (q4 >> 1) * 16384, row, 4 * (q4 & 1), v);
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) v[e] *= gn;
+                            tmem_st32(trow + TM_S + 32 * q4, v);
+                        } else if (dst) {
+#pragma unroll
+                            for (int e = 0; e < 32; e += 4)
+                                *reinterpret_cast<float4 *>(dst + 32 * q4 + e) =
+                                    make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+                        }
+                    }
+                    if (more) tmem_wait_st();
+                }
+                fence_proxy_async_smem();
+                tc_fence_before();
+                wg_sync(1);
+            }
+        }
+        if (rs.failed && tid == 0) {
+            // Every MMA this thread issued (including D_O products that no
+            // commit covered yet) completes before TMEM is released.
+            umma_commit(bars + CB_DRAIN);
+            mbar_wait(bars + CB_DRAIN, 0, 200000000ull);
+        }
+    } else {
+        // ------------------------------------------------ warpgroup 1: tiles, epilogue
+        const int wt = tid - 128;
+        int loads_issued = 0, loads_waited = 0, recs_issued = 0;
+        // Round kc's record: wait until a producer has published it in ring
+        // slot kc % RING, then bulk-load it into record slot kc & 1.
+        auto fetch_record = [&](int kc) -> bool {
+            const int slot = kc % RING;
+            if (!poll_ge(p.ready + chain * RING + slot, kc + 1, p.abort_flag)) return false;
+            fence_proxy_async_global();
+            uint64_t *bar = &bar_full[kc & 1];
+            mbar_arrive_expect_tx(bar, REC_BYTES);
+            bulk_load_g2s(smem + C_OFF_REC + (kc & 1) * REC_BYTES,
+                          p.ring + (static_cast<size_t>(chain) * RING + slot) * REC_BYTES, REC_BYTES, bar);
+            ++recs_issued;
+            return true;
+        };
+        GateIn gin{1.f, 1.f, 0.f, 0.f};  // warp 4: inputs of the gate table two chunks ahead
+        auto issue_loads = [&](int kc, const Ref &r) {
+            const uint32_t st = kc & 1;
+            uint64_t *bar = &bar_load[st];
+            uint8_t *kqs = smem + C_OFF_KQ + st * KQ_STAGE;
+            uint8_t *vv = smem + C_OFF_V + st * V_STAGE;
+            mbar_arrive_expect_tx(bar, KQV_BYTES);
+            const int t32 = static_cast<int>(r.ts);
+            tma_load_3d(kqs, tm_k, 0, r.h, t32, bar);
+            tma_load_3d(kqs + 16384, tm_k, 64, r.h, t32, bar);
+            tma_load_3d(kqs + 8192, tm_q, 0, r.h, t32, bar);
+            tma_load_3d(kqs + 24576, tm_q, 64, r.h, t32, bar);
+            tma_load_3d(vv, tm_v, 0, r.h, t32, bar);
+            tma_load_3d(vv + 8192, tm_v, 64, r.h, t32, bar);
+        };
+        auto convert = [&](int kc) {
+            const float *g = gates(kc);
+            chain_tiles_to_f16<128>(smem + C_OFF_KQ + (kc & 1) * KQ_STAGE,
+                                    smem + C_OFF_V + (kc & 1) * V_STAGE, g + G_GM, g + G_PL, wt);
+            fence_proxy_async_smem();
+        };
+
+        float *nsc = reinterpret_cast<float *>(smem + C_OFF_NORM);
+        const bool norm = p.norm_scale != nullptr;
+        if (norm) nsc[wt] = p.norm_scale[wt];  // wt < 128 = HD
+        {
+            const Ref r0 = wk.first_from(start);
+            const Ref r1 = r0.item >= 0 ? wk.next_of(r0) : r0;
+            const Ref r2 = r1.item >= 0 ? wk.next_of(r1) : r1;
+            bool fok = true;
+            if (wt == 0) {
+                if (r0.item >= 0) issue_loads(0, r0);
+                if (r1.item >= 0) issue_loads(1, r1);
+                if (r0.item >= 0) fok = fetch_record(0);
+                if (fok && r1.item >= 0) fok = fetch_record(1);
+            }
+            loads_issued = (r0.item >= 0) + (r1.item >= 0);
+            if (wg_sync_or(2, !fok)) rs.failed = true;
+            if (ww == 0) {
+                gate_tables(gates(0), gate_load(p, r0, lane), lane);
+                gate_tables(gates(1), gate_load(p, r1, lane), lane);
+                gin = gate_load(p, r2, lane);
+            }
+            if (r0.item >= 0 && !rs.failed) {
+                const bool ok = mbar_wait(&bar_load[0], 0);
+                if (wg_sync_or(2, !ok)) {
+                    rs.failed = true;
+                } else {
+                    ++loads_waited;
+                    convert(0);
+                    mbar_arrive(&bar_conv[0]);
+                }
+            }
+        }
+
+        int k = 0;
+        for (int64_t item = start; item < wk.n_items && !rs.failed; item += wk.stride) {
+            const int64_t seq = item / H;
+            const int h = static_cast<int>(item - seq * H);
+            int64_t t0, t1;
+            wk.bounds(item, t0, t1);
+            const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
+            for (int c = 0; c < nch; ++c, ++k) {
+                const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
+                const int L = static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH);
+                const Ref nxt = wk.after(item, h, t0, t1, nch, c, 1);
+                const Ref nn = wk.after(item, h, t0, t1, nch, c, 2);
+
+                // ---- gate table of chunk k + 2, then the inputs of chunk k + 3
+                if (nn.item >= 0 && ww == 0) {
+                    gate_tables(gates(k + 2), gin, lane);
+                    gin = gate_load(p, wk.after(item, h, t0, t1, nch, c, 3), lane);
+                }
+                // ---- chunk k + 1's tiles -> fp16 (under chunk k's products)
+                if (nxt.item >= 0) {
+                    const bool ok = mbar_wait(&bar_load[(k + 1) & 1], ((k + 1) >> 1) & 1);
+                    if (wg_sync_or(2, !ok)) { rs.failed = true; break; }
+                    ++loads_waited;
+                    convert(k + 1);
+                }
+                // ---- chunk k's products are done
+                {
+                    const bool ok = mbar_wait(bar_r2, k & 1);
+                    if (wg_sync_or(2, !ok)) { rs.failed = true; break; }
+                    tc_fence_after();
+                }
+                if (nxt.item >= 0) mbar_arrive(&bar_conv[(k + 1) & 1]);
+                // Stage and record slot k & 1 are free again: chunk k + 2's
+                // tiles, and its record once a producer has published it.
+                bool fok = true;
+                if (wt == 0 && nn.item >= 0) {
+                    issue_loads(k + 2, nn);
+                    fok = fetch_record(k + 2);
+                }
+                if (nn.item >= 0) ++loads_issued;
+                if (wg_sync_or(2, !fok)) { rs.failed = true; break; }
+
+                // ---- O rows of chunk k (D_O row t in lane 32 (t / 16) + t % 16),
+                // optionally RMS-normalised per head first (groupnorm_heads,
+                // norm.rs:48-60, on the fp32 accumulator)
+                {
+                    const uint32_t tO = trow + TM_O + 128 * (k & 1);
+                    const int t = 16 * ww + lane;
+                    const bool has_row = lane < 16 && t < L;
+                    __nv_bfloat16 *op = p.o + (ts + t) * tok_stride + static_cast<int64_t>(h) * HD;
+                    float inv = 1.f;
+                    if (norm) {
+                        float ss = 0.f;
+#pragma unroll 1
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            float o[32];
+                            tmem_ld32(tO + 32 * q4, o);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) ss += o[e] * o[e];
+                        }
+                        inv = 1.f / sqrtf(ss / static_cast<float>(HD) + p.norm_eps);
+                    }
+#pragma unroll 1
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        float o[32];
+                        tmem_ld32(tO + 32 * q4, o);
+                        tmem_wait_ld();
+                        if (norm) {
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) o[e] = o[e] * inv * nsc[32 * q4 + e];
+                        }
+                        if (has_row) {
+#pragma unroll
+                            for (int c8 = 0; c8 < 4; ++c8) {
+                                uint4 w;
+                                w.x = pack_bf16x2(o[8 * c8 + 0], o[8 * c8 + 1]);
+                                w.y = pack_bf16x2(o[8 * c8 + 2], o[8 * c8 + 3]);
+                                w.z = pack_bf16x2(o[8 * c8 + 4], o[8 * c8 + 5]);
+                                w.w = pack_bf16x2(o[8 * c8 + 6], o[8 * c8 + 7]);
+                                *reinterpret_cast<uint4 *>(op + 32 * q4 + 8 * c8) = w;
+                            }
+                        }
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&bar_ofree[k & 1]);
+                }
+            }
+        }
+        if (rs.failed && wt == 0) {
+            // Tile loads and record loads still in flight land before the
+            // shared memory goes away (record k was waited for by warpgroup 0
+            // only if it got that far: wait for every issued record phase).
+            for (int kk = loads_waited; kk < loads_issued; ++kk)
+                mbar_wait(&bar_load[kk & 1], (kk >> 1) & 1, 200000000ull);
+            for (int kk = (recs_issued > 2 ? recs_issued - 2 : 0); kk < recs_issued; ++kk)
+                mbar_wait(&bar_full[kk & 1], (kk >> 1) & 1, 200000000ull);
+        }
+    }
+    if (rs.failed) {
+        atomicExch(&g_grid_status, 1);
+        atomicExch(p.abort_flag, 1);
+    }
+    rs.failed = __syncthreads_or(rs.failed);
+    return rs;
+}
+
+// ------------------------------------------------------------------ producer CTA
+//
+// All eight warps build chunk k's record while the tiles of chunk k + 1 land
+// and its D1 runs; records alternate between two staging buffers, so building
+// never waits for the copy of the previous record.
+__device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k,
+                                                   const GParams &p, uint8_t *smem, const Sched &sc,
+                                                   int64_t start, uint32_t tmem) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int row = 32 * (warp & 3) + lane;  // TMEM lane
+    const int half = warp >> 2;              // column half of this thread
+    const uint32_t trow = tmem + (static_cast<uint32_t>(warp & 3) << 21);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P_OFF_BAR);
+    uint64_t *bar_load = bars + PB_LOAD, *bar_d1 = bars + PB_D1, *bar_mma = bars + PB_MMA;
+    float *Af = reinterpret_cast<float *>(smem + P_OFF_AF);
+    float *Tf = reinterpret_cast<float *>(smem + P_OFF_TF);
+    float *Xf = reinterpret_cast<float *>(smem + P_OFF_TH);  // scratch of the solve; T^ comes later
+    const uint32_t sbase = smem_u32(smem);
+    const int64_t step = p.n_prod;  // this CTA's tasks: start, start + step, ...
+    auto task_of = [&](const Ref &r) { return static_cast<int64_t>(r.r) * sc.NC + r.j; };
+    auto gates = [&](int kc) { return reinterpret_cast<float *>(smem + P_OFF_GATE) + (kc & 1) * G_SIZE; };
+    auto issue_loads = [&](int kc, const Ref &r) {
+        uint64_t *bar = &bar_load[kc & 1];
+        uint8_t *kq = smem + P_OFF_KQ + (kc & 1) * KQ_STAGE;
+        mbar_arrive_expect_tx(bar, KQ_BYTES);
+        const int t32 = static_cast<int>(r.ts);
+        tma_load_3d(kq, tm_k, 0, r.h, t32, bar);
+        tma_load_3d(kq + 16384, tm_k, 64, r.h, t32, bar);
+        tma_load_3d(kq + 8192, tm_q, 0, r.h, t32, bar);
+        tma_load_3d(kq + 24576, tm_q, 64, r.h, t32, bar);
+    };
+    // D1 = [K; Q] K^T of chunk kc on its bf16 tiles.
+    // The MMA-issue loops of both roles stay rolled: the per-chunk code of a
+    // role is larger than the instruction cache keeps warm, and a rolled issue
+    // loop (one thread, eight MMAs) costs nothing on the critical path while
+    // the unrolled copies cost instruction-fetch stalls (4.5% of the kernel on
+    // one box; the one-CTA kernel, with a different footprint, did not gain).
+    auto issue_d1 = [&](int kc) {
+        const uint32_t kq = sbase + P_OFF_KQ + (kc & 1) * KQ_STAGE;
+#pragma unroll 1
+        for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_f16(tmem + TM_D1, sdesc_sw128(kq + off, 16, 1024), sdesc_sw128(kq + off, 16, 1024),
+                     ID_D1, kk > 0);
+        }
+        umma_commit(bar_d1);
+    };
+
+    RoleState rs{false};
+    uint32_t mma_phase = 0;
+    int loads_issued = 0, loads_waited = 0;
+    // Record hand-over of the previous chunk, deferred into this chunk's
+    // first phase (thread 128, whose warp has no table block there): once the
+    // chain has taken round r - RING out of its ring, the loads of the chunk
+    // after next and the bulk store of the record into ring slot r % RING.
+    // The store is published (release flag) in the next phase, by then done.
+    bool ho_pending = false, ho_fail = false, pub_pending = false;
+    Ref ho_nn{-1, 0, 0, 0, 0, 0}, ho_cur{-1, 0, 0, 0, 0, 0}, pub{-1, 0, 0, 0, 0, 0};
+    int ho_k = 0;
+    auto handover = [&]() {
+        if (tid == 128) {
+            tc_fence_after();
+            if (ho_nn.item >= 0) issue_loads(ho_k + 2, ho_nn);
+            if (poll_ge(p.consumed + ho_cur.j, ho_cur.r - RING + 1, p.abort_flag)) {
+                fence_proxy_async_global();
+                const int slot = ho_cur.r % RING;
+                bulk_store_s2g(p.ring + (static_cast<size_t>(ho_cur.j) * RING + slot) * REC_BYTES,
+                               smem + P_OFF_STG + (ho_k & 1) * REC_BYTES, REC_BYTES);
+            } else {
+                ho_fail = true;
+            }
+        }
+        if (ho_nn.item >= 0) ++loads_issued;
+        pub = ho_cur;
+        pub_pending = true;
+        ho_pending = false;
+    };
+    auto publish = [&]() {
+        if (tid == 128 && !ho_fail) {
+            bulk_wait_all();
+            fence_proxy_async_global();
+            st_release_gpu(p.ready + pub.j * RING + pub.r % RING, pub.r + 1);
+        }
+        pub_pending = false;
+    };
+    int k = 0;
+    GateIn gin{1.f, 1.f, 0.f, 0.f};  // warp 4: inputs of the next chunk's gate table
+    Ref cur = sc.first_from(start, step);
+    Ref nxt = cur.item >= 0 ? sc.first_from(task_of(cur) + step, step) : cur;
+    {
+        const Ref second = nxt;
+        if (tid == 0) {
+            if (cur.item >= 0) issue_loads(0, cur);
+            if (second.item >= 0) issue_loads(1, second);
+        }
+        loads_issued = (cur.item >= 0) + (second.item >= 0);
+        if (cur.item >= 0) {
+            if (warp == 0) gate_tables(gates(0), gate_load(p, cur, lane), lane);
+            if (warp == 4) gin = gate_load(p, second, lane);
+            const bool ok = mbar_wait(&bar_load[0], 0);
+            if (__syncthreads_or(!ok)) {
+                rs.failed = true;
+            } else {
+                ++loads_waited;
+                if (tid == 0) {
+                    tc_fence_after();
+                    issue_d1(0);
+                }
+            }
+        }
+    }
+
+    for (; cur.item >= 0 && !rs.failed; ++k) {
+        const Ref nn = nxt.item >= 0 ? sc.first_from(task_of(nxt) + step, step) : nxt;
+        {
+            const uint32_t kq = sbase + P_OFF_KQ + (k & 1) * KQ_STAGE;
+            uint8_t *stg = smem + P_OFF_STG + (k & 1) * REC_BYTES;
+            const float *g = gates(k);
+            const int *gz = reinterpret_cast<const int *>(g + G_Z);
+
+            // ---- D1 of this chunk (issued during the previous one); staging
+            // buffer k & 1 is free (record k - 2's store completed when it was
+            // published, in the previous chunk)
+            {
+                const bool ok = mbar_wait(bar_d1, k & 1);
+                if (__syncthreads_or(!ok)) { rs.failed = true; break; }
+                tc_fence_after();
+            }
+            if (ho_pending) handover();
+
+            // ---- A = beta P (K K^T) (fp32) and M = P (Q K^T) (record, fp16), 32 columns per thread
+            {
+                const bool qk = row >= 64;
+                const int t = row & 63;
+                const int s0 = 32 * half;
+                // Warp-uniform: the whole 32 x 32 block lies above the diagonal.
+                if (half == 1 && (warp & 1) == 0) {
+                    if (qk) st_zero32(stg + REC_M, t, 4);
+                } else {
+                    const float glt = g[G_GL + t];
+                    const int zt = gz[t];
+                    const float bt = qk ? 1.f : g[G_BE + t];
+#pragma unroll 1
+                    for (int hp = 0; hp < 2; ++hp) {
+                        const int sb = s0 + 16 * hp;
+                        float v[16];
+                        tmem_ld16(trow + TM_D1 + sb, v);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j4 = 0; j4 < 4; ++j4) {
+                            const float4 g4 = *reinterpret_cast<const float4 *>(g + G_GL + sb + 4 * j4);
+                            const int4 z4 = *reinterpret_cast<const int4 *>(gz + sb + 4 * j4);
+                            const float gs[4] = {g4.x, g4.y, g4.z, g4.w};
+                            const int zs[4] = {z4.x, z4.y, z4.z, z4.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const int j = 4 * j4 + e, s = sb + j;
+                                const float pv = zs[e] == zt ? ex2(glt - gs[e]) : 0.f;
+                                const bool keep = qk ? (s <= t) : (s < t);
+                                v[j] = keep ? bt * pv * v[j] : 0.f;
+                            }
+                        }
+                        if (qk) {
+                            st_row16_f16(stg + REC_M, t, 4 * half + 2 * hp, v);
+                        } else {
+#pragma unroll
+                            for (int j4 = 0; j4 < 4; ++j4)
+                                *reinterpret_cast<float4 *>(Af + t * AST + sb + 4 * j4) =
+                                    make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncthreads();
+
+            // ---- diagonal 16 x 16 tiles of T (warps 0-3, one each) while warps
+            // 4-7 zero tiles (0,1), (2,3) of T and wait for the next chunk's
+            // tiles
+            bool prep_fail = false;
+            if (warp < 4) {
+                diag_inverse16(Af + (16 * warp) * AST + 16 * warp, Tf + (16 * warp) * AST + 16 * warp, lane);
+            } else {
+                const int wt = tid - 128;
+                for (int e = wt; e < 512; e += 128) {
+                    const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
+                    Tf[(32 * blk + rr) * AST + 32 * blk + 16 + cc] = 0.f;
+                }
+                if (nxt.item >= 0) prep_fail = !mbar_wait(&bar_load[(k + 1) & 1], ((k + 1) >> 1) & 1);
+            }
+            if (__syncthreads_or(prep_fail || ho_fail)) { rs.failed = true; break; }
+            if (pub_pending) publish();
+            // The next D1 comes from thread 128 (warps 4-7 have no part in the
+            // solve's first step; from thread 0 it delayed warp 0's).
+            if (nxt.item >= 0) {
+                ++loads_waited;
+                if (tid == 128) {
+                    tc_fence_after();
+                    issue_d1(k + 1);
+                }
+            }
+            solve_offdiag(Af, Tf, Xf, warp, lane);
+
+            // ---- T diag(beta) (record, fp16) and T diag(beta gamma) (local, as a
+            // bf16 hi + lo pair so that D_W can read K's bf16 tile as it landed)
+            {
+                const int t = tid & 63;
+                const bool hat = (tid >> 6) & 1;
+                const int hh = tid >> 7;
+                const int s0 = 32 * hh;
+                uint8_t *dstb = hat ? smem + P_OFF_TH : stg + REC_TT;
+                if (hh == 1 && t < 32) {
+                    st_zero32(dstb, t, 4);
+                    if (hat) st_zero32(dstb + 8192, t, 4);
+                } else {
+                    const float *sc = g + (hat ? G_BG : G_BE);
+#pragma unroll 1
+                    for (int hp = 0; hp < 2; ++hp) {
+                        const int sb = s0 + 16 * hp;
+                        float v[16];
+#pragma unroll
+                        for (int j4 = 0; j4 < 4; ++j4) {
+                            const float4 tv = *reinterpret_cast<const float4 *>(Tf + t * AST + sb + 4 * j4);
+                            const float4 sv = *reinterpret_cast<const float4 *>(sc + sb + 4 * j4);
+                            const int s = sb + 4 * j4;
+                            v[4 * j4 + 0] = s + 0 <= t ? tv.x * sv.x : 0.f;
+                            v[4 * j4 + 1] = s + 1 <= t ? tv.y * sv.y : 0.f;
+                            v[4 * j4 + 2] = s + 2 <= t ? tv.z * sv.z : 0.f;
+                            v[4 * j4 + 3] = s + 3 <= t ? tv.w * sv.w : 0.f;
+                        }
+                        if (hat)
+                            st_row16_bf16_split(dstb, dstb + 8192, t, 4 * hh + 2 * hp, v);
+                        else
+                            st_row16_f16(dstb, t, 4 * hh + 2 * hp, v);
+                    }
+                }
+            }
+            operands_ready();
+
+            // ---- D_W = K^T (T diag bg)^T = K^T (hi + lo)^T on bf16 operands
+            // (lane j, column t: W[t][j])
+            if (tid == 0) {
+#pragma unroll 1
+                for (int kk = 0; kk < 8; ++kk)
+                    umma_f16(tmem + TM_W, sdesc_sw128(kq + (kk & 3) * 2048, 16384, 1024),
+                             sdesc_sw128(sbase + P_OFF_TH + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
+                             ID_MK64_BF, kk > 0);
+                umma_commit(bar_mma);
+            }
+            // The next chunk's gate table, under D_W (off the solve's path:
+            // executed once per chunk by one warp, it ran mostly on
+            // instruction-fetch stalls)
+            if (warp == 4 && nxt.item >= 0) {
+                gate_tables(gates(k + 1), gin, lane);
+                gin = gate_load(p, nn, lane);
+            }
+            {
+                const bool ok = mbar_wait(bar_mma, mma_phase);
+                if (__syncthreads_or(!ok)) { rs.failed = true; break; }
+                mma_phase ^= 1u;
+                tc_fence_after();
+            }
+            {
+                float x[32];
+                tmem_ld32(trow + TM_W + 32 * half, x);
+                tmem_wait_ld();
+#pragma unroll
+                for (int t = 0; t < 32; ++t) x[t] = -x[t];
+                st_row32_f16(stg + REC_WT, row, 4 * half, x);
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncthreads();
+
+            // ---- stage k & 1 is free (D1 and D_W are done): fetch chunk k + 2;
+            // hand the record to the chain CTA (its slot k & 1 is free: the
+            // chain consumed chunk k - 2 before this staging buffer was reused)
+            ho_pending = true;
+            ho_nn = nn;
+            ho_cur = cur;
+            ho_k = k;
+        }
+        cur = nxt;
+        nxt = nn;
+    }
+    if (!rs.failed && ho_pending) handover();
+    if (!rs.failed && pub_pending) publish();
+    if (__syncthreads_or(ho_fail)) rs.failed = true;
+
+    if (rs.failed && tid == 0) {
+        for (int kk = loads_waited; kk < loads_issued; ++kk)
+            mbar_wait(&bar_load[kk & 1], (kk >> 1) & 1, 200000000ull);
+        umma_commit(bars + PB_DRAIN);  // every MMA thread 0 issued: D_W and the first D1
+        mbar_wait(bars + PB_DRAIN, 0, 200000000ull);
+        atomicExch(&g_grid_status, 1);
+        atomicExch(p.abort_flag, 1);
+    }
+    if (rs.failed && tid == 128) {
+        umma_commit(bars + PB_DRAIN2);  // the later D1s (issued by this thread)
+        mbar_wait(bars + PB_DRAIN2, 0, 200000000ull);
+        bulk_wait_all();                // a record store still reading staging
+    }
+    rs.failed = __syncthreads_or(rs.failed);
+    return rs;
+}
+
+__global__ void __launch_bounds__(NT, 1)
+    gdr_chunk_grid_kernel(const __grid_constant__ CUtensorMap tm_q,
+                          const __grid_constant__ CUtensorMap tm_k,
+                          const __grid_constant__ CUtensorMap tm_v,
+                          const __grid_constant__ GParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const bool chain = static_cast<int>(blockIdx.x) < p.n_chains;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (chain ? C_OFF_BAR : P_OFF_BAR));
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + (chain ? CB_NUM : PB_NUM));
+    const uint32_t ncols = chain ? C_TM_COLS : P_TM_COLS;
+
+    if (tid == 0) {
+        if (chain) {
+            for (int i = 0; i < CB_NUM; ++i) mbar_init(&bars[i], 1);  // loads, records, R1, R2
+            for (int i = 0; i < 2; ++i) {
+                mbar_init(&bars[CB_CONV + i], 128);   // warpgroup 1 signals
+                mbar_init(&bars[CB_OFREE + i], 128);
+            }
+        } else {
+            for (int i = 0; i < PB_NUM; ++i) mbar_init(&bars[i], 1);
+        }
+        mbar_fence_init();
+        prefetch_tmap(&tm_q);
+        prefetch_tmap(&tm_k);
+        if (chain) prefetch_tmap(&tm_v);
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, ncols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    int64_t n_seq = p.n_seq;
+    if (p.n_seq_dev) {
+        const int64_t nd = *p.n_seq_dev;
+        n_seq = nd < n_seq ? nd : n_seq;
+    }
+    const int64_t n_items = n_seq * p.H;
+    const Walk wk{&p, n_items, static_cast<int64_t>(p.n_chains), p.H};
+    if (chain) {
+        chain_role(&tm_q, &tm_k, &tm_v, p, smem, wk, blockIdx.x, tmem);
+    } else {
+        Sched sc{&p, &wk, n_items, p.n_chains, 0, 0};
+        if (p.cu_seqlens == nullptr) {
+            sc.nch = static_cast<int>((p.seq_len + CH - 1) / CH);
+            sc.n_tasks = (n_items + p.n_chains - 1) / p.n_chains * sc.nch * p.n_chains;
+        } else {
+            sc.n_tasks = static_cast<int64_t>(p.sched[0]) * p.n_chains;
+        }
+        producer_role(&tm_q, &tm_k, p, smem, sc, blockIdx.x - p.n_chains, tmem);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, ncols);
+}
+
+// Per-item round offsets of a packed stream: chain j takes items j, j + NC,
+// ... in order, and off[item] is the number of chunks of the chain's earlier
+// items (one warp per chain, 32 items per step with a warp scan). sched[0]
+// is the longest chain's round count, sched[1 + j] chain j's.
+__global__ void gdr_grid_sched_kernel(const int32_t *cu, const int32_t *n_seq_dev, int64_t n_seq_host,
+                                      int64_t total_tokens, int H, int NC, int32_t *off, int32_t *sched) {
+    const int lane = threadIdx.x & 31;
+    const int j = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (j >= NC) return;
+    int64_t n_seq = n_seq_host;
+    if (n_seq_dev) {
+        const int64_t nd = *n_seq_dev;
+        n_seq = nd < n_seq ? nd : n_seq;
+    }
+    const int64_t n_items = n_seq * H;
+    int carry = 0;
+    for (int64_t m0 = 0; j + m0 * NC < n_items; m0 += 32) {
+        const int64_t item = j + (m0 + lane) * NC;
+        int nch = 0;
+        if (item < n_items) {
+            const int64_t seq = item / H;
+            int64_t t0 = cu[seq], t1 = cu[seq + 1];
+            t0 = t0 < 0 ? 0 : (t0 > total_tokens ? total_tokens : t0);
+            t1 = t1 < t0 ? t0 : (t1 > total_tokens ? total_tokens : t1);
+            nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
+        }
+        int incl = nch;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int x = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += x;
+        }
+        if (item < n_items) off[item] = carry + incl - nch;
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+        sched[1 + j] = carry;
+        atomicMax(&sched[0], carry);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+int make_tmap(CUtensorMap *m, const void *base, int64_t tokens, int H) {
+    auto fn = encode_fn();
+    if (!fn) return set_error(RHZ_ERR_DEVICE, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(HD), static_cast<cuuint64_t>(H),
+                          static_cast<cuuint64_t>(tokens)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(HD) * 2,
+                             static_cast<cuuint64_t>(H) * HD * 2};
+    cuuint32_t box[3] = {64, 1, CH};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(RHZ_ERR_DEVICE, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return RHZ_OK;
+}
+
+}  // namespace
+
+namespace {
+
+struct GridWs {
+    size_t ready, consumed, abort, sched, off, flags_end, total;
+};
+
+GridWs grid_ws(int64_t n_items, bool packed) {
+    auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+    GridWs w;
+    const size_t ring = static_cast<size_t>(MAX_CHAINS) * RING * REC_BYTES;
+    w.ready = up(ring);
+    w.consumed = up(w.ready + static_cast<size_t>(MAX_CHAINS) * RING * sizeof(int));
+    w.abort = up(w.consumed + static_cast<size_t>(MAX_CHAINS) * sizeof(int));
+    w.sched = up(w.abort + sizeof(int));
+    w.flags_end = up(w.sched + static_cast<size_t>(1 + MAX_CHAINS) * sizeof(int));
+    w.off = w.flags_end;
+    w.total = packed ? up(w.off + static_cast<size_t>(n_items > 0 ? n_items : 0) * sizeof(int)) : w.off;
+    return w;
+}
+
+// Chains: one per item up to a share of the SMs that balances the chains'
+// per-chunk time against the producers' (RHZ_GRID_CHAINS overrides it).
+int grid_chain_cap(int sms) {
+    static int env = -1;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        const char *e = getenv("RHZ_GRID_CHAINS");
+        env = e ? atoi(e) : 0;
+    });
+    int cap = env > 0 ? env : (sms * 45 + 50) / 100;
+    if (cap > MAX_CHAINS) cap = MAX_CHAINS;
+    if (cap > sms - 1) cap = sms - 1;
+    return cap < 1 ? 1 : cap;
+}
+
+}  // namespace
+
+size_t chunk_grid_ws_bytes(int64_t n_items, bool packed) { return grid_ws(n_items, packed).total; }
+
+int chunk_grid_status(int *flag, bool clear) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_grid_status, sizeof(int));
+    if (e == cudaSuccess && clear && v) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_grid_status, &zero, sizeof(int));
+    }
+    if (e != cudaSuccess)
+        return set_error(RHZ_ERR_DEVICE, "reading the chunked kernel's status: %s", cudaGetErrorString(e));
+    *flag = v;
+    return RHZ_OK;
+}
+
+int launch_chunk_grid(const SeqArgs &a) {
+    if (a.d != HD || a.dtype != RHZ_DTYPE_BF16)
+        return set_error(RHZ_ERR_SHAPE, "tensor-core kernel needs bf16 and head_dim 128 (got %d)", a.d);
+    const int64_t tokens = a.cu_seqlens ? a.total_tokens : a.n_seq * a.seq_len;
+    if (a.n_seq == 0) return RHZ_OK;
+    if (tokens <= 0) {
+        // Every sequence is empty: final state = initial state.
+        SeqArgs b = a;
+        return launch_seq(b);
+    }
+    if (tokens > INT_MAX - CH)
+        return set_error(RHZ_ERR_SHAPE, "tensor-core kernel addresses at most %d token rows (got %lld)",
+                         INT_MAX - CH, static_cast<long long>(tokens));
+    const int64_t items = a.n_seq * a.H;
+    const bool packed = a.cu_seqlens != nullptr;
+    const GridWs w = grid_ws(items, packed);
+    if (a.ws == nullptr || a.ws_bytes < w.total)
+        return set_error(RHZ_ERR_INVALID, "workspace too small: need %zu bytes, got %zu", w.total, a.ws_bytes);
+    if (!aligned(a.ws, 256)) return set_error(RHZ_ERR_INVALID, "workspace must be 256-byte aligned");
+    CUtensorMap tq, tk, tv;
+    int st = make_tmap(&tq, a.q, tokens, a.H);
+    if (st == RHZ_OK) st = make_tmap(&tk, a.k, tokens, a.H);
+    if (st == RHZ_OK) st = make_tmap(&tv, a.v, tokens, a.H);
+    if (st != RHZ_OK) return st;
+    int sms = 148;
+    bool sm100 = true;
+    device_info(&sms, &sm100);
+    static std::once_flag attr_once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once, [] {
+        attr_err = cudaFuncSetAttribute(gdr_chunk_grid_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(SMEM_ALLOC));
+    });
+    if (attr_err != cudaSuccess)
+        return set_error(RHZ_ERR_DEVICE, "gdr_chunk_grid_kernel smem attribute: %s", cudaGetErrorString(attr_err));
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gdr_chunk_grid_kernel, NT, SMEM_ALLOC);
+    if (e != cudaSuccess || per_sm < 1)
+        return set_error(RHZ_ERR_DEVICE, "gdr_chunk_grid_kernel does not fit an SM: %s", cudaGetErrorString(e));
+    const int grid = sms;  // one CTA per SM (shared memory allows no second)
+    const int cap = grid_chain_cap(sms);
+    const int nc = static_cast<int>(items < cap ? items : cap);
+
+    char *ws = static_cast<char *>(a.ws);
+    e = cudaMemsetAsync(ws + w.ready, 0, w.flags_end - w.ready, a.stream);
+    if (e != cudaSuccess) return set_error(RHZ_ERR_DEVICE, "workspace flags: %s", cudaGetErrorString(e));
+    GParams p;
+    p.o = static_cast<__nv_bfloat16 *>(a.o);
+    p.alpha = a.alpha;
+    p.beta = a.beta;
+    p.cu_seqlens = a.cu_seqlens;
+    p.n_seq_dev = a.n_seq_dev;
+    p.n_seq = a.n_seq;
+    p.seq_len = a.seq_len;
+    p.total_tokens = tokens;
+    p.state_in = a.state_in;
+    p.in_slots = a.in_slots;
+    p.state_out = a.state_out;
+    p.out_slots = a.out_slots;
+    p.num_slots = a.num_slots;
+    p.H = a.H;
+    p.norm_scale = a.norm_scale;
+    p.norm_eps = a.norm_eps;
+    p.ring = reinterpret_cast<uint8_t *>(ws);
+    p.ready = reinterpret_cast<int *>(ws + w.ready);
+    p.consumed = reinterpret_cast<int *>(ws + w.consumed);
+    p.abort_flag = reinterpret_cast<int *>(ws + w.abort);
+    p.sched = reinterpret_cast<int32_t *>(ws + w.sched);
+    p.off = packed ? reinterpret_cast<int32_t *>(ws + w.off) : nullptr;
+    p.n_chains = nc;
+    p.n_prod = grid - nc;
+    if (packed) {
+        const int warps = 8;
+        gdr_grid_sched_kernel<<<(nc + warps - 1) / warps, 32 * warps, 0, a.stream>>>(
+            a.cu_seqlens, a.n_seq_dev, a.n_seq, tokens, a.H, nc, reinterpret_cast<int32_t *>(ws + w.off),
+            reinterpret_cast<int32_t *>(ws + w.sched));
+        {
+            const int ls = check_launch("gdr_grid_sched_kernel");
+            if (ls != RHZ_OK) return ls;
+        }
+    }
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(NT, 1, 1);
+    cfg.dynamicSmemBytes = SMEM_ALLOC;
+    cfg.stream = a.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident at once: they wait on each other
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, gdr_chunk_grid_kernel, tq, tk, tv, p);
+    if (e != cudaSuccess)
+        return set_error(RHZ_ERR_DEVICE, "gdr_chunk_grid_kernel launch: %s", cudaGetErrorString(e));
+    return check_launch("gdr_chunk_grid_kernel");
+}
+
+}  // namespace rhz

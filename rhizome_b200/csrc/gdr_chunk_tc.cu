@@ -1313,8 +1313,8 @@ std::atomic<int> g_chunk_variant{RHZ_CHUNK_AUTO};
 }
 
 int set_chunk_variant(int v, int *prev) {
-    if (v < RHZ_CHUNK_AUTO || v > RHZ_CHUNK_SOLO)
-        return set_error(RHZ_ERR_INVALID, "chunk kernel variant %d is not one of 0, 1, 2", v);
+    if (v < RHZ_CHUNK_AUTO || v > RHZ_CHUNK_GRID)
+        return set_error(RHZ_ERR_INVALID, "chunk kernel variant %d is not one of 0, 1, 2, 3", v);
     *prev = g_chunk_variant.exchange(v);
     return RHZ_OK;
 }
@@ -1334,13 +1334,8 @@ bool chunk_use_solo(int64_t items, int sms) {
 int launch_chunk_tc(const SeqArgs &a) {
     if (!chunk_tc_supports(a.d, a.dtype))
         return set_error(RHZ_ERR_SHAPE, "tensor-core kernel needs bf16 and head_dim 128 (got %d)", a.d);
-    int v = g_chunk_variant.load();
-    if (v == RHZ_CHUNK_AUTO) {
-        int sms = 148;
-        bool sm100 = true;
-        device_info(&sms, &sm100);
-        v = chunk_use_solo(a.n_seq * a.H, sms) ? RHZ_CHUNK_SOLO : RHZ_CHUNK_PAIR;
-    }
+    const int v = g_chunk_variant.load();
+    if (v == RHZ_CHUNK_AUTO || v == RHZ_CHUNK_GRID) return launch_chunk_grid(a);
     return v == RHZ_CHUNK_SOLO ? launch_chunk_solo(a) : launch_chunk_pair(a);
 }
 

@@ -43,6 +43,8 @@ struct SeqArgs {
     cudaStream_t stream;
     const float *norm_scale;    // non-null: groupnorm_heads on o (scale[0..d), norm_eps)
     float norm_eps;
+    void *ws;                   // scratch of the tensor-core grid kernel (chunk_grid_ws_bytes)
+    size_t ws_bytes;
 };
 
 // Up to Tn positions per sequence, state after each position written out
@@ -97,6 +99,11 @@ int set_chunk_variant(int v, int *prev);
 // Sticky device flags: 1 once a bounded wait of that kernel gave up.
 int chunk_pair_status(int *flag, bool clear);
 int chunk_solo_status(int *flag, bool clear);
+// The grid form (gdr_chunk_grid.cu): one cooperative launch, chain CTAs fed
+// by producer CTAs through record rings in the workspace.
+int launch_chunk_grid(const SeqArgs &a);
+size_t chunk_grid_ws_bytes(int64_t n_items, bool packed);
+int chunk_grid_status(int *flag, bool clear);
 
 // Variable-length index work (varlen.cu).
 int launch_prefix_sum(int32_t *cu, const int32_t *lengths, int64_t n, cudaStream_t s);

@@ -354,5 +354,75 @@ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t chunk16)
     return row * 128u + ((chunk16 ^ (row & 7u)) << 4);
 }
 
+// ------------------------------------------------------------------ grid-wide hand-over
+//
+// Flags in global memory between CTAs of one (co-resident) launch: release
+// stores publish this thread's earlier writes (and, after a CTA barrier, its
+// CTA's) at GPU scope; acquire loads make them visible to the reader.
+
+__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(int *p, int v) {
+    asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_relaxed_gpu(const int *p) {
+    int v;
+    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Orders this thread's generic-proxy view of global memory with its
+// async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16, both ends 16-byte aligned) from
+// global memory into this CTA's shared memory, completion counted on `bar`.
+__device__ __forceinline__ void bulk_load_g2s(void *smem_dst, const void *gsrc, uint32_t bytes,
+                                              uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Bulk copy from this CTA's shared memory to global memory, tracked as this
+// thread's next bulk group (commit, then wait with bulk_wait_all).
+__device__ __forceinline__ void bulk_store_s2g(void *gdst, const void *smem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                     reinterpret_cast<uint64_t>(gdst)),
+                 "r"(smem_u32(smem_src)), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Every bulk store this thread committed has completed (writes performed).
+__device__ __forceinline__ void bulk_wait_all() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Polls *p until it reaches `target`, or `*abort` is set, or `limit_ns` of
+// wall time pass (then false). Short sleeps between polls keep the L2 quiet.
+__device__ __forceinline__ bool poll_ge(const int *p, int target, const int *abort,
+                                        uint64_t limit_ns = 2000000000ull) {
+    if (ld_acquire_gpu(p) >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        __nanosleep(40);
+        if (ld_acquire_gpu(p) >= target) return true;
+        if ((i & 63u) == 0) {
+            if (ld_relaxed_gpu(abort) != 0) return false;
+            if (globaltimer_ns() - t0 > limit_ns) return false;
+        }
+    }
+}
+
 }  // namespace sm100
 }  // namespace rhz

@@ -85,6 +85,7 @@ class CudaSlabOps:
         self.device = device
         self.B = B
         self._cu = {}
+        self._ws = None  # the scan's scratch, shared by the slabs (one scan at a time)
 
     def rows(self, length: int) -> torch.Tensor:
         """cu_seqlens of a slab: batch row b holds packed rows [b L, (b+1) L)."""
@@ -105,10 +106,14 @@ class CudaSlabOps:
         o = torch.empty_like(q)
         H, d = q.shape[1], q.shape[2]
         flags = 1 if first else 0  # RHZ_FLAG_ZERO_INIT: the reset at t = 0
+        need = ops.varlen_workspace_bytes(self.B, H, d, q.dtype)
+        if need and (self._ws is None or self._ws.numel() < need):
+            self._ws = torch.empty(need, device=q.device, dtype=torch.uint8)
         capi.call("rhz_gdr_varlen_fwd", o.data_ptr(), pool.data_ptr(), None,
                   self.rows(length).data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
                   a.data_ptr(), b.data_ptr(), self.B, self.B * length, self.B, H, d,
-                  ops._dt(q), flags, ops._stream(q.device))
+                  ops._dt(q), flags, ops._p(self._ws) if need else None, need,
+                  ops._stream(q.device))
         return o
 
     def unshard(self, gathered: torch.Tensor) -> torch.Tensor:

@@ -155,8 +155,16 @@ def gdr_prep(xq, xk, xv, beta_logit, alpha_logit, a_head, conv_w, conv_b, conv_s
     return q, k, v, alpha, beta
 
 
-def workspace_bytes(B: int, T: int) -> int:
-    return int(capi.lib().rhz_gdr_workspace_bytes(B, T))
+def workspace_bytes(B: int, T: int, H: int = 1, d: int = 1, dtype: torch.dtype = torch.float32,
+                    has_segment: bool = True) -> int:
+    """Scratch of gdr_sequential / gdr_scan_chunked (see rhz_gdr_workspace_bytes)."""
+    return int(capi.lib().rhz_gdr_workspace_bytes(B, T, H, d, _DTYPES.get(dtype, -1),
+                                                  1 if has_segment else 0))
+
+
+def varlen_workspace_bytes(n_seq: int, H: int, d: int, dtype: torch.dtype) -> int:
+    """Scratch of gdr_varlen_fwd(_norm) for n_seq sequences."""
+    return int(capi.lib().rhz_gdr_varlen_workspace_bytes(n_seq, H, d, _DTYPES.get(dtype, -1)))
 
 
 def _seq_common(name, q, k, v, alpha, beta, segment, state_init, chunk, with_state, workspace):
@@ -169,9 +177,9 @@ def _seq_common(name, q, k, v, alpha, beta, segment, state_init, chunk, with_sta
     o = torch.empty_like(q)
     fin = torch.empty((B, H, d, d), device=q.device, dtype=torch.float32) if with_state else None
     ws, nbytes = None, 0
-    if segment is not None or workspace is not None:
-        ws, nbytes = _workspace(workspace, workspace_bytes(B, T) if segment is not None else 0,
-                                q.device)
+    need = workspace_bytes(B, T, H, d, q.dtype, segment is not None)
+    if need > 0 or workspace is not None:
+        ws, nbytes = _workspace(workspace, need, q.device)
     args = [_p(o), _p(fin), _p(q), _p(k), _p(v), _p(alpha), _p(beta), _p(segment), _p(state_init)]
     if name == "rhz_gdr_scan_chunked":
         args.append(chunk)
@@ -249,7 +257,7 @@ def gdr_scan_chunked_host(q, k, v, alpha, beta, chunk=64, segment=None, state_in
 
 
 def gdr_varlen_fwd(q, k, v, alpha, beta, cu_seqlens, state_pool=None, slot_idx=None,
-                   zero_init=False, write_state=True, out=None):
+                   zero_init=False, write_state=True, out=None, workspace=None):
     """Continuous-batching prefill over a packed stream q/k/v [tokens, H, d]:
     sequence i = rows [cu_seqlens[i], cu_seqlens[i+1]) resumes from
     state_pool[slot_idx[i]] (zeros if zero_init) and writes its final state
@@ -265,9 +273,13 @@ def gdr_varlen_fwd(q, k, v, alpha, beta, cu_seqlens, state_pool=None, slot_idx=N
     if out is not None:
         _need(out, "out", q.dtype, tuple(q.shape))
     o = torch.empty_like(q) if out is None else out
+    ws, nbytes = None, 0
+    need = varlen_workspace_bytes(n_seq, H, d, q.dtype)
+    if need > 0 or workspace is not None:
+        ws, nbytes = _workspace(workspace, need, q.device)
     capi.call("rhz_gdr_varlen_fwd", _p(o), _p(state_pool), _p(slot_idx), _p(cu_seqlens), _p(q),
               _p(k), _p(v), _p(alpha), _p(beta), n_seq, tokens, num_slots, H, d, _dt(q), flags,
-              _stream(q.device))
+              _p(ws), nbytes, _stream(q.device))
     return o
 
 
@@ -294,7 +306,8 @@ def gdr_scan_chunked_bwd(q, k, v, alpha, beta, d_o, segment=None, d_state_final=
 
 
 def gdr_varlen_fwd_norm(q, k, v, alpha, beta, cu_seqlens, norm_scale, norm_eps=1e-6,
-                        state_pool=None, slot_idx=None, zero_init=False, write_state=True):
+                        state_pool=None, slot_idx=None, zero_init=False, write_state=True,
+                        workspace=None):
     """gdr_varlen_fwd followed by the per-head output norm groupnorm_heads
     (norm.rs:48-60): each output row o[t, h] becomes
     o / sqrt(mean(o^2) + norm_eps) * norm_scale[:d]. Fused into the
@@ -311,9 +324,13 @@ def gdr_varlen_fwd_norm(q, k, v, alpha, beta, cu_seqlens, norm_scale, norm_eps=1
     if slot_idx is not None:
         _need(slot_idx, "slot_idx", torch.int32, (n_seq,))
     o = torch.empty_like(q)
+    ws, nbytes = None, 0
+    need = varlen_workspace_bytes(n_seq, H, d, q.dtype)
+    if need > 0 or workspace is not None:
+        ws, nbytes = _workspace(workspace, need, q.device)
     capi.call("rhz_gdr_varlen_fwd_norm", _p(o), _p(state_pool), _p(slot_idx), _p(cu_seqlens),
               _p(q), _p(k), _p(v), _p(alpha), _p(beta), _p(norm_scale), float(norm_eps), n_seq,
-              tokens, num_slots, H, d, _dt(q), flags, _stream(q.device))
+              tokens, num_slots, H, d, _dt(q), flags, _p(ws), nbytes, _stream(q.device))
     return o
 
 
@@ -425,10 +442,12 @@ def device_status(clear: bool = False) -> bool:
 
 
 def set_chunk_kernel(variant: str) -> str:
-    """Pick the tensor-core chunked form process-wide: "auto" (by item count
-    against SM count), "pair" (2-CTA cluster per item) or "solo" (one CTA per
-    item). Returns the previous setting."""
-    names = {"auto": capi.RHZ_CHUNK_AUTO, "pair": capi.RHZ_CHUNK_PAIR, "solo": capi.RHZ_CHUNK_SOLO}
+    """Pick the tensor-core chunked form process-wide: "auto" (the grid
+    form), "grid" (chain CTAs fed by producer CTAs over every SM), "pair"
+    (2-CTA cluster per item) or "solo" (one CTA per item). Returns the
+    previous setting."""
+    names = {"auto": capi.RHZ_CHUNK_AUTO, "pair": capi.RHZ_CHUNK_PAIR, "solo": capi.RHZ_CHUNK_SOLO,
+             "grid": capi.RHZ_CHUNK_GRID}
     if variant not in names:
         raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"unknown chunk kernel {variant!r}")
     prev = ctypes.c_int32(0)

@@ -50,7 +50,7 @@ def test_library_does_not_depend_on_torch_or_libcuda():
 def test_abi_version(lib):
     hdr = open(os.path.join(ROOT, "include", "rhizome_gdr.h")).read()
     declared = int(re.search(r"#define RHZ_ABI_VERSION (\d+)", hdr).group(1))
-    assert lib.rhz_abi_version() == declared == 101
+    assert lib.rhz_abi_version() == declared == 200
 
 
 def test_chunk_form_setting_without_gpu(lib):
@@ -61,6 +61,9 @@ def test_chunk_form_setting_without_gpu(lib):
     assert prev.value == capi.RHZ_CHUNK_AUTO
     assert lib.rhz_gdr_set_chunk_kernel(capi.RHZ_CHUNK_AUTO, C.byref(prev)) == capi.RHZ_OK
     assert prev.value == capi.RHZ_CHUNK_SOLO
+    assert lib.rhz_gdr_set_chunk_kernel(capi.RHZ_CHUNK_GRID, C.byref(prev)) == capi.RHZ_OK
+    assert lib.rhz_gdr_set_chunk_kernel(capi.RHZ_CHUNK_AUTO, C.byref(prev)) == capi.RHZ_OK
+    assert prev.value == capi.RHZ_CHUNK_GRID
     assert lib.rhz_gdr_set_chunk_kernel(capi.RHZ_CHUNK_AUTO, None) == capi.RHZ_OK
 
 
@@ -153,21 +156,38 @@ def test_sequential_validation(lib):
     assert call(dt=2) == capi.RHZ_ERR_DTYPE
     assert call(seg=FAKE + 4) == capi.RHZ_ERR_INVALID  # int64 ids need 8-byte alignment
     assert call(B=0) == capi.RHZ_OK or call(B=0) == capi.RHZ_ERR_DEVICE
-    ws = lib.rhz_gdr_workspace_bytes(4, 4096)
-    assert ws >= (4 * 4096 + 1) * 4 * 2
+    # segment tables; plus the tensor-core kernel's rings on the bf16 d=128 path
+    ws_seg = lib.rhz_gdr_workspace_bytes(4, 4096, 16, 32, capi.RHZ_DTYPE_F32, 1)
+    assert ws_seg >= (4 * 4096 + 1) * 4 * 2
+    assert lib.rhz_gdr_workspace_bytes(4, 4096, 16, 32, capi.RHZ_DTYPE_F32, 0) == 0
+    ws_tc = lib.rhz_gdr_workspace_bytes(4, 4096, 16, 128, capi.RHZ_DTYPE_BF16, 0)
+    assert ws_tc >= 128 * 4 * 32768  # 128 chains x 4 ring slots x 32 KB records
+    assert lib.rhz_gdr_workspace_bytes(4, 4096, 16, 128, capi.RHZ_DTYPE_BF16, 1) > ws_tc + ws_seg // 2
+    assert lib.rhz_gdr_workspace_bytes(-1, 4, 1, 4, 0, 0) == 0
+    # the bf16 d=128 path refuses a missing workspace before any device work
+    assert f(FAKE, None, FAKE, FAKE, FAKE, FAKE, FAKE, None, None, 1, 64, 2, 128, 1, None, 0,
+             None) == capi.RHZ_ERR_INVALID
+    assert b"workspace too small" in lib.rhz_last_error()
     assert lib.rhz_gdr_scan_chunked(FAKE, None, FAKE, FAKE, FAKE, FAKE, FAKE, None, None, -1, 1,
                                     8, 1, 4, 0, None, 0, None) == capi.RHZ_ERR_SHAPE
 
 
 def test_varlen_validation(lib):
     f = lib.rhz_gdr_varlen_fwd
-    base = [FAKE, FAKE, None, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 2, 10, 4, 2, 32, 0, 0, None]
+    base = [FAKE, FAKE, None, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 2, 10, 4, 2, 32, 0, 0, None, 0,
+            None]
     bad_flags = list(base)
     bad_flags[15] = 8
     assert f(*bad_flags) == capi.RHZ_ERR_INVALID
     too_many = list(base)
     too_many[9] = 5  # 5 sequences, 4 slots, identity slot map
     assert f(*too_many) == capi.RHZ_ERR_SHAPE
+    assert lib.rhz_gdr_varlen_workspace_bytes(2, 2, 32, 0) == 0
+    need = lib.rhz_gdr_varlen_workspace_bytes(2, 2, 128, 1)
+    assert need >= 128 * 4 * 32768 + 4 * 4  # rings + one round offset per item
+    short = list(base)
+    short[13], short[14], short[16], short[17] = 128, 1, FAKE, need - 256
+    assert f(*short) == capi.RHZ_ERR_INVALID and b"workspace too small" in lib.rhz_last_error()
     assert lib.rhz_varlen_pack_tokens(FAKE, FAKE, FAKE, 2, 4, 6, None) == capi.RHZ_ERR_SHAPE
     assert lib.rhz_varlen_chunk_map(FAKE, FAKE, FAKE, FAKE, 2, 0, 8, FAKE, 256, None) == capi.RHZ_ERR_SHAPE
 

@@ -1,8 +1,9 @@
 """GPU parity of the tcgen05 chunked prefill (bf16 in, fp32 state) against
 the f64 oracle on the same (bf16-rounded) inputs, through the C ABI, at the
 bf16 tolerance (<= 2e-2 relative to max|ref|, <= 1e-2 absolute, and
-1e-2 RMS(ref) + 2e-2 |ref| elementwise). Every case runs on both forms of the
-kernel (the 2-CTA cluster per item and the one-CTA kernel), pinned through
+1e-2 RMS(ref) + 2e-2 |ref| elementwise). Every case runs on each form of the
+kernel (the grid form: chain CTAs fed by producer CTAs through record rings;
+the 2-CTA cluster per item; the one-CTA kernel), pinned through
 rhz_gdr_set_chunk_kernel."""
 import numpy as np
 import pytest
@@ -17,7 +18,7 @@ pytestmark = pytest.mark.gpu
 D = 128
 
 
-@pytest.fixture(autouse=True, params=["pair", "solo"])
+@pytest.fixture(autouse=True, params=["grid", "pair", "solo"])
 def form(request):
     with chunk_form(request.param):
         yield request.param
@@ -185,33 +186,43 @@ def test_varlen_prefill_config_full_size():
     assert_bf16(host(dpool), rpool, "cfg3 pool")
 
 
-def test_forms_agree_and_auto_dispatch():
-    """The two forms agree within the bf16 tolerance of each other's rounding
-    (they round at the same points but accumulate in different orders), and
-    the default picks the cluster pair for few items and the one-CTA kernel
-    for more items than the pairs cover at once."""
-    B, T, H = 2, 300, 4
-    q, k, v, a, b = dense_case(55, B, T, H)
-    with chunk_form("pair"):
-        op, sp = run_dense(q, k, v, a, b, B, T)
-    with chunk_form("solo"):
-        os_, ss = run_dense(q, k, v, a, b, B, T)
+def test_forms_agree_and_grid_is_the_default():
+    """The grid form computes every record and every chain step with the
+    pair's arithmetic, so the two agree bitwise, whatever the item count;
+    the one-CTA kernel rounds at the same points but accumulates in another
+    order, so it agrees within the bf16 tolerance. "auto" is the grid form."""
+    for seed, (B, T, H) in ((55, (2, 300, 4)), (56, (2, 70, 128))):
+        q, k, v, a, b = dense_case(seed, B, T, H)
+        with chunk_form("pair"):
+            op, sp = run_dense(q, k, v, a, b, B, T)
+        with chunk_form("grid"):
+            og, sg = run_dense(q, k, v, a, b, B, T)
+        with chunk_form("auto"):
+            oa, sa = run_dense(q, k, v, a, b, B, T)
+        with chunk_form("solo"):
+            os_, ss = run_dense(q, k, v, a, b, B, T)
+        assert torch.equal(og, op) and torch.equal(sg, sp), (B, T, H)
+        assert torch.equal(oa, og) and torch.equal(sa, sg), (B, T, H)
+        assert_bf16(host(os_), host(og), "solo vs grid o")
+        assert_bf16(host(ss), host(sg), "solo vs grid state")
+
+
+def test_batch_invariance_of_the_default_form():
+    """A sequence's output and final state do not depend on how many other
+    sequences share the call (docs/determinism.md:3-6): the same sequence
+    alone, among 8 items and among 256 items, bitwise."""
+    T, H = 200, 2
+    q, k, v, a, b = dense_case(58, 1, T, H)
     with chunk_form("auto"):
-        oa, sa = run_dense(q, k, v, a, b, B, T)
-    assert torch.equal(oa, op) and torch.equal(sa, sp)  # 8 items: pair
-    ro, rs = O.gdr_dense(*(x.reshape(B, T, *x.shape[1:]) for x in (q, k, v, a, b)))
-    assert_bf16(host(os_), ro, "solo o")
-    assert_bf16(host(os_), host(op), "solo vs pair o")
-    assert_bf16(host(ss), host(sp), "solo vs pair state")
-    # 2 x 128 heads = 256 items: four passes of 74 pairs against two of 148
-    # single CTAs, so the one-CTA kernel
-    B, T, H = 2, 70, 128
-    q, k, v, a, b = dense_case(56, B, T, H)
-    with chunk_form("solo"):
-        os_, ss = run_dense(q, k, v, a, b, B, T)
-    with chunk_form("auto"):
-        oa, sa = run_dense(q, k, v, a, b, B, T)
-    assert torch.equal(oa, os_) and torch.equal(sa, ss)
+        o1, s1 = run_dense(q, k, v, a, b, 1, T)
+        for B, Hx in ((4, 2), (2, 128)):
+            qx, kx, vx, ax, bx = dense_case(59 + B, B, T, Hx)
+            # sequence 1, heads 0..H-1 carry the probe inputs
+            for dst, src in ((qx, q), (kx, k), (vx, v), (ax, a), (bx, b)):
+                dst.reshape(B, T, *dst.shape[1:])[1, :, :H] = src.reshape(1, T, *src.shape[1:])[0]
+            o, s = run_dense(qx, kx, vx, ax, bx, B, T)
+            assert torch.equal(o[1, :, :H], o1[0]), (B, Hx)
+            assert torch.equal(s[1, :H], s1[0]), (B, Hx)
 
 
 def test_device_status_clear_after_runs():
