@@ -80,7 +80,7 @@ using namespace sm100;
 
 constexpr int CH = 64;    // chunk length
 constexpr int HD = 128;   // head dim (d_k = d_v)
-constexpr int NT = 256;   // threads per CTA
+constexpr int NT = 512;   // threads per CTA (chain: two warpgroups work; producer: two contexts)
 constexpr int AST = 68;   // fp32 row stride of the A / T tables (16-byte rows, bank spread)
 
 constexpr uint32_t KQ_STAGE = 32768;  // [half][K rows | Q rows], 64 x 64 bf16 boxes
@@ -117,30 +117,34 @@ constexpr uint32_t C_OFF_NORM = C_OFF_BAR + 128;  // output-norm scale, HD float
 constexpr uint32_t C_USED = C_OFF_NORM + HD * 4;
 static_assert(C_OFF_NORM >= C_OFF_BAR + CB_NUM * 8 + 16, "chain barriers overlap the norm scale");
 
-// Producer CTA shared memory.
+// Producer CTA: PCTX independent contexts of 256 threads, each building the
+// records of its own task stream in its own slice of shared memory (two
+// chunks in flight per SM hide each other's dependent phases).
+constexpr int PCTX = 2;
 constexpr uint32_t P_OFF_KQ = 0;             // 2 stages of K, Q tiles
-constexpr uint32_t P_OFF_STG = 65536;        // 2 records being built
-constexpr uint32_t P_OFF_TH = 131072;        // T diag(beta gamma) [t][s] as bf16 hi, lo (2 x 8 KB); earlier the solve's scratch
-constexpr uint32_t P_OFF_AF = 147456;        // A fp32 [64][AST]
-constexpr uint32_t P_OFF_TF = P_OFF_AF + 64 * AST * 4;   // T fp32 [64][AST]
-constexpr uint32_t P_OFF_GATE = P_OFF_TF + 64 * AST * 4; // 2 gate tables
+constexpr uint32_t P_OFF_AF = 65536;         // A fp32 [64][AST]; after the solve, T diag(beta gamma) as bf16 hi, lo (2 x 8 KB)
+constexpr uint32_t P_OFF_TF = P_OFF_AF + 64 * AST * 4;  // T fp32 [64][AST]
+constexpr uint32_t P_OFF_X = P_OFF_TF + 64 * AST * 4;   // the solve's scratch (4 KB)
+constexpr uint32_t P_OFF_GATE = P_OFF_X + 4096;         // 2 gate tables
 constexpr uint32_t P_OFF_BAR = P_OFF_GATE + 2 * G_BYTES;
-// Producer barriers: tiles landed [2], D1 done, D_W done, failure-path drain
-// of every MMA issued (one per issuing thread).
+// Producer barriers (per context): tiles landed [2], D1 done, D_W done,
+// failure-path drain of every MMA issued (one per issuing thread).
 constexpr int PB_LOAD = 0, PB_D1 = 2, PB_MMA = 3, PB_DRAIN = 4, PB_DRAIN2 = 5, PB_NUM = 6;
-constexpr uint32_t P_USED = P_OFF_BAR + PB_NUM * 8 + 16;  // + TMEM base
+constexpr uint32_t P_CTX_BYTES = (P_OFF_BAR + PB_NUM * 8 + 1023) / 1024 * 1024;
+constexpr uint32_t P_OFF_TMEM = PCTX * P_CTX_BYTES;     // TMEM base (both contexts)
+constexpr uint32_t P_USED = P_OFF_TMEM + 16;
+static_assert(P_OFF_TF >= P_OFF_AF + 16384, "T diag(beta gamma) hi + lo must fit the A table");
 
 constexpr uint32_t SMEM_USED = C_USED > P_USED ? C_USED : P_USED;
 constexpr size_t SMEM_ALLOC = SMEM_USED + 1024;  // slack for 1024-byte alignment
 static_assert(C_OFF_GATE >= C_OFF_DT + 16384, "chain map overlaps");
-static_assert(P_OFF_AF >= P_OFF_TH + 16384, "producer map overlaps");
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in shared memory");
 
 // TMEM columns (f32). Chain: D_U (128 lanes x 64), D_S (128 x 128) and two
 // D_O buffers (M = 64: row t in lane 32 (t / 16) + t % 16, 128 columns).
-// Producer: D1 (128 x 64) and D_W (128 x 64).
+// Producer: D1 (128 x 64) and D_W (128 x 64) per context.
 constexpr uint32_t TM_U = 0, TM_S = 64, TM_O = 192, C_TM_COLS = 512;
-constexpr uint32_t TM_D1 = 0, TM_W = 64, P_TM_COLS = 128;
+constexpr uint32_t TM_D1 = 0, TM_W = 64, P_TM_CTX = 128, P_TM_COLS = PCTX * P_TM_CTX;
 
 constexpr uint32_t ID_D1 = idesc_bf16(128, 64, false, false);
 constexpr uint32_t ID_MK64 = idesc_f16(128, 64, true, false);
@@ -417,8 +421,9 @@ __device__ __forceinline__ void diag_inverse16(const float *A, float *T, int lan
 // recursion: T_{2p+1,2p} = -D_{2p+1} (A_{2p+1,2p} D_{2p}) for p = 0, 1, then
 // T[32:64, 0:32] = -T[32:64, 32:64] (A[32:64, 0:32] T[0:32, 0:32]). The
 // products run on mma.sync with fp16 operands (T is rounded to fp16 for the
-// tcgen05 products anyway), on all eight warps. Ends synchronised.
-__device__ void solve_offdiag(const float *Af, float *Tf, float *Xf, int warp, int lane) {
+// tcgen05 products anyway), on the eight warps of one producer context
+// (named barrier `bar`). Ends synchronised.
+__device__ void solve_offdiag(const float *Af, float *Tf, float *Xf, int warp, int lane, int bar) {
     if (warp < 4) {
         const int pb = warp >> 1, nt = warp & 1;
         const int r0 = 32 * pb + 16, c0 = 32 * pb;  // tile (2p+1, 2p)
@@ -436,7 +441,7 @@ __device__ void solve_offdiag(const float *Af, float *Tf, float *Xf, int warp, i
         mma16816(y, a, b);
         st_frag_c(Tf + r0 * AST + c0 + 8 * nt, AST, lane, y, -1.f);
     }
-    __syncthreads();
+    nbar_sync(bar, 256);
     const int mt = warp >> 2, nt = warp & 3;
     {
         float y[4] = {0.f, 0.f, 0.f, 0.f};
@@ -449,7 +454,7 @@ __device__ void solve_offdiag(const float *Af, float *Tf, float *Xf, int warp, i
         }
         st_frag_c(Xf + (16 * mt) * 32 + 8 * nt, 32, lane, y, 1.f);  // Y [32][32]
     }
-    __syncthreads();
+    nbar_sync(bar, 256);
     {
         float y[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -461,15 +466,7 @@ __device__ void solve_offdiag(const float *Af, float *Tf, float *Xf, int warp, i
         }
         st_frag_c(Tf + (32 + 16 * mt) * AST + 8 * nt, AST, lane, y, -1.f);
     }
-    __syncthreads();
-}
-
-// Make thread-written smem operands and TMEM stores visible to the MMA issuer.
-__device__ __forceinline__ void operands_ready() {
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
+    nbar_sync(bar, 256);
 }
 
 struct Ref {
@@ -686,6 +683,13 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
         // ------------------------------------------------ warpgroup 0: state path
         const int row = tid;  // state row i = TMEM lane
         int k = 0;
+        bool u_pre = false;  // thread 0: the next R1's U part is already issued
+        auto issue_u = [&](uint32_t vbase, uint32_t rbase) {
+#pragma unroll 1
+            for (int kk = 0; kk < 4; ++kk)
+                umma_f16(tmem + TM_U, sdesc_sw128(vbase + kk * 2048, 8192, 1024),
+                         sdesc_sw128(rbase + REC_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
+        };
         for (int64_t item = start; item < wk.n_items && !rs.failed; item += wk.stride) {
             const int64_t seq = item / H;
             const int h = static_cast<int>(item - seq * H);
@@ -753,10 +757,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 // ---- R1: D_U = V^T (T diag b)^T + S (-W^T) ; D_O[k & 1] = Q~ S^T
                 if (tid == 0) {
                     tc_fence_after();
-#pragma unroll 1
-                    for (int kk = 0; kk < 4; ++kk)
-                        umma_f16(tmem + TM_U, sdesc_sw128(vb + kk * 2048, 8192, 1024),
-                                 sdesc_sw128(rec + REC_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
+                    if (!u_pre) issue_u(vb, rec);
 #pragma unroll 1
                     for (int kk = 0; kk < 8; ++kk) {
                         const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
@@ -770,6 +771,24 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                         umma_f16(tO, sdesc_sw128(kq + off + 8192, 16, 1024),
                                  sdesc_sw128(sbase + C_OFF_S + off, 16, 1024), ID_O, kk > 0);
                     }
+                }
+                // ---- D_S pre-scaled by this chunk's gamma_{C-1} while R1 runs
+                // (R1 does not touch D_S; R2, which accumulates into it, is
+                // issued after every thread's next barrier). The first chunk
+                // of an item set D_S = gamma S0 above.
+                if (c > 0) {
+                    tc_fence_after();
+                    const float gC = gates(k)[G_GM + 63];
+#pragma unroll 1
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        float v[32];
+                        tmem_ld32(trow + TM_S + 32 * q4, v);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] *= gC;
+                        tmem_st32(trow + TM_S + 32 * q4, v);
+                    }
+                    tmem_wait_st();
                 }
                 ok = mbar_wait(bar_r1, k & 1);
                 if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
@@ -802,34 +821,44 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                         umma_f16(tO, sdesc_sw128(rec + REC_M + kk * 32, 16, 1024),
                                  sdesc_sw128(sbase + C_OFF_DT + kk * 32, 16, 1024), ID_O, 1);
                     umma_commit(bar_r2);
+                    // The next chunk's V^T (T diag b)^T part of D_U, off its
+                    // critical path, when its record and tiles are already in
+                    // (D_U was read out before this round was issued).
+                    u_pre = false;
+                    const int kn = k + 1;
+                    if (c + 1 < nch && mbar_try_wait(&bar_full[kn & 1], (kn >> 1) & 1) &&
+                        mbar_try_wait(&bar_conv[kn & 1], (kn >> 1) & 1)) {
+                        issue_u(sbase + C_OFF_V + (kn & 1) * V_STAGE, sbase + C_OFF_REC + (kn & 1) * REC_BYTES);
+                        u_pre = true;
+                    }
                 }
                 ok = mbar_wait(bar_r2s, k & 1);
                 if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
                 tc_fence_after();
 
-                // ---- state: fp16 copy for the next chunk and D_S pre-scaled
-                // by its gamma_{C-1}, or the final state
-                {
-                    const bool more = c + 1 < nch;
-                    const float gn = more ? gates(k + 1)[G_GM + 63] : 1.f;
+                // ---- state: the fp16 copy the next chunk's R1 reads (its only
+                // wait on this chunk), or the final state
+                if (c + 1 < nch) {
+#pragma unroll 1
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        float v[32], w[32];
+                        tmem_ld32(trow + TM_S + 64 * h2, v);
+                        tmem_ld32(trow + TM_S + 64 * h2 + 32, w);
+                        tmem_wait_ld();
+                        st_row32_f16(smem + C_OFF_S + h2 * 16384, row, 0, v);
+                        st_row32_f16(smem + C_OFF_S + h2 * 16384, row, 4, w);
+                    }
+                } else if (dst) {
 #pragma unroll 1
                     for (int q4 = 0; q4 < 4; ++q4) {
                         float v[32];
                         tmem_ld32(trow + TM_S + 32 * q4, v);
                         tmem_wait_ld();
-                        if (more) {
-                            st_row32_f16(smem + C_OFF_S + (q4 >> 1) * 16384, row, 4 * (q4 & 1), v);
 #pragma unroll
-                            for (int e = 0; e < 32; ++e) v[e] *= gn;
-                            tmem_st32(trow + TM_S + 32 * q4, v);
-                        } else if (dst) {
-#pragma unroll
-                            for (int e = 0; e < 32; e += 4)
-                                *reinterpret_cast<float4 *>(dst + 32 * q4 + e) =
-                                    make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-                        }
+                        for (int e = 0; e < 32; e += 4)
+                            *reinterpret_cast<float4 *>(dst + 32 * q4 + e) =
+                                make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
                     }
-                    if (more) tmem_wait_st();
                 }
                 fence_proxy_async_smem();
                 tc_fence_before();
@@ -842,7 +871,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
             umma_commit(bars + CB_DRAIN);
             mbar_wait(bars + CB_DRAIN, 0, 200000000ull);
         }
-    } else {
+    } else if (tid < 256) {
         // ------------------------------------------------ warpgroup 1: tiles, epilogue
         const int wt = tid - 128;
         int loads_issued = 0, loads_waited = 0, recs_issued = 0;
@@ -938,6 +967,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     if (wg_sync_or(2, !ok)) { rs.failed = true; break; }
                     ++loads_waited;
                     convert(k + 1);
+                    mbar_arrive(&bar_conv[(k + 1) & 1]);
                 }
                 // ---- chunk k's products are done
                 {
@@ -945,7 +975,6 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     if (wg_sync_or(2, !ok)) { rs.failed = true; break; }
                     tc_fence_after();
                 }
-                if (nxt.item >= 0) mbar_arrive(&bar_conv[(k + 1) & 1]);
                 // Stage and record slot k & 1 are free again: chunk k + 2's
                 // tiles, and its record once a producer has published it.
                 bool fok = true;
@@ -1023,13 +1052,17 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
 
 // ------------------------------------------------------------------ producer CTA
 //
-// All eight warps build chunk k's record while the tiles of chunk k + 1 land
-// and its D1 runs; records alternate between two staging buffers, so building
-// never waits for the copy of the previous record.
+// One context (256 threads, its own slice of shared memory, TMEM columns and
+// named barrier) builds the records of its tasks one after the other: chunk
+// k's record while the tiles of chunk k + 1 land and its D1 runs. A record is
+// written straight into its ring slot (generic stores of the swizzled fp16
+// images) once the chain has taken round r - RING out of that slot, and
+// published with a release flag when complete.
 __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k,
                                                    const GParams &p, uint8_t *smem, const Sched &sc,
-                                                   int64_t start, uint32_t tmem) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+                                                   int64_t start, int64_t step, uint32_t tmem,
+                                                   int lt, int bar_id) {
+    const int warp = lt >> 5, lane = lt & 31;
     const int row = 32 * (warp & 3) + lane;  // TMEM lane
     const int half = warp >> 2;              // column half of this thread
     const uint32_t trow = tmem + (static_cast<uint32_t>(warp & 3) << 21);
@@ -1037,9 +1070,11 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
     uint64_t *bar_load = bars + PB_LOAD, *bar_d1 = bars + PB_D1, *bar_mma = bars + PB_MMA;
     float *Af = reinterpret_cast<float *>(smem + P_OFF_AF);
     float *Tf = reinterpret_cast<float *>(smem + P_OFF_TF);
-    float *Xf = reinterpret_cast<float *>(smem + P_OFF_TH);  // scratch of the solve; T^ comes later
+    float *Xf = reinterpret_cast<float *>(smem + P_OFF_X);
+    uint8_t *th = smem + P_OFF_AF;  // T diag(beta gamma) hi, lo: the A table is dead by then
     const uint32_t sbase = smem_u32(smem);
-    const int64_t step = p.n_prod;  // this CTA's tasks: start, start + step, ...
+    auto csync = [&]() { nbar_sync(bar_id, 256); };
+    auto csync_or = [&](bool x) { return nbar_sync_or(bar_id, 256, x); };
     auto task_of = [&](const Ref &r) { return static_cast<int64_t>(r.r) * sc.NC + r.j; };
     auto gates = [&](int kc) { return reinterpret_cast<float *>(smem + P_OFF_GATE) + (kc & 1) * G_SIZE; };
     auto issue_loads = [&](int kc, const Ref &r) {
@@ -1053,11 +1088,10 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         tma_load_3d(kq + 24576, tm_q, 64, r.h, t32, bar);
     };
     // D1 = [K; Q] K^T of chunk kc on its bf16 tiles.
-    // The MMA-issue loops of both roles stay rolled: the per-chunk code of a
-    // role is larger than the instruction cache keeps warm, and a rolled issue
-    // loop (one thread, eight MMAs) costs nothing on the critical path while
-    // the unrolled copies cost instruction-fetch stalls (4.5% of the kernel on
-    // one box; the one-CTA kernel, with a different footprint, did not gain).
+    // The MMA-issue loops stay rolled: the per-chunk code is larger than the
+    // instruction cache keeps warm, and a rolled issue loop (one thread, eight
+    // MMAs) costs nothing on the critical path while unrolled copies cost
+    // instruction-fetch stalls.
     auto issue_d1 = [&](int kc) {
         const uint32_t kq = sbase + P_OFF_KQ + (kc & 1) * KQ_STAGE;
 #pragma unroll 1
@@ -1072,245 +1106,219 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
     RoleState rs{false};
     uint32_t mma_phase = 0;
     int loads_issued = 0, loads_waited = 0;
-    // Record hand-over of the previous chunk, deferred into this chunk's
-    // first phase (thread 128, whose warp has no table block there): once the
-    // chain has taken round r - RING out of its ring, the loads of the chunk
-    // after next and the bulk store of the record into ring slot r % RING.
-    // The store is published (release flag) in the next phase, by then done.
-    bool ho_pending = false, ho_fail = false, pub_pending = false;
-    Ref ho_nn{-1, 0, 0, 0, 0, 0}, ho_cur{-1, 0, 0, 0, 0, 0}, pub{-1, 0, 0, 0, 0, 0};
-    int ho_k = 0;
-    auto handover = [&]() {
-        if (tid == 128) {
-            tc_fence_after();
-            if (ho_nn.item >= 0) issue_loads(ho_k + 2, ho_nn);
-            if (poll_ge(p.consumed + ho_cur.j, ho_cur.r - RING + 1, p.abort_flag)) {
-                fence_proxy_async_global();
-                const int slot = ho_cur.r % RING;
-                bulk_store_s2g(p.ring + (static_cast<size_t>(ho_cur.j) * RING + slot) * REC_BYTES,
-                               smem + P_OFF_STG + (ho_k & 1) * REC_BYTES, REC_BYTES);
-            } else {
-                ho_fail = true;
-            }
-        }
-        if (ho_nn.item >= 0) ++loads_issued;
-        pub = ho_cur;
-        pub_pending = true;
-        ho_pending = false;
-    };
-    auto publish = [&]() {
-        if (tid == 128 && !ho_fail) {
-            bulk_wait_all();
-            fence_proxy_async_global();
-            st_release_gpu(p.ready + pub.j * RING + pub.r % RING, pub.r + 1);
-        }
-        pub_pending = false;
-    };
+    // Loads of the chunk after next, deferred into the next chunk's first
+    // phase (thread 128, whose warp has no table block there): the stage is
+    // free once that chunk's D1 and D_W are done.
+    bool ld_pending = false;
+    Ref ld_ref{-1, 0, 0, 0, 0, 0};
+    int ld_k = 0;
     int k = 0;
     GateIn gin{1.f, 1.f, 0.f, 0.f};  // warp 4: inputs of the next chunk's gate table
     Ref cur = sc.first_from(start, step);
     Ref nxt = cur.item >= 0 ? sc.first_from(task_of(cur) + step, step) : cur;
-    {
-        const Ref second = nxt;
-        if (tid == 0) {
-            if (cur.item >= 0) issue_loads(0, cur);
-            if (second.item >= 0) issue_loads(1, second);
+    if (cur.item >= 0) {
+        if (lt == 0) {
+            issue_loads(0, cur);
+            if (nxt.item >= 0) issue_loads(1, nxt);
         }
-        loads_issued = (cur.item >= 0) + (second.item >= 0);
-        if (cur.item >= 0) {
-            if (warp == 0) gate_tables(gates(0), gate_load(p, cur, lane), lane);
-            if (warp == 4) gin = gate_load(p, second, lane);
-            const bool ok = mbar_wait(&bar_load[0], 0);
-            if (__syncthreads_or(!ok)) {
-                rs.failed = true;
-            } else {
-                ++loads_waited;
-                if (tid == 0) {
-                    tc_fence_after();
-                    issue_d1(0);
-                }
+        loads_issued = 1 + (nxt.item >= 0);
+        if (warp == 0) gate_tables(gates(0), gate_load(p, cur, lane), lane);
+        if (warp == 4) gin = gate_load(p, nxt, lane);
+        const bool ok = mbar_wait(&bar_load[0], 0);
+        if (csync_or(!ok)) {
+            rs.failed = true;
+        } else {
+            ++loads_waited;
+            if (lt == 0) {
+                tc_fence_after();
+                issue_d1(0);
             }
         }
     }
 
     for (; cur.item >= 0 && !rs.failed; ++k) {
         const Ref nn = nxt.item >= 0 ? sc.first_from(task_of(nxt) + step, step) : nxt;
+        const uint32_t kq = sbase + P_OFF_KQ + (k & 1) * KQ_STAGE;
+        const float *g = gates(k);
+        const int *gz = reinterpret_cast<const int *>(g + G_Z);
+        const int slot = cur.r % RING;
+        uint8_t *rec = p.ring + (static_cast<size_t>(cur.j) * RING + slot) * REC_BYTES;
+
+        // ---- D1 of this chunk (issued during the previous one), and the ring
+        // slot: the chain has taken round r - RING out of it
         {
-            const uint32_t kq = sbase + P_OFF_KQ + (k & 1) * KQ_STAGE;
-            uint8_t *stg = smem + P_OFF_STG + (k & 1) * REC_BYTES;
-            const float *g = gates(k);
-            const int *gz = reinterpret_cast<const int *>(g + G_Z);
-
-            // ---- D1 of this chunk (issued during the previous one); staging
-            // buffer k & 1 is free (record k - 2's store completed when it was
-            // published, in the previous chunk)
-            {
-                const bool ok = mbar_wait(bar_d1, k & 1);
-                if (__syncthreads_or(!ok)) { rs.failed = true; break; }
+            bool ok = mbar_wait(bar_d1, k & 1);
+            if (lt == 0 && ok) ok = poll_ge(p.consumed + cur.j, cur.r - RING + 1, p.abort_flag);
+            if (csync_or(!ok)) { rs.failed = true; break; }
+            tc_fence_after();
+        }
+        if (ld_pending) {
+            if (lt == 128) {
                 tc_fence_after();
+                issue_loads(ld_k, ld_ref);
             }
-            if (ho_pending) handover();
+            ++loads_issued;
+            ld_pending = false;
+        }
 
-            // ---- A = beta P (K K^T) (fp32) and M = P (Q K^T) (record, fp16), 32 columns per thread
-            {
-                const bool qk = row >= 64;
-                const int t = row & 63;
-                const int s0 = 32 * half;
-                // Warp-uniform: the whole 32 x 32 block lies above the diagonal.
-                if (half == 1 && (warp & 1) == 0) {
-                    if (qk) st_zero32(stg + REC_M, t, 4);
-                } else {
-                    const float glt = g[G_GL + t];
-                    const int zt = gz[t];
-                    const float bt = qk ? 1.f : g[G_BE + t];
-#pragma unroll 1
-                    for (int hp = 0; hp < 2; ++hp) {
-                        const int sb = s0 + 16 * hp;
-                        float v[16];
-                        tmem_ld16(trow + TM_D1 + sb, v);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int j4 = 0; j4 < 4; ++j4) {
-                            const float4 g4 = *reinterpret_cast<const float4 *>(g + G_GL + sb + 4 * j4);
-                            const int4 z4 = *reinterpret_cast<const int4 *>(gz + sb + 4 * j4);
-                            const float gs[4] = {g4.x, g4.y, g4.z, g4.w};
-                            const int zs[4] = {z4.x, z4.y, z4.z, z4.w};
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const int j = 4 * j4 + e, s = sb + j;
-                                const float pv = zs[e] == zt ? ex2(glt - gs[e]) : 0.f;
-                                const bool keep = qk ? (s <= t) : (s < t);
-                                v[j] = keep ? bt * pv * v[j] : 0.f;
-                            }
-                        }
-                        if (qk) {
-                            st_row16_f16(stg + REC_M, t, 4 * half + 2 * hp, v);
-                        } else {
-#pragma unroll
-                            for (int j4 = 0; j4 < 4; ++j4)
-                                *reinterpret_cast<float4 *>(Af + t * AST + sb + 4 * j4) =
-                                    make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
-                        }
-                    }
-                }
-            }
-            tc_fence_before();
-            __syncthreads();
-
-            // ---- diagonal 16 x 16 tiles of T (warps 0-3, one each) while warps
-            // 4-7 zero tiles (0,1), (2,3) of T and wait for the next chunk's
-            // tiles
-            bool prep_fail = false;
-            if (warp < 4) {
-                diag_inverse16(Af + (16 * warp) * AST + 16 * warp, Tf + (16 * warp) * AST + 16 * warp, lane);
+        // ---- A = beta P (K K^T) (fp32) and M = P (Q K^T) (record, fp16), 32 columns per thread
+        {
+            const bool qk = row >= 64;
+            const int t = row & 63;
+            const int s0 = 32 * half;
+            // Warp-uniform: the whole 32 x 32 block lies above the diagonal.
+            if (half == 1 && (warp & 1) == 0) {
+                if (qk) st_zero32(rec + REC_M, t, 4);
             } else {
-                const int wt = tid - 128;
-                for (int e = wt; e < 512; e += 128) {
-                    const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
-                    Tf[(32 * blk + rr) * AST + 32 * blk + 16 + cc] = 0.f;
-                }
-                if (nxt.item >= 0) prep_fail = !mbar_wait(&bar_load[(k + 1) & 1], ((k + 1) >> 1) & 1);
-            }
-            if (__syncthreads_or(prep_fail || ho_fail)) { rs.failed = true; break; }
-            if (pub_pending) publish();
-            // The next D1 comes from thread 128 (warps 4-7 have no part in the
-            // solve's first step; from thread 0 it delayed warp 0's).
-            if (nxt.item >= 0) {
-                ++loads_waited;
-                if (tid == 128) {
-                    tc_fence_after();
-                    issue_d1(k + 1);
-                }
-            }
-            solve_offdiag(Af, Tf, Xf, warp, lane);
-
-            // ---- T diag(beta) (record, fp16) and T diag(beta gamma) (local, as a
-            // bf16 hi + lo pair so that D_W can read K's bf16 tile as it landed)
-            {
-                const int t = tid & 63;
-                const bool hat = (tid >> 6) & 1;
-                const int hh = tid >> 7;
-                const int s0 = 32 * hh;
-                uint8_t *dstb = hat ? smem + P_OFF_TH : stg + REC_TT;
-                if (hh == 1 && t < 32) {
-                    st_zero32(dstb, t, 4);
-                    if (hat) st_zero32(dstb + 8192, t, 4);
-                } else {
-                    const float *sc = g + (hat ? G_BG : G_BE);
+                const float glt = g[G_GL + t];
+                const int zt = gz[t];
+                const float bt = qk ? 1.f : g[G_BE + t];
 #pragma unroll 1
-                    for (int hp = 0; hp < 2; ++hp) {
-                        const int sb = s0 + 16 * hp;
-                        float v[16];
+                for (int hp = 0; hp < 2; ++hp) {
+                    const int sb = s0 + 16 * hp;
+                    float v[16];
+                    tmem_ld16(trow + TM_D1 + sb, v);
+                    tmem_wait_ld();
 #pragma unroll
-                        for (int j4 = 0; j4 < 4; ++j4) {
-                            const float4 tv = *reinterpret_cast<const float4 *>(Tf + t * AST + sb + 4 * j4);
-                            const float4 sv = *reinterpret_cast<const float4 *>(sc + sb + 4 * j4);
-                            const int s = sb + 4 * j4;
-                            v[4 * j4 + 0] = s + 0 <= t ? tv.x * sv.x : 0.f;
-                            v[4 * j4 + 1] = s + 1 <= t ? tv.y * sv.y : 0.f;
-                            v[4 * j4 + 2] = s + 2 <= t ? tv.z * sv.z : 0.f;
-                            v[4 * j4 + 3] = s + 3 <= t ? tv.w * sv.w : 0.f;
+                    for (int j4 = 0; j4 < 4; ++j4) {
+                        const float4 g4 = *reinterpret_cast<const float4 *>(g + G_GL + sb + 4 * j4);
+                        const int4 z4 = *reinterpret_cast<const int4 *>(gz + sb + 4 * j4);
+                        const float gs[4] = {g4.x, g4.y, g4.z, g4.w};
+                        const int zs[4] = {z4.x, z4.y, z4.z, z4.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int j = 4 * j4 + e, s = sb + j;
+                            const float pv = zs[e] == zt ? ex2(glt - gs[e]) : 0.f;
+                            const bool keep = qk ? (s <= t) : (s < t);
+                            v[j] = keep ? bt * pv * v[j] : 0.f;
                         }
-                        if (hat)
-                            st_row16_bf16_split(dstb, dstb + 8192, t, 4 * hh + 2 * hp, v);
-                        else
-                            st_row16_f16(dstb, t, 4 * hh + 2 * hp, v);
+                    }
+                    if (qk) {
+                        st_row16_f16(rec + REC_M, t, 4 * half + 2 * hp, v);
+                    } else {
+#pragma unroll
+                        for (int j4 = 0; j4 < 4; ++j4)
+                            *reinterpret_cast<float4 *>(Af + t * AST + sb + 4 * j4) =
+                                make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
                     }
                 }
             }
-            operands_ready();
+        }
+        tc_fence_before();
+        csync();
 
-            // ---- D_W = K^T (T diag bg)^T = K^T (hi + lo)^T on bf16 operands
-            // (lane j, column t: W[t][j])
-            if (tid == 0) {
-#pragma unroll 1
-                for (int kk = 0; kk < 8; ++kk)
-                    umma_f16(tmem + TM_W, sdesc_sw128(kq + (kk & 3) * 2048, 16384, 1024),
-                             sdesc_sw128(sbase + P_OFF_TH + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
-                             ID_MK64_BF, kk > 0);
-                umma_commit(bar_mma);
+        // ---- diagonal 16 x 16 tiles of T (warps 0-3, one each) while warps
+        // 4-7 zero tiles (0,1), (2,3) of T and wait for the next chunk's
+        // tiles
+        bool prep_fail = false;
+        if (warp < 4) {
+            diag_inverse16(Af + (16 * warp) * AST + 16 * warp, Tf + (16 * warp) * AST + 16 * warp, lane);
+        } else {
+            const int wt = lt - 128;
+            for (int e = wt; e < 512; e += 128) {
+                const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
+                Tf[(32 * blk + rr) * AST + 32 * blk + 16 + cc] = 0.f;
             }
-            // The next chunk's gate table, under D_W (off the solve's path:
-            // executed once per chunk by one warp, it ran mostly on
-            // instruction-fetch stalls)
-            if (warp == 4 && nxt.item >= 0) {
-                gate_tables(gates(k + 1), gin, lane);
-                gin = gate_load(p, nn, lane);
-            }
-            {
-                const bool ok = mbar_wait(bar_mma, mma_phase);
-                if (__syncthreads_or(!ok)) { rs.failed = true; break; }
-                mma_phase ^= 1u;
+            if (nxt.item >= 0) prep_fail = !mbar_wait(&bar_load[(k + 1) & 1], ((k + 1) >> 1) & 1);
+        }
+        if (csync_or(prep_fail)) { rs.failed = true; break; }
+        // The next D1 comes from thread 128 (warps 4-7 have no part in the
+        // solve's first step).
+        if (nxt.item >= 0) {
+            ++loads_waited;
+            if (lt == 128) {
                 tc_fence_after();
+                issue_d1(k + 1);
             }
-            {
-                float x[32];
-                tmem_ld32(trow + TM_W + 32 * half, x);
-                tmem_wait_ld();
-#pragma unroll
-                for (int t = 0; t < 32; ++t) x[t] = -x[t];
-                st_row32_f16(stg + REC_WT, row, 4 * half, x);
-            }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            __syncthreads();
+        }
+        solve_offdiag(Af, Tf, Xf, warp, lane, bar_id);
 
-            // ---- stage k & 1 is free (D1 and D_W are done): fetch chunk k + 2;
-            // hand the record to the chain CTA (its slot k & 1 is free: the
-            // chain consumed chunk k - 2 before this staging buffer was reused)
-            ho_pending = true;
-            ho_nn = nn;
-            ho_cur = cur;
-            ho_k = k;
+        // ---- T diag(beta) (record, fp16) and T diag(beta gamma) (local, as a
+        // bf16 hi + lo pair so that D_W can read K's bf16 tile as it landed)
+        {
+            const int t = lt & 63;
+            const bool hat = (lt >> 6) & 1;
+            const int hh = lt >> 7;
+            const int s0 = 32 * hh;
+            uint8_t *dstb = hat ? th : rec + REC_TT;
+            if (hh == 1 && t < 32) {
+                st_zero32(dstb, t, 4);
+                if (hat) st_zero32(dstb + 8192, t, 4);
+            } else {
+                const float *scl = g + (hat ? G_BG : G_BE);
+#pragma unroll 1
+                for (int hp = 0; hp < 2; ++hp) {
+                    const int sb = s0 + 16 * hp;
+                    float v[16];
+#pragma unroll
+                    for (int j4 = 0; j4 < 4; ++j4) {
+                        const float4 tv = *reinterpret_cast<const float4 *>(Tf + t * AST + sb + 4 * j4);
+                        const float4 sv = *reinterpret_cast<const float4 *>(scl + sb + 4 * j4);
+                        const int s = sb + 4 * j4;
+                        v[4 * j4 + 0] = s + 0 <= t ? tv.x * sv.x : 0.f;
+                        v[4 * j4 + 1] = s + 1 <= t ? tv.y * sv.y : 0.f;
+                        v[4 * j4 + 2] = s + 2 <= t ? tv.z * sv.z : 0.f;
+                        v[4 * j4 + 3] = s + 3 <= t ? tv.w * sv.w : 0.f;
+                    }
+                    if (hat)
+                        st_row16_bf16_split(dstb, dstb + 8192, t, 4 * hh + 2 * hp, v);
+                    else
+                        st_row16_f16(dstb, t, 4 * hh + 2 * hp, v);
+                }
+            }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        csync();
+        tc_fence_after();
+
+        // ---- D_W = K^T (T diag bg)^T = K^T (hi + lo)^T on bf16 operands
+        // (lane j, column t: W[t][j])
+        if (lt == 0) {
+#pragma unroll 1
+            for (int kk = 0; kk < 8; ++kk)
+                umma_f16(tmem + TM_W, sdesc_sw128(kq + (kk & 3) * 2048, 16384, 1024),
+                         sdesc_sw128(smem_u32(th) + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
+                         ID_MK64_BF, kk > 0);
+            umma_commit(bar_mma);
+        }
+        // The next chunk's gate table, under D_W.
+        if (warp == 4 && nxt.item >= 0) {
+            gate_tables(gates(k + 1), gin, lane);
+            gin = gate_load(p, nn, lane);
+        }
+        {
+            const bool ok = mbar_wait(bar_mma, mma_phase);
+            if (csync_or(!ok)) { rs.failed = true; break; }
+            mma_phase ^= 1u;
+            tc_fence_after();
+        }
+        {
+            float x[32];
+            tmem_ld32(trow + TM_W + 32 * half, x);
+            tmem_wait_ld();
+#pragma unroll
+            for (int t = 0; t < 32; ++t) x[t] = -x[t];
+            st_row32_f16(rec + REC_WT, row, 4 * half, x);
+        }
+        tc_fence_before();
+        csync();
+        // ---- record complete: publish it; stage k & 1 is free (D1 and D_W
+        // are done), so chunk k + 2's loads go out in the next phase
+        if (lt == 0) {
+            fence_proxy_async_global();
+            st_release_gpu(p.ready + cur.j * RING + slot, cur.r + 1);
+        }
+        if (nn.item >= 0) {
+            ld_pending = true;
+            ld_ref = nn;
+            ld_k = k + 2;
         }
         cur = nxt;
         nxt = nn;
     }
-    if (!rs.failed && ho_pending) handover();
-    if (!rs.failed && pub_pending) publish();
-    if (__syncthreads_or(ho_fail)) rs.failed = true;
 
-    if (rs.failed && tid == 0) {
+    if (rs.failed && lt == 0) {
         for (int kk = loads_waited; kk < loads_issued; ++kk)
             mbar_wait(&bar_load[kk & 1], (kk >> 1) & 1, 200000000ull);
         umma_commit(bars + PB_DRAIN);  // every MMA thread 0 issued: D_W and the first D1
@@ -1318,12 +1326,11 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         atomicExch(&g_grid_status, 1);
         atomicExch(p.abort_flag, 1);
     }
-    if (rs.failed && tid == 128) {
+    if (rs.failed && lt == 128) {
         umma_commit(bars + PB_DRAIN2);  // the later D1s (issued by this thread)
         mbar_wait(bars + PB_DRAIN2, 0, 200000000ull);
-        bulk_wait_all();                // a record store still reading staging
     }
-    rs.failed = __syncthreads_or(rs.failed);
+    rs.failed = csync_or(rs.failed);
     return rs;
 }
 
@@ -1337,19 +1344,23 @@ __global__ void __launch_bounds__(NT, 1)
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const int tid = threadIdx.x, warp = tid >> 5;
     const bool chain = static_cast<int>(blockIdx.x) < p.n_chains;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (chain ? C_OFF_BAR : P_OFF_BAR));
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + (chain ? CB_NUM : PB_NUM));
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(
+        chain ? smem + C_OFF_BAR + CB_NUM * 8 : smem + P_OFF_TMEM);
     const uint32_t ncols = chain ? C_TM_COLS : P_TM_COLS;
 
     if (tid == 0) {
         if (chain) {
+            uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C_OFF_BAR);
             for (int i = 0; i < CB_NUM; ++i) mbar_init(&bars[i], 1);  // loads, records, R1, R2
             for (int i = 0; i < 2; ++i) {
                 mbar_init(&bars[CB_CONV + i], 128);   // warpgroup 1 signals
                 mbar_init(&bars[CB_OFREE + i], 128);
             }
         } else {
-            for (int i = 0; i < PB_NUM; ++i) mbar_init(&bars[i], 1);
+            for (int c = 0; c < PCTX; ++c) {
+                uint64_t *bars = reinterpret_cast<uint64_t *>(smem + c * P_CTX_BYTES + P_OFF_BAR);
+                for (int i = 0; i < PB_NUM; ++i) mbar_init(&bars[i], 1);
+            }
         }
         mbar_fence_init();
         prefetch_tmap(&tm_q);
@@ -1382,7 +1393,12 @@ __global__ void __launch_bounds__(NT, 1)
         } else {
             sc.n_tasks = static_cast<int64_t>(p.sched[0]) * p.n_chains;
         }
-        producer_role(&tm_q, &tm_k, p, smem, sc, blockIdx.x - p.n_chains, tmem);
+        // Context c of producer CTA b takes tasks PCTX (b - n_chains) + c,
+        // then every PCTX n_prod-th after it.
+        const int ctx = tid >> 8;
+        const int64_t first = static_cast<int64_t>(PCTX) * (blockIdx.x - p.n_chains) + ctx;
+        producer_role(&tm_q, &tm_k, p, smem + ctx * P_CTX_BYTES, sc, first,
+                      static_cast<int64_t>(PCTX) * p.n_prod, tmem + ctx * P_TM_CTX, tid & 255, 3 + ctx);
     }
     tc_fence_before();
     __syncthreads();

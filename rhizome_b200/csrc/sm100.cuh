@@ -48,6 +48,25 @@ __device__ __forceinline__ void wg_sync(int id) {
     asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory");
 }
 
+// Named barrier over `count` threads (a multiple of 32), and the same with an
+// OR-reduction of a predicate.
+__device__ __forceinline__ void nbar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ bool nbar_sync_or(int id, int count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 __device__ __forceinline__ bool wg_sync_or(int id, bool pred) {
     uint32_t r;
     asm volatile(
