@@ -92,6 +92,17 @@ int rhz_abi_version(void);
 int rhz_device_status(int32_t *timed_out, int clear);
 
 /*
+ * rhz_gdr_set_wait_test -- test hook of the failure path above, an addition
+ * of this library. mode 1: in every later grid-form launch each chain CTA
+ * waits for a record flag that no producer sets, with waits on other CTAs'
+ * flags bounded at limit_ns (1 us .. 2 s); the wait runs out, the kernel
+ * drains, returns early and sets the device flag, exactly as a real timeout
+ * would (outputs undefined). mode 0 (the default) turns it off.
+ * Process-wide; not for production use.
+ */
+int rhz_gdr_set_wait_test(int32_t mode, int64_t limit_ns);
+
+/*
  * Which tensor-core form runs the bf16, d == 128 chunked scan
  * (rhz_gdr_scan_chunked, rhz_gdr_varlen_fwd): GRID (the default, AUTO) is
  * one launch over every SM in which chain CTAs carry each (sequence, head)

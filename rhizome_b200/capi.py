@@ -102,6 +102,7 @@ SIGNATURES = {
                                             _i64, _i64, _i32, _i32, _i32, _vp, _sz, _vp]),
     "rhz_gdr_host_workspace_bytes": (_sz, [_i64, _i64, _i32, _i32, _i32, C.c_int]),
     "rhz_gdr_set_chunk_kernel": (C.c_int, [_i32, _vp]),
+    "rhz_gdr_set_wait_test": (C.c_int, [_i32, _i64]),
 }
 
 # Forms of the tensor-core chunked scan (enum rhz_chunk_kernel).

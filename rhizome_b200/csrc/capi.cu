@@ -251,6 +251,11 @@ int rhz_device_status(int32_t *timed_out, int clear) {
     return RHZ_OK;
 }
 
+int rhz_gdr_set_wait_test(int32_t mode, int64_t limit_ns) {
+    clear_error();
+    return set_wait_test(mode, limit_ns);
+}
+
 int rhz_gdr_set_chunk_kernel(int32_t variant, int32_t *previous) {
     clear_error();
     int prev = 0;

@@ -179,6 +179,8 @@ struct GParams {
     const int32_t *sched; // packed streams: [0] rounds of the longest chain, [1 + j] rounds of chain j
     int n_chains;
     int n_prod;           // producer CTAs
+    uint64_t poll_ns;     // bound of every wait on another CTA's flag
+    int never_ready;      // test hook: chains wait for a record flag no producer sets
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -724,7 +726,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 // ---- R1's inputs: record k (bulk-loaded from the ring by
                 // warpgroup 1; once it has landed the ring slot is free again),
                 // tiles k in fp16, D_O buffer k & 1 read out
-                bool ok = mbar_wait(&bar_full[k & 1], (k >> 1) & 1);
+                bool ok = mbar_wait(&bar_full[k & 1], (k >> 1) & 1, p.poll_ns);
                 if (ok && tid == 0) st_release_gpu(consumed, k + 1);
                 ok = ok && mbar_wait(&bar_conv[k & 1], (k >> 1) & 1);
                 if (k >= 2) ok = ok && mbar_wait(&bar_ofree[k & 1], ((k >> 1) + 1) & 1);
@@ -879,7 +881,8 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
         // slot kc % RING, then bulk-load it into record slot kc & 1.
         auto fetch_record = [&](int kc) -> bool {
             const int slot = kc % RING;
-            if (!poll_ge(p.ready + chain * RING + slot, kc + 1, p.abort_flag)) return false;
+            const int target = p.never_ready ? kc + 1 + (1 << 30) : kc + 1;
+            if (!poll_ge(p.ready + chain * RING + slot, target, p.abort_flag, p.poll_ns)) return false;
             fence_proxy_async_global();
             uint64_t *bar = &bar_full[kc & 1];
             mbar_arrive_expect_tx(bar, REC_BYTES);
@@ -1148,7 +1151,7 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         // slot: the chain has taken round r - RING out of it
         {
             bool ok = mbar_wait(bar_d1, k & 1);
-            if (lt == 0 && ok) ok = poll_ge(p.consumed + cur.j, cur.r - RING + 1, p.abort_flag);
+            if (lt == 0 && ok) ok = poll_ge(p.consumed + cur.j, cur.r - RING + 1, p.abort_flag, p.poll_ns);
             if (csync_or(!ok)) { rs.failed = true; break; }
             tc_fence_after();
         }
@@ -1513,7 +1516,21 @@ int grid_chain_cap(int sms) {
     return cap < 1 ? 1 : cap;
 }
 
+// Test hook (rhz_gdr_set_wait_test): off, or every chain waits for a record
+// flag that no producer sets, with cross-CTA waits bounded at g_test_ns.
+std::atomic<int> g_test_mode{0};
+std::atomic<int64_t> g_test_ns{0};
+
 }  // namespace
+
+int set_wait_test(int mode, int64_t limit_ns) {
+    if (mode != 0 && mode != 1) return set_error(RHZ_ERR_INVALID, "wait test mode %d is not 0 or 1", mode);
+    if (mode == 1 && (limit_ns < 1000 || limit_ns > 2000000000LL))
+        return set_error(RHZ_ERR_INVALID, "wait limit %lld ns outside [1 us, 2 s]", static_cast<long long>(limit_ns));
+    g_test_ns.store(mode ? limit_ns : 0);
+    g_test_mode.store(mode);
+    return RHZ_OK;
+}
 
 size_t chunk_grid_ws_bytes(int64_t n_items, bool packed) { return grid_ws(n_items, packed).total; }
 
@@ -1601,6 +1618,8 @@ int launch_chunk_grid(const SeqArgs &a) {
     p.off = packed ? reinterpret_cast<int32_t *>(ws + w.off) : nullptr;
     p.n_chains = nc;
     p.n_prod = grid - nc;
+    p.never_ready = g_test_mode.load();
+    p.poll_ns = p.never_ready ? static_cast<uint64_t>(g_test_ns.load()) : 2000000000ull;
     if (packed) {
         const int warps = 8;
         gdr_grid_sched_kernel<<<(nc + warps - 1) / warps, 32 * warps, 0, a.stream>>>(

@@ -104,6 +104,9 @@ int chunk_solo_status(int *flag, bool clear);
 int launch_chunk_grid(const SeqArgs &a);
 size_t chunk_grid_ws_bytes(int64_t n_items, bool packed);
 int chunk_grid_status(int *flag, bool clear);
+// Test hook of the grid form's failure path (mode 1: chains wait for a flag
+// nothing sets, bounded at limit_ns; mode 0: off).
+int set_wait_test(int mode, int64_t limit_ns);
 
 // Variable-length index work (varlen.cu).
 int launch_prefix_sum(int32_t *cu, const int32_t *lengths, int64_t n, cudaStream_t s);

@@ -67,6 +67,14 @@ def test_chunk_form_setting_without_gpu(lib):
     assert lib.rhz_gdr_set_chunk_kernel(capi.RHZ_CHUNK_AUTO, None) == capi.RHZ_OK
 
 
+def test_wait_test_hook_validates_without_gpu(lib):
+    assert lib.rhz_gdr_set_wait_test(2, 1000000) == capi.RHZ_ERR_INVALID
+    assert lib.rhz_gdr_set_wait_test(1, 10) == capi.RHZ_ERR_INVALID  # below 1 us
+    assert lib.rhz_gdr_set_wait_test(1, 3_000_000_000) == capi.RHZ_ERR_INVALID
+    assert lib.rhz_gdr_set_wait_test(1, 20_000_000) == capi.RHZ_OK
+    assert lib.rhz_gdr_set_wait_test(0, 0) == capi.RHZ_OK
+
+
 def test_device_status_without_gpu(lib):
     assert lib.rhz_device_status(None, 0) == capi.RHZ_ERR_INVALID
     flag = C.c_int32(0)
