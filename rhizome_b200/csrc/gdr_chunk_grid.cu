@@ -25,15 +25,18 @@
 // sequential chain of each (sequence, head) item. The kernel is one
 // cooperative launch of one CTA per SM in two roles:
 //   chains (the first n_chains CTAs): item j, j + n_chains, ... one after
-//     the other, S in TMEM (fp32) for the whole sequence, an fp16 copy in
-//     shared memory as the MMA operand, and two MMA rounds per chunk:
+//     the other, S in TMEM (fp32) for the whole sequence, an fp16 image of S
+//     in TMEM that the products read as their A operand, and two MMA rounds
+//     per chunk:
 //       R1: D_U  = V^T (T diag b)^T + S (-W^T)   (128 x 64, = Delta^T)
-//           D_O  = Q~ S^T                         ( 64 x 128), Q~ = diag(gamma) Q
-//       R2: D_O += M Delta                        ( 64 x 128)
-//           D_S += Delta^T K~                     (128 x 128), K~ = diag(P[C-1]) K
-//     with D_S pre-scaled by gamma_{C-1} when the previous chunk's state is
-//     refreshed. Its tiles arrive by TMA one chunk ahead and are converted to
-//     fp16 in place (Q and K rows scaled on the way) under the R1 products.
+//           O^T  = S Q~^T                         (128 x 64), Q~ = diag(gamma) Q
+//       R2: D_S += Delta^T K~                     (128 x 128), K~ = diag(P[C-1]) K
+//           O^T += Delta^T M^T                    (128 x 64)
+//     with Delta^T's fp16 image also in TMEM and D_S pre-scaled by
+//     gamma_{C-1} while R1 runs. Neither S nor Delta passes through shared
+//     memory; O^T leaves through a bf16 [t][i] staging tile. The tiles arrive
+//     by TMA one chunk ahead and are converted to fp16 in place (Q and K rows
+//     scaled on the way) under the R1 products.
 //   producers (the other CTAs): chunk records for every chain, in
 //     round-major order (round r of every chain before round r + 1 of any),
 //     so all chains are fed evenly. A record is the 32 KB {-W^T, T diag(beta),
@@ -102,8 +105,8 @@ constexpr uint32_t G_BYTES = G_SIZE * 4;
 constexpr uint32_t C_OFF_KQ = 0;             // 2 stages
 constexpr uint32_t C_OFF_V = 65536;          // 2 stages
 constexpr uint32_t C_OFF_REC = 98304;        // 2 record slots
-constexpr uint32_t C_OFF_S = 163840;         // fp16 state [half j][128 rows i][64 j]
-constexpr uint32_t C_OFF_DT = 196608;        // fp16 Delta^T [i = 128 rows][s]
+constexpr uint32_t C_OFF_OST = 163840;       // O rows of a chunk, bf16 [64 t][128 i] (epilogue staging)
+constexpr uint32_t C_OFF_NPART = 196608;     // output norm: per-warp partial sums [4][64], then 1/rms [64]
 constexpr uint32_t C_OFF_GATE = 212992;      // ring of 4 gate tables
 constexpr uint32_t C_OFF_BAR = C_OFF_GATE + 4 * G_BYTES;
 // Chain barriers: tiles landed [2], record landed [2] (bulk load from the
@@ -137,13 +140,15 @@ static_assert(P_OFF_TF >= P_OFF_AF + 16384, "T diag(beta gamma) hi + lo must fit
 
 constexpr uint32_t SMEM_USED = C_USED > P_USED ? C_USED : P_USED;
 constexpr size_t SMEM_ALLOC = SMEM_USED + 1024;  // slack for 1024-byte alignment
-static_assert(C_OFF_GATE >= C_OFF_DT + 16384, "chain map overlaps");
+static_assert(C_OFF_NPART >= C_OFF_OST + 16384 && C_OFF_GATE >= C_OFF_NPART + 2048, "chain map overlaps");
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in shared memory");
 
-// TMEM columns (f32). Chain: D_U (128 lanes x 64), D_S (128 x 128) and two
-// D_O buffers (M = 64: row t in lane 32 (t / 16) + t % 16, 128 columns).
-// Producer: D1 (128 x 64) and D_W (128 x 64) per context.
-constexpr uint32_t TM_U = 0, TM_S = 64, TM_O = 192, C_TM_COLS = 512;
+// TMEM columns (32-bit). Chain: D_U (Delta^T, 128 lanes x 64), D_S
+// (128 x 128), two O^T accumulators (lane i, column t; 128 x 64 each), and
+// the fp16 images of S (128 x 128 -> 64 columns) and Delta^T (128 x 64 -> 32
+// columns) that the products read as their A operand straight from tensor
+// memory. Producer: D1 (128 x 64) and D_W (128 x 64) per context.
+constexpr uint32_t TM_U = 0, TM_S = 64, TM_OT = 192, TM_S16 = 320, TM_D16 = 384, C_TM_COLS = 512;
 constexpr uint32_t TM_D1 = 0, TM_W = 64, P_TM_CTX = 128, P_TM_COLS = PCTX * P_TM_CTX;
 
 constexpr uint32_t ID_D1 = idesc_bf16(128, 64, false, false);
@@ -151,7 +156,7 @@ constexpr uint32_t ID_MK64 = idesc_f16(128, 64, true, false);
 constexpr uint32_t ID_MK64_BF = idesc_bf16(128, 64, true, false);
 constexpr uint32_t ID_KM64 = idesc_f16(128, 64, false, true);
 constexpr uint32_t ID_KM128 = idesc_f16(128, 128, false, true);
-constexpr uint32_t ID_O = idesc_f16(64, 128, false, false);
+constexpr uint32_t ID_OT = idesc_f16(128, 64, false, false);
 
 // Record ring: RING slots of REC_BYTES per chain; flags in the workspace.
 constexpr int RING = 4;
@@ -193,11 +198,6 @@ __device__ __forceinline__ float lg2(float x) {
     float y;
     asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
-}
-
-__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t *>(&v);
 }
 
 __device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
@@ -721,7 +721,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 const uint32_t kq = sbase + C_OFF_KQ + (k & 1) * KQ_STAGE;
                 const uint32_t vb = sbase + C_OFF_V + (k & 1) * V_STAGE;
                 const uint32_t rec = sbase + C_OFF_REC + (k & 1) * REC_BYTES;
-                const uint32_t tO = tmem + TM_O + 128 * (k & 1);
+                const uint32_t tO = tmem + TM_OT + 64 * (k & 1);
 
                 // ---- R1's inputs: record k (bulk-loaded from the ring by
                 // warpgroup 1; once it has landed the ring slot is free again),
@@ -732,46 +732,50 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 if (k >= 2) ok = ok && mbar_wait(&bar_ofree[k & 1], ((k >> 1) + 1) & 1);
                 if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
 
-                // ---- first chunk of the item: fp16 copy of S0 (unscaled) and
+                // ---- first chunk of the item: fp16 image of S0 (unscaled) and
                 // D_S = gamma_{C-1} S0
                 if (c == 0) {
                     const float gC = gates(k)[G_GM + 63];
 #pragma unroll 1
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        float v[32];
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        uint32_t w[32];
 #pragma unroll
-                        for (int e = 0; e < 32; e += 4) {
-                            const float4 f = have ? *reinterpret_cast<const float4 *>(src + 32 * q4 + e)
-                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-                            v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
+                        for (int q2 = 0; q2 < 2; ++q2) {
+                            float v[32];
+#pragma unroll
+                            for (int e = 0; e < 32; e += 4) {
+                                const float4 f = have ? *reinterpret_cast<const float4 *>(src + 64 * h2 + 32 * q2 + e)
+                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                                v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
+                            }
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) w[16 * q2 + e] = pack_f16x2(v[2 * e], v[2 * e + 1]);
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) v[e] *= gC;
+                            tmem_st32(trow + TM_S + 64 * h2 + 32 * q2, v);
                         }
-                        st_row32_f16(smem + C_OFF_S + (q4 >> 1) * 16384, row, 4 * (q4 & 1), v);
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) v[e] *= gC;
-                        tmem_st32(trow + TM_S + 32 * q4, v);
+                        tmem_st32u(trow + TM_S16 + 32 * h2, w);
                     }
                     tmem_wait_st();
-                    fence_proxy_async_smem();
                     tc_fence_before();
                     wg_sync(1);
                 }
 
-                // ---- R1: D_U = V^T (T diag b)^T + S (-W^T) ; D_O[k & 1] = Q~ S^T
+                // ---- R1: D_U = V^T (T diag b)^T + S (-W^T) ; O^T[k & 1] = S Q~^T,
+                // S read as the A operand from its fp16 image in TMEM
                 if (tid == 0) {
                     tc_fence_after();
                     if (!u_pre) issue_u(vb, rec);
 #pragma unroll 1
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                        umma_f16(tmem + TM_U, sdesc_sw128(sbase + C_OFF_S + off, 16, 1024),
-                                 sdesc_sw128(rec + REC_WT + kk * 2048, 8192, 1024), ID_KM64, 1);
-                    }
-                    umma_commit(bar_r1);  // Delta^T is ready; D_O runs on behind it
+                    for (int kk = 0; kk < 8; ++kk)
+                        umma_f16_ta(tmem + TM_U, tmem + TM_S16 + 8 * kk,
+                                    sdesc_sw128(rec + REC_WT + kk * 2048, 8192, 1024), ID_KM64, 1);
+                    umma_commit(bar_r1);  // Delta^T is ready; O^T runs on behind it
 #pragma unroll 1
                     for (int kk = 0; kk < 8; ++kk) {
                         const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                        umma_f16(tO, sdesc_sw128(kq + off + 8192, 16, 1024),
-                                 sdesc_sw128(sbase + C_OFF_S + off, 16, 1024), ID_O, kk > 0);
+                        umma_f16_ta(tO, tmem + TM_S16 + 8 * kk, sdesc_sw128(kq + off + 8192, 16, 1024),
+                                    ID_OT, kk > 0);
                     }
                 }
                 // ---- D_S pre-scaled by this chunk's gamma_{C-1} while R1 runs
@@ -796,32 +800,38 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
                 tc_fence_after();
 
-                // ---- Delta^T (fp16): row i, all 64 positions
+                // ---- Delta^T (fp16) into its TMEM image: row i, all 64 positions
                 {
                     float x[32], y[32];
                     tmem_ld32(trow + TM_U, x);
                     tmem_ld32(trow + TM_U + 32, y);
                     tmem_wait_ld();
-                    st_row32_f16(smem + C_OFF_DT, row, 0, x);
-                    st_row32_f16(smem + C_OFF_DT, row, 4, y);
+                    uint32_t w[32];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        w[e] = pack_f16x2(x[2 * e], x[2 * e + 1]);
+                        w[16 + e] = pack_f16x2(y[2 * e], y[2 * e + 1]);
+                    }
+                    tmem_st32u(trow + TM_D16, w);
+                    tmem_wait_st();
                 }
-                fence_proxy_async_smem();
                 tc_fence_before();
                 wg_sync(1);
 
                 // ---- R2: D_S += Delta^T K~ (the state refresh waits for this
-                // part only), then D_O[k & 1] += M Delta
+                // part only; it also covers O^T = S Q~^T, so S's image is free),
+                // then O^T[k & 1] += Delta^T M^T
                 if (tid == 0) {
                     tc_fence_after();
 #pragma unroll 1
                     for (int kk = 0; kk < 4; ++kk)
-                        umma_f16(tmem + TM_S, sdesc_sw128(sbase + C_OFF_DT + kk * 32, 16, 1024),
-                                 sdesc_sw128(kq + kk * 2048, 16384, 1024), ID_KM128, 1);
+                        umma_f16_ta(tmem + TM_S, tmem + TM_D16 + 8 * kk,
+                                    sdesc_sw128(kq + kk * 2048, 16384, 1024), ID_KM128, 1);
                     umma_commit(bar_r2s);
 #pragma unroll 1
                     for (int kk = 0; kk < 4; ++kk)
-                        umma_f16(tO, sdesc_sw128(rec + REC_M + kk * 32, 16, 1024),
-                                 sdesc_sw128(sbase + C_OFF_DT + kk * 32, 16, 1024), ID_O, 1);
+                        umma_f16_ta(tO, tmem + TM_D16 + 8 * kk, sdesc_sw128(rec + REC_M + kk * 32, 16, 1024),
+                                    ID_OT, 1);
                     umma_commit(bar_r2);
                     // The next chunk's V^T (T diag b)^T part of D_U, off its
                     // critical path, when its record and tiles are already in
@@ -838,18 +848,24 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
                 tc_fence_after();
 
-                // ---- state: the fp16 copy the next chunk's R1 reads (its only
+                // ---- state: the fp16 image the next chunk's R1 reads (its only
                 // wait on this chunk), or the final state
                 if (c + 1 < nch) {
 #pragma unroll 1
                     for (int h2 = 0; h2 < 2; ++h2) {
-                        float v[32], w[32];
+                        float v[32], x[32];
                         tmem_ld32(trow + TM_S + 64 * h2, v);
-                        tmem_ld32(trow + TM_S + 64 * h2 + 32, w);
+                        tmem_ld32(trow + TM_S + 64 * h2 + 32, x);
                         tmem_wait_ld();
-                        st_row32_f16(smem + C_OFF_S + h2 * 16384, row, 0, v);
-                        st_row32_f16(smem + C_OFF_S + h2 * 16384, row, 4, w);
+                        uint32_t w[32];
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {
+                            w[e] = pack_f16x2(v[2 * e], v[2 * e + 1]);
+                            w[16 + e] = pack_f16x2(x[2 * e], x[2 * e + 1]);
+                        }
+                        tmem_st32u(trow + TM_S16 + 32 * h2, w);
                     }
+                    tmem_wait_st();
                 } else if (dst) {
 #pragma unroll 1
                     for (int q4 = 0; q4 < 4; ++q4) {
@@ -862,7 +878,6 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                                 make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
                     }
                 }
-                fence_proxy_async_smem();
                 tc_fence_before();
                 wg_sync(1);
             }
@@ -988,50 +1003,78 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 if (nn.item >= 0) ++loads_issued;
                 if (wg_sync_or(2, !fok)) { rs.failed = true; break; }
 
-                // ---- O rows of chunk k (D_O row t in lane 32 (t / 16) + t % 16),
+                // ---- O rows of chunk k from O^T[k & 1] (lane i, column t),
                 // optionally RMS-normalised per head first (groupnorm_heads,
-                // norm.rs:48-60, on the fp32 accumulator)
+                // norm.rs:48-60, on the fp32 accumulator): each thread turns its
+                // column i into bf16 in a [t][i] staging tile, then the rows go
+                // out as 16-byte stores.
                 {
-                    const uint32_t tO = trow + TM_O + 128 * (k & 1);
-                    const int t = 16 * ww + lane;
-                    const bool has_row = lane < 16 && t < L;
-                    __nv_bfloat16 *op = p.o + (ts + t) * tok_stride + static_cast<int64_t>(h) * HD;
-                    float inv = 1.f;
+                    const uint32_t tOT = trow + TM_OT + 64 * (k & 1);
+                    float *npart = reinterpret_cast<float *>(smem + C_OFF_NPART);
+                    float *ninv = npart + 4 * 64;
                     if (norm) {
-                        float ss = 0.f;
-#pragma unroll 1
-                        for (int q4 = 0; q4 < 4; ++q4) {
-                            float o[32];
-                            tmem_ld32(tO + 32 * q4, o);
+                        // sum over i of o[t][i]^2 for every t: a transposing
+                        // butterfly over the warp's 32 lanes (lane l ends with
+                        // t = 2l, 2l + 1), then the four warps through shared memory
+                        float r[32];
+                        {
+                            float x[32], y[32];
+                            tmem_ld32(tOT, x);
+                            tmem_ld32(tOT + 32, y);
                             tmem_wait_ld();
+                            const bool up = lane & 16;
 #pragma unroll
-                            for (int e = 0; e < 32; ++e) ss += o[e] * o[e];
-                        }
-                        inv = 1.f / sqrtf(ss / static_cast<float>(HD) + p.norm_eps);
-                    }
-#pragma unroll 1
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        float o[32];
-                        tmem_ld32(tO + 32 * q4, o);
-                        tmem_wait_ld();
-                        if (norm) {
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) o[e] = o[e] * inv * nsc[32 * q4 + e];
-                        }
-                        if (has_row) {
-#pragma unroll
-                            for (int c8 = 0; c8 < 4; ++c8) {
-                                uint4 w;
-                                w.x = pack_bf16x2(o[8 * c8 + 0], o[8 * c8 + 1]);
-                                w.y = pack_bf16x2(o[8 * c8 + 2], o[8 * c8 + 3]);
-                                w.z = pack_bf16x2(o[8 * c8 + 4], o[8 * c8 + 5]);
-                                w.w = pack_bf16x2(o[8 * c8 + 6], o[8 * c8 + 7]);
-                                *reinterpret_cast<uint4 *>(op + 32 * q4 + 8 * c8) = w;
+                            for (int j = 0; j < 32; ++j) {
+                                const float sx = x[j] * x[j], sy = y[j] * y[j];
+                                r[j] = (up ? sy : sx) + __shfl_xor_sync(0xffffffffu, up ? sx : sy, 16);
                             }
+                        }
+#pragma unroll
+                        for (int step = 0; step < 4; ++step) {
+                            const int m = 8 >> step, n = 16 >> step;
+                            const bool up = lane & m;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                if (j < n) {
+                                    const float lo = r[j], hi = r[j + n];
+                                    r[j] = (up ? hi : lo) + __shfl_xor_sync(0xffffffffu, up ? lo : hi, m);
+                                }
+                            }
+                        }
+                        npart[ww * 64 + 2 * lane] = r[0];
+                        npart[ww * 64 + 2 * lane + 1] = r[1];
+                        wg_sync(2);
+                        if (wt < 64) {
+                            const float ss = npart[wt] + npart[64 + wt] + npart[128 + wt] + npart[192 + wt];
+                            ninv[wt] = 1.f / sqrtf(ss / static_cast<float>(HD) + p.norm_eps);
+                        }
+                        wg_sync(2);
+                    }
+                    uint16_t *stg = reinterpret_cast<uint16_t *>(smem + C_OFF_OST);
+                    const float sc = norm ? nsc[wt] : 1.f;
+#pragma unroll 1
+                    for (int hf = 0; hf < 2; ++hf) {
+                        float x[32];
+                        tmem_ld32(tOT + 32 * hf, x);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int t = 32 * hf + j;
+                            const float v = norm ? x[j] * ninv[t] * sc : x[j];
+                            stg[t * HD + wt] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
                         }
                     }
                     tc_fence_before();
                     mbar_arrive(&bar_ofree[k & 1]);
+                    wg_sync(2);
+                    __nv_bfloat16 *orow = p.o + ts * tok_stride + static_cast<int64_t>(h) * HD;
+#pragma unroll
+                    for (int c8 = 0; c8 < 8; ++c8) {
+                        const int idx = wt + 128 * c8, t = idx >> 4, ch = idx & 15;
+                        if (t < L)
+                            *reinterpret_cast<uint4 *>(orow + t * tok_stride + 8 * ch) =
+                                *reinterpret_cast<const uint4 *>(stg + t * HD + 8 * ch);
+                    }
                 }
             }
         }
