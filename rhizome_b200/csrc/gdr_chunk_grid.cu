@@ -86,39 +86,44 @@ constexpr int HD = 128;   // head dim (d_k = d_v)
 constexpr int NT = 512;   // threads per CTA (chain: two warpgroups work; producer: two contexts)
 constexpr int AST = 68;   // fp32 row stride of the A / T tables (16-byte rows, bank spread)
 
-constexpr uint32_t KQ_STAGE = 32768;  // [half][K rows | Q rows], 64 x 64 bf16 boxes
-constexpr uint32_t V_STAGE = 16384;   // [half][V rows]
+constexpr uint32_t KQ_STAGE = 32768;  // producer tiles: [half][K rows | Q rows], 64 x 64 bf16 boxes
 constexpr uint32_t KQ_BYTES = 4 * 8192;
 constexpr uint32_t KQV_BYTES = 6 * 8192;
 
-// Producer -> chain record: fp16 operand images, 128-byte swizzle.
-constexpr uint32_t REC_WT = 0;        // -W^T [j = 128 rows][t = 64]     (MN-major B of R1)
-constexpr uint32_t REC_TT = 16384;    // T diag(beta) [t = 64 rows][s]   (K-major B of R1)
-constexpr uint32_t REC_M = 24576;     // M = P (Q K^T) [t rows][s]        (K-major A of R2)
+// Producer -> chain record: fp16 operand images, 128-byte swizzle, in the
+// pieces the chain's bulk copies place next to its own tiles.
+constexpr uint32_t REC_W = 0;         // -W [j half][t = 64 rows][64 j]   (K-major rows 64..127 of R1's B)
+constexpr uint32_t REC_MT = 16384;    // M^T [s = 64 rows][64 t]           (third MN-major atom of R2's B)
+constexpr uint32_t REC_TT = 24576;    // T diag(beta) [t = 64 rows][64 s]  (K-major B of the U product)
 constexpr uint32_t REC_BYTES = 32768;
 
 // Gate table layout (floats): gl[64] z[64] (int) beta[64] gamma[64] P[C-1][.][64] beta*gamma[64].
 constexpr int G_GL = 0, G_Z = 64, G_BE = 128, G_GM = 192, G_PL = 256, G_BG = 320, G_SIZE = 384;
 constexpr uint32_t G_BYTES = G_SIZE * 4;
 
-// Chain CTA shared memory.
-constexpr uint32_t C_OFF_KQ = 0;             // 2 stages
-constexpr uint32_t C_OFF_V = 65536;          // 2 stages
-constexpr uint32_t C_OFF_REC = 98304;        // 2 record slots
-constexpr uint32_t C_OFF_OST = 163840;       // O rows of a chunk, bf16 [64 t][128 i] (epilogue staging)
-constexpr uint32_t C_OFF_NPART = 196608;     // output norm: per-warp partial sums [4][64], then 1/rms [64]
-constexpr uint32_t C_OFF_GATE = 212992;      // ring of 4 gate tables
+// Chain CTA shared memory: two stages (chunk k in stage k & 1) of
+//   B1 [j half][Q~ rows t 0..63 | -W rows t 64..127]   K-major B of R1 (N = 128)
+//   B2 [K~ j 0..63 | K~ j 64..127 | M^T] (rows s)      MN-major B of R2 (N = 192, atoms 8 KB apart)
+//   V  [i half][rows s]                                 MN-major A of the U product
+//   TT T diag(beta) [t][s]                              K-major B of the U product
+// The Q, K, V tiles come by TMA, the -W, M^T and T diag(beta) pieces by bulk
+// copies from the record ring.
+constexpr uint32_t CS_B1 = 0, CS_B2 = 32768, CS_V = 57344, CS_TT = 73728, C_STAGE = 81920;
+constexpr uint32_t C_OFF_OST = 2 * C_STAGE;           // O rows of a chunk, bf16 [64 t][128 i] (epilogue staging)
+constexpr uint32_t C_OFF_NPART = C_OFF_OST + 16384;   // output norm: per-warp partial sums [4][64], then 1/rms [64]
+constexpr uint32_t C_OFF_GATE = C_OFF_NPART + 2048;   // ring of 4 gate tables
 constexpr uint32_t C_OFF_BAR = C_OFF_GATE + 4 * G_BYTES;
-// Chain barriers: tiles landed [2], record landed [2] (bulk load from the
-// ring), D_U done (R1), D_S
-// done (R2), all of a chunk's products done, tiles converted [2] (warpgroup
-// 1 -> 0), D_O buffer read out [2] (1 -> 0), and a barrier that only the
-// failure path uses to wait for every MMA issued.
-constexpr int CB_LOAD = 0, CB_FULL = 2, CB_R1 = 4, CB_R2S = 5, CB_R2 = 6, CB_CONV = 7, CB_OFREE = 9,
+// Chain barriers: tiles landed [2], record landed [2] (bulk copies from the
+// ring), D_U done (R1), all of a chunk's products done (R2), tiles converted
+// [2] (warpgroup 1 -> 0), O^T read out and cleared [2] (1 -> 0, by chunk
+// parity), and a barrier that only the failure path uses to wait for every
+// MMA issued.
+constexpr int CB_LOAD = 0, CB_FULL = 2, CB_R1 = 4, CB_R2 = 6, CB_CONV = 7, CB_OFREE = 9,
               CB_DRAIN = 11, CB_NUM = 12;
 constexpr uint32_t C_OFF_NORM = C_OFF_BAR + 128;  // output-norm scale, HD floats
 constexpr uint32_t C_USED = C_OFF_NORM + HD * 4;
 static_assert(C_OFF_NORM >= C_OFF_BAR + CB_NUM * 8 + 16, "chain barriers overlap the norm scale");
+static_assert(C_STAGE % 1024 == 0 && CS_TT + 8192 <= C_STAGE, "chain stage map");
 
 // Producer CTA: PCTX independent contexts of 256 threads, each building the
 // records of its own task stream in its own slice of shared memory (two
@@ -140,23 +145,22 @@ static_assert(P_OFF_TF >= P_OFF_AF + 16384, "T diag(beta gamma) hi + lo must fit
 
 constexpr uint32_t SMEM_USED = C_USED > P_USED ? C_USED : P_USED;
 constexpr size_t SMEM_ALLOC = SMEM_USED + 1024;  // slack for 1024-byte alignment
-static_assert(C_OFF_NPART >= C_OFF_OST + 16384 && C_OFF_GATE >= C_OFF_NPART + 2048, "chain map overlaps");
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in shared memory");
 
-// TMEM columns (32-bit). Chain: D_U (Delta^T, 128 lanes x 64), D_S
-// (128 x 128), two O^T accumulators (lane i, column t; 128 x 64 each), and
-// the fp16 images of S (128 x 128 -> 64 columns) and Delta^T (128 x 64 -> 32
+// TMEM columns (32-bit). Chain: one contiguous accumulator [D_S 128 | O^T 64 |
+// D_U 64] (lane i; O^T column t, D_U = Delta^T column s), so that R1 writes
+// [O^T | D_U] and R2 writes [D_S | O^T] as single wide products, and the
+// fp16 images of S (128 x 128 -> 64 columns) and Delta^T (128 x 64 -> 32
 // columns) that the products read as their A operand straight from tensor
 // memory. Producer: D1 (128 x 64) and D_W (128 x 64) per context.
-constexpr uint32_t TM_U = 0, TM_S = 64, TM_OT = 192, TM_S16 = 320, TM_D16 = 384, C_TM_COLS = 512;
+constexpr uint32_t TM_DS = 0, TM_OT = 128, TM_DU = 192, TM_S16 = 256, TM_D16 = 320, C_TM_COLS = 512;
 constexpr uint32_t TM_D1 = 0, TM_W = 64, P_TM_CTX = 128, P_TM_COLS = PCTX * P_TM_CTX;
 
 constexpr uint32_t ID_D1 = idesc_bf16(128, 64, false, false);
 constexpr uint32_t ID_MK64 = idesc_f16(128, 64, true, false);
 constexpr uint32_t ID_MK64_BF = idesc_bf16(128, 64, true, false);
-constexpr uint32_t ID_KM64 = idesc_f16(128, 64, false, true);
-constexpr uint32_t ID_KM128 = idesc_f16(128, 128, false, true);
-constexpr uint32_t ID_OT = idesc_f16(128, 64, false, false);
+constexpr uint32_t ID_R1 = idesc_f16(128, 128, false, false);  // S [Q~ | -W]^T: A from TMEM, B K-major
+constexpr uint32_t ID_R2 = idesc_f16(128, 192, false, true);   // Delta^T [K~ | M^T]: B MN-major
 
 // Record ring: RING slots of REC_BYTES per chain; flags in the workspace.
 constexpr int RING = 4;
@@ -215,23 +219,15 @@ __device__ __forceinline__ uint4 pack8_f16(const float *v) {
     return w;
 }
 
-// 32 values as fp16 into 16-byte chunks c0 .. c0+3 of row `row` of a
+// 16 values as fp16 into 16-byte chunks c0, c0+1 of row `row` of a
 // 128-byte-swizzled block of 128-byte rows (canonical SWIZZLE_128B layout).
-__device__ __forceinline__ void st_row32_f16(uint8_t *blk, uint32_t row, uint32_t c0,
-                                             const float *v) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-        *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + c)) = pack8_f16(v + 8 * c);
-}
-
-// 16 values as fp16 into 16-byte chunks c0, c0+1 (same layout as st_row32_f16).
 __device__ __forceinline__ void st_row16_f16(uint8_t *blk, uint32_t row, uint32_t c0, const float *v) {
     *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0)) = pack8_f16(v);
     *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + 1)) = pack8_f16(v + 8);
 }
 
 // 16 values as a bf16 pair hi = bf16(v), lo = bf16(v - hi) into chunks c0,
-// c0+1 of row `row` of two blocks of the st_row32_f16 layout (hi + lo
+// c0+1 of row `row` of two blocks of the st_row16_f16 layout (hi + lo
 // carries ~16 mantissa bits).
 __device__ __forceinline__ void st_row16_bf16_split(uint8_t *hi_blk, uint8_t *lo_blk, uint32_t row,
                                                     uint32_t c0, const float *v) {
@@ -257,57 +253,60 @@ __device__ __forceinline__ void st_zero32(uint8_t *blk, uint32_t row, uint32_t c
         *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + c)) = make_uint4(0, 0, 0, 0);
 }
 
+// One fp16 element at (row r, column e) of a block of 128-byte rows of 64
+// columns stored with the 128-byte swizzle.
+__device__ __forceinline__ void st_sw_f16(uint8_t *blk, int r, int e, float v) {
+    *reinterpret_cast<__half *>(blk + r * 128 + (((e >> 3) ^ (r & 7)) << 4) + (e & 7) * 2) =
+        __float2half_rn(v);
+}
+
 __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x, float s) {
     __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162 *>(&x);
     return pack_f16x2(__low2float(b) * s, __high2float(b) * s);
 }
 
-// Chain: one stage's K, Q (32 KB) and V (16 KB) tiles bf16 -> fp16 in place,
-// Q rows scaled by gamma_t and K rows by P[C-1][s]; this thread's 16-byte
-// chunks are first, first + STRIDE, ... of the K/Q stage (2048 chunks) and of
-// the V stage (1024). The swizzle permutes chunks within a row only, so chunk
-// i of a K/Q half lies in row (i / 8) % 128 (rows 0..63 K, 64..127 Q).
+// Chain: one stage's Q, K and V tiles (16 KB each) bf16 -> fp16 in place, Q
+// rows (in B1) scaled by gamma_t and K rows (in B2) by P[C-1][s]. The stage
+// holds 3072 16-byte chunks: Q (B1 half h, rows 0..63), K (B2, contiguous),
+// V; this thread's are first, first + STRIDE, ... The swizzle permutes
+// chunks within a row only, so a chunk's row (and scale) follows from its
+// index.
 template <int STRIDE>
-__device__ __forceinline__ void chain_tiles_to_f16(uint8_t *kq, uint8_t *vv, const float *gm,
-                                                   const float *pl, int first) {
-    static_assert(2048 % (8 * STRIDE) == 0 && 1024 % (8 * STRIDE) == 0, "batches of 8 chunks");
-    // Eight loads in flight, then eight converted stores (batches rolled to
-    // keep the code small).
+__device__ __forceinline__ void chain_tiles_to_f16(uint8_t *stage, const float *gm, const float *pl,
+                                                   int first) {
+    static_assert(1024 % (8 * STRIDE) == 0, "batches of 8 chunks");
 #pragma unroll 1
-    for (int b = 0; b < 2048 / STRIDE; b += 8) {
-        uint4 x[8];
-        float sc[8];
-#pragma unroll
-        for (int m = 0; m < 8; ++m) {
-            const int i = first + (b + m) * STRIDE;
-            const int r = (i >> 3) & 127;
-            x[m] = *reinterpret_cast<const uint4 *>(kq + i * 16);
-            sc[m] = r < 64 ? pl[r] : gm[r - 64];
-        }
-#pragma unroll
-        for (int m = 0; m < 8; ++m) {
-            const int i = first + (b + m) * STRIDE;
-            uint4 w = x[m];
-            w.x = bf16x2_to_f16x2(w.x, sc[m]);
-            w.y = bf16x2_to_f16x2(w.y, sc[m]);
-            w.z = bf16x2_to_f16x2(w.z, sc[m]);
-            w.w = bf16x2_to_f16x2(w.w, sc[m]);
-            *reinterpret_cast<uint4 *>(kq + i * 16) = w;
-        }
-    }
+    for (int part = 0; part < 3; ++part) {
 #pragma unroll 1
-    for (int b = 0; b < 1024 / STRIDE; b += 8) {
-        uint4 x[8];
+        for (int b = 0; b < 1024 / STRIDE; b += 8) {
+            uint4 x[8];
+            uint8_t *ad[8];
+            float sc[8];
 #pragma unroll
-        for (int m = 0; m < 8; ++m) x[m] = *reinterpret_cast<const uint4 *>(vv + (first + (b + m) * STRIDE) * 16);
+            for (int m = 0; m < 8; ++m) {
+                const int i = first + (b + m) * STRIDE;  // chunk within the part
+                const int r = (i >> 3) & 63;
+                if (part == 0) {
+                    ad[m] = stage + CS_B1 + (i >> 9) * 16384 + r * 128 + (i & 7) * 16;
+                    sc[m] = gm[r];
+                } else if (part == 1) {
+                    ad[m] = stage + CS_B2 + i * 16;
+                    sc[m] = pl[r];
+                } else {
+                    ad[m] = stage + CS_V + i * 16;
+                    sc[m] = 1.f;
+                }
+                x[m] = *reinterpret_cast<const uint4 *>(ad[m]);
+            }
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-            uint4 w = x[m];
-            w.x = bf16x2_to_f16x2(w.x, 1.f);
-            w.y = bf16x2_to_f16x2(w.y, 1.f);
-            w.z = bf16x2_to_f16x2(w.z, 1.f);
-            w.w = bf16x2_to_f16x2(w.w, 1.f);
-            *reinterpret_cast<uint4 *>(vv + (first + (b + m) * STRIDE) * 16) = w;
+            for (int m = 0; m < 8; ++m) {
+                uint4 w = x[m];
+                w.x = bf16x2_to_f16x2(w.x, sc[m]);
+                w.y = bf16x2_to_f16x2(w.y, sc[m]);
+                w.z = bf16x2_to_f16x2(w.z, sc[m]);
+                w.w = bf16x2_to_f16x2(w.w, sc[m]);
+                *reinterpret_cast<uint4 *>(ad[m]) = w;
+            }
         }
     }
 }
@@ -655,13 +654,15 @@ struct RoleState {
 // ------------------------------------------------------------------ chain CTA
 //
 // Warpgroup 0 runs the serial state path of every chunk k: record k, tiles k
-// converted and D_O buffer k & 1 free -> R1 -> Delta^T -> R2 -> state
-// refresh. Warpgroup 1 works beside it: gate tables two chunks ahead, the
-// fp16 conversion of chunk k + 1's tiles under chunk k's products, and, once
-// R2(k) is done, the release of stage / record slot k & 1, the loads of chunk
-// k + 2 and the O rows of chunk k from D_O[k & 1]. Every barrier phase has a
-// single producer and is consumed before it can be reused, so parities never
-// alias.
+// converted and O^T of chunk k - 1 read out -> R1 -> Delta^T -> R2 -> state
+// refresh. A dependent run of MMAs into one accumulator costs about the same
+// per instruction for N = 64 ... 192 on B200, so each round is one wide
+// product over the contiguous [D_S | O^T | D_U] accumulator: R1 (8 steps,
+// N = 128) and R2 (4 steps, N = 192). Warpgroup 1 works beside it: gate
+// tables two chunks ahead, the fp16 conversion of chunk k + 1's tiles under
+// chunk k's products, and, once R2(k) is done, the loads of chunk k + 2 into
+// stage k & 1 and the O rows of chunk k. Every barrier phase has a single
+// producer and is consumed before it can be reused, so parities never alias.
 __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k,
                                                 const CUtensorMap *tm_v, const GParams &p,
                                                 uint8_t *smem, const Walk &wk, int64_t start,
@@ -671,12 +672,12 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
     const uint32_t trow = tmem + (static_cast<uint32_t>(ww) << 21);  // lanes 32 ww .. 32 ww + 31
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C_OFF_BAR);
     uint64_t *bar_load = bars + CB_LOAD, *bar_full = bars + CB_FULL, *bar_r1 = bars + CB_R1,
-             *bar_r2s = bars + CB_R2S, *bar_r2 = bars + CB_R2, *bar_conv = bars + CB_CONV,
-             *bar_ofree = bars + CB_OFREE;
+             *bar_r2 = bars + CB_R2, *bar_conv = bars + CB_CONV, *bar_ofree = bars + CB_OFREE;
     const uint32_t sbase = smem_u32(smem);
     const int H = p.H;
     const int64_t tok_stride = static_cast<int64_t>(H) * HD;
     auto gates = [&](int kc) { return reinterpret_cast<float *>(smem + C_OFF_GATE) + (kc & 3) * G_SIZE; };
+    auto stage = [&](int kc) { return sbase + (kc & 1) * C_STAGE; };
     const int chain = static_cast<int>(start);
     int *consumed = p.consumed + chain;
     RoleState rs{false};
@@ -686,12 +687,25 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
         const int row = tid;  // state row i = TMEM lane
         int k = 0;
         bool u_pre = false;  // thread 0: the next R1's U part is already issued
-        auto issue_u = [&](uint32_t vbase, uint32_t rbase) {
+        // D_U = V^T (T diag b)^T (starts D_U; R1 accumulates onto it)
+        auto issue_u = [&](uint32_t st) {
 #pragma unroll 1
             for (int kk = 0; kk < 4; ++kk)
-                umma_f16(tmem + TM_U, sdesc_sw128(vbase + kk * 2048, 8192, 1024),
-                         sdesc_sw128(rbase + REC_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
+                umma_f16(tmem + TM_DU, sdesc_sw128(st + CS_V + kk * 2048, 8192, 1024),
+                         sdesc_sw128(st + CS_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
         };
+        // O^T starts at zero: R1 accumulates onto it (warpgroup 1 clears it
+        // again after reading each chunk's rows).
+        {
+            uint32_t z[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) z[e] = 0u;
+            tmem_st32u(trow + TM_OT, z);
+            tmem_st32u(trow + TM_OT + 32, z);
+            tmem_wait_st();
+            tc_fence_before();
+            wg_sync(1);
+        }
         for (int64_t item = start; item < wk.n_items && !rs.failed; item += wk.stride) {
             const int64_t seq = item / H;
             const int h = static_cast<int>(item - seq * H);
@@ -716,20 +730,15 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 continue;
             }
             for (int c = 0; c < nch; ++c, ++k) {
-                const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
-                (void)ts;
-                const uint32_t kq = sbase + C_OFF_KQ + (k & 1) * KQ_STAGE;
-                const uint32_t vb = sbase + C_OFF_V + (k & 1) * V_STAGE;
-                const uint32_t rec = sbase + C_OFF_REC + (k & 1) * REC_BYTES;
-                const uint32_t tO = tmem + TM_OT + 64 * (k & 1);
+                const uint32_t st = stage(k);
 
-                // ---- R1's inputs: record k (bulk-loaded from the ring by
+                // ---- R1's inputs: record k (bulk-copied from the ring by
                 // warpgroup 1; once it has landed the ring slot is free again),
-                // tiles k in fp16, D_O buffer k & 1 read out
+                // tiles k in fp16, O^T of chunk k - 1 read out and cleared
                 bool ok = mbar_wait(&bar_full[k & 1], (k >> 1) & 1, p.poll_ns);
                 if (ok && tid == 0) st_release_gpu(consumed, k + 1);
                 ok = ok && mbar_wait(&bar_conv[k & 1], (k >> 1) & 1);
-                if (k >= 2) ok = ok && mbar_wait(&bar_ofree[k & 1], ((k >> 1) + 1) & 1);
+                if (k >= 1) ok = ok && mbar_wait(&bar_ofree[(k - 1) & 1], ((k - 1) >> 1) & 1);
                 if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
 
                 // ---- first chunk of the item: fp16 image of S0 (unscaled) and
@@ -752,7 +761,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                             for (int e = 0; e < 16; ++e) w[16 * q2 + e] = pack_f16x2(v[2 * e], v[2 * e + 1]);
 #pragma unroll
                             for (int e = 0; e < 32; ++e) v[e] *= gC;
-                            tmem_st32(trow + TM_S + 64 * h2 + 32 * q2, v);
+                            tmem_st32(trow + TM_DS + 64 * h2 + 32 * q2, v);
                         }
                         tmem_st32u(trow + TM_S16 + 32 * h2, w);
                     }
@@ -761,22 +770,17 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     wg_sync(1);
                 }
 
-                // ---- R1: D_U = V^T (T diag b)^T + S (-W^T) ; O^T[k & 1] = S Q~^T,
-                // S read as the A operand from its fp16 image in TMEM
+                // ---- R1: [O^T | D_U] += S [Q~ | -W]^T (one N = 128 product,
+                // S read from its fp16 image in TMEM; D_U starts as the U part)
                 if (tid == 0) {
                     tc_fence_after();
-                    if (!u_pre) issue_u(vb, rec);
+                    if (!u_pre) issue_u(st);
 #pragma unroll 1
                     for (int kk = 0; kk < 8; ++kk)
-                        umma_f16_ta(tmem + TM_U, tmem + TM_S16 + 8 * kk,
-                                    sdesc_sw128(rec + REC_WT + kk * 2048, 8192, 1024), ID_KM64, 1);
-                    umma_commit(bar_r1);  // Delta^T is ready; O^T runs on behind it
-#pragma unroll 1
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                        umma_f16_ta(tO, tmem + TM_S16 + 8 * kk, sdesc_sw128(kq + off + 8192, 16, 1024),
-                                    ID_OT, kk > 0);
-                    }
+                        umma_f16_ta(tmem + TM_OT, tmem + TM_S16 + 8 * kk,
+                                    sdesc_sw128(st + CS_B1 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                                    ID_R1, 1);
+                    umma_commit(bar_r1);
                 }
                 // ---- D_S pre-scaled by this chunk's gamma_{C-1} while R1 runs
                 // (R1 does not touch D_S; R2, which accumulates into it, is
@@ -788,11 +792,11 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
 #pragma unroll 1
                     for (int q4 = 0; q4 < 4; ++q4) {
                         float v[32];
-                        tmem_ld32(trow + TM_S + 32 * q4, v);
+                        tmem_ld32(trow + TM_DS + 32 * q4, v);
                         tmem_wait_ld();
 #pragma unroll
                         for (int e = 0; e < 32; ++e) v[e] *= gC;
-                        tmem_st32(trow + TM_S + 32 * q4, v);
+                        tmem_st32(trow + TM_DS + 32 * q4, v);
                     }
                     tmem_wait_st();
                 }
@@ -803,8 +807,8 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 // ---- Delta^T (fp16) into its TMEM image: row i, all 64 positions
                 {
                     float x[32], y[32];
-                    tmem_ld32(trow + TM_U, x);
-                    tmem_ld32(trow + TM_U + 32, y);
+                    tmem_ld32(trow + TM_DU, x);
+                    tmem_ld32(trow + TM_DU + 32, y);
                     tmem_wait_ld();
                     uint32_t w[32];
 #pragma unroll
@@ -818,33 +822,26 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 tc_fence_before();
                 wg_sync(1);
 
-                // ---- R2: D_S += Delta^T K~ (the state refresh waits for this
-                // part only; it also covers O^T = S Q~^T, so S's image is free),
-                // then O^T[k & 1] += Delta^T M^T
+                // ---- R2: [D_S | O^T] += Delta^T [K~ | M^T] (one N = 192 product)
                 if (tid == 0) {
                     tc_fence_after();
 #pragma unroll 1
                     for (int kk = 0; kk < 4; ++kk)
-                        umma_f16_ta(tmem + TM_S, tmem + TM_D16 + 8 * kk,
-                                    sdesc_sw128(kq + kk * 2048, 16384, 1024), ID_KM128, 1);
-                    umma_commit(bar_r2s);
-#pragma unroll 1
-                    for (int kk = 0; kk < 4; ++kk)
-                        umma_f16_ta(tO, tmem + TM_D16 + 8 * kk, sdesc_sw128(rec + REC_M + kk * 32, 16, 1024),
-                                    ID_OT, 1);
+                        umma_f16_ta(tmem + TM_DS, tmem + TM_D16 + 8 * kk,
+                                    sdesc_sw128(st + CS_B2 + kk * 2048, 8192, 1024), ID_R2, 1);
                     umma_commit(bar_r2);
-                    // The next chunk's V^T (T diag b)^T part of D_U, off its
-                    // critical path, when its record and tiles are already in
-                    // (D_U was read out before this round was issued).
+                    // The next chunk's U part of D_U, off its critical path,
+                    // when its record and tiles are already in (D_U was read
+                    // out before this round was issued).
                     u_pre = false;
                     const int kn = k + 1;
                     if (c + 1 < nch && mbar_try_wait(&bar_full[kn & 1], (kn >> 1) & 1) &&
                         mbar_try_wait(&bar_conv[kn & 1], (kn >> 1) & 1)) {
-                        issue_u(sbase + C_OFF_V + (kn & 1) * V_STAGE, sbase + C_OFF_REC + (kn & 1) * REC_BYTES);
+                        issue_u(stage(kn));
                         u_pre = true;
                     }
                 }
-                ok = mbar_wait(bar_r2s, k & 1);
+                ok = mbar_wait(bar_r2, k & 1);
                 if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
                 tc_fence_after();
 
@@ -854,8 +851,8 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
 #pragma unroll 1
                     for (int h2 = 0; h2 < 2; ++h2) {
                         float v[32], x[32];
-                        tmem_ld32(trow + TM_S + 64 * h2, v);
-                        tmem_ld32(trow + TM_S + 64 * h2 + 32, x);
+                        tmem_ld32(trow + TM_DS + 64 * h2, v);
+                        tmem_ld32(trow + TM_DS + 64 * h2 + 32, x);
                         tmem_wait_ld();
                         uint32_t w[32];
 #pragma unroll
@@ -870,7 +867,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
 #pragma unroll 1
                     for (int q4 = 0; q4 < 4; ++q4) {
                         float v[32];
-                        tmem_ld32(trow + TM_S + 32 * q4, v);
+                        tmem_ld32(trow + TM_DS + 32 * q4, v);
                         tmem_wait_ld();
 #pragma unroll
                         for (int e = 0; e < 32; e += 4)
@@ -883,8 +880,8 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
             }
         }
         if (rs.failed && tid == 0) {
-            // Every MMA this thread issued (including D_O products that no
-            // commit covered yet) completes before TMEM is released.
+            // Every MMA this thread issued (including a pre-issued U part that
+            // no commit covered yet) completes before TMEM is released.
             umma_commit(bars + CB_DRAIN);
             mbar_wait(bars + CB_DRAIN, 0, 200000000ull);
         }
@@ -893,38 +890,39 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
         const int wt = tid - 128;
         int loads_issued = 0, loads_waited = 0, recs_issued = 0;
         // Round kc's record: wait until a producer has published it in ring
-        // slot kc % RING, then bulk-load it into record slot kc & 1.
+        // slot kc % RING, then bulk-copy its pieces next to stage kc & 1's tiles.
         auto fetch_record = [&](int kc) -> bool {
             const int slot = kc % RING;
             const int target = p.never_ready ? kc + 1 + (1 << 30) : kc + 1;
             if (!poll_ge(p.ready + chain * RING + slot, target, p.abort_flag, p.poll_ns)) return false;
             fence_proxy_async_global();
             uint64_t *bar = &bar_full[kc & 1];
+            uint8_t *stp = smem + (kc & 1) * C_STAGE;
+            const uint8_t *rec = p.ring + (static_cast<size_t>(chain) * RING + slot) * REC_BYTES;
             mbar_arrive_expect_tx(bar, REC_BYTES);
-            bulk_load_g2s(smem + C_OFF_REC + (kc & 1) * REC_BYTES,
-                          p.ring + (static_cast<size_t>(chain) * RING + slot) * REC_BYTES, REC_BYTES, bar);
+            bulk_load_g2s(stp + CS_B1 + 8192, rec + REC_W, 8192, bar);
+            bulk_load_g2s(stp + CS_B1 + 16384 + 8192, rec + REC_W + 8192, 8192, bar);
+            bulk_load_g2s(stp + CS_B2 + 16384, rec + REC_MT, 8192, bar);
+            bulk_load_g2s(stp + CS_TT, rec + REC_TT, 8192, bar);
             ++recs_issued;
             return true;
         };
         GateIn gin{1.f, 1.f, 0.f, 0.f};  // warp 4: inputs of the gate table two chunks ahead
         auto issue_loads = [&](int kc, const Ref &r) {
-            const uint32_t st = kc & 1;
-            uint64_t *bar = &bar_load[st];
-            uint8_t *kqs = smem + C_OFF_KQ + st * KQ_STAGE;
-            uint8_t *vv = smem + C_OFF_V + st * V_STAGE;
+            uint64_t *bar = &bar_load[kc & 1];
+            uint8_t *stp = smem + (kc & 1) * C_STAGE;
             mbar_arrive_expect_tx(bar, KQV_BYTES);
             const int t32 = static_cast<int>(r.ts);
-            tma_load_3d(kqs, tm_k, 0, r.h, t32, bar);
-            tma_load_3d(kqs + 16384, tm_k, 64, r.h, t32, bar);
-            tma_load_3d(kqs + 8192, tm_q, 0, r.h, t32, bar);
-            tma_load_3d(kqs + 24576, tm_q, 64, r.h, t32, bar);
-            tma_load_3d(vv, tm_v, 0, r.h, t32, bar);
-            tma_load_3d(vv + 8192, tm_v, 64, r.h, t32, bar);
+            tma_load_3d(stp + CS_B1, tm_q, 0, r.h, t32, bar);
+            tma_load_3d(stp + CS_B1 + 16384, tm_q, 64, r.h, t32, bar);
+            tma_load_3d(stp + CS_B2, tm_k, 0, r.h, t32, bar);
+            tma_load_3d(stp + CS_B2 + 8192, tm_k, 64, r.h, t32, bar);
+            tma_load_3d(stp + CS_V, tm_v, 0, r.h, t32, bar);
+            tma_load_3d(stp + CS_V + 8192, tm_v, 64, r.h, t32, bar);
         };
         auto convert = [&](int kc) {
             const float *g = gates(kc);
-            chain_tiles_to_f16<128>(smem + C_OFF_KQ + (kc & 1) * KQ_STAGE,
-                                    smem + C_OFF_V + (kc & 1) * V_STAGE, g + G_GM, g + G_PL, wt);
+            chain_tiles_to_f16<128>(smem + (kc & 1) * C_STAGE, g + G_GM, g + G_PL, wt);
             fence_proxy_async_smem();
         };
 
@@ -993,8 +991,8 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     if (wg_sync_or(2, !ok)) { rs.failed = true; break; }
                     tc_fence_after();
                 }
-                // Stage and record slot k & 1 are free again: chunk k + 2's
-                // tiles, and its record once a producer has published it.
+                // Stage k & 1 is free again: chunk k + 2's tiles, and its
+                // record once a producer has published it.
                 bool fok = true;
                 if (wt == 0 && nn.item >= 0) {
                     issue_loads(k + 2, nn);
@@ -1003,13 +1001,13 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 if (nn.item >= 0) ++loads_issued;
                 if (wg_sync_or(2, !fok)) { rs.failed = true; break; }
 
-                // ---- O rows of chunk k from O^T[k & 1] (lane i, column t),
-                // optionally RMS-normalised per head first (groupnorm_heads,
-                // norm.rs:48-60, on the fp32 accumulator): each thread turns its
-                // column i into bf16 in a [t][i] staging tile, then the rows go
-                // out as 16-byte stores.
+                // ---- O rows of chunk k from O^T (lane i, column t), optionally
+                // RMS-normalised per head first (groupnorm_heads, norm.rs:48-60,
+                // on the fp32 accumulator): each thread turns its column i into
+                // bf16 in a [t][i] staging tile and clears O^T for the next
+                // chunk, then the rows go out as 16-byte stores.
                 {
-                    const uint32_t tOT = trow + TM_OT + 64 * (k & 1);
+                    const uint32_t tOT = trow + TM_OT;
                     float *npart = reinterpret_cast<float *>(smem + C_OFF_NPART);
                     float *ninv = npart + 4 * 64;
                     if (norm) {
@@ -1064,6 +1062,14 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                             stg[t * HD + wt] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
                         }
                     }
+                    {
+                        uint32_t z[32];
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) z[e] = 0u;
+                        tmem_st32u(tOT, z);
+                        tmem_st32u(tOT + 32, z);
+                        tmem_wait_st();
+                    }
                     tc_fence_before();
                     mbar_arrive(&bar_ofree[k & 1]);
                     wg_sync(2);
@@ -1079,9 +1085,8 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
             }
         }
         if (rs.failed && wt == 0) {
-            // Tile loads and record loads still in flight land before the
-            // shared memory goes away (record k was waited for by warpgroup 0
-            // only if it got that far: wait for every issued record phase).
+            // Tile loads and record copies still in flight land before the
+            // shared memory goes away.
             for (int kk = loads_waited; kk < loads_issued; ++kk)
                 mbar_wait(&bar_load[kk & 1], (kk >> 1) & 1, 200000000ull);
             for (int kk = (recs_issued > 2 ? recs_issued - 2 : 0); kk < recs_issued; ++kk)
@@ -1118,6 +1123,7 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
     float *Tf = reinterpret_cast<float *>(smem + P_OFF_TF);
     float *Xf = reinterpret_cast<float *>(smem + P_OFF_X);
     uint8_t *th = smem + P_OFF_AF;  // T diag(beta gamma) hi, lo: the A table is dead by then
+    uint8_t *pst = smem + P_OFF_TF; // record pieces staged in the T table's space while it is dead
     const uint32_t sbase = smem_u32(smem);
     auto csync = [&]() { nbar_sync(bar_id, 256); };
     auto csync_or = [&](bool x) { return nbar_sync_or(bar_id, 256, x); };
@@ -1214,7 +1220,8 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             const int s0 = 32 * half;
             // Warp-uniform: the whole 32 x 32 block lies above the diagonal.
             if (half == 1 && (warp & 1) == 0) {
-                if (qk) st_zero32(rec + REC_M, t, 4);
+                if (qk)
+                    for (int s = 32; s < 64; ++s) st_sw_f16(pst, s, t, 0.f);
             } else {
                 const float glt = g[G_GL + t];
                 const int zt = gz[t];
@@ -1240,7 +1247,8 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                         }
                     }
                     if (qk) {
-                        st_row16_f16(rec + REC_M, t, 4 * half + 2 * hp, v);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) st_sw_f16(pst, sb + j, t, v[j]);  // M^T[s][t]
                     } else {
 #pragma unroll
                         for (int j4 = 0; j4 < 4; ++j4)
@@ -1251,6 +1259,10 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             }
         }
         tc_fence_before();
+        csync();
+        // M^T into the record; the T table's space is free again afterwards
+        for (int i = lt; i < 8192 / 16; i += 256)
+            reinterpret_cast<uint4 *>(rec + REC_MT)[i] = reinterpret_cast<const uint4 *>(pst)[i];
         csync();
 
         // ---- diagonal 16 x 16 tiles of T (warps 0-3, one each) while warps
@@ -1340,14 +1352,19 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             tc_fence_after();
         }
         {
+            // -W K-major [j half][t][64 j], staged (the T table is dead), then
+            // copied into the record with 16-byte stores
             float x[32];
             tmem_ld32(trow + TM_W + 32 * half, x);
             tmem_wait_ld();
+            uint8_t *blk = pst + (row >> 6) * 8192;
 #pragma unroll
-            for (int t = 0; t < 32; ++t) x[t] = -x[t];
-            st_row32_f16(rec + REC_WT, row, 4 * half, x);
+            for (int t = 0; t < 32; ++t) st_sw_f16(blk, 32 * half + t, row & 63, -x[t]);
         }
         tc_fence_before();
+        csync();
+        for (int i = lt; i < 16384 / 16; i += 256)
+            reinterpret_cast<uint4 *>(rec + REC_W)[i] = reinterpret_cast<const uint4 *>(pst)[i];
         csync();
         // ---- record complete: publish it; stage k & 1 is free (D1 and D_W
         // are done), so chunk k + 2's loads go out in the next phase
