@@ -116,11 +116,11 @@ constexpr uint32_t C_OFF_BAR = C_OFF_GATE + 4 * G_BYTES;
 // Chain barriers: tiles landed [2], record landed [2] (bulk copies from the
 // ring), D_U done (R1), all of a chunk's products done (R2), tiles converted
 // [2] (warpgroup 1 -> 0), O^T read out and cleared [2] (1 -> 0, by chunk
-// parity), the U part of D_U done [2] (issued by warpgroup 1), and two
-// barriers that only the failure path uses to wait for every MMA issued.
+// parity), and a barrier that only the failure path uses to wait for every
+// MMA issued.
 constexpr int CB_LOAD = 0, CB_FULL = 2, CB_R1 = 4, CB_R2 = 6, CB_CONV = 7, CB_OFREE = 9,
-              CB_DRAIN = 11, CB_U = 12, CB_DRAIN2 = 14, CB_NUM = 15;
-constexpr uint32_t C_OFF_NORM = C_OFF_BAR + 256;  // output-norm scale, HD floats
+              CB_DRAIN = 11, CB_NUM = 12;
+constexpr uint32_t C_OFF_NORM = C_OFF_BAR + 128;  // output-norm scale, HD floats
 constexpr uint32_t C_USED = C_OFF_NORM + HD * 4;
 static_assert(C_OFF_NORM >= C_OFF_BAR + CB_NUM * 8 + 16, "chain barriers overlap the norm scale");
 static_assert(C_STAGE % 1024 == 0 && CS_TT + 8192 <= C_STAGE, "chain stage map");
@@ -149,14 +149,11 @@ static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in shared memory");
 
 // TMEM columns (32-bit). Chain: one contiguous accumulator [D_S 128 | O^T 64 |
 // D_U 64] (lane i; O^T column t, D_U = Delta^T column s), so that R1 writes
-// [O^T | D_U] and R2 writes [D_S | O^T] as single wide products; a second
-// pair [O^T | D_U] that takes R1's odd K steps (two independent
-// accumulators interleave, a dependent run does not), summed on read; and the
+// [O^T | D_U] and R2 writes [D_S | O^T] as single wide products, and the
 // fp16 images of S (128 x 128 -> 64 columns) and Delta^T (128 x 64 -> 32
 // columns) that the products read as their A operand straight from tensor
 // memory. Producer: D1 (128 x 64) and D_W (128 x 64) per context.
-constexpr uint32_t TM_DS = 0, TM_OT = 128, TM_DU = 192, TM_OTB = 256, TM_DUB = 320, TM_S16 = 384,
-                   TM_D16 = 448, C_TM_COLS = 512;
+constexpr uint32_t TM_DS = 0, TM_OT = 128, TM_DU = 192, TM_S16 = 256, TM_D16 = 320, C_TM_COLS = 512;
 constexpr uint32_t TM_D1 = 0, TM_W = 64, P_TM_CTX = 128, P_TM_COLS = PCTX * P_TM_CTX;
 
 constexpr uint32_t ID_D1 = idesc_bf16(128, 64, false, false);
@@ -675,8 +672,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
     const uint32_t trow = tmem + (static_cast<uint32_t>(ww) << 21);  // lanes 32 ww .. 32 ww + 31
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C_OFF_BAR);
     uint64_t *bar_load = bars + CB_LOAD, *bar_full = bars + CB_FULL, *bar_r1 = bars + CB_R1,
-             *bar_r2 = bars + CB_R2, *bar_conv = bars + CB_CONV, *bar_ofree = bars + CB_OFREE,
-             *bar_u = bars + CB_U;
+             *bar_r2 = bars + CB_R2, *bar_conv = bars + CB_CONV, *bar_ofree = bars + CB_OFREE;
     const uint32_t sbase = smem_u32(smem);
     const int H = p.H;
     const int64_t tok_stride = static_cast<int64_t>(H) * HD;
@@ -690,6 +686,14 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
         // ------------------------------------------------ warpgroup 0: state path
         const int row = tid;  // state row i = TMEM lane
         int k = 0;
+        bool u_pre = false;  // thread 0: the next R1's U part is already issued
+        // D_U = V^T (T diag b)^T (starts D_U; R1 accumulates onto it)
+        auto issue_u = [&](uint32_t st) {
+#pragma unroll 1
+            for (int kk = 0; kk < 4; ++kk)
+                umma_f16(tmem + TM_DU, sdesc_sw128(st + CS_V + kk * 2048, 8192, 1024),
+                         sdesc_sw128(st + CS_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
+        };
         // O^T starts at zero: R1 accumulates onto it (warpgroup 1 clears it
         // again after reading each chunk's rows).
         {
@@ -734,7 +738,6 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 bool ok = mbar_wait(&bar_full[k & 1], (k >> 1) & 1, p.poll_ns);
                 if (ok && tid == 0) st_release_gpu(consumed, k + 1);
                 ok = ok && mbar_wait(&bar_conv[k & 1], (k >> 1) & 1);
-                ok = ok && mbar_wait(&bar_u[k & 1], (k >> 1) & 1);
                 if (k >= 1) ok = ok && mbar_wait(&bar_ofree[(k - 1) & 1], ((k - 1) >> 1) & 1);
                 if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
 
@@ -767,17 +770,16 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     wg_sync(1);
                 }
 
-                // ---- R1: [O^T | D_U] += S [Q~ | -W]^T, one N = 128 product (S
-                // read from its fp16 image in TMEM; D_U starts as the U part
-                // that warpgroup 1 issued), its odd K steps into the second
-                // pair so that the two runs interleave
+                // ---- R1: [O^T | D_U] += S [Q~ | -W]^T (one N = 128 product,
+                // S read from its fp16 image in TMEM; D_U starts as the U part)
                 if (tid == 0) {
                     tc_fence_after();
+                    if (!u_pre) issue_u(st);
 #pragma unroll 1
                     for (int kk = 0; kk < 8; ++kk)
-                        umma_f16_ta(tmem + ((kk & 1) ? TM_OTB : TM_OT), tmem + TM_S16 + 8 * kk,
+                        umma_f16_ta(tmem + TM_OT, tmem + TM_S16 + 8 * kk,
                                     sdesc_sw128(st + CS_B1 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                                    ID_R1, (kk & 1) ? (kk > 1) : 1);
+                                    ID_R1, 1);
                     umma_commit(bar_r1);
                 }
                 // ---- D_S pre-scaled by this chunk's gamma_{C-1} while R1 runs
@@ -802,19 +804,17 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
                 tc_fence_after();
 
-                // ---- Delta^T = D_U + D_U' (fp16) into its TMEM image: row i,
-                // all 64 positions
+                // ---- Delta^T (fp16) into its TMEM image: row i, all 64 positions
                 {
+                    float x[32], y[32];
+                    tmem_ld32(trow + TM_DU, x);
+                    tmem_ld32(trow + TM_DU + 32, y);
+                    tmem_wait_ld();
                     uint32_t w[32];
 #pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {
-                        float x[32], y[32];
-                        tmem_ld32(trow + TM_DU + 32 * hf, x);
-                        tmem_ld32(trow + TM_DUB + 32 * hf, y);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int e = 0; e < 16; ++e)
-                            w[16 * hf + e] = pack_f16x2(x[2 * e] + y[2 * e], x[2 * e + 1] + y[2 * e + 1]);
+                    for (int e = 0; e < 16; ++e) {
+                        w[e] = pack_f16x2(x[2 * e], x[2 * e + 1]);
+                        w[16 + e] = pack_f16x2(y[2 * e], y[2 * e + 1]);
                     }
                     tmem_st32u(trow + TM_D16, w);
                     tmem_wait_st();
@@ -830,6 +830,16 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                         umma_f16_ta(tmem + TM_DS, tmem + TM_D16 + 8 * kk,
                                     sdesc_sw128(st + CS_B2 + kk * 2048, 8192, 1024), ID_R2, 1);
                     umma_commit(bar_r2);
+                    // The next chunk's U part of D_U, off its critical path,
+                    // when its record and tiles are already in (D_U was read
+                    // out before this round was issued).
+                    u_pre = false;
+                    const int kn = k + 1;
+                    if (c + 1 < nch && mbar_try_wait(&bar_full[kn & 1], (kn >> 1) & 1) &&
+                        mbar_try_wait(&bar_conv[kn & 1], (kn >> 1) & 1)) {
+                        issue_u(stage(kn));
+                        u_pre = true;
+                    }
                 }
                 ok = mbar_wait(bar_r2, k & 1);
                 if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
@@ -870,7 +880,8 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
             }
         }
         if (rs.failed && tid == 0) {
-            // Every MMA this thread issued completes before TMEM is released.
+            // Every MMA this thread issued (including a pre-issued U part that
+            // no commit covered yet) completes before TMEM is released.
             umma_commit(bars + CB_DRAIN);
             mbar_wait(bars + CB_DRAIN, 0, 200000000ull);
         }
@@ -914,23 +925,6 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
             chain_tiles_to_f16<128>(smem + (kc & 1) * C_STAGE, g + G_GM, g + G_PL, wt);
             fence_proxy_async_smem();
         };
-        // Thread 0 of this warpgroup: D_U = V^T (T diag b)^T for chunk kc (R1
-        // accumulates onto it), once its record has landed; D_U is free (the
-        // previous chunk's Delta^T was read before its R2 was issued, and R2
-        // is done). Its tiles were converted by this warpgroup.
-        bool u_issued = false;
-        auto issue_u = [&](int kc) -> bool {
-            if (!mbar_wait(&bar_full[kc & 1], (kc >> 1) & 1, p.poll_ns)) return false;
-            tc_fence_after();
-            const uint32_t st = stage(kc);
-#pragma unroll 1
-            for (int kk = 0; kk < 4; ++kk)
-                umma_f16(tmem + TM_DU, sdesc_sw128(st + CS_V + kk * 2048, 8192, 1024),
-                         sdesc_sw128(st + CS_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
-            umma_commit(&bar_u[kc & 1]);
-            u_issued = true;
-            return true;
-        };
 
         float *nsc = reinterpret_cast<float *>(smem + C_OFF_NORM);
         const bool norm = p.norm_scale != nullptr;
@@ -961,8 +955,6 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     ++loads_waited;
                     convert(0);
                     mbar_arrive(&bar_conv[0]);
-                    const bool uok = wt != 0 || issue_u(0);
-                    if (wg_sync_or(2, !uok)) rs.failed = true;
                 }
             }
         }
@@ -999,12 +991,10 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     if (wg_sync_or(2, !ok)) { rs.failed = true; break; }
                     tc_fence_after();
                 }
-                // The next chunk's U part (off warpgroup 0's path). Stage k & 1
-                // is free again: chunk k + 2's tiles, and its record once a
-                // producer has published it.
+                // Stage k & 1 is free again: chunk k + 2's tiles, and its
+                // record once a producer has published it.
                 bool fok = true;
-                if (wt == 0 && nxt.item >= 0) fok = issue_u(k + 1);
-                if (wt == 0 && fok && nn.item >= 0) {
+                if (wt == 0 && nn.item >= 0) {
                     issue_loads(k + 2, nn);
                     fok = fetch_record(k + 2);
                 }
@@ -1017,7 +1007,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 // bf16 in a [t][i] staging tile and clears O^T for the next
                 // chunk, then the rows go out as 16-byte stores.
                 {
-                    const uint32_t tOT = trow + TM_OT, tOTB = trow + TM_OTB;
+                    const uint32_t tOT = trow + TM_OT;
                     float *npart = reinterpret_cast<float *>(smem + C_OFF_NPART);
                     float *ninv = npart + 4 * 64;
                     if (norm) {
@@ -1026,17 +1016,10 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                         // t = 2l, 2l + 1), then the four warps through shared memory
                         float r[32];
                         {
-                            float x[32], y[32], xb[32];
+                            float x[32], y[32];
                             tmem_ld32(tOT, x);
-                            tmem_ld32(tOTB, xb);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int j = 0; j < 32; ++j) x[j] += xb[j];
                             tmem_ld32(tOT + 32, y);
-                            tmem_ld32(tOTB + 32, xb);
                             tmem_wait_ld();
-#pragma unroll
-                            for (int j = 0; j < 32; ++j) y[j] += xb[j];
                             const bool up = lane & 16;
 #pragma unroll
                             for (int j = 0; j < 32; ++j) {
@@ -1069,13 +1052,11 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     const float sc = norm ? nsc[wt] : 1.f;
 #pragma unroll 1
                     for (int hf = 0; hf < 2; ++hf) {
-                        float x[32], xb[32];
+                        float x[32];
                         tmem_ld32(tOT + 32 * hf, x);
-                        tmem_ld32(tOTB + 32 * hf, xb);
                         tmem_wait_ld();
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
-                            x[j] += xb[j];
                             const int t = 32 * hf + j;
                             const float v = norm ? x[j] * ninv[t] * sc : x[j];
                             stg[t * HD + wt] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
@@ -1102,11 +1083,6 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     }
                 }
             }
-        }
-        if (rs.failed && wt == 0 && u_issued) {
-            // the U products this thread issued complete before TMEM goes away
-            umma_commit(bars + CB_DRAIN2);
-            mbar_wait(bars + CB_DRAIN2, 0, 200000000ull);
         }
         if (rs.failed && wt == 0) {
             // Tile loads and record copies still in flight land before the
