@@ -322,7 +322,7 @@ size_t rhz_gdr_bwd_workspace_bytes(int64_t B, int64_t T, int32_t H, int32_t d);
  * rhz_gdr_workspace_bytes -- scratch needed by rhz_gdr_sequential /
  * rhz_gdr_scan_chunked for B x T positions of H heads of width d in
  * `dtype`, with or without a segment array: the tensor-core kernel's
- * record rings and schedule (bf16, d == 128: about 17 MB) plus, with
+ * record rings and schedule (bf16, d == 128: about 34 MB) plus, with
  * segments, the segment-boundary tables. 0 when nothing is needed.
  */
 size_t rhz_gdr_workspace_bytes(int64_t B, int64_t T, int32_t H, int32_t d, int32_t dtype,

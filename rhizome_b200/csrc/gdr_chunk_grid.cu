@@ -163,7 +163,7 @@ constexpr uint32_t ID_R1 = idesc_f16(128, 128, false, false);  // S [Q~ | -W]^T:
 constexpr uint32_t ID_R2 = idesc_f16(128, 192, false, true);   // Delta^T [K~ | M^T]: B MN-major
 
 // Record ring: RING slots of REC_BYTES per chain; flags in the workspace.
-constexpr int RING = 4;
+constexpr int RING = 8;
 constexpr int MAX_CHAINS = 128;
 
 struct GParams {

@@ -169,7 +169,7 @@ def test_sequential_validation(lib):
     assert ws_seg >= (4 * 4096 + 1) * 4 * 2
     assert lib.rhz_gdr_workspace_bytes(4, 4096, 16, 32, capi.RHZ_DTYPE_F32, 0) == 0
     ws_tc = lib.rhz_gdr_workspace_bytes(4, 4096, 16, 128, capi.RHZ_DTYPE_BF16, 0)
-    assert ws_tc >= 128 * 4 * 32768  # 128 chains x 4 ring slots x 32 KB records
+    assert ws_tc >= 128 * 8 * 32768  # 128 chains x 8 ring slots x 32 KB records
     assert lib.rhz_gdr_workspace_bytes(4, 4096, 16, 128, capi.RHZ_DTYPE_BF16, 1) > ws_tc + ws_seg // 2
     assert lib.rhz_gdr_workspace_bytes(-1, 4, 1, 4, 0, 0) == 0
     # the bf16 d=128 path refuses a missing workspace before any device work
@@ -192,7 +192,7 @@ def test_varlen_validation(lib):
     assert f(*too_many) == capi.RHZ_ERR_SHAPE
     assert lib.rhz_gdr_varlen_workspace_bytes(2, 2, 32, 0) == 0
     need = lib.rhz_gdr_varlen_workspace_bytes(2, 2, 128, 1)
-    assert need >= 128 * 4 * 32768 + 4 * 4  # rings + one round offset per item
+    assert need >= 128 * 8 * 32768 + 4 * 4  # rings + one round offset per item
     short = list(base)
     short[13], short[14], short[16], short[17] = 128, 1, FAKE, need - 256
     assert f(*short) == capi.RHZ_ERR_INVALID and b"workspace too small" in lib.rhz_last_error()
