@@ -61,12 +61,6 @@ def algorithmic_bytes(b, t, h, d, with_state_in=False):
     return tok_heads * per + states
 
 
-def solo_form(items, sms):
-    """The library's choice between its two chunked forms (launch_chunk_tc)."""
-    pairs = max(sms // 2, 1)
-    return 10 * -(-items // pairs) > 16 * -(-items // sms)
-
-
 def decode_bytes(n, h, d):
     # state read + write (f32), q/k/v in, o out (bf16), alpha/beta
     return n * h * (2 * d * d * 4 + 3 * d * 2 + 8 + d * 2)
@@ -332,7 +326,7 @@ def run_ours(args):
                 "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
                 "traffic": args.traffic if args.traffic else NCU_TRAFFIC_BYTES,
                 "peaks": f"of {peaks_kind}",
-                "kernel": "gdr_chunk_tc_kernel", "kernel_ms": round(kernel_ms, 4),
+                "kernel": "gdr_chunk_grid_kernel", "kernel_ms": round(kernel_ms, 4),
                 "algorithmic_bytes": abytes, "algorithmic_flops": aflops,
                 "tensor": {"achieved": round(tflops, 1), "peak": peaks["bf16_tflops"],
                            "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4)}}
@@ -505,13 +499,12 @@ def run_ours(args):
     vflops = FLOP_PER_TOKEN_HEAD * vtok * H
     vgbs = vbytes / (vl_ms / 1e3) / 1e9
     vtf = vflops / (vl_ms / 1e3) / 1e12
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
     varlen_line = {
         "metric": "GDR varlen prefill tokens/s", "value": vtok * world / (vl_ms / 1e3),
         "unit": "tokens/s", "ms_per_step": round(vl_ms, 4),
         "config": {"sequences": VL_N, "tokens": vtok, "lengths": "U{1..8192}, seeded",
                    "heads": H, "head_dim": D, "slots": VL_SLOTS,
-                   "kernel_form": "one CTA per item" if solo_form(VL_N * H, sms) else "2-CTA cluster"},
+                   "kernel_form": "grid (chain and producer CTAs)"},
         "roofline": {"bound": "hbm", "achieved": round(vgbs, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(vgbs / peaks["hbm_gbs"], 4),
                      "algorithmic_bytes": vbytes, "algorithmic_flops": vflops,
@@ -787,8 +780,8 @@ def run_case(args):
         def fn():
             capi.call("rhz_groupnorm_heads", x.data_ptr(), x.data_ptr(), scale.data_ptr(),
                       4 * B * T, H, D, 1e-6, capi.RHZ_DTYPE_BF16, sptr)
-    elif args.case in ("pair", "solo"):  # the two forms of the chunked kernel
-        Bc, Tc, Hc = (4, 4096, 16) if args.case == "pair" else (8, 1024, 64)
+    elif args.case in ("grid", "pair", "solo"):  # the forms of the chunked kernel
+        Bc, Tc, Hc = (8, 1024, 64) if args.case == "solo" else (4, 4096, 16)
         q, k, v, a, b = qkv(Bc, Tc, Hc, D)
         ops.set_chunk_kernel(args.case)
 
@@ -824,7 +817,7 @@ def main():
     ap.add_argument("--slab", type=int, default=0,
                     help="--workload layer: overlap the all-gather with compute in slabs of this "
                          "many positions (a multiple of 64; 0 = one call, then one all-gather)")
-    ap.add_argument("--case", default=None, choices=["decode", "gather", "pack", "norm", "pair", "solo"],
+    ap.add_argument("--case", default=None, choices=["decode", "gather", "pack", "norm", "grid", "pair", "solo"],
                     help="launch one kernel at a profiling size instead of the benchmark")
     ap.add_argument("--traffic", type=float, default=None,
                     help="measured DRAM bytes per launch of the dominant kernel (ncu)")
