@@ -116,10 +116,10 @@ constexpr uint32_t C_OFF_BAR = C_OFF_GATE + 4 * G_BYTES;
 // Chain barriers: tiles landed [2], record landed [2] (bulk copies from the
 // ring), D_U done (R1), all of a chunk's products done (R2), tiles converted
 // [2] (warpgroup 1 -> 0), O^T read out and cleared [2] (1 -> 0, by chunk
-// parity), and a barrier that only the failure path uses to wait for every
-// MMA issued.
+// parity), a barrier that only the failure path uses to wait for every MMA
+// issued, and the state and Delta^T images ready (warpgroup 0 -> MMA warp).
 constexpr int CB_LOAD = 0, CB_FULL = 2, CB_R1 = 4, CB_R2 = 6, CB_CONV = 7, CB_OFREE = 9,
-              CB_DRAIN = 11, CB_NUM = 12;
+              CB_DRAIN = 11, CB_S16 = 12, CB_D16 = 13, CB_NUM = 14;
 constexpr uint32_t C_OFF_NORM = C_OFF_BAR + 128;  // output-norm scale, HD floats
 constexpr uint32_t C_USED = C_OFF_NORM + HD * 4;
 static_assert(C_OFF_NORM >= C_OFF_BAR + CB_NUM * 8 + 16, "chain barriers overlap the norm scale");
@@ -672,7 +672,8 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
     const uint32_t trow = tmem + (static_cast<uint32_t>(ww) << 21);  // lanes 32 ww .. 32 ww + 31
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C_OFF_BAR);
     uint64_t *bar_load = bars + CB_LOAD, *bar_full = bars + CB_FULL, *bar_r1 = bars + CB_R1,
-             *bar_r2 = bars + CB_R2, *bar_conv = bars + CB_CONV, *bar_ofree = bars + CB_OFREE;
+             *bar_r2 = bars + CB_R2, *bar_conv = bars + CB_CONV, *bar_ofree = bars + CB_OFREE,
+             *bar_s16 = bars + CB_S16, *bar_d16 = bars + CB_D16;
     const uint32_t sbase = smem_u32(smem);
     const int H = p.H;
     const int64_t tok_stride = static_cast<int64_t>(H) * HD;
@@ -684,18 +685,13 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
 
     if (tid < 128) {
         // ------------------------------------------------ warpgroup 0: state path
+        // Moves the state and Delta^T between their fp32 accumulators and the
+        // fp16 images the products read; the MMA warp issues the products.
         const int row = tid;  // state row i = TMEM lane
         int k = 0;
-        bool u_pre = false;  // thread 0: the next R1's U part is already issued
-        // D_U = V^T (T diag b)^T (starts D_U; R1 accumulates onto it)
-        auto issue_u = [&](uint32_t st) {
-#pragma unroll 1
-            for (int kk = 0; kk < 4; ++kk)
-                umma_f16(tmem + TM_DU, sdesc_sw128(st + CS_V + kk * 2048, 8192, 1024),
-                         sdesc_sw128(st + CS_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
-        };
         // O^T starts at zero: R1 accumulates onto it (warpgroup 1 clears it
-        // again after reading each chunk's rows).
+        // again after reading each chunk's rows); ordered before the first
+        // R1 by the first state-image arrival.
         {
             uint32_t z[32];
 #pragma unroll
@@ -703,8 +699,6 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
             tmem_st32u(trow + TM_OT, z);
             tmem_st32u(trow + TM_OT + 32, z);
             tmem_wait_st();
-            tc_fence_before();
-            wg_sync(1);
         }
         for (int64_t item = start; item < wk.n_items && !rs.failed; item += wk.stride) {
             const int64_t seq = item / H;
@@ -730,19 +724,8 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 continue;
             }
             for (int c = 0; c < nch; ++c, ++k) {
-                const uint32_t st = stage(k);
-
-                // ---- R1's inputs: record k (bulk-copied from the ring by
-                // warpgroup 1; once it has landed the ring slot is free again),
-                // tiles k in fp16, O^T of chunk k - 1 read out and cleared
-                bool ok = mbar_wait(&bar_full[k & 1], (k >> 1) & 1, p.poll_ns);
-                if (ok && tid == 0) st_release_gpu(consumed, k + 1);
-                ok = ok && mbar_wait(&bar_conv[k & 1], (k >> 1) & 1);
-                if (k >= 1) ok = ok && mbar_wait(&bar_ofree[(k - 1) & 1], ((k - 1) >> 1) & 1);
-                if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
-
                 // ---- first chunk of the item: fp16 image of S0 (unscaled) and
-                // D_S = gamma_{C-1} S0
+                // D_S = gamma_{C-1} S0 (the previous item's products are done)
                 if (c == 0) {
                     const float gC = gates(k)[G_GM + 63];
 #pragma unroll 1
@@ -767,26 +750,11 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     }
                     tmem_wait_st();
                     tc_fence_before();
-                    wg_sync(1);
-                }
-
-                // ---- R1: [O^T | D_U] += S [Q~ | -W]^T (one N = 128 product,
-                // S read from its fp16 image in TMEM; D_U starts as the U part)
-                if (tid == 0) {
-                    tc_fence_after();
-                    if (!u_pre) issue_u(st);
-#pragma unroll 1
-                    for (int kk = 0; kk < 8; ++kk)
-                        umma_f16_ta(tmem + TM_OT, tmem + TM_S16 + 8 * kk,
-                                    sdesc_sw128(st + CS_B1 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                                    ID_R1, 1);
-                    umma_commit(bar_r1);
-                }
-                // ---- D_S pre-scaled by this chunk's gamma_{C-1} while R1 runs
-                // (R1 does not touch D_S; R2, which accumulates into it, is
-                // issued after every thread's next barrier). The first chunk
-                // of an item set D_S = gamma S0 above.
-                if (c > 0) {
+                    mbar_arrive(bar_s16);
+                } else {
+                    // ---- D_S pre-scaled by this chunk's gamma_{C-1} while R1
+                    // runs (R1 does not touch D_S; R2, which accumulates into
+                    // it, waits for this thread's Delta^T arrival below)
                     tc_fence_after();
                     const float gC = gates(k)[G_GM + 63];
 #pragma unroll 1
@@ -800,7 +768,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     }
                     tmem_wait_st();
                 }
-                ok = mbar_wait(bar_r1, k & 1);
+                bool ok = mbar_wait(bar_r1, k & 1, p.poll_ns);
                 if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
                 tc_fence_after();
 
@@ -820,28 +788,8 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     tmem_wait_st();
                 }
                 tc_fence_before();
-                wg_sync(1);
-
-                // ---- R2: [D_S | O^T] += Delta^T [K~ | M^T] (one N = 192 product)
-                if (tid == 0) {
-                    tc_fence_after();
-#pragma unroll 1
-                    for (int kk = 0; kk < 4; ++kk)
-                        umma_f16_ta(tmem + TM_DS, tmem + TM_D16 + 8 * kk,
-                                    sdesc_sw128(st + CS_B2 + kk * 2048, 8192, 1024), ID_R2, 1);
-                    umma_commit(bar_r2);
-                    // The next chunk's U part of D_U, off its critical path,
-                    // when its record and tiles are already in (D_U was read
-                    // out before this round was issued).
-                    u_pre = false;
-                    const int kn = k + 1;
-                    if (c + 1 < nch && mbar_try_wait(&bar_full[kn & 1], (kn >> 1) & 1) &&
-                        mbar_try_wait(&bar_conv[kn & 1], (kn >> 1) & 1)) {
-                        issue_u(stage(kn));
-                        u_pre = true;
-                    }
-                }
-                ok = mbar_wait(bar_r2, k & 1);
+                mbar_arrive(bar_d16);
+                ok = mbar_wait(bar_r2, k & 1, p.poll_ns);
                 if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
                 tc_fence_after();
 
@@ -863,6 +811,8 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                         tmem_st32u(trow + TM_S16 + 32 * h2, w);
                     }
                     tmem_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(bar_s16);
                 } else if (dst) {
 #pragma unroll 1
                     for (int q4 = 0; q4 < 4; ++q4) {
@@ -875,13 +825,70 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                                 make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
                     }
                 }
-                tc_fence_before();
-                wg_sync(1);
             }
         }
-        if (rs.failed && tid == 0) {
-            // Every MMA this thread issued (including a pre-issued U part that
-            // no commit covered yet) completes before TMEM is released.
+    } else if (tid == 256) {
+        // ------------------------------------------------ MMA warp (one thread)
+        // Issues every product of the chain, so that a thread held up by a
+        // full MMA queue holds up no warpgroup.
+        int k = 0;
+        bool u_pre = false;  // the next R1's U part is already issued
+        // D_U = V^T (T diag b)^T (starts D_U; R1 accumulates onto it)
+        auto issue_u = [&](uint32_t st) {
+#pragma unroll 1
+            for (int kk = 0; kk < 4; ++kk)
+                umma_f16(tmem + TM_DU, sdesc_sw128(st + CS_V + kk * 2048, 8192, 1024),
+                         sdesc_sw128(st + CS_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
+        };
+        for (int64_t item = start; item < wk.n_items && !rs.failed; item += wk.stride) {
+            int64_t t0, t1;
+            wk.bounds(item, t0, t1);
+            const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
+            for (int c = 0; c < nch; ++c, ++k) {
+                const uint32_t st = stage(k);
+                // ---- R1's inputs: record k (its ring slot is free again once
+                // it has landed), tiles k in fp16, O^T of chunk k - 1 read out
+                // and cleared, S's fp16 image
+                bool ok = mbar_wait(&bar_full[k & 1], (k >> 1) & 1, p.poll_ns);
+                if (ok) st_release_gpu(consumed, k + 1);
+                ok = ok && mbar_wait(&bar_conv[k & 1], (k >> 1) & 1, p.poll_ns);
+                if (k >= 1) ok = ok && mbar_wait(&bar_ofree[(k - 1) & 1], ((k - 1) >> 1) & 1, p.poll_ns);
+                ok = ok && mbar_wait(bar_s16, k & 1, p.poll_ns);
+                if (!ok) { rs.failed = true; break; }
+                tc_fence_after();
+                // ---- R1: [O^T | D_U] += S [Q~ | -W]^T, one N = 128 product (S
+                // read from its fp16 image in TMEM; D_U starts as the U part)
+                if (!u_pre) issue_u(st);
+#pragma unroll 1
+                for (int kk = 0; kk < 8; ++kk)
+                    umma_f16_ta(tmem + TM_OT, tmem + TM_S16 + 8 * kk,
+                                sdesc_sw128(st + CS_B1 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                                ID_R1, 1);
+                umma_commit(bar_r1);
+                // ---- R2: [D_S | O^T] += Delta^T [K~ | M^T] (one N = 192 product)
+                if (!mbar_wait(bar_d16, k & 1, p.poll_ns)) { rs.failed = true; break; }
+                tc_fence_after();
+#pragma unroll 1
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_f16_ta(tmem + TM_DS, tmem + TM_D16 + 8 * kk,
+                                sdesc_sw128(st + CS_B2 + kk * 2048, 8192, 1024), ID_R2, 1);
+                umma_commit(bar_r2);
+                // ---- the next chunk's U part, under the state refresh (D_U
+                // was read out before Delta^T's arrival)
+                u_pre = false;
+                if (c + 1 < nch) {
+                    const int kn = k + 1;
+                    ok = mbar_wait(&bar_full[kn & 1], (kn >> 1) & 1, p.poll_ns) &&
+                         mbar_wait(&bar_conv[kn & 1], (kn >> 1) & 1, p.poll_ns);
+                    if (!ok) { rs.failed = true; break; }
+                    tc_fence_after();
+                    issue_u(stage(kn));
+                    u_pre = true;
+                }
+            }
+        }
+        if (rs.failed) {
+            // Every MMA issued completes before TMEM is released.
             umma_commit(bars + CB_DRAIN);
             mbar_wait(bars + CB_DRAIN, 0, 200000000ull);
         }
@@ -1419,6 +1426,8 @@ __global__ void __launch_bounds__(NT, 1)
                 mbar_init(&bars[CB_CONV + i], 128);   // warpgroup 1 signals
                 mbar_init(&bars[CB_OFREE + i], 128);
             }
+            mbar_init(&bars[CB_S16], 128);            // warpgroup 0 signals
+            mbar_init(&bars[CB_D16], 128);
         } else {
             for (int c = 0; c < PCTX; ++c) {
                 uint64_t *bars = reinterpret_cast<uint64_t *>(smem + c * P_CTX_BYTES + P_OFF_BAR);
