@@ -724,6 +724,12 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 continue;
             }
             for (int c = 0; c < nch; ++c, ++k) {
+                // Chunk k's gate table (gamma) is in once warpgroup 1 has
+                // converted its tiles: it builds the tables ahead of that.
+                {
+                    const bool ok = mbar_wait(&bar_conv[k & 1], (k >> 1) & 1, p.poll_ns);
+                    if (wg_sync_or(1, !ok)) { rs.failed = true; break; }
+                }
                 // ---- first chunk of the item: fp16 image of S0 (unscaled) and
                 // D_S = gamma_{C-1} S0 (the previous item's products are done)
                 if (c == 0) {
