@@ -186,6 +186,8 @@ struct GParams {
     int *abort_flag;      // set by any CTA whose bounded wait ran out
     const int32_t *off;   // packed streams: [items] first round of each item in its chain
     const int32_t *sched; // packed streams: [0] rounds of the longest chain, [1 + j] rounds of chain j
+    const int32_t *order; // packed streams: sequences by chunk count, longest first (null: as given)
+    int snake;            // chains take positions in snake order (packed streams)
     int n_chains;
     int n_prod;           // producer CTAs
     uint64_t poll_ns;     // bound of every wait on another CTA's flag
@@ -474,16 +476,37 @@ struct Ref {
     int64_t item, ts;  // item < 0: no chunk
     int L, h;
     int r, j;          // producer tasks: round and chain
+    int64_t m;         // the item's place in its chain's sequence
 };
 
-// The chunks a chain processes, in order: items start, start + stride, ...
-// (stride = number of chains) and within an item its chunks of CH positions
+// The chunks chain j processes, in order: the items at positions
+// pos(j, 0), pos(j, 1), ... and within an item its chunks of CH positions
 // from the sequence start; the k-th chunk is the chain's round k and uses
 // tile stage, record slot and gate table k & 1 (k & 3 for gate tables).
+// Dense batches: position q is item q and chain j takes j, j + NC, ...
+// Packed streams (lengths differ): position q is the item of the
+// (q / H)-th longest sequence (`order`, longest first) and head q % H, and
+// the chains take positions in snake order (row m of NC positions left to
+// right when m is even, right to left when odd), which spreads the long
+// sequences evenly over the chains.
 struct Walk {
     const GParams *p;
     int64_t n_items, stride;
     int H;
+
+    __device__ int64_t pos(int j, int64_t m) const {
+        if (!p->snake) return j + m * stride;
+        return m * stride + ((m & 1) ? stride - 1 - j : j);
+    }
+    __device__ int64_t item_at(int64_t q) const {
+        if (!p->order) return q;
+        return static_cast<int64_t>(p->order[q / H]) * H + q % H;
+    }
+    // Number of items chain j takes.
+    __device__ int64_t count(int j) const {
+        const int64_t full = n_items / stride;
+        return full + ((full * stride < n_items && pos(j, full) < n_items) ? 1 : 0);
+    }
 
     __device__ void bounds(int64_t item, int64_t &t0, int64_t &t1) const {
         const int64_t seq = item / H;
@@ -498,36 +521,41 @@ struct Walk {
             t1 = t0 + p->seq_len;
         }
     }
-    // First chunk at or after item `it` (skipping empty sequences).
-    __device__ Ref first_from(int64_t it) const {
-        for (; it < n_items; it += stride) {
+    // First chunk of chain j's items at or after place m (skipping empty sequences).
+    __device__ Ref first_from(int j, int64_t m) const {
+        for (;; ++m) {
+            const int64_t q = pos(j, m);
+            if (q >= n_items) break;
+            const int64_t it = item_at(q);
             int64_t t0, t1;
             bounds(it, t0, t1);
             if (t1 > t0) {
                 const int64_t seq = it / H;
                 return Ref{it, t0, static_cast<int>((t1 - t0) < CH ? (t1 - t0) : CH),
-                           static_cast<int>(it - seq * H), 0, 0};
+                           static_cast<int>(it - seq * H), 0, j, m};
             }
         }
-        return Ref{-1, 0, 0, 0, 0, 0};
+        return Ref{-1, 0, 0, 0, 0, j, 0};
     }
     __device__ Ref next_of(const Ref &r) const {
         int64_t t0, t1;
         bounds(r.item, t0, t1);
         const int64_t tn = r.ts + CH;
-        if (tn < t1) return Ref{r.item, tn, static_cast<int>((t1 - tn) < CH ? (t1 - tn) : CH), r.h, 0, 0};
-        return first_from(r.item + stride);
+        if (tn < t1)
+            return Ref{r.item, tn, static_cast<int>((t1 - tn) < CH ? (t1 - tn) : CH), r.h, 0, r.j, r.m};
+        return first_from(r.j, r.m + 1);
     }
-    // The chunk n steps after chunk c of `item` (bounds [t0, t1), nch chunks,
-    // head h): arithmetic inside the item, the walk only past its end (once
-    // per item rather than once per chunk).
-    __device__ Ref after(int64_t item, int h, int64_t t0, int64_t t1, int nch, int c, int n) const {
+    // The chunk n steps after chunk c of chain j's item at place m (bounds
+    // [t0, t1), nch chunks, head h): arithmetic inside the item, the walk
+    // only past its end (once per item rather than once per chunk).
+    __device__ Ref after(int j, int64_t m, int64_t item, int h, int64_t t0, int64_t t1, int nch, int c,
+                         int n) const {
         const int cc = c + n;
         if (cc < nch) {
             const int64_t ts = t0 + static_cast<int64_t>(cc) * CH;
-            return Ref{item, ts, static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH), h, 0, 0};
+            return Ref{item, ts, static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH), h, 0, j, m};
         }
-        Ref r = first_from(item + stride);
+        Ref r = first_from(j, m + 1);
         for (int i = nch; i < cc && r.item >= 0; ++i) r = next_of(r);
         return r;
     }
@@ -535,10 +563,10 @@ struct Walk {
 
 // Producer tasks in round-major order: task t is round t / n_chains of chain
 // t % n_chains. Dense batches (every item has nch chunks) map a round to its
-// item by arithmetic; packed streams use the per-item round offsets `off`
-// that gdr_grid_sched_kernel computed (the item is the last one of its chain
-// whose offset is <= r; an empty item shares its offset with the next item,
-// which comes later in the chain, so the search never lands on it).
+// item by arithmetic; packed streams use the per-position round offsets
+// `off` that gdr_grid_sched_kernel computed (the item is the chain's last
+// one whose offset is <= r; an empty item shares its offset with the next
+// item, which comes later in the chain, so the search never lands on it).
 struct Sched {
     const GParams *p;
     const Walk *wk;
@@ -548,31 +576,29 @@ struct Sched {
     int64_t n_tasks;
 
     __device__ int rounds(int j) const {
-        if (nch > 0) {
-            const int64_t m = (n_items - j + NC - 1) / NC;
-            return m > 0 ? static_cast<int>(m * nch) : 0;
-        }
+        if (nch > 0) return static_cast<int>(wk->count(j) * nch);
         return p->sched[1 + j];
     }
     // Task t, or item < 0 if that chain has no round t / NC.
     __device__ Ref at(int64_t t) const {
         const int r = static_cast<int>(t / NC), j = static_cast<int>(t - static_cast<int64_t>(r) * NC);
-        Ref out{-1, 0, 0, 0, r, j};
+        Ref out{-1, 0, 0, 0, r, j, 0};
         if (r >= rounds(j)) return out;
         int64_t item;
         int c;
         if (nch > 0) {
             const int m = r / nch;
             c = r - m * nch;
-            item = j + static_cast<int64_t>(m) * NC;
+            item = wk->item_at(wk->pos(j, m));
         } else {
-            int64_t lo = 0, hi = (n_items - j + NC - 1) / NC - 1;  // largest m with off <= r
+            int64_t lo = 0, hi = wk->count(j) - 1;  // largest m with off <= r
             while (lo < hi) {
                 const int64_t mid = (lo + hi + 1) >> 1;
-                if (p->off[j + mid * NC] <= r) lo = mid; else hi = mid - 1;
+                if (p->off[wk->pos(j, mid)] <= r) lo = mid; else hi = mid - 1;
             }
-            item = j + lo * NC;
-            c = r - p->off[item];
+            const int64_t q = wk->pos(j, lo);
+            item = wk->item_at(q);
+            c = r - p->off[q];
         }
         int64_t t0, t1;
         wk->bounds(item, t0, t1);
@@ -589,7 +615,7 @@ struct Sched {
             const Ref r = at(t);
             if (r.item >= 0) return r;
         }
-        return Ref{-1, 0, 0, 0, 0, 0};
+        return Ref{-1, 0, 0, 0, 0, 0, 0};
     }
 };
 
@@ -700,7 +726,10 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
             tmem_st32u(trow + TM_OT + 32, z);
             tmem_wait_st();
         }
-        for (int64_t item = start; item < wk.n_items && !rs.failed; item += wk.stride) {
+        for (int64_t m = 0; !rs.failed; ++m) {
+            const int64_t q = wk.pos(chain, m);
+            if (q >= wk.n_items) break;
+            const int64_t item = wk.item_at(q);
             const int64_t seq = item / H;
             const int h = static_cast<int>(item - seq * H);
             int64_t t0, t1;
@@ -846,7 +875,10 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 umma_f16(tmem + TM_DU, sdesc_sw128(st + CS_V + kk * 2048, 8192, 1024),
                          sdesc_sw128(st + CS_TT + kk * 32, 16, 1024), ID_MK64, kk > 0);
         };
-        for (int64_t item = start; item < wk.n_items && !rs.failed; item += wk.stride) {
+        for (int64_t m = 0; !rs.failed; ++m) {
+            const int64_t q = wk.pos(chain, m);
+            if (q >= wk.n_items) break;
+            const int64_t item = wk.item_at(q);
             int64_t t0, t1;
             wk.bounds(item, t0, t1);
             const int nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
@@ -943,7 +975,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
         const bool norm = p.norm_scale != nullptr;
         if (norm) nsc[wt] = p.norm_scale[wt];  // wt < 128 = HD
         {
-            const Ref r0 = wk.first_from(start);
+            const Ref r0 = wk.first_from(chain, 0);
             const Ref r1 = r0.item >= 0 ? wk.next_of(r0) : r0;
             const Ref r2 = r1.item >= 0 ? wk.next_of(r1) : r1;
             bool fok = true;
@@ -973,7 +1005,10 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
         }
 
         int k = 0;
-        for (int64_t item = start; item < wk.n_items && !rs.failed; item += wk.stride) {
+        for (int64_t m = 0; !rs.failed; ++m) {
+            const int64_t q = wk.pos(chain, m);
+            if (q >= wk.n_items) break;
+            const int64_t item = wk.item_at(q);
             const int64_t seq = item / H;
             const int h = static_cast<int>(item - seq * H);
             int64_t t0, t1;
@@ -982,13 +1017,13 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
             for (int c = 0; c < nch; ++c, ++k) {
                 const int64_t ts = t0 + static_cast<int64_t>(c) * CH;
                 const int L = static_cast<int>((t1 - ts) < CH ? (t1 - ts) : CH);
-                const Ref nxt = wk.after(item, h, t0, t1, nch, c, 1);
-                const Ref nn = wk.after(item, h, t0, t1, nch, c, 2);
+                const Ref nxt = wk.after(chain, m, item, h, t0, t1, nch, c, 1);
+                const Ref nn = wk.after(chain, m, item, h, t0, t1, nch, c, 2);
 
                 // ---- gate table of chunk k + 2, then the inputs of chunk k + 3
                 if (nn.item >= 0 && ww == 0) {
                     gate_tables(gates(k + 2), gin, lane);
-                    gin = gate_load(p, wk.after(item, h, t0, t1, nch, c, 3), lane);
+                    gin = gate_load(p, wk.after(chain, m, item, h, t0, t1, nch, c, 3), lane);
                 }
                 // ---- chunk k + 1's tiles -> fp16 (under chunk k's products)
                 if (nxt.item >= 0) {
@@ -1483,31 +1518,77 @@ __global__ void __launch_bounds__(NT, 1)
     if (warp == 0) tmem_dealloc(tmem, ncols);
 }
 
-// Per-item round offsets of a packed stream: chain j takes items j, j + NC,
-// ... in order, and off[item] is the number of chunks of the chain's earlier
-// items (one warp per chain, 32 items per step with a warp scan). sched[0]
-// is the longest chain's round count, sched[1 + j] chain j's.
+__device__ __forceinline__ int64_t seq_chunks(const int32_t *cu, int64_t seq, int64_t total_tokens) {
+    int64_t t0 = cu[seq], t1 = cu[seq + 1];
+    t0 = t0 < 0 ? 0 : (t0 > total_tokens ? total_tokens : t0);
+    t1 = t1 < t0 ? t0 : (t1 > total_tokens ? total_tokens : t1);
+    return (t1 - t0 + CH - 1) / CH;
+}
+
+__device__ __forceinline__ int64_t dev_n_seq(const int32_t *n_seq_dev, int64_t n_seq_host) {
+    if (!n_seq_dev) return n_seq_host;
+    const int64_t nd = *n_seq_dev;
+    return nd < n_seq_host ? nd : n_seq_host;
+}
+
+// Packed streams of at most this many sequences are ordered longest first;
+// longer lists keep the caller's order.
+constexpr int GRID_RANK_MAX = 4096;
+constexpr int GRID_RANK_THREADS = 256;
+constexpr int GRID_RANK_BLOCKS = GRID_RANK_MAX / GRID_RANK_THREADS;
+
+// Sequences of a packed stream by chunk count, longest first (ties by
+// index): order[rank(i)] = i, rank(i) = #{j : n_j > n_i or (n_j = n_i and
+// j < i)}. Each block holds every sequence's chunk count in shared memory and
+// each thread ranks one sequence against all of them. The sequence count is
+// read on the device; above GRID_RANK_MAX the order is the identity.
+__global__ void __launch_bounds__(GRID_RANK_THREADS)
+    gdr_grid_rank_kernel(const int32_t *cu, const int32_t *n_seq_dev, int64_t n_seq_host,
+                         int64_t total_tokens, int32_t *order) {
+    __shared__ int cnt[GRID_RANK_MAX];
+    const int64_t n = dev_n_seq(n_seq_dev, n_seq_host);
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (n > GRID_RANK_MAX) {  // the same branch for every thread of the grid
+        for (int64_t i = i0; i < n; i += stride) order[i] = static_cast<int32_t>(i);
+        return;
+    }
+    const int ni32 = static_cast<int>(n);
+    for (int i = threadIdx.x; i < ni32; i += blockDim.x) cnt[i] = static_cast<int>(seq_chunks(cu, i, total_tokens));
+    __syncthreads();
+    for (int64_t i = i0; i < n; i += stride) {
+        const int c = cnt[i];
+        int rank = 0;
+        for (int j = 0; j < ni32; ++j) {
+            const int cj = cnt[j];
+            rank += (cj > c || (cj == c && j < i)) ? 1 : 0;
+        }
+        order[rank] = static_cast<int32_t>(i);
+    }
+}
+
+// Per-position round offsets of a packed stream: chain j takes the items at
+// positions pos(j, 0), pos(j, 1), ... (snake order over positions sorted
+// longest first) and off[pos] is the number of chunks of the chain's
+// earlier items (one warp per chain, 32 items per step with a warp scan).
+// sched[0] is the longest chain's round count, sched[1 + j] chain j's.
 __global__ void gdr_grid_sched_kernel(const int32_t *cu, const int32_t *n_seq_dev, int64_t n_seq_host,
-                                      int64_t total_tokens, int H, int NC, int32_t *off, int32_t *sched) {
+                                      int64_t total_tokens, int H, int NC, const int32_t *order,
+                                      int32_t *off, int32_t *sched) {
     const int lane = threadIdx.x & 31;
     const int j = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (j >= NC) return;
-    int64_t n_seq = n_seq_host;
-    if (n_seq_dev) {
-        const int64_t nd = *n_seq_dev;
-        n_seq = nd < n_seq ? nd : n_seq;
-    }
-    const int64_t n_items = n_seq * H;
+    const int64_t n_items = dev_n_seq(n_seq_dev, n_seq_host) * H;
     int carry = 0;
-    for (int64_t m0 = 0; j + m0 * NC < n_items; m0 += 32) {
-        const int64_t item = j + (m0 + lane) * NC;
+    for (int64_t m0 = 0;; m0 += 32) {
+        const int64_t m = m0 + lane;
+        const int64_t q = m * NC + ((m & 1) ? NC - 1 - j : j);
+        const int64_t q0 = m0 * NC + ((m0 & 1) ? NC - 1 - j : j);
+        if (q0 >= n_items) break;
         int nch = 0;
-        if (item < n_items) {
-            const int64_t seq = item / H;
-            int64_t t0 = cu[seq], t1 = cu[seq + 1];
-            t0 = t0 < 0 ? 0 : (t0 > total_tokens ? total_tokens : t0);
-            t1 = t1 < t0 ? t0 : (t1 > total_tokens ? total_tokens : t1);
-            nch = static_cast<int>((t1 - t0 + CH - 1) / CH);
+        if (q < n_items) {
+            const int64_t item = order ? static_cast<int64_t>(order[q / H]) * H + q % H : q;
+            nch = static_cast<int>(seq_chunks(cu, item / H, total_tokens));
         }
         int incl = nch;
 #pragma unroll
@@ -1515,7 +1596,7 @@ __global__ void gdr_grid_sched_kernel(const int32_t *cu, const int32_t *n_seq_de
             const int x = __shfl_up_sync(0xffffffffu, incl, o);
             if (lane >= o) incl += x;
         }
-        if (item < n_items) off[item] = carry + incl - nch;
+        if (q < n_items) off[q] = carry + incl - nch;
         carry += __shfl_sync(0xffffffffu, incl, 31);
     }
     if (lane == 0) {
@@ -1559,7 +1640,7 @@ int make_tmap(CUtensorMap *m, const void *base, int64_t tokens, int H) {
 namespace {
 
 struct GridWs {
-    size_t ready, consumed, abort, sched, off, flags_end, total;
+    size_t ready, consumed, abort, sched, off, order, flags_end, total;
 };
 
 GridWs grid_ws(int64_t n_items, bool packed) {
@@ -1571,8 +1652,10 @@ GridWs grid_ws(int64_t n_items, bool packed) {
     w.abort = up(w.consumed + static_cast<size_t>(MAX_CHAINS) * sizeof(int));
     w.sched = up(w.abort + sizeof(int));
     w.flags_end = up(w.sched + static_cast<size_t>(1 + MAX_CHAINS) * sizeof(int));
+    const size_t ni = static_cast<size_t>(n_items > 0 ? n_items : 0);
     w.off = w.flags_end;
-    w.total = packed ? up(w.off + static_cast<size_t>(n_items > 0 ? n_items : 0) * sizeof(int)) : w.off;
+    w.order = up(w.off + ni * sizeof(int));  // at most one entry per sequence, sized per item
+    w.total = packed ? up(w.order + ni * sizeof(int)) : w.off;
     return w;
 }
 
@@ -1691,15 +1774,23 @@ int launch_chunk_grid(const SeqArgs &a) {
     p.abort_flag = reinterpret_cast<int *>(ws + w.abort);
     p.sched = reinterpret_cast<int32_t *>(ws + w.sched);
     p.off = packed ? reinterpret_cast<int32_t *>(ws + w.off) : nullptr;
+    p.order = packed ? reinterpret_cast<int32_t *>(ws + w.order) : nullptr;
+    p.snake = packed ? 1 : 0;
     p.n_chains = nc;
     p.n_prod = grid - nc;
     p.never_ready = g_test_mode.load();
     p.poll_ns = p.never_ready ? static_cast<uint64_t>(g_test_ns.load()) : 2000000000ull;
     if (packed) {
+        gdr_grid_rank_kernel<<<GRID_RANK_BLOCKS, GRID_RANK_THREADS, 0, a.stream>>>(
+            a.cu_seqlens, a.n_seq_dev, a.n_seq, tokens, const_cast<int32_t *>(p.order));
+        {
+            const int ls = check_launch("gdr_grid_rank_kernel");
+            if (ls != RHZ_OK) return ls;
+        }
         const int warps = 8;
         gdr_grid_sched_kernel<<<(nc + warps - 1) / warps, 32 * warps, 0, a.stream>>>(
-            a.cu_seqlens, a.n_seq_dev, a.n_seq, tokens, a.H, nc, reinterpret_cast<int32_t *>(ws + w.off),
-            reinterpret_cast<int32_t *>(ws + w.sched));
+            a.cu_seqlens, a.n_seq_dev, a.n_seq, tokens, a.H, nc, p.order,
+            reinterpret_cast<int32_t *>(ws + w.off), reinterpret_cast<int32_t *>(ws + w.sched));
         {
             const int ls = check_launch("gdr_grid_sched_kernel");
             if (ls != RHZ_OK) return ls;
