@@ -81,8 +81,8 @@ int rhz_abi_version(void);
 
 /*
  * Device-side failure status -- an addition of this library (the reference's
- * ops run on the CPU and have no device waits). The tensor-core kernels
- * bound every wait on a barrier or a copy; a wait that runs out makes the
+ * ops run on the CPU and have no device waits). The tensor-core kernels and
+ * the input producer's TMA form bound every wait on a barrier or a copy; a wait that runs out makes the
  * kernel drain its copies, release its resources and return early, leaving
  * that launch's outputs undefined, and sets a sticky flag on the device.
  * rhz_device_status reads the flags of the current device (synchronising

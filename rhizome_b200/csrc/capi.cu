@@ -242,12 +242,13 @@ int rhz_abi_version(void) { return RHZ_ABI_VERSION; }
 int rhz_device_status(int32_t *timed_out, int clear) {
     clear_error();
     if (!timed_out) return set_error(RHZ_ERR_INVALID, "timed_out must not be NULL");
-    int a = 0, b = 0, c = 0;
+    int a = 0, b = 0, c = 0, e = 0;
     int st = chunk_pair_status(&a, clear != 0);
     if (st == RHZ_OK) st = chunk_solo_status(&b, clear != 0);
     if (st == RHZ_OK) st = chunk_grid_status(&c, clear != 0);
+    if (st == RHZ_OK) st = prep_status(&e, clear != 0);
     if (st != RHZ_OK) return st;
-    *timed_out = (a | b | c) ? 1 : 0;
+    *timed_out = (a | b | c | e) ? 1 : 0;
     return RHZ_OK;
 }
 

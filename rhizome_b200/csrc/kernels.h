@@ -83,6 +83,8 @@ struct PrepArgs {
 
 int launch_step(const StepArgs &a);
 int launch_prep(const PrepArgs &a);
+// Sticky flag of the input producer's bounded TMA wait (1: a wait ran out).
+int prep_status(int *flag, bool clear);
 int launch_multistep(const MultistepArgs &a);
 int launch_seq(const SeqArgs &a);
 // Tensor-core chunked kernel (bf16, d == 128). Returns RHZ_ERR_SHAPE for

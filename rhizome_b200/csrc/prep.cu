@@ -10,25 +10,37 @@
 // [tokens][H] f32; a_head [H]; conv_w [3][H][d][4]; conv_b [3][H][d];
 // conv_state [num_slots][3][H][d][3] f32 (samples oldest first).
 //
-// One warp per (64-token tile, head), four consecutive channels per lane:
-// conv weights in registers, a 3-sample window per channel sliding along the
-// tile (restarted from the slot's carried samples at each sequence start).
-// Rows are read and written with 8/16-byte vector accesses, norms are
-// warp-shuffle sums. HBM traffic is one read of x and logits (plus a 3-row
-// halo per tile) and one write of q, k, v, alpha, beta.
-// A second kernel writes each sequence's last three samples back to its slot
-// once every token has read the old state.
+// Three forms, all with conv weights in registers and a 3-sample window per
+// channel sliding along consecutive tokens (restarted from the slot's carried
+// samples at each sequence start), four channels per lane, norms as
+// warp-shuffle sums:
+//   gdr_prep_tma_kernel  bf16, d = 128, 16-byte aligned inputs: a CTA per
+//                        (64 tokens, head), rows staged by TMA, each row's
+//                        sequence looked up once per CTA;
+//   gdr_prep_tile_kernel rows of 256 bytes otherwise (and d = 64): the same
+//                        tiles staged by 16-byte loads of all threads;
+//   gdr_prep_kernel      any other width: a warp per (64 tokens, head) with
+//                        one token of look-ahead.
+// HBM traffic is one read of x and logits (plus a 3-row halo per tile) and
+// one write of q, k, v, alpha, beta. A second kernel writes each sequence's
+// last three samples back to its slot once every token has read the old
+// state.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <climits>
 #include <cstdint>
 #include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "sm100.cuh"
+#include "tmap.h"
 
 namespace rhz {
 namespace {
+
+using namespace sm100;
 
 constexpr int WARPS = 4;
 
@@ -421,6 +433,201 @@ __global__ void __launch_bounds__(32 * TWARPS, 3) gdr_prep_tile_kernel(const Pre
     }
 }
 
+// TMA form for bf16 rows of d = 128 (the model's shape): one CTA per (tile
+// of MT tokens, head). One thread copies the tile's rows of xq, xk and xv
+// plus a 3-row halo with three TMA boxes ([MT + 3 rows][128 channels] each;
+// rows above the first token or past the last read as zeros) while the
+// first MT threads look up each row's sequence once: its depth (rows of the
+// same sequence before it, capped at 3; DEPTH_NONE for a row no sequence
+// covers) and its conv-state slot (-1: zeros). Each warp then runs its
+// MPER rows of one array at a time, four channels per lane, the weights and
+// a 3-sample window per channel in registers; the window slides along the
+// rows and a row of depth < 3 (the first rows of a sequence) takes its
+// missing samples from the slot. The norms use rsqrtf (within 2 ulp) and
+// four rows' shuffle reductions run side by side.
+constexpr int MT = 64;
+constexpr int MROWS = MT + 3;
+constexpr int MWARPS = 8;
+constexpr int MPER = MT / MWARPS;
+constexpr int MD = 128;
+constexpr int DEPTH_NONE = 4;
+constexpr uint32_t M_ARRAY_BYTES = MROWS * MD * 2;
+constexpr uint32_t M_OFF_BAR = 3 * M_ARRAY_BYTES;
+constexpr uint32_t M_OFF_DEPTH = M_OFF_BAR + 64;
+constexpr uint32_t M_OFF_SLOT = M_OFF_DEPTH + MT * 4;
+constexpr uint32_t M_SMEM = M_OFF_SLOT + MT * 4;
+static_assert(M_ARRAY_BYTES % 128 == 0, "TMA destinations stay 128-byte aligned");
+
+__device__ int g_prep_status = 0;
+
+__device__ __forceinline__ void lds4_bf16(const __nv_bfloat16 *p, float (&x)[4]) {
+    const uint2 t = *reinterpret_cast<const uint2 *>(p);
+    const float2 fa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&t.x));
+    const float2 fb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&t.y));
+    x[0] = fa.x; x[1] = fa.y; x[2] = fb.x; x[3] = fb.y;
+}
+
+__global__ void __launch_bounds__(32 * MWARPS, 3)
+    gdr_prep_tma_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const PrepArgs p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const __nv_bfloat16 *rows = reinterpret_cast<const __nv_bfloat16 *>(smem);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + M_OFF_BAR);
+    int *mdepth = reinterpret_cast<int *>(smem + M_OFF_DEPTH);
+    int *mslot = reinterpret_cast<int *>(smem + M_OFF_SLOT);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int H = p.H;
+    const int64_t tile = blockIdx.x / H;
+    const int h = static_cast<int>(blockIdx.x - tile * H);
+    const int64_t tok0 = tile * MT;
+
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        mbar_arrive_expect_tx(bar, 3 * M_ARRAY_BYTES);
+        const int y0 = static_cast<int>(tok0) - 3;
+        tma_load_3d(smem, &tm_q, 0, h, y0, bar);
+        tma_load_3d(smem + M_ARRAY_BYTES, &tm_k, 0, h, y0, bar);
+        tma_load_3d(smem + 2 * M_ARRAY_BYTES, &tm_v, 0, h, y0, bar);
+    }
+    // ---- each row's sequence (under the copies)
+    if (tid < MT) {
+        const int64_t tok = tok0 + tid;
+        int depth = DEPTH_NONE, slot_out = -1;
+        if (tok < p.total_tokens) {
+            int64_t seq, t0, t1;
+            if (p.cu_seqlens) {
+                int64_t lo = 0, hi = p.n_seq - 1;  // largest i with cu[i] <= tok
+                while (lo < hi) {
+                    const int64_t mid = (lo + hi + 1) >> 1;
+                    if (static_cast<int64_t>(p.cu_seqlens[mid]) <= tok) lo = mid;
+                    else hi = mid - 1;
+                }
+                seq = lo;
+                t0 = p.cu_seqlens[lo];
+                t1 = p.cu_seqlens[lo + 1];
+                t0 = t0 < 0 ? 0 : t0;  // offsets are caller data
+            } else {
+                seq = tok / p.seq_len;
+                t0 = seq * p.seq_len;
+                t1 = t0 + p.seq_len;
+            }
+            if (tok >= t0 && tok < t1) {
+                depth = tok - t0 < 3 ? static_cast<int>(tok - t0) : 3;
+                const int64_t slot = p.slots ? static_cast<int64_t>(p.slots[seq]) : seq;
+                if (p.conv_state && !p.zero_init && slot >= 0 && slot < p.num_slots)
+                    slot_out = static_cast<int>(slot);
+            }
+        }
+        mdepth[tid] = depth;
+        mslot[tid] = slot_out;
+    }
+    const int r0 = MPER * warp;  // this warp's first row, relative to tok0
+    // Gate logits of the warp's rows, one per lane, fetched before the wait.
+    float bl = 0.f, al = 0.f;
+    const int64_t gtok = tok0 + r0 + lane;
+    if (lane < MPER && gtok < p.total_tokens) {
+        bl = p.beta_logit[gtok * H + h];
+        al = p.alpha_logit[gtok * H + h];
+    }
+    const float sp_a = softplus_f(p.a_head[h]);
+    __syncthreads();
+    if (!mbar_wait(bar, 0)) {
+        // The copies never landed: record it, and give them a last bounded
+        // chance to finish before this CTA's shared memory is released.
+        atomicExch(&g_prep_status, 1);
+        mbar_wait(bar, 0, 200000000ull);
+        return;
+    }
+
+    if (lane < MPER && mdepth[r0 + lane] != DEPTH_NONE) {
+        const int64_t i = gtok * H + h;
+        p.beta[i] = sigmoid_f(bl);
+        p.alpha[i] = expf(-sp_a * softplus_f(al));
+    }
+
+    const int c0 = 4 * lane;
+    const int64_t rs = static_cast<int64_t>(H) * MD;
+#pragma unroll 1
+    for (int a = 0; a < 3; ++a) {
+        float w[4][4], bias[4];
+        {
+            const float *wp = p.conv_w + ((static_cast<int64_t>(a) * H + h) * MD + c0) * 4;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float4 f = *reinterpret_cast<const float4 *>(wp + 4 * e);
+                w[e][0] = f.x; w[e][1] = f.y; w[e][2] = f.z; w[e][3] = f.w;
+            }
+            const float4 bf = *reinterpret_cast<const float4 *>(p.conv_b + (static_cast<int64_t>(a) * H + h) * MD + c0);
+            bias[0] = bf.x; bias[1] = bf.y; bias[2] = bf.z; bias[3] = bf.w;
+        }
+        const __nv_bfloat16 *xr = rows + a * MROWS * MD + c0;  // smem row i = token tok0 - 3 + i
+        __nv_bfloat16 *yp = static_cast<__nv_bfloat16 *>(a == 0 ? p.q : a == 1 ? p.k : p.v) +
+                            (tok0 + r0) * rs + static_cast<int64_t>(h) * MD + c0;
+        const float scale = a == 0 ? p.q_scale : 1.f;
+        float win[3][4];  // samples of the three rows before the current one, oldest first
+#pragma unroll
+        for (int m = 0; m < 3; ++m) lds4_bf16(xr + (r0 + m) * MD, win[m]);
+#pragma unroll
+        for (int g = 0; g < MPER; g += 4) {
+            float y[4][4], ss[4];
+            bool live[4];
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int r = r0 + g + jj;
+                const int depth = mdepth[r];
+                live[jj] = depth != DEPTH_NONE;
+                if (depth < 3) {  // the first rows of a sequence: samples before it from its slot
+                    const int slot = mslot[r];
+                    const float *st = slot >= 0
+                        ? p.conv_state + (((static_cast<int64_t>(slot) * 3 + a) * H + h) * MD + c0) * 3
+                        : nullptr;
+#pragma unroll
+                    for (int m = 0; m < 3; ++m) {
+                        if (m < 3 - depth) {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) win[m][e] = st ? st[3 * e + depth + m] : 0.f;
+                        }
+                    }
+                }
+                float x[4];
+                lds4_bf16(xr + (r + 3) * MD, x);
+                ss[jj] = 0.f;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    // weight[0] state[0] + weight[1] state[1] + weight[2] state[2] + weight[3] x + bias
+                    y[jj][e] = w[e][0] * win[0][e] + w[e][1] * win[1][e] + w[e][2] * win[2][e] +
+                               w[e][3] * x[e] + bias[e];
+                    win[0][e] = win[1][e];
+                    win[1][e] = win[2][e];
+                    win[2][e] = x[e];
+                    ss[jj] += y[jj][e] * y[jj][e];
+                }
+            }
+            if (a < 2) {
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) ss[jj] += __shfl_xor_sync(0xffffffffu, ss[jj], off);
+                }
+            }
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                if (!live[jj]) continue;
+                // x / max(|x|, 1e-12) * scale
+                const float mul = a < 2 ? scale * (ss[jj] >= 1e-24f ? rsqrtf(ss[jj]) : 1e12f) : 1.f;
+                float o[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[e] = y[jj][e] * mul;
+                store4(yp + (g + jj) * rs, o);
+            }
+        }
+    }
+}
+
 // Each sequence's last three samples (older ones from its previous state
 // where it is shorter than three) back to its slot: one thread per
 // (sequence, q/k/v, head, channel).
@@ -461,11 +668,50 @@ __global__ void gdr_conv_state_kernel(const PrepArgs p) {
     for (int m = 0; m < 3; ++m) st[m] = nw[m];
 }
 
+// The TMA form takes bf16 rows of d = 128 whose arrays start on 16-byte
+// boundaries (TMA's rule) and token counts that fit its 32-bit coordinates.
+bool prep_tma_fits(const PrepArgs &a) {
+    auto al16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    return a.dtype == RHZ_DTYPE_BF16 && a.d == MD && a.total_tokens > 0 &&
+           a.total_tokens <= static_cast<int64_t>(INT_MAX) - 2 * MT && al16(a.xq) && al16(a.xk) &&
+           al16(a.xv) && a.total_tokens * a.H / MT <= static_cast<int64_t>(INT_MAX);
+}
+
+int launch_prep_tma(const PrepArgs &a) {
+    CUtensorMap tm[3];
+    const void *src[3] = {a.xq, a.xk, a.xv};
+    const uint64_t dims[3] = {MD, static_cast<uint64_t>(a.H), static_cast<uint64_t>(a.total_tokens)};
+    const uint64_t strides[2] = {MD * 2, static_cast<uint64_t>(a.H) * MD * 2};
+    const uint32_t box[3] = {MD, 1, MROWS};
+    for (int i = 0; i < 3; ++i) {
+        const int st = encode_tmap(&tm[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, src[i], dims, strides, box,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st != RHZ_OK) return st;
+    }
+    static std::once_flag attr_once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once, [] {
+        attr_err = cudaFuncSetAttribute(gdr_prep_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(M_SMEM));
+    });
+    if (attr_err != cudaSuccess)
+        return set_error(RHZ_ERR_DEVICE, "gdr_prep_tma_kernel smem attribute: %s", cudaGetErrorString(attr_err));
+    const int64_t blocks = (a.total_tokens + MT - 1) / MT * a.H;
+    gdr_prep_tma_kernel<<<static_cast<unsigned>(blocks), 32 * MWARPS, M_SMEM, a.stream>>>(tm[0], tm[1], tm[2], a);
+    return check_launch("gdr_prep_tma_kernel");
+}
+
 template <typename T>
 int launch_prep_t(const PrepArgs &a) {
     const size_t row_bytes = static_cast<size_t>(a.d) * sizeof(T);
-    const bool tiled = (a.d == 128 && sizeof(T) == 2) || a.d == 64;
-    if (a.total_tokens > 0 && tiled) {
+    auto al16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    // 16-byte row copies: the arrays must start on 16-byte boundaries (bf16
+    // callers only guarantee 8; the warp form reads 8 bytes at a time)
+    const bool tiled = ((a.d == 128 && sizeof(T) == 2) || a.d == 64) && al16(a.xq) && al16(a.xk) && al16(a.xv);
+    if (prep_tma_fits(a)) {
+        const int st = launch_prep_tma(a);
+        if (st != RHZ_OK) return st;
+    } else if (a.total_tokens > 0 && tiled) {
         const int64_t blocks = (a.total_tokens + TT - 1) / TT * a.H;
         const size_t smem = 3 * (TT + 3) * row_bytes;
         void (*kern)(const PrepArgs) = gdr_prep_tile_kernel<T, 64>;
@@ -507,6 +753,19 @@ int launch_prep_t(const PrepArgs &a) {
 }
 
 }  // namespace
+
+int prep_status(int *flag, bool clear) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_prep_status, sizeof(int));
+    if (e == cudaSuccess && clear && v) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_prep_status, &zero, sizeof(int));
+    }
+    if (e != cudaSuccess)
+        return set_error(RHZ_ERR_DEVICE, "reading the input producer's status: %s", cudaGetErrorString(e));
+    *flag = v;
+    return RHZ_OK;
+}
 
 int launch_prep(const PrepArgs &a) {
     return a.dtype == RHZ_DTYPE_BF16 ? launch_prep_t<__nv_bfloat16>(a) : launch_prep_t<float>(a);

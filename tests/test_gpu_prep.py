@@ -190,3 +190,72 @@ def test_prep_then_recurrence_matches_oracle():
     torch.cuda.synchronize()
     assert_bf16(host(o), ro, "prep -> recurrence o")
     assert_bf16(host(dpool), rpool, "prep -> recurrence states")
+
+
+def test_inputs_on_8_byte_boundaries():
+    """bf16 inputs that start 8 bytes past a 16-byte boundary (all the C ABI
+    asks of bf16 arrays) take the form with 8-byte loads and give the same
+    answer as aligned inputs, within one bf16 rounding of the oracle."""
+    rng = np.random.default_rng(16)
+    H, d = 4, 128
+    lens = np.array([70, 1, 129, 3])
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    tokens = int(cu[-1])
+    xs_bl_al = raw(rng, tokens, H, d, "bf16")
+    ah, w, b = params(rng, H, d)
+    cs = f32(rng.normal(size=(4, 3, H, d, 3)))
+    slots = np.array([2, 0, 3, 1], dtype=np.int32)
+    ref = O.gdr_prep(cu, *xs_bl_al[:3], xs_bl_al[3], xs_bl_al[4], ah, w, b, cs, slots, False, True,
+                     math.sqrt(d))
+    X = []
+    for x in xs_bl_al[:3]:
+        buf = torch.empty(tokens * H * d + 4, dtype=torch.bfloat16, device="cuda")
+        view = buf[4:].view(tokens, H, d)
+        view.copy_(to_dev(x, torch.bfloat16))
+        assert view.data_ptr() % 16 == 8
+        X.append(view)
+    dev_cs = to_dev(cs, torch.float32)
+    out = ops.gdr_prep(*X, to_dev(xs_bl_al[3], torch.float32), to_dev(xs_bl_al[4], torch.float32),
+                       to_dev(ah, torch.float32), to_dev(w, torch.float32), to_dev(b, torch.float32),
+                       conv_state=dev_cs, slot_idx=to_dev(slots, torch.int32),
+                       cu_seqlens=to_dev(cu, torch.int32), q_scale=math.sqrt(d))
+    got = [host(t) for t in out] + [host(dev_cs)]
+    check("bf16", got, ref, "8-byte boundaries")
+
+
+def test_rows_outside_sequences_bf16_d128():
+    """A packed stream whose offsets leave rows before the first sequence and
+    after the last uncovered, with an empty sequence and sequences that start
+    and end inside 64-token tiles: covered rows match the oracle, uncovered
+    rows of the outputs are left as they were."""
+    from rhizome_b200 import capi
+    rng = np.random.default_rng(17)
+    H, d = 3, 128
+    tokens = 300
+    cu = np.array([5, 69, 69, 70, 133, 200, 293], dtype=np.int32)
+    xs_bl_al = raw(rng, tokens, H, d, "bf16")
+    ah, w, b = params(rng, H, d)
+    cs = f32(rng.normal(size=(7, 3, H, d, 3)))
+    slots = np.array([6, 1, 0, 3, 2, 5], dtype=np.int32)
+    ref = O.gdr_prep(cu, *xs_bl_al[:3], xs_bl_al[3], xs_bl_al[4], ah, w, b, cs, slots, False, True,
+                     1.0)
+    X = [to_dev(x, torch.bfloat16) for x in xs_bl_al[:3]]
+    dev_cs = to_dev(cs, torch.float32)
+    sentinel = -7.0
+    outs = [torch.full((tokens, H, d), sentinel, dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+    outs += [torch.full((tokens, H), sentinel, dtype=torch.float32, device="cuda") for _ in range(2)]
+    # every device argument stays referenced until the call has run
+    args = [to_dev(xs_bl_al[3], torch.float32), to_dev(xs_bl_al[4], torch.float32),
+            to_dev(ah, torch.float32), to_dev(w, torch.float32), to_dev(b, torch.float32), dev_cs,
+            to_dev(slots, torch.int32), to_dev(cu, torch.int32)]
+    capi.call("rhz_gdr_prep", *[t.data_ptr() for t in outs], *[t.data_ptr() for t in X],
+              *[t.data_ptr() for t in args], len(slots), 0, tokens, 7, H, d, 1.0,
+              capi.RHZ_DTYPE_BF16, 0, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    got = [host(t) for t in outs] + [host(dev_cs)]
+    inside = np.zeros(tokens, dtype=bool)
+    inside[cu[0]:cu[-1]] = True
+    for g in got[:5]:
+        assert np.all(g[~inside] == sentinel), "an uncovered row was written"
+    check("bf16", [g[inside] for g in got[:5]] + [got[5]], [r[inside] for r in ref[:5]] + [ref[5]],
+          "uncovered rows")
