@@ -115,6 +115,17 @@ int rhz_gdr_set_wait_test(int32_t mode, int64_t limit_ns);
 enum rhz_chunk_kernel { RHZ_CHUNK_AUTO = 0, RHZ_CHUNK_PAIR = 1, RHZ_CHUNK_SOLO = 2, RHZ_CHUNK_GRID = 3 };
 int rhz_gdr_set_chunk_kernel(int32_t variant, int32_t *previous);
 
+/*
+ * Which form runs rhz_gdr_scan_chunked_bwd: AUTO (the default) takes the
+ * chunked tensor-core form for bf16 inputs with d == 128, no segments and
+ * 16-byte aligned q, k, v, d_o, and the fp32 reverse scan otherwise; SCAN
+ * forces the fp32 reverse scan everywhere. Process-wide; the previous
+ * setting goes to *previous unless it is NULL. Anything else returns
+ * RHZ_ERR_INVALID.
+ */
+enum rhz_bwd_kernel { RHZ_BWD_AUTO = 0, RHZ_BWD_SCAN = 1 };
+int rhz_gdr_set_bwd_kernel(int32_t variant, int32_t *previous);
+
 /* --------------------------------------------------------------------- */
 /* GDR op family                                                          */
 /* --------------------------------------------------------------------- */
@@ -303,10 +314,15 @@ int rhz_gdr_prep(void *q, void *k, void *v, float *alpha, float *beta, const voi
  * [B][T] int64 or NULL), exactly as in the forward. Given d_o [B][T][H][d]
  * (the gradient of o) and d_state_final [B][H][d][d] (the gradient of the
  * final state, or NULL for zero), writes dq, dk, dv [B][T][H][d] (dtype)
- * and dalpha, dbeta [B][T][H] f32. fp32 arithmetic for f32 and bf16 inputs;
- * d a multiple of 4, at most 128. Needs `workspace` of
- * rhz_gdr_bwd_workspace_bytes(B, T, H, d) bytes (state checkpoints every 8
- * positions and per-row-block partial sums; the result is deterministic).
+ * and dalpha, dbeta [B][T][H] f32. d a multiple of 4, at most 128. Two
+ * forms (rhz_gdr_set_bwd_kernel): bf16 inputs with d == 128 and no segments
+ * run the chunked tensor-core form (fp16 products, fp32 accumulation, the
+ * upstream gradients scaled by an exact power of two; per-chunk records and
+ * the states at chunk boundaries in the workspace); everything else runs an
+ * fp32 reverse scan (state checkpoints every 8 positions and per-row-block
+ * partial sums). Needs `workspace` of rhz_gdr_bwd_workspace_bytes(B, T, H,
+ * d) bytes (the larger of the two forms' needs). Both forms are
+ * deterministic.
  */
 int rhz_gdr_scan_chunked_bwd(void *dq, void *dk, void *dv, float *dalpha, float *dbeta,
                              const void *q, const void *k, const void *v, const float *alpha,

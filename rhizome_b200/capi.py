@@ -102,11 +102,13 @@ SIGNATURES = {
                                             _i64, _i64, _i32, _i32, _i32, _vp, _sz, _vp]),
     "rhz_gdr_host_workspace_bytes": (_sz, [_i64, _i64, _i32, _i32, _i32, C.c_int]),
     "rhz_gdr_set_chunk_kernel": (C.c_int, [_i32, _vp]),
+    "rhz_gdr_set_bwd_kernel": (C.c_int, [_i32, _vp]),
     "rhz_gdr_set_wait_test": (C.c_int, [_i32, _i64]),
 }
 
 # Forms of the tensor-core chunked scan (enum rhz_chunk_kernel).
 RHZ_CHUNK_AUTO, RHZ_CHUNK_PAIR, RHZ_CHUNK_SOLO, RHZ_CHUNK_GRID = 0, 1, 2, 3
+RHZ_BWD_AUTO, RHZ_BWD_SCAN = 0, 1
 
 # Largest B*T rhz_varlen_segments_to_cu_seqlens_noalloc accepts.
 RHZ_NOALLOC_MAX_POSITIONS = 1 << 26

@@ -265,6 +265,14 @@ int rhz_gdr_set_chunk_kernel(int32_t variant, int32_t *previous) {
     return st;
 }
 
+int rhz_gdr_set_bwd_kernel(int32_t variant, int32_t *previous) {
+    clear_error();
+    int prev = 0;
+    const int st = set_bwd_form(variant, &prev);
+    if (st == RHZ_OK && previous) *previous = prev;
+    return st;
+}
+
 int rhz_gdr_step(void *o, float *state_pool, const int32_t *slot_idx, const void *q,
                  const void *k, const void *v, const float *alpha, const float *beta, int64_t n,
                  int64_t num_slots, int32_t H, int32_t d, int32_t dtype, rhz_stream_t stream) {

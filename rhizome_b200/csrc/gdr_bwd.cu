@@ -9,6 +9,9 @@
 //   G <- alpha (G - beta g k^T), and G <- 0 at a reset (t = 0, segment change).
 // fp32 throughout (inputs f32 or bf16), d <= 128 with d % 4 == 0.
 //
+// This fp32 reverse scan serves f32 inputs, segments and other widths; bf16
+// inputs of d = 128 take the chunked tensor-core form (gdr_bwd_tc.cu).
+//
 // Rows of S and G evolve independently, so one CTA (4 warps, 4 rows each)
 // owns 16 rows of one (sequence, head); a lane holds 4 consecutive columns.
 // Pass 1 runs the recurrence forward and stores the CTA's rows of the state
@@ -279,16 +282,20 @@ __global__ void gdr_bwd_reduce_kernel(const BwdParams p) {
 
 }  // namespace
 
+// The larger of the two forms' needs: the query does not know the dtype.
 size_t bwd_ws_bytes(int64_t B, int64_t T, int H, int d) {
     const int64_t nrb = (d + R - 1) / R;
     const int64_t nck = (T + CK - 1) / CK;
     const int64_t blocks = B * H * nrb;
     const int64_t ck = blocks * nck * R * d * 4;
     const int64_t pt = blocks * T * (2 * d + PW) * 4;
-    return static_cast<size_t>(((ck + 255) / 256) * 256 + pt);
+    const size_t scan = static_cast<size_t>(((ck + 255) / 256) * 256 + pt);
+    const size_t tc = bwd_tc_ws_bytes(B, T, H, d);
+    return scan > tc ? scan : tc;
 }
 
 int launch_bwd(const BwdArgs &a) {
+    if (a.B > 0 && a.T > 0 && bwd_tc_supports(a)) return launch_bwd_tc(a);
     BwdParams p;
     p.dq = a.dq; p.dk = a.dk; p.dv = a.dv; p.dalpha = a.dalpha; p.dbeta = a.dbeta;
     p.q = a.q; p.k = a.k; p.v = a.v; p.d_o = a.d_o;

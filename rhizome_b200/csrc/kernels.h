@@ -136,6 +136,12 @@ struct BwdArgs {
 };
 size_t bwd_ws_bytes(int64_t B, int64_t T, int H, int d);
 int launch_bwd(const BwdArgs &a);
+// Chunked tensor-core backward (gdr_bwd_tc.cu): bf16, d = 128, no segments,
+// 16-byte aligned q/k/v/d_o. set_bwd_form(1) forces the fp32 reverse scan.
+bool bwd_tc_supports(const BwdArgs &a);
+size_t bwd_tc_ws_bytes(int64_t B, int64_t T, int H, int d);
+int launch_bwd_tc(const BwdArgs &a);
+int set_bwd_form(int form, int *prev);
 
 // groupnorm_heads over rows x H slices of d values (norm.cu); out may be x.
 int launch_groupnorm_heads(void *out, const void *x, const float *scale, int64_t rows, int H, int d,

@@ -453,3 +453,16 @@ def set_chunk_kernel(variant: str) -> str:
     prev = ctypes.c_int32(0)
     capi.call("rhz_gdr_set_chunk_kernel", names[variant], ctypes.byref(prev))
     return {v: k for k, v in names.items()}[prev.value]
+
+
+def set_bwd_kernel(variant: str) -> str:
+    """Pick the backward's form process-wide: "auto" (the chunked
+    tensor-core form for bf16, d = 128 without segments, the fp32 reverse
+    scan otherwise) or "scan" (the fp32 reverse scan always). Returns the
+    previous setting."""
+    names = {"auto": capi.RHZ_BWD_AUTO, "scan": capi.RHZ_BWD_SCAN}
+    if variant not in names:
+        raise capi.InvalidArgument(capi.RHZ_ERR_INVALID, f"unknown backward kernel {variant!r}")
+    prev = ctypes.c_int32(0)
+    capi.call("rhz_gdr_set_bwd_kernel", names[variant], ctypes.byref(prev))
+    return {v: k for k, v in names.items()}[prev.value]

@@ -67,6 +67,17 @@ def test_chunk_form_setting_without_gpu(lib):
     assert lib.rhz_gdr_set_chunk_kernel(capi.RHZ_CHUNK_AUTO, None) == capi.RHZ_OK
 
 
+def test_bwd_form_setting_without_gpu(lib):
+    prev = C.c_int32(-1)
+    assert lib.rhz_gdr_set_bwd_kernel(2, C.byref(prev)) == capi.RHZ_ERR_INVALID
+    assert b"backward form 2" in lib.rhz_last_error()
+    assert lib.rhz_gdr_set_bwd_kernel(capi.RHZ_BWD_SCAN, C.byref(prev)) == capi.RHZ_OK
+    assert prev.value == capi.RHZ_BWD_AUTO
+    assert lib.rhz_gdr_set_bwd_kernel(capi.RHZ_BWD_AUTO, C.byref(prev)) == capi.RHZ_OK
+    assert prev.value == capi.RHZ_BWD_SCAN
+    assert lib.rhz_gdr_set_bwd_kernel(capi.RHZ_BWD_AUTO, None) == capi.RHZ_OK
+
+
 def test_wait_test_hook_validates_without_gpu(lib):
     assert lib.rhz_gdr_set_wait_test(2, 1000000) == capi.RHZ_ERR_INVALID
     assert lib.rhz_gdr_set_wait_test(1, 10) == capi.RHZ_ERR_INVALID  # below 1 us

@@ -95,3 +95,94 @@ def test_deterministic():
     b = [host(x) for x in run_gpu("f32", *inp)]
     for x, y in zip(a, b):
         assert np.array_equal(x, y)
+
+
+# ---- the chunked tensor-core form (bf16, d = 128, no segments)
+
+def bwd_form(name):
+    import contextlib
+
+    @contextlib.contextmanager
+    def ctx():
+        prev = ops.set_bwd_kernel(name)
+        try:
+            yield
+        finally:
+            ops.set_bwd_kernel(prev)
+    return ctx()
+
+
+def check_bf16_grads(got, ref, what):
+    # fp16 products with fp32 accumulation: every output, dalpha and dbeta
+    # included, is held to the bf16 bounds (relative and RMS-scaled)
+    for g, r, n in zip(got, ref, NAMES):
+        assert_bf16(g, r, f"{what} {n}", abs_bound=False)
+
+
+@pytest.mark.parametrize("B,T,H,final_grad", [
+    (1, 1, 1, False),      # one position, a one-row chunk
+    (1, 64, 2, True),      # exactly one chunk
+    (2, 130, 2, True),     # ragged last chunk of 2 positions
+    (1, 257, 3, False),    # five chunks, last of one position
+])
+def test_tc_matches_adjoint_oracle(B, T, H, final_grad):
+    inp = case(1000 + T, B, T, H, 128, "bf16", False, final_grad)
+    with bwd_form("auto"):
+        got = [host(x) for x in run_gpu("bf16", *inp)]
+    check_bf16_grads(got, oracle_bwd(*inp), f"T={T}")
+
+
+def test_tc_zero_alphas_exact_dalpha():
+    """alpha = 0 at some positions (a full decay inside chunks and at a chunk
+    start): dalpha there is finite and matches the adjoint; the division-free
+    form needs no special case."""
+    inp = list(case(77, 1, 192, 2, 128, "bf16", False, True))
+    a = inp[3].copy()
+    a[0, [5, 64, 100, 101, 191], :] = 0.0
+    inp[3] = a
+    with bwd_form("auto"):
+        got = [host(x) for x in run_gpu("bf16", *inp)]
+    check_bf16_grads(got, oracle_bwd(*inp), "zero alphas")
+
+
+def test_tc_gradient_scale_invariance():
+    """The upstream gradients enter scaled by an exact power of two: d_o and
+    d_state_final multiplied by 2^-20 give the gradients multiplied by 2^-20
+    (the same bits), far below fp16's normal range unscaled."""
+    inp = list(case(33, 1, 130, 2, 128, "bf16", False, True))
+    with bwd_form("auto"):
+        a = [host(x) for x in run_gpu("bf16", *inp)]
+        inp[5] = inp[5] * 2.0 ** -20
+        inp[7] = inp[7] * 2.0 ** -20
+        b = [host(x) for x in run_gpu("bf16", *inp)]
+    for x, y, n in zip(a, b, NAMES):
+        assert np.array_equal(x * 2.0 ** -20, y), n
+
+
+def test_tc_agrees_with_scan_at_config_size():
+    """configs[1] shape (B=4, T=4096, H=16): the tensor-core form against the
+    fp32 reverse scan (itself pinned to the f64 adjoint above), same inputs."""
+    B, T, H, d = 4, 4096, 16, 128
+    g = torch.Generator(device="cuda").manual_seed(4096)
+    nrm = torch.nn.functional.normalize
+    q = nrm(torch.randn(B, T, H, d, device="cuda", generator=g), dim=-1).to(torch.bfloat16)
+    k = nrm(torch.randn(B, T, H, d, device="cuda", generator=g), dim=-1).to(torch.bfloat16)
+    v = torch.randn(B, T, H, d, device="cuda", generator=g).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn(B, T, H, device="cuda", generator=g))
+    alpha = torch.exp(-torch.nn.functional.softplus(torch.randn(B, T, H, device="cuda", generator=g) + 2))
+    d_o = torch.randn(B, T, H, d, device="cuda", generator=g).to(torch.bfloat16)
+    dsf = torch.randn(B, H, d, d, device="cuda", generator=g) * 0.1
+    with bwd_form("auto"):
+        tc = [host(x) for x in ops.gdr_scan_chunked_bwd(q, k, v, alpha, beta, d_o, d_state_final=dsf)]
+    with bwd_form("scan"):
+        sc = [host(x) for x in ops.gdr_scan_chunked_bwd(q, k, v, alpha, beta, d_o, d_state_final=dsf)]
+    check_bf16_grads(tc, sc, "configs[1]")
+
+
+def test_tc_deterministic():
+    inp = case(21, 2, 200, 2, 128, "bf16", False, True)
+    with bwd_form("auto"):
+        a = [host(x) for x in run_gpu("bf16", *inp)]
+        b = [host(x) for x in run_gpu("bf16", *inp)]
+    for x, y in zip(a, b):
+        assert np.array_equal(x, y)
