@@ -36,6 +36,14 @@ sys.path.insert(0, ROOT)
 
 B, T, H, D, CHUNK = 4, 4096, 16, 128, 64
 FLOP_PER_TOKEN_HEAD = 6 * D * D + 2 * CHUNK * (3 * D + 2 * D) + (2 / 3) * CHUNK * CHUNK  # 182,955
+# Backward products per 64-position chunk of a (sequence, head), in
+# multiply-adds: records [K; Q] K^T and W (1,572,864), forward state chain
+# V^T (T b)^T, S W^T, Delta^T pL K (2,621,440), adjoint chain dO^T M,
+# dS (pL K)^T, dDelta^T W, dO^T gamma Q (3,670,016), per-chunk gradients
+# (9,699,328: [K; Q] K^T, dO Delta^T, Delta dS, dO S0, (dM.P) K, (dM.P)^T Q,
+# dDelta S0, T^T dDelta, T^T dW, dDelta V^T, dW K^T, dT T^T, T^T E1,
+# dKK K twice, dP P^T); the triangular solve is left out.
+BWD_FLOP_PER_CHUNK = 2 * (1_572_864 + 2_621_440 + 3_670_016 + 9_699_328)
 DEC_N, DEC_SLOTS = 512, 1024
 VL_N, VL_SLOTS = 64, 96
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -550,8 +558,10 @@ def run_ours(args):
                                      "frac": round(pk_gbs / peaks["hbm_gbs"], 4),
                                      "kernel": "pack_tokens_kernel"}}}
 
-    # Backward of the scan at the prefill shape (fp32 reverse scan with state
-    # checkpoints every 8 positions): latency-bound, reported for its time.
+    # Backward of the scan at the prefill shape: the chunked tensor-core form
+    # (records, forward and adjoint state chains, per-chunk gradients), with
+    # the fp32 reverse scan (state checkpoints every 8 positions) timed
+    # beside it for reference.
     dO = torch.randn((B, T, H, D), device=dev, generator=gp).to(torch.bfloat16)
     bws_bytes = int(capi.lib().rhz_gdr_bwd_workspace_bytes(B, T, H, D))
     bws = torch.empty(bws_bytes, device=dev, dtype=torch.uint8)
@@ -566,12 +576,24 @@ def run_ours(args):
                   capi.RHZ_DTYPE_BF16, bws.data_ptr(), bws_bytes, sptr)
 
     bw_ms = timed(bwd, 3)
+    prev_form = ops.set_bwd_kernel("scan")
+    try:
+        scan_ms = timed(bwd, 1)
+    finally:
+        ops.set_bwd_kernel(prev_form)
+    bw_flops = BWD_FLOP_PER_CHUNK * B * H * ((T + CHUNK - 1) // CHUNK)
+    bw_tf = bw_flops / (bw_ms / 1e3) / 1e12
     backward = {"metric": "GDR backward tokens/s", "value": B * T * world / (bw_ms / 1e3),
                 "unit": "tokens/s", "ms_per_step": round(bw_ms, 4),
+                "algorithmic_flops": bw_flops,
+                "tensor": {"achieved": round(bw_tf, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                           "frac": round(bw_tf / peaks["bf16_tflops"], 4),
+                           "note": "mma.sync fp16 products against the tcgen05 bf16 GEMM peak"},
                 "config": {"workload": f"backward of the chunked prefill B={B} T={T} H={H} d={D}",
-                           "dtype": "bf16 inputs and gradients, fp32 arithmetic"},
-                "bound": "latency (a sequential reverse scan per (sequence, head) row block)",
-                "kernel": "gdr_bwd_kernel"}
+                           "dtype": "bf16 inputs and gradients; fp16 operands, fp32 accumulation"},
+                "kernels": ["gdr_bwdtc_rec_kernel", "gdr_bwdtc_chain_kernel<forward>",
+                            "gdr_bwdtc_chain_kernel<adjoint>", "gdr_bwdtc_grad_kernel"],
+                "fp32_scan_ms": round(scan_ms, 3)}
     del dO, bws, gq, gk, gv
     # Clock samples from inside the headline timed region and every timed
     # sub-measurement above (the headline region alone lasts a few ms).
@@ -787,6 +809,31 @@ def run_case(args):
 
         def fn():
             ops.gdr_scan_chunked(q, k, v, a, b)
+    elif args.case == "bwd":  # the backward at half the prefill batch (B=2, T=4096, H=16)
+        q, k, v, a, b = qkv(2, T, H, D)
+        d_o = torch.randn((2, T, H, D), device=dev, generator=g).to(torch.bfloat16)
+        ws_n = int(capi.lib().rhz_gdr_bwd_workspace_bytes(2, T, H, D))
+        ws = torch.empty(ws_n, device=dev, dtype=torch.uint8)
+
+        def fn():
+            ops.gdr_scan_chunked_bwd(q, k, v, a, b, d_o, workspace=ws)
+    elif args.case == "varlen":  # configs[3]: the varlen prefill line's packed stream
+        import numpy as np
+        lens = np.random.default_rng(8192).integers(1, 8193, size=VL_N)
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
+        ntok = int(lens.sum())
+        q, k, v, a, b = qkv(ntok, H, D)
+        pool = torch.randn((VL_SLOTS, H, D, D), device=dev, generator=g) * 0.02
+        slots = torch.randperm(VL_SLOTS, device=dev, generator=g)[:VL_N].to(torch.int32)
+        o = torch.empty_like(q)
+        ws_n = int(capi.lib().rhz_gdr_varlen_workspace_bytes(VL_N, H, D, capi.RHZ_DTYPE_BF16))
+        ws = torch.empty(max(ws_n, 1), device=dev, dtype=torch.uint8)
+
+        def fn():
+            capi.call("rhz_gdr_varlen_fwd", o.data_ptr(), pool.data_ptr(), slots.data_ptr(),
+                      cu.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), a.data_ptr(),
+                      b.data_ptr(), VL_N, ntok, VL_SLOTS, H, D, capi.RHZ_DTYPE_BF16, 0,
+                      ws.data_ptr(), ws_n, sptr)
     else:
         raise SystemExit(f"unknown case {args.case}")
     for _ in range(args.warmup):
@@ -817,7 +864,7 @@ def main():
     ap.add_argument("--slab", type=int, default=0,
                     help="--workload layer: overlap the all-gather with compute in slabs of this "
                          "many positions (a multiple of 64; 0 = one call, then one all-gather)")
-    ap.add_argument("--case", default=None, choices=["decode", "gather", "pack", "norm", "grid", "pair", "solo"],
+    ap.add_argument("--case", default=None, choices=["decode", "gather", "pack", "norm", "grid", "pair", "solo", "varlen", "bwd"],
                     help="launch one kernel at a profiling size instead of the benchmark")
     ap.add_argument("--traffic", type=float, default=None,
                     help="measured DRAM bytes per launch of the dominant kernel (ncu)")
