@@ -772,15 +772,10 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                     if (wg_sync_or(2, !ok)) { rs.failed = true; break; }
                     tc_fence_after();
                 }
-                // Stage k & 1 is free again: chunk k + 2's tiles, and its
-                // record once a producer has published it.
-                bool fok = true;
-                if (wt == 0 && nn.item >= 0) {
-                    issue_loads(k + 2, nn);
-                    fok = fetch_record(k + 2);
-                }
+                // Stage k & 1 is free again: chunk k + 2's tiles now, its
+                // record after chunk k's O rows (below).
+                if (wt == 0 && nn.item >= 0) issue_loads(k + 2, nn);
                 if (nn.item >= 0) ++loads_issued;
-                if (wg_sync_or(2, !fok)) { rs.failed = true; break; }
 
                 // ---- O rows of chunk k from O^T (lane i, column t), optionally
                 // RMS-normalised per head first (groupnorm_heads, norm.rs:48-60,
@@ -862,6 +857,17 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                             *reinterpret_cast<uint4 *>(orow + t * tok_stride + 8 * ch) =
                                 *reinterpret_cast<const uint4 *>(stg + t * HD + 8 * ch);
                     }
+                }
+                // ---- chunk k + 2's record into stage k & 1 once a producer
+                // has published it. It comes after chunk k's O rows: the next
+                // chunk's R1 waits for those (O^T read out), and a record that
+                // is late only holds up its own chunk, two rounds on, instead
+                // of the chain. (This barrier also keeps the staging tile's
+                // next writes after this chunk's reads.)
+                {
+                    bool fok = true;
+                    if (wt == 0 && nn.item >= 0) fok = fetch_record(k + 2);
+                    if (wg_sync_or(2, !fok)) { rs.failed = true; break; }
                 }
             }
         }
