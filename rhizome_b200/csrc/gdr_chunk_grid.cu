@@ -197,18 +197,18 @@ __device__ __forceinline__ void st_sw_f16(uint8_t *blk, int r, int e, float v) {
         __float2half_rn(v);
 }
 
-// Chain: one stage's Q, K and V tiles (16 KB each) bf16 -> fp16 in place, Q
-// rows (in B1) scaled by gamma_t and K rows (in B2) by P[C-1][s]. The stage
-// holds 3072 16-byte chunks: Q (B1 half h, rows 0..63), K (B2, contiguous),
-// V; this thread's are first, first + STRIDE, ... The swizzle permutes
-// chunks within a row only, so a chunk's row (and scale) follows from its
-// index.
-template <int STRIDE>
+// Chain: parts P0 .. P1 - 1 of one stage's Q, K and V tiles (16 KB each)
+// bf16 -> fp16 in place, Q rows (in B1) scaled by gamma_t and K rows (in B2)
+// by P[C-1][s]. The stage holds 3072 16-byte chunks: Q (B1 half h, rows
+// 0..63), K (B2, contiguous), V; this thread's are first, first + STRIDE,
+// ... The swizzle permutes chunks within a row only, so a chunk's row (and
+// scale) follows from its index.
+template <int STRIDE, int P0, int P1>
 __device__ __forceinline__ void chain_tiles_to_f16(uint8_t *stage, const float *gm, const float *pl,
                                                    int first) {
     static_assert(1024 % (8 * STRIDE) == 0, "batches of 8 chunks");
 #pragma unroll 1
-    for (int part = 0; part < 3; ++part) {
+    for (int part = P0; part < P1; ++part) {
 #pragma unroll 1
         for (int b = 0; b < 1024 / STRIDE; b += 8) {
             uint4 x[8];
@@ -459,6 +459,25 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
             tmem_st32u(trow + TM_OT + 32, z);
             tmem_wait_st();
         }
+        // This warpgroup converts the K and V tiles of chunks 1, 2, ... and
+        // the V tile of chunk 0 (warpgroup 1, busy with the O rows and the
+        // records, converts every Q tile and chunk 0's K): chunk kc's, once its
+        // tiles landed, into stage kc & 1, then its share of that chunk's
+        // conversion barrier. K's scale (P[C-1]) is in chunk kc's gate table,
+        // which warpgroup 1 wrote before its conversion arrival for chunk
+        // kc - 1, which this warpgroup has waited for.
+        auto convert_kv = [&](int kc) -> bool {
+            const bool ok = mbar_wait(&bar_load[kc & 1], (kc >> 1) & 1, p.poll_ns);
+            if (wg_sync_or(1, !ok)) return false;
+            if (kc == 0)
+                chain_tiles_to_f16<128, 2, 3>(smem, nullptr, nullptr, row);
+            else
+                chain_tiles_to_f16<128, 1, 3>(smem + (kc & 1) * C_STAGE, nullptr, gates(kc) + G_PL, row);
+            fence_proxy_async_smem();
+            mbar_arrive(&bar_conv[kc & 1]);
+            return true;
+        };
+        if (wk.first_from(chain, 0).item >= 0 && !convert_kv(0)) rs.failed = true;
         for (int64_t m = 0; !rs.failed; ++m) {
             const int64_t q = wk.pos(chain, m);
             if (q >= wk.n_items) break;
@@ -593,6 +612,11 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                                 make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
                     }
                 }
+                // ---- the next chunk's K and V tiles (under the next R1's other waits)
+                if (wk.after(chain, m, item, h, t0, t1, nch, c, 1).item >= 0 && !convert_kv(k + 1)) {
+                    rs.failed = true;
+                    break;
+                }
             }
         }
     } else if (tid == 256) {
@@ -621,7 +645,6 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                 // it has landed), tiles k in fp16, O^T of chunk k - 1 read out
                 // and cleared, S's fp16 image
                 bool ok = mbar_wait(&bar_full[k & 1], (k >> 1) & 1, p.poll_ns);
-                if (ok) st_release_gpu(consumed, k + 1);
                 ok = ok && mbar_wait(&bar_conv[k & 1], (k >> 1) & 1, p.poll_ns);
                 if (k >= 1) ok = ok && mbar_wait(&bar_ofree[(k - 1) & 1], ((k - 1) >> 1) & 1, p.poll_ns);
                 ok = ok && mbar_wait(bar_s16, k & 1, p.poll_ns);
@@ -636,6 +659,11 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                                 sdesc_sw128(st + CS_B1 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
                                 ID_R1, 1);
                 umma_commit(bar_r1);
+                // The record's ring slot is free again: the bulk copies that
+                // read it completed before this thread's (acquiring) wait on
+                // bar_full, so a relaxed store publishes it; a release store's
+                // GPU-scope fence cost ~1,200-2,000 cycles on this path.
+                st_relaxed_gpu(consumed, k + 1);
                 // ---- R2: [D_S | O^T] += Delta^T [K~ | M^T] (one N = 192 product)
                 if (!mbar_wait(bar_d16, k & 1, p.poll_ns)) { rs.failed = true; break; }
                 tc_fence_after();
@@ -667,12 +695,20 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
         // ------------------------------------------------ warpgroup 1: tiles, epilogue
         const int wt = tid - 128;
         int loads_issued = 0, loads_waited = 0, recs_issued = 0;
+        bool rec_pending = false;  // thread 0: the next chunk's record not fetched yet
         // Round kc's record: wait until a producer has published it in ring
         // slot kc % RING, then bulk-copy its pieces next to stage kc & 1's tiles.
-        auto fetch_record = [&](int kc) -> bool {
+        // (blocking: waits, bounded, for the record; otherwise returns at once
+        // with *fetched = false when it is not published yet)
+        auto fetch_record = [&](int kc, bool blocking = true, bool *fetched = nullptr) -> bool {
             const int slot = kc % RING;
             const int target = p.never_ready ? kc + 1 + (1 << 30) : kc + 1;
-            if (!poll_ge(p.ready + chain * RING + slot, target, p.abort_flag, p.poll_ns)) return false;
+            if (!blocking) {
+                *fetched = ld_acquire_gpu(p.ready + chain * RING + slot) >= target;
+                if (!*fetched) return true;
+            } else if (!poll_ge(p.ready + chain * RING + slot, target, p.abort_flag, p.poll_ns)) {
+                return false;
+            }
             fence_proxy_async_global();
             uint64_t *bar = &bar_full[kc & 1];
             uint8_t *stp = smem + (kc & 1) * C_STAGE;
@@ -698,9 +734,13 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
             tma_load_3d(stp + CS_V, tm_v, 0, r.h, t32, bar);
             tma_load_3d(stp + CS_V + 8192, tm_v, 64, r.h, t32, bar);
         };
+        // Q tiles (chunk 0: Q and K; warpgroup 0 converts the rest).
         auto convert = [&](int kc) {
             const float *g = gates(kc);
-            chain_tiles_to_f16<128>(smem + (kc & 1) * C_STAGE, g + G_GM, g + G_PL, wt);
+            if (kc == 0)
+                chain_tiles_to_f16<128, 0, 2>(smem, g + G_GM, g + G_PL, wt);
+            else
+                chain_tiles_to_f16<128, 0, 1>(smem + (kc & 1) * C_STAGE, g + G_GM, nullptr, wt);
             fence_proxy_async_smem();
         };
 
@@ -858,15 +898,27 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
                                 *reinterpret_cast<const uint4 *>(stg + t * HD + 8 * ch);
                     }
                 }
-                // ---- chunk k + 2's record into stage k & 1 once a producer
-                // has published it. It comes after chunk k's O rows: the next
-                // chunk's R1 waits for those (O^T read out), and a record that
-                // is late only holds up its own chunk, two rounds on, instead
-                // of the chain. (This barrier also keeps the staging tile's
-                // next writes after this chunk's reads.)
+                // ---- records. Chunk k + 1's, if it was not published when
+                // last tried: now it is needed (the next R1 waits for it), so
+                // wait for it. Chunk k + 2's into stage k & 1: taken if it is
+                // published, else left for the end of the next chunk, so that
+                // a late record holds up neither chunk k + 1's tile conversion
+                // nor chunk k + 1's O rows. Thread 0 alone tracks the pending
+                // record. (The barrier also keeps the staging tile's next
+                // writes after this chunk's reads.)
                 {
                     bool fok = true;
-                    if (wt == 0 && nn.item >= 0) fok = fetch_record(k + 2);
+                    if (wt == 0) {
+                        if (rec_pending) {
+                            fok = fetch_record(k + 1);
+                            rec_pending = false;
+                        }
+                        if (fok && nn.item >= 0) {
+                            bool fetched = false;
+                            fok = fetch_record(k + 2, false, &fetched);
+                            rec_pending = !fetched;
+                        }
+                    }
                     if (wg_sync_or(2, !fok)) { rs.failed = true; break; }
                 }
             }
@@ -1203,7 +1255,7 @@ __global__ void __launch_bounds__(NT, 1)
             uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C_OFF_BAR);
             for (int i = 0; i < CB_NUM; ++i) mbar_init(&bars[i], 1);  // loads, records, R1, R2
             for (int i = 0; i < 2; ++i) {
-                mbar_init(&bars[CB_CONV + i], 128);   // warpgroup 1 signals
+                mbar_init(&bars[CB_CONV + i], 256);   // both warpgroups signal (V tile by 0, Q and K by 1)
                 mbar_init(&bars[CB_OFREE + i], 128);
             }
             mbar_init(&bars[CB_S16], 128);            // warpgroup 0 signals

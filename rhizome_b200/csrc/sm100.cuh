@@ -416,6 +416,13 @@ __device__ __forceinline__ void st_release_gpu(int *p, int v) {
     asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// A relaxed store (GPU scope): no fence, for flags whose writer has already
+// ordered what they publish (e.g. after an mbarrier wait that saw the copies
+// that read a buffer complete).
+__device__ __forceinline__ void st_relaxed_gpu(int *p, int v) {
+    asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ int ld_relaxed_gpu(const int *p) {
     int v;
     asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
