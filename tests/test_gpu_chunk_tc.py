@@ -232,3 +232,26 @@ def test_device_status_clear_after_runs():
     q, k, v, a, b = dense_case(57, B, T, H)
     run_dense(q, k, v, a, b, B, T)
     assert not ops.device_status()
+
+
+def test_grid_few_items_many_rounds():
+    """8 items of 64 chunks: the grid form's producer contexts then take
+    tasks 35 rounds apart, so a context's next ring-slot wait depends on a
+    chain far ahead of the record it has just built; that record must be
+    published before such a wait (a held record would stall the chain until
+    the bounded waits gave up). Grid against the 2-CTA form within the bf16
+    tolerance, and no device timeout."""
+    from rhizome_b200 import capi
+    import ctypes
+    B, T, H = 2, 4096, 4
+    q, k, v, a, b = dense_case(57, B, T, H)
+    with chunk_form("grid"):
+        og, sg = run_dense(q, k, v, a, b, B, T)
+    with chunk_form("pair"):
+        op, sp = run_dense(q, k, v, a, b, B, T)
+    torch.cuda.synchronize()
+    flag = ctypes.c_int32(-1)
+    capi.call("rhz_device_status", ctypes.byref(flag), 1)
+    assert flag.value == 0
+    assert_bf16(host(og), host(op), "grid vs pair o")
+    assert_bf16(host(sg), host(sp), "grid vs pair state")
