@@ -997,12 +997,6 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
     RoleState rs{false};
     uint32_t mma_phase = 0;
     int loads_issued = 0, loads_waited = 0;
-    // Loads of the chunk after next, deferred into the next chunk's first
-    // phase (thread 128, whose warp has no table block there): the stage is
-    // free once that chunk's D1 and D_W are done.
-    bool ld_pending = false;
-    Ref ld_ref{-1, 0, 0, 0, 0, 0};
-    int ld_k = 0;
     int k = 0;
     GateIn gin{1.f, 1.f, 0.f, 0.f};  // warp 4: inputs of the next chunk's gate table
     Ref cur = sc.first_from(start, step);
@@ -1042,14 +1036,6 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             if (lt == 0 && ok) ok = poll_ge(p.consumed + cur.j, cur.r - RING + 1, p.abort_flag, p.poll_ns);
             if (csync_or(!ok)) { rs.failed = true; break; }
             tc_fence_after();
-        }
-        if (ld_pending) {
-            if (lt == 128) {
-                tc_fence_after();
-                issue_loads(ld_k, ld_ref);
-            }
-            ++loads_issued;
-            ld_pending = false;
         }
 
         // ---- A = beta P (K K^T) (fp32) and M = P (Q K^T) (record, fp16), 32 columns per thread
@@ -1190,6 +1176,12 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             mma_phase ^= 1u;
             tc_fence_after();
         }
+        // Stage k & 1 is free (this chunk's D1 and D_W are done): chunk k + 2's
+        // tiles go out now, under the W staging and the publish.
+        if (nn.item >= 0) {
+            if (lt == 128) issue_loads(k + 2, nn);
+            ++loads_issued;
+        }
         {
             // -W K-major [j half][t][64 j], staged (the T table is dead), then
             // copied into the record with 16-byte stores
@@ -1205,16 +1197,10 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         for (int i = lt; i < 16384 / 16; i += 256)
             reinterpret_cast<uint4 *>(rec + REC_W)[i] = reinterpret_cast<const uint4 *>(pst)[i];
         csync();
-        // ---- record complete: publish it; stage k & 1 is free (D1 and D_W
-        // are done), so chunk k + 2's loads go out in the next phase
+        // ---- record complete: publish it
         if (lt == 0) {
             fence_proxy_async_global();
             st_release_gpu(p.ready + cur.j * RING + slot, cur.r + 1);
-        }
-        if (nn.item >= 0) {
-            ld_pending = true;
-            ld_ref = nn;
-            ld_k = k + 2;
         }
         cur = nxt;
         nxt = nn;
@@ -1420,19 +1406,41 @@ GridWs grid_ws(int64_t n_items, bool packed) {
     return w;
 }
 
-// Chains: one per item up to a share of the SMs that balances the chains'
-// per-chunk time against the producers' (RHZ_GRID_CHAINS overrides it).
-int grid_chain_cap(int sms) {
+// Chains. Up to 45% of the SMs every item gets its own chain (one pass).
+// Beyond that a chain runs several items one after another:
+//   - equal-length items (the batched layout): the fewest chains that keep
+//     the pass count of the 45% split, leaving the rest of the SMs to the
+//     producers;
+//   - packed (ragged) items, balanced by longest-first scheduling: 35% of
+//     the SMs, near where a chain's per-chunk time (about 6.2K cycles)
+//     matches the record rate of the producers' two contexts (about 18.5K
+//     cycles a record each).
+// RHZ_GRID_CHAINS overrides the split.
+int grid_chains(int sms, int64_t items, bool packed) {
     static int env = -1;
     static std::once_flag once;
     std::call_once(once, [] {
         const char *e = getenv("RHZ_GRID_CHAINS");
         env = e ? atoi(e) : 0;
     });
-    int cap = env > 0 ? env : (sms * 45 + 50) / 100;
-    if (cap > MAX_CHAINS) cap = MAX_CHAINS;
-    if (cap > sms - 1) cap = sms - 1;
-    return cap < 1 ? 1 : cap;
+    int64_t nc;
+    if (env > 0) {
+        nc = env;
+    } else {
+        const int64_t hi = (static_cast<int64_t>(sms) * 45 + 50) / 100;
+        if (items <= hi) {
+            nc = items;
+        } else if (packed) {
+            nc = (static_cast<int64_t>(sms) * 35 + 50) / 100;
+        } else {
+            const int64_t passes = (items + hi - 1) / hi;
+            nc = (items + passes - 1) / passes;
+        }
+    }
+    if (nc > items) nc = items;
+    if (nc > MAX_CHAINS) nc = MAX_CHAINS;
+    if (nc > sms - 1) nc = sms - 1;
+    return nc < 1 ? 1 : static_cast<int>(nc);
 }
 
 // Test hook (rhz_gdr_set_wait_test): off, or every chain waits for a record
@@ -1506,8 +1514,7 @@ int launch_chunk_grid(const SeqArgs &a) {
     if (e != cudaSuccess || per_sm < 1)
         return set_error(RHZ_ERR_DEVICE, "gdr_chunk_grid_kernel does not fit an SM: %s", cudaGetErrorString(e));
     const int grid = sms;  // one CTA per SM (shared memory allows no second)
-    const int cap = grid_chain_cap(sms);
-    const int nc = static_cast<int>(items < cap ? items : cap);
+    const int nc = grid_chains(sms, items, packed);
 
     char *ws = static_cast<char *>(a.ws);
     e = cudaMemsetAsync(ws + w.ready, 0, w.flags_end - w.ready, a.stream);
