@@ -160,6 +160,11 @@ constexpr uint32_t ID_R2 = idesc_f16(128, 192, false, true);   // Delta^T [K~ | 
 
 // Record ring: RING slots of REC_BYTES per chain; flags in the workspace.
 constexpr int RING = 8;
+// Each chain's flags (ready[RING], consumed) sit on their own 128-byte line:
+// producers ahead of the chains poll them, and lines shared by several
+// chains turned those polls into one L2 hot spot.
+constexpr int FLAG_STRIDE = 32;
+static_assert(RING <= FLAG_STRIDE, "a chain's ready flags fit its line");
 constexpr int MAX_CHAINS = 128;
 
 struct GParams {
@@ -177,8 +182,8 @@ struct GParams {
     float norm_eps;
     // grid
     uint8_t *ring;        // [n_chains][RING][REC_BYTES]
-    int *ready;           // [n_chains][RING]: round + 1 of the record the slot holds
-    int *consumed;        // [n_chains]: rounds the chain has taken out of its ring
+    int *ready;           // [n_chains][FLAG_STRIDE]: round + 1 of the record ring slot i holds (i < RING)
+    int *consumed;        // [n_chains][FLAG_STRIDE]: rounds the chain has taken out of its ring
     int *abort_flag;      // set by any CTA whose bounded wait ran out
     const int32_t *off;   // packed streams: [items] first round of each item in its chain
     const int32_t *sched; // packed streams: [0] rounds of the longest chain, [1 + j] rounds of chain j
@@ -439,7 +444,7 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
     auto gates = [&](int kc) { return reinterpret_cast<float *>(smem + C_OFF_GATE) + (kc & 3) * G_SIZE; };
     auto stage = [&](int kc) { return sbase + (kc & 1) * C_STAGE; };
     const int chain = static_cast<int>(start);
-    int *consumed = p.consumed + chain;
+    int *consumed = p.consumed + chain * FLAG_STRIDE;
     RoleState rs{false};
 
     if (tid < 128) {
@@ -704,9 +709,9 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
             const int slot = kc % RING;
             const int target = p.never_ready ? kc + 1 + (1 << 30) : kc + 1;
             if (!blocking) {
-                *fetched = ld_acquire_gpu(p.ready + chain * RING + slot) >= target;
+                *fetched = ld_acquire_gpu(p.ready + chain * FLAG_STRIDE + slot) >= target;
                 if (!*fetched) return true;
-            } else if (!poll_ge(p.ready + chain * RING + slot, target, p.abort_flag, p.poll_ns)) {
+            } else if (!poll_ge(p.ready + chain * FLAG_STRIDE + slot, target, p.abort_flag, p.poll_ns)) {
                 return false;
             }
             fence_proxy_async_global();
@@ -997,6 +1002,7 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
     RoleState rs{false};
     uint32_t mma_phase = 0;
     int loads_issued = 0, loads_waited = 0;
+    int slot_seen = INT_MIN;  // thread 128: consumed flag of the next record's chain, read early
     int k = 0;
     GateIn gin{1.f, 1.f, 0.f, 0.f};  // warp 4: inputs of the next chunk's gate table
     Ref cur = sc.first_from(start, step);
@@ -1030,16 +1036,22 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         uint8_t *rec = p.ring + (static_cast<size_t>(cur.j) * RING + slot) * REC_BYTES;
 
         // ---- D1 of this chunk (issued during the previous one), and the ring
-        // slot: the chain has taken round r - RING out of it
-        {
-            bool ok = mbar_wait(bar_d1, k & 1);
-            if (lt == 0 && ok) ok = poll_ge(p.consumed + cur.j, cur.r - RING + 1, p.abort_flag, p.poll_ns);
-            if (csync_or(!ok)) { rs.failed = true; break; }
-            tc_fence_after();
-        }
+        // slot: the chain has taken round r - RING out of it. Thread 128, whose
+        // warp has no block in the A / M phase, checks the slot (after
+        // publishing the previous record) and its answer joins the barrier
+        // that ends the phase: nothing writes the slot before it. A flag value
+        // read during the previous record skips the poll when it already
+        // shows the slot free (the chain's copies out of the slot completed
+        // before it stored the flag).
+        const bool d1_ok = __all_sync(0xffffffffu, mbar_wait(bar_d1, k & 1));
+        tc_fence_after();
+        bool slot_ok = true;
+        if (lt == 128 && d1_ok && slot_seen < cur.r - RING + 1)
+            slot_ok = poll_ge_backoff(p.consumed + cur.j * FLAG_STRIDE, cur.r - RING + 1, p.abort_flag,
+                                      p.poll_ns);
 
         // ---- A = beta P (K K^T) (fp32) and M = P (Q K^T) (record, fp16), 32 columns per thread
-        {
+        if (d1_ok) {
             const bool qk = row >= 64;
             const int t = row & 63;
             const int s0 = 32 * half;
@@ -1084,7 +1096,7 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             }
         }
         tc_fence_before();
-        csync();
+        if (csync_or(!d1_ok || !slot_ok)) { rs.failed = true; break; }
         // M^T into the record; the T table's space is free again afterwards
         for (int i = lt; i < 8192 / 16; i += 256)
             reinterpret_cast<uint4 *>(rec + REC_MT)[i] = reinterpret_cast<const uint4 *>(pst)[i];
@@ -1182,6 +1194,7 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
             if (lt == 128) issue_loads(k + 2, nn);
             ++loads_issued;
         }
+        if (lt == 128 && nxt.item >= 0) slot_seen = ld_relaxed_gpu(p.consumed + nxt.j * FLAG_STRIDE);
         {
             // -W K-major [j half][t][64 j], staged (the T table is dead), then
             // copied into the record with 16-byte stores
@@ -1197,10 +1210,11 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         for (int i = lt; i < 16384 / 16; i += 256)
             reinterpret_cast<uint4 *>(rec + REC_W)[i] = reinterpret_cast<const uint4 *>(pst)[i];
         csync();
-        // ---- record complete: publish it
-        if (lt == 0) {
+        // ---- record complete: publish it (thread 128: its fence's wait for
+        // the record's stores runs under the next record's A / M phase)
+        if (lt == 128) {
             fence_proxy_async_global();
-            st_release_gpu(p.ready + cur.j * RING + slot, cur.r + 1);
+            st_release_gpu(p.ready + cur.j * FLAG_STRIDE + slot, cur.r + 1);
         }
         cur = nxt;
         nxt = nn;
@@ -1395,8 +1409,8 @@ GridWs grid_ws(int64_t n_items, bool packed) {
     GridWs w;
     const size_t ring = static_cast<size_t>(MAX_CHAINS) * RING * REC_BYTES;
     w.ready = up(ring);
-    w.consumed = up(w.ready + static_cast<size_t>(MAX_CHAINS) * RING * sizeof(int));
-    w.abort = up(w.consumed + static_cast<size_t>(MAX_CHAINS) * sizeof(int));
+    w.consumed = up(w.ready + static_cast<size_t>(MAX_CHAINS) * FLAG_STRIDE * sizeof(int));
+    w.abort = up(w.consumed + static_cast<size_t>(MAX_CHAINS) * FLAG_STRIDE * sizeof(int));
     w.sched = up(w.abort + sizeof(int));
     w.flags_end = up(w.sched + static_cast<size_t>(1 + MAX_CHAINS) * sizeof(int));
     const size_t ni = static_cast<size_t>(n_items > 0 ? n_items : 0);
@@ -1411,10 +1425,9 @@ GridWs grid_ws(int64_t n_items, bool packed) {
 //   - equal-length items (the batched layout): the fewest chains that keep
 //     the pass count of the 45% split, leaving the rest of the SMs to the
 //     producers;
-//   - packed (ragged) items, balanced by longest-first scheduling: 35% of
+//   - packed (ragged) items, balanced by longest-first scheduling: 39% of
 //     the SMs, near where a chain's per-chunk time (about 6.2K cycles)
-//     matches the record rate of the producers' two contexts (about 18.5K
-//     cycles a record each).
+//     matches the record rate of the producers' two contexts.
 // RHZ_GRID_CHAINS overrides the split.
 int grid_chains(int sms, int64_t items, bool packed) {
     static int env = -1;
@@ -1431,7 +1444,7 @@ int grid_chains(int sms, int64_t items, bool packed) {
         if (items <= hi) {
             nc = items;
         } else if (packed) {
-            nc = (static_cast<int64_t>(sms) * 35 + 50) / 100;
+            nc = (static_cast<int64_t>(sms) * 39 + 50) / 100;
         } else {
             const int64_t passes = (items + hi - 1) / hi;
             nc = (items + passes - 1) / passes;

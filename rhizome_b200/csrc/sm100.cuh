@@ -477,5 +477,24 @@ __device__ __forceinline__ bool poll_ge(const int *p, int target, const int *abo
     }
 }
 
+// poll_ge for waits that are not latency-critical (a producer ahead of its
+// consumer): the sleep between polls doubles from 64 ns to 1 us, so many
+// waiting threads put little load on the flag's L2 line.
+__device__ __forceinline__ bool poll_ge_backoff(const int *p, int target, const int *abort,
+                                                uint64_t limit_ns = 2000000000ull) {
+    if (ld_acquire_gpu(p) >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t ns = 64;
+    for (uint32_t i = 1;; ++i) {
+        __nanosleep(ns);
+        if (ns < 1024) ns <<= 1;
+        if (ld_acquire_gpu(p) >= target) return true;
+        if ((i & 15u) == 0) {
+            if (ld_relaxed_gpu(abort) != 0) return false;
+            if (globaltimer_ns() - t0 > limit_ns) return false;
+        }
+    }
+}
+
 }  // namespace sm100
 }  // namespace rhz
