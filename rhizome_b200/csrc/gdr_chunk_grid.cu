@@ -967,7 +967,7 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
     float *Tf = reinterpret_cast<float *>(smem + P_OFF_TF);
     float *Xf = reinterpret_cast<float *>(smem + P_OFF_X);
     uint8_t *th = smem + P_OFF_AF;  // T diag(beta gamma) hi, lo: the A table is dead by then
-    uint8_t *pst = smem + P_OFF_TF; // record pieces staged in the T table's space while it is dead
+    uint8_t *pst = smem + P_OFF_TF; // M^T staged in the T table's space while it is dead
     const uint32_t sbase = smem_u32(smem);
     auto csync = [&]() { nbar_sync(bar_id, 256); };
     auto csync_or = [&](bool x) { return nbar_sync_or(bar_id, 256, x); };
@@ -1196,19 +1196,19 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         }
         if (lt == 128 && nxt.item >= 0) slot_seen = ld_relaxed_gpu(p.consumed + nxt.j * FLAG_STRIDE);
         {
-            // -W K-major [j half][t][64 j], staged (the T table is dead), then
-            // copied into the record with 16-byte stores
+            // -W K-major [j half][t][64 j] straight into the record: lane j
+            // writes its 32 t's, and for each t a warp's 32 consecutive j fill
+            // one aligned 64-byte half of the 128-byte row (the swizzle
+            // permutes 16-byte chunks within aligned groups of four), two
+            // whole sectors per store instruction
             float x[32];
             tmem_ld32(trow + TM_W + 32 * half, x);
             tmem_wait_ld();
-            uint8_t *blk = pst + (row >> 6) * 8192;
+            uint8_t *blk = rec + REC_W + (row >> 6) * 8192;
 #pragma unroll
             for (int t = 0; t < 32; ++t) st_sw_f16(blk, 32 * half + t, row & 63, -x[t]);
         }
         tc_fence_before();
-        csync();
-        for (int i = lt; i < 16384 / 16; i += 256)
-            reinterpret_cast<uint4 *>(rec + REC_W)[i] = reinterpret_cast<const uint4 *>(pst)[i];
         csync();
         // ---- record complete: publish it (thread 128: its fence's wait for
         // the record's stores runs under the next record's A / M phase)
