@@ -202,6 +202,17 @@ __device__ __forceinline__ void st_sw_f16(uint8_t *blk, int r, int e, float v) {
         __float2half_rn(v);
 }
 
+// The same place, given the fp16 bits.
+__device__ __forceinline__ void st_sw_h(uint8_t *blk, int r, int e, uint16_t h) {
+    *reinterpret_cast<uint16_t *>(blk + r * 128 + (((e >> 3) ^ (r & 7)) << 4) + (e & 7) * 2) = h;
+}
+
+// Two floats as an fp16 pair (round to nearest even; the first in the low half).
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
 // Chain: parts P0 .. P1 - 1 of one stage's Q, K and V tiles (16 KB each)
 // bf16 -> fp16 in place, Q rows (in B1) scaled by gamma_t and K rows (in B2)
 // by P[C-1][s]. The stage holds 3072 16-byte chunks: Q (B1 half h, rows
@@ -967,7 +978,6 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
     float *Tf = reinterpret_cast<float *>(smem + P_OFF_TF);
     float *Xf = reinterpret_cast<float *>(smem + P_OFF_X);
     uint8_t *th = smem + P_OFF_AF;  // T diag(beta gamma) hi, lo: the A table is dead by then
-    uint8_t *pst = smem + P_OFF_TF; // M^T staged in the T table's space while it is dead
     const uint32_t sbase = smem_u32(smem);
     auto csync = [&]() { nbar_sync(bar_id, 256); };
     auto csync_or = [&](bool x) { return nbar_sync_or(bar_id, 256, x); };
@@ -1051,15 +1061,14 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                                       p.poll_ns);
 
         // ---- A = beta P (K K^T) (fp32) and M = P (Q K^T) (record, fp16), 32 columns per thread
-        if (d1_ok) {
-            const bool qk = row >= 64;
+        const bool qk = row >= 64;
+        // Warp-uniform: the whole 32 x 32 block lies above the diagonal.
+        const bool upper = half == 1 && (warp & 1) == 0;
+        uint32_t mt0[8] = {}, mt1[8] = {};  // qk threads: M^T[s][t] for s = 32 half + 0..15, + 16..31 (fp16 pairs)
+        if (d1_ok && !upper) {
             const int t = row & 63;
             const int s0 = 32 * half;
-            // Warp-uniform: the whole 32 x 32 block lies above the diagonal.
-            if (half == 1 && (warp & 1) == 0) {
-                if (qk)
-                    for (int s = 32; s < 64; ++s) st_sw_f16(pst, s, t, 0.f);
-            } else {
+            {
                 const float glt = g[G_GL + t];
                 const int zt = gz[t];
                 const float bt = qk ? 1.f : g[G_BE + t];
@@ -1085,7 +1094,10 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
                     }
                     if (qk) {
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) st_sw_f16(pst, sb + j, t, v[j]);  // M^T[s][t]
+                        for (int jp = 0; jp < 8; ++jp) {
+                            const uint32_t w = pack_f16x2(v[2 * jp], v[2 * jp + 1]);
+                            if (hp == 0) mt0[jp] = w; else mt1[jp] = w;
+                        }
                     } else {
 #pragma unroll
                         for (int j4 = 0; j4 < 4; ++j4)
@@ -1097,10 +1109,26 @@ __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, cons
         }
         tc_fence_before();
         if (csync_or(!d1_ok || !slot_ok)) { rs.failed = true; break; }
-        // M^T into the record; the T table's space is free again afterwards
-        for (int i = lt; i < 8192 / 16; i += 256)
-            reinterpret_cast<uint4 *>(rec + REC_MT)[i] = reinterpret_cast<const uint4 *>(pst)[i];
-        csync();
+        // M^T into the record straight from registers, now that the slot is
+        // free: for each s a warp's 32 consecutive t fill one aligned 64-byte
+        // half of the 128-byte row (two whole sectors per store instruction)
+        if (qk) {
+            const int t = row & 63;
+            uint8_t *mtb = rec + REC_MT;
+            if (upper) {
+#pragma unroll 4
+                for (int s = 32; s < 64; ++s) st_sw_h(mtb, s, t, 0);
+            } else {
+                const int s0 = 32 * half;
+#pragma unroll
+                for (int jp = 0; jp < 8; ++jp) {
+                    st_sw_h(mtb, s0 + 2 * jp, t, static_cast<uint16_t>(mt0[jp]));
+                    st_sw_h(mtb, s0 + 2 * jp + 1, t, static_cast<uint16_t>(mt0[jp] >> 16));
+                    st_sw_h(mtb, s0 + 16 + 2 * jp, t, static_cast<uint16_t>(mt1[jp]));
+                    st_sw_h(mtb, s0 + 17 + 2 * jp, t, static_cast<uint16_t>(mt1[jp] >> 16));
+                }
+            }
+        }
 
         // ---- diagonal 16 x 16 tiles of T (warps 0-3, one each) while warps
         // 4-7 zero tiles (0,1), (2,3) of T and wait for the next chunk's
