@@ -45,9 +45,10 @@
 //     16 x 16 tiles by the product formula, the rest by a 2 x 2 recursion on
 //     mma.sync), D_W = K^T (T diag(beta gamma))^T on tcgen05.
 // Records travel through a ring of RING slots per chain in the caller's
-// workspace (L2-resident: a few MB): the producer bulk-stores the record and
-// publishes the slot with a release flag; the chain acquires the flag, bulk-
-// loads the record into shared memory and releases the slot. Every product
+// workspace (L2-resident: a few MB): the producer writes the record's images
+// with generic stores and publishes the slot with a release flag; the chain
+// acquires the flag, bulk-loads the record into shared memory and releases
+// the slot. Each chain's flags sit on their own 128-byte line. Every product
 // takes fp16 operands except D1 (A and B of one MMA always share a type);
 // fp16 intermediates bound |q.k|, |v|, |S| to < 65504 (unit-norm keys, as
 // the reference specifies, keep them far below).
@@ -963,7 +964,11 @@ __device__ __forceinline__ RoleState chain_role(const CUtensorMap *tm_q, const C
 // k's record while the tiles of chunk k + 1 land and its D1 runs. A record is
 // written straight into its ring slot (generic stores of the swizzled fp16
 // images) once the chain has taken round r - RING out of that slot, and
-// published with a release flag when complete.
+// published with a release flag when complete. Thread 128, whose warp has no
+// block in the A / M phase, publishes each record and then checks the next
+// record's slot, under that phase; the phase's closing barrier carries its
+// answer, and nothing writes the slot before it. A record is therefore always
+// published before its producer waits on any chain.
 __device__ __forceinline__ RoleState producer_role(const CUtensorMap *tm_q, const CUtensorMap *tm_k,
                                                    const GParams &p, uint8_t *smem, const Sched &sc,
                                                    int64_t start, int64_t step, uint32_t tmem,
